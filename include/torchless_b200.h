@@ -1,0 +1,205 @@
+/*
+ * torchless_b200.h -- C ABI of the B200 (sm_100a) torchless hot path.
+ *
+ * Drop-in boundary for the reference's CPU backend (ryansenn/torchless).
+ * Every entry point cites the reference function it replaces.  Conventions:
+ *
+ *   - Output first, like the reference (src/common/kernels.h:11-29).
+ *   - Op-level entry points take DEVICE pointers and a cudaStream_t passed as
+ *     void* (NULL = the legacy default stream).  They are asynchronous.
+ *     In-place use (xout == x) is allowed wherever the reference allows it
+ *     (modules.cpp:61-62, 81, 105, 111).
+ *   - Model-level entry points take HOST buffers and are synchronous.
+ *   - Every call returns tl_status; nothing exits or aborts.  The reference
+ *     asserts (compiled out under NDEBUG) or calls std::exit(1)
+ *     (src/loader/parameters.cpp:13-26, 99-102); here the same conditions
+ *     return TL_ERR_* and tl_last_error() holds the message.
+ *   - Pointer/size arguments are plain C types; no torch types cross this ABI.
+ */
+#ifndef TORCHLESS_B200_H
+#define TORCHLESS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TL_API __attribute__((visibility("default")))
+
+typedef enum tl_status {
+    TL_OK = 0,
+    TL_ERR_INVALID_ARGUMENT = 1, /* shape/pointer checks (reference: assert)            */
+    TL_ERR_UNSUPPORTED = 2,      /* valid for the reference, not built here             */
+    TL_ERR_IO = 3,               /* open/stat/read/mmap failed (reference: std::exit)   */
+    TL_ERR_FORMAT = 4,           /* malformed header or tensor table                    */
+    TL_ERR_CUDA = 5,             /* CUDA runtime error                                  */
+    TL_ERR_OUT_OF_MEMORY = 6,
+    TL_ERR_CAPACITY = 7,         /* KV cache full (reference overruns silently)         */
+    TL_ERR_TIMEOUT = 8           /* a bounded device-side wait gave up                  */
+} tl_status;
+
+/* Message for the last failing call on this host thread ("" if none). */
+TL_API const char* tl_last_error(void);
+TL_API const char* tl_status_name(tl_status s);
+
+/* ------------------------------------------------------------------------ */
+/* Op level: src/common/kernels.h (bodies in src/backend/cpu/kernels.cpp).   */
+/* ------------------------------------------------------------------------ */
+
+/* kernels.h:11  matmul(Tensor<float>& xout, Tensor<float>& w, Tensor<float>& x)
+ * xout[n] = W[n,d] @ x[d], fp32 (kernels.cpp:6-19). */
+TL_API tl_status tl_matmul_f32(float* xout, const float* w, const float* x, size_t n, size_t d,
+                               void* stream);
+
+/* kernels.h:12  matmul(Tensor<float>& xout, Tensor<int8_t>& w, Tensor<float>& x)
+ * xout[i] = sum_j (w[i,j] / scales[n_scales*(i*d+j)/(n*d)]) * x[j]
+ * (kernels.cpp:21-33 with Tensor<int8_t>::get, tensor.cpp:101-104).
+ * `scales` are the stored export scales (127/absmax), n_scales of them. */
+TL_API tl_status tl_matmul_i8(float* xout, const int8_t* w, const float* scales, size_t n_scales,
+                              const float* x, size_t n, size_t d, void* stream);
+
+/* kernels.h:13  row_matmul(xout, x, w): xout[d] = x[n] @ W[n,d] (kernels.cpp:37-49). */
+TL_API tl_status tl_row_matmul(float* xout, const float* x, const float* w, size_t n, size_t d,
+                               void* stream);
+
+/* kernels.h:15  softmax(xout, x) over n elements (kernels.cpp:55-63). */
+TL_API tl_status tl_softmax(float* xout, const float* x, size_t n, void* stream);
+
+/* kernels.h:16  rope(xout, x, cos, sin): x is [n_heads, head_dim]; pairs
+ * (i, i + head_dim/2) of every head rotate by cos/sin[i] (kernels.cpp:78-95). */
+TL_API tl_status tl_rope(float* xout, const float* x, const float* cos_, const float* sin_,
+                         size_t n_heads, size_t head_dim, void* stream);
+
+/* kernels.h:18  silu(xout, x) = x / (1 + exp(-x)) (kernels.cpp:98-102). */
+TL_API tl_status tl_silu(float* xout, const float* x, size_t n, void* stream);
+
+/* kernels.h:20  float sum(x); the result is written to *out (device). */
+TL_API tl_status tl_sum(float* out, const float* x, size_t n, void* stream);
+
+/* kernels.h:22-23  add(xout, x, y) and add(xout, x, c). */
+TL_API tl_status tl_add(float* xout, const float* x, const float* y, size_t n, void* stream);
+TL_API tl_status tl_add_scalar(float* xout, const float* x, float c, size_t n, void* stream);
+
+/* kernels.h:25-26  mul(xout, x, y) and mul(xout, x, c). */
+TL_API tl_status tl_mul(float* xout, const float* x, const float* y, size_t n, void* stream);
+TL_API tl_status tl_mul_scalar(float* xout, const float* x, float c, size_t n, void* stream);
+
+/* kernels.h:28-29  pow(xout, x, e) and sqrt(xout, x). */
+TL_API tl_status tl_pow(float* xout, const float* x, int e, size_t n, void* stream);
+TL_API tl_status tl_sqrt(float* xout, const float* x, size_t n, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Module level pieces (src/model/mistral/modules.cpp, main.cpp,             */
+/* export_mistral.py), as device ops.                                        */
+/* ------------------------------------------------------------------------ */
+
+/* RMSNorm::forward (modules.cpp:31-46): xout = x * (1/sqrt(sum(x^2)/n + eps)) * g.
+ * The reference hard-codes eps = 1e-5f (modules.h:24). */
+TL_API tl_status tl_rmsnorm(float* xout, const float* x, const float* g, size_t n, float eps,
+                            void* stream);
+
+/* RotaryEmbedding::forward (modules.cpp:22-27): cos/sin[i] of inv_freq[i % n_freq] * pos
+ * for i < head_dim.  inv_freq from RotaryEmbedding::init_freq (modules.cpp:12-17). */
+TL_API tl_status tl_rotary(float* cos_, float* sin_, const float* inv_freq, size_t n_freq,
+                           size_t head_dim, size_t pos, void* stream);
+
+/* sample_max (main.cpp:10-21): index of the first strict maximum of logits[n],
+ * written to *out (device).  Uses a library-owned device workspace that is
+ * allocated on the first call on each device. */
+TL_API tl_status tl_argmax(uint32_t* out, const float* logits, size_t n, void* stream);
+
+/* MLP<T>::forward first half (modules.cpp:99-112), fused:
+ * out[i] = silu(W1[i,:] @ x) * (W3[i,:] @ x), int8 W1/W3 [n, d] with stored scales. */
+TL_API tl_status tl_mlp_gate_up(float* out, const int8_t* w1, const float* s1, const int8_t* w3,
+                                const float* s3, const float* x, size_t n, size_t d,
+                                void* stream);
+
+/* quantize (export_mistral.py:53-68): per group of `group` elements
+ * scales[g] = fl(fl(1/max|x|) * 127), q = round_half_even(x * scales[g]). */
+TL_API tl_status tl_quantize_i8(int8_t* q, float* scales, const float* x, size_t numel,
+                                size_t group, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Model level: Parameters + InferenceState + Model<T> on one device.        */
+/* ------------------------------------------------------------------------ */
+
+/* Config (src/loader/parameters.h:10-23). */
+typedef struct tl_config {
+    size_t hidden_size, intermediate_size, n_layers, n_heads, n_kv_heads, vocab_size, head_dim,
+        sliding_window, max_position_embeddings;
+    float rope_theta, norm_eps;
+    char quant[16];
+} tl_config;
+
+typedef struct tl_model_options {
+    int device;     /* CUDA device ordinal                                        */
+    size_t max_seq; /* KV cache capacity in positions; 0 -> 1024                  */
+    int use_graph;  /* 1: each decode step is one CUDA-graph replay (default)    */
+} tl_model_options;
+
+typedef struct tl_model tl_model;
+
+/* Parameters::load_parameters (parameters.cpp:95-129) + InferenceState(Config&)
+ * (inference_state.h:45-71) + Model<int8_t>(params) (modules.h:116-120).
+ * Reads the export_mistral.py binary, uploads every weight once to HBM and
+ * allocates the fp32 KV cache on the device.  opts may be NULL. */
+TL_API tl_status tl_model_load(const char* path, const tl_model_options* opts, tl_model** out);
+
+/* Same, from a host buffer holding the whole file (header + payload). */
+TL_API tl_status tl_model_load_buffer(const void* data, size_t size, const tl_model_options* opts,
+                                      tl_model** out);
+
+TL_API tl_status tl_model_destroy(tl_model* m);
+TL_API tl_status tl_model_config(const tl_model* m, tl_config* out);
+
+/* Model<T>::forward (modules.cpp:154-171) for one token at the current
+ * position, then pos++.  logits (host, vocab_size floats) and next_token
+ * (host; sample_max of the logits, main.cpp:10-21) are optional outputs. */
+TL_API tl_status tl_model_forward(tl_model* m, uint32_t token, float* logits, uint32_t* next_token);
+
+/* The greedy loop of main.cpp:69-77 on the device: forwards prompt[0..n_prompt-1]
+ * then n_new times forwards the last argmax; writes the n_new generated ids
+ * to out (host).  Only the ids cross the PCIe bus. */
+TL_API tl_status tl_model_generate(tl_model* m, const uint32_t* prompt, size_t n_prompt,
+                                   size_t n_new, uint32_t* out);
+
+/* InferenceState::pos (inference_state.h:12). */
+TL_API tl_status tl_model_get_pos(const tl_model* m, size_t* pos);
+TL_API tl_status tl_model_set_pos(tl_model* m, size_t pos);
+
+/* Layer<T>::forward (modules.cpp:118-143) on a host hidden state [hidden_size]
+ * at the current position (pos is not advanced), as in test_modules.cpp:3-24. */
+TL_API tl_status tl_model_layer_forward(tl_model* m, int layer, float* hidden);
+
+/* Reads the KV cache rows written by push_kv (inference_state.h:38-43) for
+ * (layer, pos): k and v are host buffers of n_kv_heads * head_dim floats. */
+TL_API tl_status tl_model_read_kv(const tl_model* m, int layer, size_t pos, float* k, float* v);
+
+/* Device time (ms, CUDA events on the model's stream) of n greedy decode steps
+ * starting from `token` at the current position, graph replays back to back;
+ * the generated ids go to out (host, may be NULL). */
+TL_API tl_status tl_model_time_decode(tl_model* m, uint32_t token, size_t n, uint32_t* out,
+                                      float* ms);
+
+/* Per-kernel device times (ms per launch, averaged over n eager decode steps
+ * with an event pair around every launch).  kinds[] receives up to max_kinds
+ * entries of {name, launches, total_ms}; *n_kinds the count. */
+typedef struct tl_kernel_time {
+    char name[32];
+    int launches;
+    double total_ms;
+    double bytes_per_launch; /* algorithmic bytes of one launch */
+} tl_kernel_time;
+TL_API tl_status tl_model_profile(tl_model* m, uint32_t token, size_t n, tl_kernel_time* kinds,
+                                  int max_kinds, int* n_kinds);
+
+/* Number of kernel launches one decode step issues (all of them this library's). */
+TL_API tl_status tl_model_launches_per_step(const tl_model* m, int* launches);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TORCHLESS_B200_H */

@@ -1,0 +1,171 @@
+"""Regenerates the golden fixtures in tests/golden/ from the reference itself.
+
+Run in a container that has the reference tree (default /root/reference):
+
+    python tests/golden/make_golden.py [--reference /root/reference]
+
+Writes:
+  reference_expected.json  weight-independent vectors of the reference's own
+                           fixture file test/mistral/expected.txt (inv_freq,
+                           cos0/sin0/cos3/sin3, rope0..3, norm_x/norm_g/norm_y)
+                           and the known-answer cases of
+                           test/mistral/test_cpu_kernels.cpp:32-105.
+  export_hashes.json       sha256 of the binaries produced by the reference's
+                           own export_mistral.py for the seeded TINY and SMALL
+                           models (torchless_b200.synthetic); the numpy writer
+                           must reproduce them byte for byte.
+  ref_greedy_<cfg>.npz     the reference's Model<int8_t> (oracle/_ref, built
+                           from its own sources) on those models: prompt,
+                           greedy ids and per-step logits.
+  ref_ops.npz              reference kernels.cpp ops on seeded inputs.
+
+The tests read only these files; nothing at test time touches the reference
+tree.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import subprocess
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+import oracle  # noqa: E402
+from torchless_b200 import synthetic as S  # noqa: E402
+from torchless_b200.binfmt import ModelFile  # noqa: E402
+
+WEIGHT_INDEPENDENT = ["inv_freq", "cos0", "sin0", "cos3", "sin3", "rope0", "rope1", "rope2", "rope3",
+                      "norm_x", "norm_g", "norm_y"]
+
+# Seeds and sizes of the checked models (shared with tests/conftest.py).
+MODELS = {"tiny": (S.TINY, 7), "small": (S.SMALL, 3)}
+PROMPT_LEN, N_NEW = 16, 24
+
+
+def read_expected(path: str) -> dict:
+    """Name line then value line, as load_expected_values (setup/context.cpp:22-39)."""
+    out = {}
+    with open(path) as f:
+        lines = f.read().split("\n")
+    i = 0
+    while i < len(lines):
+        name = lines[i].strip()
+        i += 1
+        if not name or name.startswith("#"):
+            continue
+        vals = [float(v) for v in lines[i].split()] if i < len(lines) else []
+        i += 1
+        out[name] = vals
+    return out
+
+
+def kats() -> dict:
+    """Known answers written in test_cpu_kernels.cpp (file:line)."""
+    return {
+        "matmul": {"src": "test/mistral/test_cpu_kernels.cpp:32-48",
+                   "w": [[1, 2, 3], [4, 5, 6]], "x": [10, 20, 30], "y": [140, 320]},
+        "row_matmul": {"src": "test/mistral/test_cpu_kernels.cpp:50-68",
+                       "w": [[1, 2], [3, 4], [5, 6]], "x": [10, 20, 30], "y": [220, 280]},
+        "softmax": {"src": "test/mistral/test_cpu_kernels.cpp:71-85",
+                    "x": [1.0, 2.0, 3.0], "y": [0.09003057, 0.24472848, 0.66524094]},
+        "silu": {"src": "test/mistral/test_cpu_kernels.cpp:88-105",
+                 "x": [-2.0, -1.0, 0.0, 1.0, 2.0], "y": [-0.2384, -0.2689, 0.0, 0.7311, 1.7616]},
+        "rope_input": {"src": "test/mistral/test_cpu_kernels.cpp:4-29",
+                       "rule": "q[i] = (i % 128) / 256, shape [1, 128], positions 0..3"},
+        "tolerance": {"src": "test/mistral/setup/context.cpp:41-45", "atol": 5e-2},
+    }
+
+
+def sha256(b) -> str:
+    return hashlib.sha256(bytes(b)).hexdigest()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    ref = args.reference
+
+    exp = read_expected(os.path.join(ref, "test/mistral/expected.txt"))
+    with open(os.path.join(HERE, "reference_expected.json"), "w") as f:
+        json.dump({"source": "test/mistral/expected.txt",
+                   "vectors": {k: exp[k] for k in WEIGHT_INDEPENDENT},
+                   "kats": kats()}, f)
+
+    oracle.build(reference=True)
+    hashes = {}
+    for name, (cfg, seed) in MODELS.items():
+        tmp = tempfile.mkdtemp()
+        tensors = dict(S.numpy_tensors(cfg, seed=seed, norm="random"))
+        S.write_hf_dir(os.path.join(tmp, "hf"), cfg, tensors)
+        out = os.path.join(tmp, "ref.bin")
+        subprocess.run([sys.executable, os.path.join(ref, "export_mistral.py"), "--model_dir",
+                        os.path.join(tmp, "hf"), "--out", out, "--quant", "int8"], check=True,
+                       capture_output=True)
+        ref_bytes = np.fromfile(out, dtype=np.uint8)
+        mine = S.make_numpy_model(cfg, seed=seed, norm="random").buf
+        assert np.array_equal(ref_bytes, mine), f"numpy exporter differs from export_mistral.py ({name})"
+        hashes[name] = {"seed": seed, "norm": "random", "sha256": sha256(ref_bytes), "size": int(ref_bytes.size)}
+
+        rng = np.random.default_rng(1000 + seed)
+        prompt = rng.integers(0, cfg["vocab_size"], PROMPT_LEN).astype(np.int64)
+        rm = oracle.RefModel(ref_bytes, max_seq=PROMPT_LEN + N_NEW + 8)
+        ids, logits = oracle.greedy(rm, prompt.tolist(), N_NEW)
+        rm.close()
+        np.savez_compressed(os.path.join(HERE, f"ref_greedy_{name}.npz"), prompt=prompt,
+                            ids=np.array(ids, dtype=np.int64), logits=np.stack(logits))
+
+    with open(os.path.join(HERE, "export_hashes.json"), "w") as f:
+        json.dump(hashes, f, indent=1)
+
+    # Op-level outputs of the reference kernels on seeded inputs.
+    L = oracle.ref_lib()
+    rng = np.random.default_rng(42)
+    ops = {}
+    n, d = 48, 320
+    q = rng.integers(-127, 128, (n, d), dtype=np.int8)
+    for tag, ns in (("g64", n * d // 64), ("g80", n * d // 80), ("g7", 7)):
+        s = np.abs(rng.standard_normal(ns).astype(np.float32)) * 0.01 + 0.001
+        x = rng.standard_normal(d).astype(np.float32)
+        y = np.zeros(n, np.float32)
+        L.ref_matmul_i8(y.ctypes.data, q.ctypes.data, s.ctypes.data, ns, x.ctypes.data, n, d)
+        ops[f"i8_{tag}_s"], ops[f"i8_{tag}_x"], ops[f"i8_{tag}_y"] = s, x, y
+    ops["i8_q"] = q
+    w = rng.standard_normal((7, 33)).astype(np.float32)
+    x = rng.standard_normal(33).astype(np.float32)
+    y = np.zeros(7, np.float32)
+    L.ref_matmul_f32(y.ctypes.data, w.ctypes.data, x.ctypes.data, 7, 33)
+    ops.update(f32_w=w, f32_x=x, f32_y=y)
+    w = rng.standard_normal((9, 17)).astype(np.float32)
+    x = rng.standard_normal(9).astype(np.float32)
+    y = np.zeros(17, np.float32)
+    L.ref_row_matmul(y.ctypes.data, x.ctypes.data, w.ctypes.data, 9, 17)
+    ops.update(row_w=w, row_x=x, row_y=y)
+    x = (rng.standard_normal(13) * 3).astype(np.float32)
+    y = np.zeros(13, np.float32)
+    L.ref_softmax(y.ctypes.data, x.ctypes.data, 13)
+    ops.update(softmax_x=x, softmax_y=y)
+    x = rng.standard_normal((3, 16)).astype(np.float32)
+    c = rng.standard_normal(16).astype(np.float32)
+    sn = rng.standard_normal(16).astype(np.float32)
+    y = np.zeros((3, 16), np.float32)
+    L.ref_rope(y.ctypes.data, x.ctypes.data, c.ctypes.data, sn.ctypes.data, 3, 16)
+    ops.update(rope_x=x, rope_c=c, rope_s=sn, rope_y=y)
+    x = (rng.standard_normal(11) * 4).astype(np.float32)
+    y = np.zeros(11, np.float32)
+    L.ref_silu(y.ctypes.data, x.ctypes.data, 11)
+    ops.update(silu_x=x, silu_y=y)
+    np.savez_compressed(os.path.join(HERE, "ref_ops.npz"), **ops)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

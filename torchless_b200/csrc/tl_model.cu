@@ -1,0 +1,809 @@
+// tl_model.cu -- device-resident Mistral model behind the model-level C ABI.
+//
+// Stands in for three reference types at once:
+//   Parameters      (src/loader/parameters.cpp:95-155): parses the same binary
+//                   header, but uploads every tensor once into HBM instead of
+//                   keeping views into an mmap;
+//   InferenceState  (src/model/mistral/inference_state.h): fp32 KV cache
+//                   [L][KV][max_seq][hd] and all activations live on the
+//                   device; `pos` is a device counter mirrored on the host;
+//   Model<int8_t>   (src/model/mistral/modules.cpp:118-171): one decode step is
+//                   a fixed sequence of 2 + 5 L kernel launches, captured once
+//                   into a CUDA graph with programmatic dependent launch
+//                   between kernels and replayed per token.
+//
+// HBM layout (per layer, 256-byte aligned blocks):
+//   int8   [q_proj; k_proj; v_proj] rows concatenated   [(H + 2 KV) hd, D]
+//          o_proj [D, H hd], gate_proj [F, D], up_proj [F, D], down_proj [D, F]
+//   fp32   1/scale for each of the above (same order as the file's scales)
+//          input/post-attention norm gains [D]
+// global:  embedding [V, D], final norm [D], lm_head [V, D] (fp32, as exported)
+//
+// Per step: embed -> L x {qkv(+RMSNorm), attention(+RoPE, push_kv),
+// o_proj(+residual), gate/up(+RMSNorm, SiLU*up), down_proj(+residual)}
+// -> lm_head(+RMSNorm, argmax, pos++).
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cerrno>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "tl_common.cuh"
+#include "tl_gemv.cuh"
+#include "tl_json.h"
+#include "tl_kernels.h"
+
+namespace tl {
+namespace {
+
+struct TensorRec {
+    std::string dtype;
+    std::vector<int64_t> shape;
+    uint64_t offset = 0, scale_offset = 0, scale_size = 0;
+    bool has_scales = false;
+    uint64_t numel() const {
+        uint64_t n = 1;
+        for (auto d : shape) n *= static_cast<uint64_t>(d);
+        return n;
+    }
+};
+
+struct Header {
+    tl_config cfg = {};
+    std::map<std::string, TensorRec> tensors;
+    const uint8_t* payload = nullptr;
+    uint64_t payload_size = 0;
+};
+
+// std::stoi / std::stof semantics of Parameters::load_config
+// (parameters.cpp:32-47): metadata values are strings.
+bool meta_num(const JValue& m, const char* key, double& out) {
+    const JValue* v = m.get(key);
+    if (!v) return false;
+    if (v->type == JValue::Str) {
+        char* e = nullptr;
+        out = std::strtod(v->s.c_str(), &e);
+        return e != v->s.c_str();
+    }
+    if (v->is_num()) {
+        out = v->f;
+        return true;
+    }
+    return false;
+}
+
+tl_status parse_header(const uint8_t* data, size_t size, Header& h) {
+    if (size < 8) return set_error(TL_ERR_FORMAT, "model binary shorter than its 8-byte header length");
+    uint64_t hsize = 0;
+    std::memcpy(&hsize, data, 8);
+    if (hsize > size - 8) return set_error(TL_ERR_FORMAT, "header length %llu exceeds the file (%zu bytes)",
+                                           static_cast<unsigned long long>(hsize), size);
+    // The header is zero-padded to a 64-byte boundary (export_mistral.py:145-150);
+    // the reference parses up to the first NUL (parameters.cpp:108-112).
+    size_t jlen = 0;
+    while (jlen < hsize && data[8 + jlen] != 0) jlen++;
+    JValue root;
+    std::string err;
+    JsonParser parser(reinterpret_cast<const char*>(data + 8), jlen);
+    if (!parser.parse(root, err)) return set_error(TL_ERR_FORMAT, "header JSON: %s", err.c_str());
+    const JValue* meta = root.get("metadata");
+    const JValue* tens = root.get("tensors");
+    if (!meta || meta->type != JValue::Obj || !tens || tens->type != JValue::Obj)
+        return set_error(TL_ERR_FORMAT, "header lacks metadata/tensors objects");
+
+    double v[9];
+    const char* keys[9] = {"hidden_size", "intermediate_size", "n_layers", "n_heads", "n_kv_heads",
+                           "vocab_size", "max_position_embeddings", "rope_theta", "norm_eps"};
+    for (int k = 0; k < 9; k++)
+        if (!meta_num(*meta, keys[k], v[k])) return set_error(TL_ERR_FORMAT, "metadata.%s missing or not a number", keys[k]);
+    tl_config& c = h.cfg;
+    c.hidden_size = static_cast<size_t>(v[0]);
+    c.intermediate_size = static_cast<size_t>(v[1]);
+    c.n_layers = static_cast<size_t>(v[2]);
+    c.n_heads = static_cast<size_t>(v[3]);
+    c.n_kv_heads = static_cast<size_t>(v[4]);
+    c.vocab_size = static_cast<size_t>(v[5]);
+    c.max_position_embeddings = static_cast<size_t>(v[6]);
+    c.rope_theta = static_cast<float>(v[7]);
+    c.norm_eps = static_cast<float>(v[8]);
+    double sw = 0;
+    c.sliding_window = meta_num(*meta, "sliding_window", sw) ? static_cast<size_t>(sw) : 0;
+    if (c.n_heads == 0 || c.hidden_size == 0) return set_error(TL_ERR_FORMAT, "hidden_size/n_heads must be positive");
+    c.head_dim = c.hidden_size / c.n_heads;  // parameters.cpp:45
+    const JValue* q = meta->get("quant");
+    std::snprintf(c.quant, sizeof(c.quant), "%s", (q && q->type == JValue::Str) ? q->s.c_str() : "");
+
+    for (const auto& kv : tens->obj) {
+        const JValue& t = kv.second;
+        TensorRec r;
+        const JValue* dt = t.get("dtype");
+        const JValue* sh = t.get("shape");
+        const JValue* off = t.get("offset");
+        if (!dt || dt->type != JValue::Str || !sh || sh->type != JValue::Arr || !off || !off->is_num())
+            return set_error(TL_ERR_FORMAT, "tensor %s: missing dtype/shape/offset", kv.first.c_str());
+        r.dtype = dt->s;
+        for (const auto& d : sh->arr) {
+            if (!d.is_num() || d.i <= 0) return set_error(TL_ERR_FORMAT, "tensor %s: bad shape", kv.first.c_str());
+            r.shape.push_back(d.i);
+        }
+        r.offset = static_cast<uint64_t>(off->i);
+        if (r.dtype == "int8") {
+            const JValue* so = t.get("scale_offset");
+            const JValue* ss = t.get("scale_size");
+            if (!so || !so->is_num() || !ss || !ss->is_num())
+                return set_error(TL_ERR_FORMAT, "tensor %s: int8 without scales", kv.first.c_str());
+            r.scale_offset = static_cast<uint64_t>(so->i);
+            r.scale_size = static_cast<uint64_t>(ss->i);
+            r.has_scales = true;
+        } else if (r.dtype != "f32") {
+            return set_error(TL_ERR_FORMAT, "tensor %s: unknown dtype %s", kv.first.c_str(), r.dtype.c_str());
+        }
+        h.tensors[kv.first] = r;
+    }
+    h.payload = data + 8 + hsize;
+    h.payload_size = size - 8 - hsize;
+    return TL_OK;
+}
+
+// Bump allocator over one cudaMalloc, 256-byte aligned pieces.
+struct DeviceArena {
+    char* base = nullptr;
+    size_t cap = 0, used = 0;
+    tl_status reserve(size_t bytes) {
+        cap = bytes;
+        cudaError_t e = cudaMalloc(&base, bytes > 0 ? bytes : 256);
+        if (e != cudaSuccess) {
+            base = nullptr;
+            return set_error(e == cudaErrorMemoryAllocation ? TL_ERR_OUT_OF_MEMORY : TL_ERR_CUDA,
+                             "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
+        }
+        return TL_OK;
+    }
+    template <typename T>
+    T* take(size_t count) {
+        const size_t bytes = (count * sizeof(T) + 255) & ~static_cast<size_t>(255);
+        if (used + bytes > cap) return nullptr;
+        T* p = reinterpret_cast<T*>(base + used);
+        used += bytes;
+        return p;
+    }
+    static size_t pad(size_t bytes) { return (bytes + 255) & ~static_cast<size_t>(255); }
+    void release() {
+        if (base) cudaFree(base);
+        base = nullptr;
+    }
+};
+
+__global__ void k_invert(float* s, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        s[i] = 1.0f / s[i];
+}
+
+struct LayerW {
+    int8_t *wqkv, *wo, *w1, *w3, *w2;
+    float *sqkv, *so, *s1, *s3, *s2;
+    float *g_in, *g_post;
+};
+
+struct Step {
+    std::string name;
+    std::function<double()> bytes;  // algorithmic bytes of this launch
+    std::function<tl_status(cudaStream_t, bool)> launch;
+};
+
+}  // namespace
+}  // namespace tl
+
+using namespace tl;
+
+struct tl_model {
+    tl_config cfg = {};
+    int device = 0;
+    size_t max_seq = 0;
+    int splits = 4;
+    bool use_graph = true;
+    bool pdl = true;
+    cudaStream_t stream = nullptr;
+    DeviceArena weights, state;
+    std::vector<LayerW> layers;
+    float *embed = nullptr, *norm = nullptr, *lm_head = nullptr;
+    float *kc = nullptr, *vc = nullptr, *cos_tab = nullptr, *sin_tab = nullptr;
+    float *h = nullptr, *qkv = nullptr, *ctx = nullptr, *act = nullptr, *logits = nullptr;
+    float *attn_part = nullptr, *am_v = nullptr;
+    unsigned *attn_cnt = nullptr, *am_cnt = nullptr, *d_pos = nullptr;
+    uint32_t *am_i = nullptr, *d_token = nullptr, *d_hist = nullptr, *d_prompt = nullptr;
+    uint32_t* h_pinned = nullptr;  // [2]: token in, token out
+    size_t pos = 0;
+    std::vector<Step> steps;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+};
+
+namespace tl {
+namespace {
+
+size_t layer_kv_floats(const tl_model* m) { return m->cfg.n_kv_heads * m->max_seq * m->cfg.head_dim; }
+
+tl_status check_shapes(const Header& h) {
+    const tl_config& c = h.cfg;
+    if (std::string(c.quant) != "int8")
+        return set_error(TL_ERR_UNSUPPORTED, "quant \"%s\": only int8 models (export_mistral.py --quant int8) are built",
+                         c.quant);
+    if (c.n_heads != 4 * c.n_kv_heads)
+        return set_error(TL_ERR_UNSUPPORTED,
+                         "n_heads (%zu) != 4 * n_kv_heads (%zu): the reference hard-codes kv head = h/4",
+                         c.n_heads, c.n_kv_heads);
+    if (c.head_dim * c.n_heads != c.hidden_size)
+        return set_error(TL_ERR_UNSUPPORTED, "hidden_size not divisible by n_heads");
+    if (!(c.head_dim == 32 || c.head_dim == 64 || c.head_dim == 128 || c.head_dim == 256))
+        return set_error(TL_ERR_UNSUPPORTED, "head_dim %zu not in {32, 64, 128, 256}", c.head_dim);
+    if (c.hidden_size % 512 || c.intermediate_size % 512 || c.hidden_size > 16384 || c.intermediate_size > 16384)
+        return set_error(TL_ERR_UNSUPPORTED,
+                         "hidden_size (%zu) and intermediate_size (%zu) must be multiples of 512, <= 16384",
+                         c.hidden_size, c.intermediate_size);
+    if (c.n_layers == 0 || c.vocab_size == 0) return set_error(TL_ERR_FORMAT, "empty model");
+    return TL_OK;
+}
+
+tl_status find(const Header& h, const std::string& name, const char* dtype, std::vector<int64_t> shape,
+               const TensorRec*& out) {
+    auto it = h.tensors.find(name);
+    if (it == h.tensors.end()) return set_error(TL_ERR_FORMAT, "tensor %s not found", name.c_str());
+    const TensorRec& r = it->second;
+    if (r.dtype != dtype)
+        return set_error(TL_ERR_FORMAT, "tensor %s has dtype %s, expected %s", name.c_str(), r.dtype.c_str(), dtype);
+    if (r.shape != shape) return set_error(TL_ERR_FORMAT, "tensor %s has an unexpected shape", name.c_str());
+    const uint64_t bytes = r.numel() * (r.dtype == "int8" ? 1 : 4);
+    if (r.offset > h.payload_size || bytes > h.payload_size - r.offset)
+        return set_error(TL_ERR_FORMAT, "tensor %s extends past the end of the file", name.c_str());
+    if (r.has_scales) {
+        if (r.scale_size * 64 != r.numel())
+            return set_error(TL_ERR_UNSUPPORTED, "tensor %s: %llu scales for %llu weights (group 64 expected)",
+                             name.c_str(), static_cast<unsigned long long>(r.scale_size),
+                             static_cast<unsigned long long>(r.numel()));
+        if (r.scale_offset > h.payload_size || r.scale_size * 4 > h.payload_size - r.scale_offset)
+            return set_error(TL_ERR_FORMAT, "scales of %s extend past the end of the file", name.c_str());
+    }
+    out = &r;
+    return TL_OK;
+}
+
+tl_status upload(void* dst, const Header& h, uint64_t offset, size_t bytes) {
+    TL_CUDA_TRY(cudaMemcpy(dst, h.payload + offset, bytes, cudaMemcpyHostToDevice));
+    return TL_OK;
+}
+
+tl_status build_steps(tl_model* m);
+tl_status capture_graph(tl_model* m);
+
+tl_status create_model(const uint8_t* data, size_t size, const tl_model_options* opts, tl_model** out) {
+    Header h;
+    TL_TRY(parse_header(data, size, h));
+    TL_TRY(check_shapes(h));
+    const tl_config& c = h.cfg;
+    const int64_t D = c.hidden_size, F = c.intermediate_size, H = c.n_heads, KV = c.n_kv_heads,
+                  HD = c.head_dim, V = c.vocab_size, L = c.n_layers;
+    const int64_t NQKV = (H + 2 * KV) * HD;
+
+    // Resolve and validate every tensor before touching the device.
+    struct LayerRecs { const TensorRec *q, *k, *v, *o, *g, *u, *d, *ni, *np; };
+    std::vector<LayerRecs> recs(L);
+    const TensorRec *emb, *nrm, *lmh;
+    TL_TRY(find(h, "model.embed_tokens.weight", "f32", {V, D}, emb));
+    TL_TRY(find(h, "model.norm.weight", "f32", {D}, nrm));
+    TL_TRY(find(h, "lm_head.weight", "f32", {V, D}, lmh));
+    for (int64_t l = 0; l < L; l++) {
+        const std::string p = "model.layers." + std::to_string(l) + ".";
+        LayerRecs& r = recs[l];
+        TL_TRY(find(h, p + "self_attn.q_proj.weight", "int8", {H * HD, D}, r.q));
+        TL_TRY(find(h, p + "self_attn.k_proj.weight", "int8", {KV * HD, D}, r.k));
+        TL_TRY(find(h, p + "self_attn.v_proj.weight", "int8", {KV * HD, D}, r.v));
+        TL_TRY(find(h, p + "self_attn.o_proj.weight", "int8", {D, H * HD}, r.o));
+        TL_TRY(find(h, p + "mlp.gate_proj.weight", "int8", {F, D}, r.g));
+        TL_TRY(find(h, p + "mlp.up_proj.weight", "int8", {F, D}, r.u));
+        TL_TRY(find(h, p + "mlp.down_proj.weight", "int8", {D, F}, r.d));
+        TL_TRY(find(h, p + "input_layernorm.weight", "f32", {D}, r.ni));
+        TL_TRY(find(h, p + "post_attention_layernorm.weight", "f32", {D}, r.np));
+    }
+
+    std::unique_ptr<tl_model> m(new tl_model());
+    m->cfg = c;
+    m->device = opts ? opts->device : 0;
+    m->max_seq = (opts && opts->max_seq) ? opts->max_seq : 1024;
+    m->use_graph = opts ? opts->use_graph != 0 : true;
+    if (const char* e = std::getenv("TL_NO_PDL")) m->pdl = (e[0] == '0');
+    if (m->max_seq > (1u << 24))
+        return set_error(TL_ERR_INVALID_ARGUMENT, "max_seq %zu too large (positions are exact in fp32 up to 2^24)",
+                         m->max_seq);
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    TL_CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    m->splits = static_cast<int>(std::min<size_t>(32, std::max<size_t>(4, m->max_seq / 256)));
+
+    // ---- weights arena ----
+    using A = DeviceArena;
+    size_t wbytes = A::pad(V * D * 4) * 2 + A::pad(D * 4);
+    const size_t per_layer = A::pad(NQKV * D) + A::pad(D * H * HD) + 2 * A::pad(F * D) + A::pad(D * F) +
+                             A::pad(NQKV * D / 64 * 4) + A::pad(D * H * HD / 64 * 4) + 2 * A::pad(F * D / 64 * 4) +
+                             A::pad(D * F / 64 * 4) + 2 * A::pad(D * 4);
+    wbytes += per_layer * L;
+    TL_TRY(m->weights.reserve(wbytes));
+    m->embed = m->weights.take<float>(V * D);
+    m->lm_head = m->weights.take<float>(V * D);
+    m->norm = m->weights.take<float>(D);
+    TL_TRY(upload(m->embed, h, emb->offset, V * D * 4));
+    TL_TRY(upload(m->lm_head, h, lmh->offset, V * D * 4));
+    TL_TRY(upload(m->norm, h, nrm->offset, D * 4));
+    m->layers.resize(L);
+    for (int64_t l = 0; l < L; l++) {
+        LayerW& w = m->layers[l];
+        const LayerRecs& r = recs[l];
+        w.wqkv = m->weights.take<int8_t>(NQKV * D);
+        w.wo = m->weights.take<int8_t>(D * H * HD);
+        w.w1 = m->weights.take<int8_t>(F * D);
+        w.w3 = m->weights.take<int8_t>(F * D);
+        w.w2 = m->weights.take<int8_t>(D * F);
+        w.sqkv = m->weights.take<float>(NQKV * D / 64);
+        w.so = m->weights.take<float>(D * H * HD / 64);
+        w.s1 = m->weights.take<float>(F * D / 64);
+        w.s3 = m->weights.take<float>(F * D / 64);
+        w.s2 = m->weights.take<float>(D * F / 64);
+        w.g_in = m->weights.take<float>(D);
+        w.g_post = m->weights.take<float>(D);
+        if (!w.g_post) return set_error(TL_ERR_OUT_OF_MEMORY, "weights arena too small (internal)");
+        // q, k, v rows back to back: one GEMV produces [q | k | v].
+        TL_TRY(upload(w.wqkv, h, r.q->offset, H * HD * D));
+        TL_TRY(upload(w.wqkv + H * HD * D, h, r.k->offset, KV * HD * D));
+        TL_TRY(upload(w.wqkv + (H + KV) * HD * D, h, r.v->offset, KV * HD * D));
+        TL_TRY(upload(w.sqkv, h, r.q->scale_offset, H * HD * D / 64 * 4));
+        TL_TRY(upload(w.sqkv + H * HD * D / 64, h, r.k->scale_offset, KV * HD * D / 64 * 4));
+        TL_TRY(upload(w.sqkv + (H + KV) * HD * D / 64, h, r.v->scale_offset, KV * HD * D / 64 * 4));
+        TL_TRY(upload(w.wo, h, r.o->offset, D * H * HD));
+        TL_TRY(upload(w.so, h, r.o->scale_offset, D * H * HD / 64 * 4));
+        TL_TRY(upload(w.w1, h, r.g->offset, F * D));
+        TL_TRY(upload(w.s1, h, r.g->scale_offset, F * D / 64 * 4));
+        TL_TRY(upload(w.w3, h, r.u->offset, F * D));
+        TL_TRY(upload(w.s3, h, r.u->scale_offset, F * D / 64 * 4));
+        TL_TRY(upload(w.w2, h, r.d->offset, D * F));
+        TL_TRY(upload(w.s2, h, r.d->scale_offset, D * F / 64 * 4));
+        TL_TRY(upload(w.g_in, h, r.ni->offset, D * 4));
+        TL_TRY(upload(w.g_post, h, r.np->offset, D * 4));
+        // Stored scales s = 127/absmax become 1/s: the GEMV multiplies.
+        const size_t ns[5] = {static_cast<size_t>(NQKV * D / 64), static_cast<size_t>(D * H * HD / 64),
+                              static_cast<size_t>(F * D / 64), static_cast<size_t>(F * D / 64),
+                              static_cast<size_t>(D * F / 64)};
+        float* sp[5] = {w.sqkv, w.so, w.s1, w.s3, w.s2};
+        for (int k = 0; k < 5; k++) k_invert<<<256, 256, 0, m->stream>>>(sp[k], ns[k]);
+        TL_TRY(check_launch("invert scales"));
+    }
+
+    // ---- state arena: KV cache, RoPE tables, activations, scratch ----
+    const size_t kv = L * layer_kv_floats(m.get());
+    const size_t half = HD / 2;
+    const int am_grid = gemv_f32_grid(V, D, true, true);
+    size_t sbytes = 2 * A::pad(kv * 4) + 2 * A::pad(m->max_seq * half * 4) + A::pad(D * 4) + A::pad(NQKV * 4) +
+                    A::pad(H * HD * 4) + A::pad(F * 4) + A::pad(V * 4) + A::pad(H * m->splits * (HD + 2) * 4) +
+                    A::pad(H * 4) + A::pad(am_grid * 4) * 2 + A::pad(4) * 3 + A::pad(m->max_seq * 4) * 2;
+    TL_TRY(m->state.reserve(sbytes));
+    TL_CUDA_TRY(cudaMemsetAsync(m->state.base, 0, sbytes, m->stream));
+    m->kc = m->state.take<float>(kv);
+    m->vc = m->state.take<float>(kv);
+    m->cos_tab = m->state.take<float>(m->max_seq * half);
+    m->sin_tab = m->state.take<float>(m->max_seq * half);
+    m->h = m->state.take<float>(D);
+    m->qkv = m->state.take<float>(NQKV);
+    m->ctx = m->state.take<float>(H * HD);
+    m->act = m->state.take<float>(F);
+    m->logits = m->state.take<float>(V);
+    m->attn_part = m->state.take<float>(H * m->splits * (HD + 2));
+    m->attn_cnt = m->state.take<unsigned>(H);
+    m->am_v = m->state.take<float>(am_grid);
+    m->am_i = m->state.take<uint32_t>(am_grid);
+    m->am_cnt = m->state.take<unsigned>(1);
+    m->d_pos = m->state.take<unsigned>(1);
+    m->d_token = m->state.take<uint32_t>(1);
+    m->d_hist = m->state.take<uint32_t>(m->max_seq);
+    m->d_prompt = m->state.take<uint32_t>(m->max_seq);
+    if (!m->d_prompt) return set_error(TL_ERR_OUT_OF_MEMORY, "state arena too small (internal)");
+
+    // RotaryEmbedding::init_freq + ::forward (modules.cpp:12-27) with the
+    // reference's float arithmetic and libm, for every position up front.
+    {
+        std::vector<float> inv(half), ct(m->max_seq * half), st(m->max_seq * half);
+        for (size_t i = 0; i < half; i++)
+            inv[i] = 1.0f / powf(c.rope_theta, static_cast<float>(i) / static_cast<float>(half));
+        for (size_t p = 0; p < m->max_seq; p++)
+            for (size_t i = 0; i < half; i++) {
+                const float a = inv[i] * static_cast<float>(p);
+                ct[p * half + i] = cosf(a);
+                st[p * half + i] = sinf(a);
+            }
+        TL_CUDA_TRY(cudaMemcpy(m->cos_tab, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice));
+        TL_CUDA_TRY(cudaMemcpy(m->sin_tab, st.data(), st.size() * 4, cudaMemcpyHostToDevice));
+    }
+    TL_CUDA_TRY(cudaMallocHost(&m->h_pinned, 4 * sizeof(uint32_t)));
+    TL_CUDA_TRY(cudaStreamSynchronize(m->stream));
+
+    TL_TRY(build_steps(m.get()));
+    if (m->use_graph) TL_TRY(capture_graph(m.get()));
+    *out = m.release();
+    return TL_OK;
+}
+
+// ---------------------------------------------------------------------------
+// The launch sequence of one decode step.
+// ---------------------------------------------------------------------------
+
+void add_layer_steps(tl_model* m, int l, std::vector<Step>& steps) {
+    const tl_config& c = m->cfg;
+    const int D = c.hidden_size, F = c.intermediate_size, H = c.n_heads, KV = c.n_kv_heads, HD = c.head_dim;
+    const int NQKV = (H + 2 * KV) * HD;
+    const LayerW* w = &m->layers[l];
+    const float eps = 1e-5f;  // RMSNorm::e, hard-coded in modules.h:24
+
+    steps.push_back({"gemv_qkv_rmsnorm",
+                     [=] { return double(NQKV) * D * (1 + 4.0 / 64) + 8.0 * D + 4.0 * NQKV; },
+                     [=](cudaStream_t s, bool pdl) {
+                         GemvI8Args a = {};
+                         a.w = w->wqkv; a.s = w->sqkv; a.x = m->h; a.g = w->g_in; a.eps = eps;
+                         a.y = m->qkv; a.n = NQKV; a.d = D;
+                         return launch_gemv_i8(a, I8Mode::Store, true, true, s, pdl);
+                     }});
+    steps.push_back({"attention_decode",
+                     [=] {
+                         const double npos = double(m->pos) + 1;
+                         return 2.0 * KV * npos * HD * 4 + 4.0 * NQKV + 4.0 * H * HD;
+                     },
+                     [=](cudaStream_t s, bool pdl) {
+                         AttnArgs a = {};
+                         a.qkv = m->qkv;
+                         a.k_cache = m->kc + static_cast<size_t>(l) * layer_kv_floats(m);
+                         a.v_cache = m->vc + static_cast<size_t>(l) * layer_kv_floats(m);
+                         a.cos_tab = m->cos_tab; a.sin_tab = m->sin_tab; a.pos = m->d_pos;
+                         a.ctx = m->ctx; a.part = m->attn_part; a.counters = m->attn_cnt;
+                         a.n_heads = H; a.n_kv_heads = KV; a.head_dim = HD;
+                         a.max_seq = static_cast<int>(m->max_seq); a.splits = m->splits;
+                         a.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
+                         return launch_attention(a, s, pdl);
+                     }});
+    steps.push_back({"gemv_o_residual",
+                     [=] { return double(D) * H * HD * (1 + 4.0 / 64) + 4.0 * H * HD + 8.0 * D; },
+                     [=](cudaStream_t s, bool pdl) {
+                         GemvI8Args a = {};
+                         a.w = w->wo; a.s = w->so; a.x = m->ctx; a.y = m->h; a.res = m->h;
+                         a.n = D; a.d = H * HD;
+                         return launch_gemv_i8(a, I8Mode::AddResidual, true, false, s, pdl);
+                     }});
+    steps.push_back({"gemv_gate_up_silu",
+                     [=] { return 2.0 * F * D * (1 + 4.0 / 64) + 8.0 * D + 4.0 * F; },
+                     [=](cudaStream_t s, bool pdl) {
+                         GemvI8Args a = {};
+                         a.w = w->w1; a.s = w->s1; a.w2 = w->w3; a.s2 = w->s3; a.x = m->h; a.g = w->g_post;
+                         a.eps = eps; a.y = m->act; a.n = F; a.d = D;
+                         return launch_gemv_i8(a, I8Mode::SwiGLU, true, true, s, pdl);
+                     }});
+    steps.push_back({"gemv_down_residual",
+                     [=] { return double(D) * F * (1 + 4.0 / 64) + 4.0 * F + 8.0 * D; },
+                     [=](cudaStream_t s, bool pdl) {
+                         GemvI8Args a = {};
+                         a.w = w->w2; a.s = w->s2; a.x = m->act; a.y = m->h; a.res = m->h;
+                         a.n = D; a.d = F;
+                         return launch_gemv_i8(a, I8Mode::AddResidual, true, false, s, pdl);
+                     }});
+}
+
+tl_status build_steps(tl_model* m) {
+    const tl_config& c = m->cfg;
+    const int D = c.hidden_size, V = c.vocab_size;
+    m->steps.clear();
+    m->steps.push_back({"embed", [=] { return 8.0 * D; },
+                        [=](cudaStream_t s, bool pdl) {
+                            return launch_embed(m->h, m->embed, m->d_token, D, s, pdl);
+                        }});
+    for (int l = 0; l < static_cast<int>(c.n_layers); l++) add_layer_steps(m, l, m->steps);
+    m->steps.push_back({"gemv_lm_head_argmax", [=] { return double(V) * D * 4 + 8.0 * D + 4.0 * V; },
+                        [=](cudaStream_t s, bool pdl) {
+                            GemvF32Args a = {};
+                            a.w = m->lm_head; a.x = m->h; a.g = m->norm; a.eps = 1e-5f; a.y = m->logits;
+                            a.n = V; a.d = D;
+                            a.part_v = m->am_v; a.part_i = m->am_i; a.counter = m->am_cnt;
+                            a.out_token = m->d_token; a.history = m->d_hist; a.pos = m->d_pos;
+                            return launch_gemv_f32(a, true, true, s, pdl);
+                        }});
+    return TL_OK;
+}
+
+tl_status run_steps_eager(tl_model* m) {
+    for (size_t i = 0; i < m->steps.size(); i++) TL_TRY(m->steps[i].launch(m->stream, m->pdl && i > 0));
+    return TL_OK;
+}
+
+tl_status capture_graph(tl_model* m) {
+    TL_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    tl_status st = run_steps_eager(m);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (st != TL_OK) {
+        if (g) cudaGraphDestroy(g);
+        return st;
+    }
+    if (e != cudaSuccess) return set_error(TL_ERR_CUDA, "graph capture failed: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&m->graph_exec, g, 0);
+    if (e != cudaSuccess) {
+        cudaGraphDestroy(g);
+        return set_error(TL_ERR_CUDA, "graph instantiate failed: %s", cudaGetErrorString(e));
+    }
+    m->graph = g;
+    return TL_OK;
+}
+
+tl_status run_step(tl_model* m) {
+    if (m->graph_exec) {
+        TL_CUDA_TRY(cudaGraphLaunch(m->graph_exec, m->stream));
+        return TL_OK;
+    }
+    return run_steps_eager(m);
+}
+
+tl_status set_token(tl_model* m, uint32_t token) {
+    if (token >= m->cfg.vocab_size)
+        return set_error(TL_ERR_INVALID_ARGUMENT, "token %u >= vocab_size %zu", token, m->cfg.vocab_size);
+    m->h_pinned[0] = token;
+    TL_CUDA_TRY(cudaMemcpyAsync(m->d_token, m->h_pinned, 4, cudaMemcpyHostToDevice, m->stream));
+    return TL_OK;
+}
+
+tl_status check_capacity(const tl_model* m, size_t steps) {
+    if (m->pos + steps > m->max_seq)
+        return set_error(TL_ERR_CAPACITY, "KV cache full: pos %zu + %zu steps > max_seq %zu", m->pos, steps,
+                         m->max_seq);
+    return TL_OK;
+}
+
+tl_status sync(tl_model* m) {
+    cudaError_t e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return set_error(TL_ERR_CUDA, "decode step failed: %s", cudaGetErrorString(e));
+    return TL_OK;
+}
+
+}  // namespace
+}  // namespace tl
+
+extern "C" {
+
+tl_status tl_model_load_buffer(const void* data, size_t size, const tl_model_options* opts, tl_model** out) {
+    clear_error();
+    TL_REQUIRE(data && out, "tl_model_load_buffer: null argument");
+    *out = nullptr;
+    return create_model(static_cast<const uint8_t*>(data), size, opts, out);
+}
+
+tl_status tl_model_load(const char* path, const tl_model_options* opts, tl_model** out) {
+    clear_error();
+    TL_REQUIRE(path && out, "tl_model_load: null argument");
+    *out = nullptr;
+    // Parameters::map_file (parameters.cpp:10-29): read-only private mapping.
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) return set_error(TL_ERR_IO, "cannot open %s: %s", path, std::strerror(errno));
+    struct stat st;
+    if (fstat(fd, &st) < 0) {
+        close(fd);
+        return set_error(TL_ERR_IO, "cannot stat %s: %s", path, std::strerror(errno));
+    }
+    const size_t size = static_cast<size_t>(st.st_size);
+    void* p = size ? mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0) : MAP_FAILED;
+    close(fd);
+    if (p == MAP_FAILED) return set_error(TL_ERR_IO, "cannot map %s (%zu bytes)", path, size);
+    const tl_status s = create_model(static_cast<const uint8_t*>(p), size, opts, out);
+    munmap(p, size);
+    return s;
+}
+
+tl_status tl_model_destroy(tl_model* m) {
+    clear_error();
+    if (!m) return TL_OK;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    m->weights.release();
+    m->state.release();
+    if (m->h_pinned) cudaFreeHost(m->h_pinned);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+    return TL_OK;
+}
+
+tl_status tl_model_config(const tl_model* m, tl_config* out) {
+    clear_error();
+    TL_REQUIRE(m && out, "tl_model_config: null argument");
+    *out = m->cfg;
+    return TL_OK;
+}
+
+tl_status tl_model_forward(tl_model* m, uint32_t token, float* logits, uint32_t* next_token) {
+    clear_error();
+    TL_REQUIRE(m, "tl_model_forward: null model");
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    TL_TRY(check_capacity(m, 1));
+    TL_TRY(set_token(m, token));
+    TL_TRY(run_step(m));
+    if (logits)
+        TL_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, m->stream));
+    if (next_token)
+        TL_CUDA_TRY(cudaMemcpyAsync(m->h_pinned + 1, m->d_token, 4, cudaMemcpyDeviceToHost, m->stream));
+    TL_TRY(sync(m));
+    m->pos++;
+    if (next_token) *next_token = m->h_pinned[1];
+    return TL_OK;
+}
+
+tl_status tl_model_generate(tl_model* m, const uint32_t* prompt, size_t n_prompt, size_t n_new, uint32_t* out) {
+    clear_error();
+    TL_REQUIRE(m && prompt && n_prompt > 0 && (out || n_new == 0), "tl_model_generate: bad arguments");
+    TL_REQUIRE(n_new > 0, "tl_model_generate: n_new must be positive (the last prompt token is forwarded by it)");
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    TL_TRY(check_capacity(m, n_prompt - 1 + n_new));
+    for (size_t i = 0; i < n_prompt; i++)
+        TL_REQUIRE(prompt[i] < m->cfg.vocab_size, "prompt token %u >= vocab_size", prompt[i]);
+    TL_CUDA_TRY(cudaMemcpyAsync(m->d_prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, m->stream));
+    // main.cpp:69-71: forward every prompt token but the last.
+    for (size_t i = 0; i + 1 < n_prompt; i++) {
+        TL_CUDA_TRY(cudaMemcpyAsync(m->d_token, m->d_prompt + i, 4, cudaMemcpyDeviceToDevice, m->stream));
+        TL_TRY(run_step(m));
+    }
+    // main.cpp:73-77: t = last prompt token; n_new times t = argmax(forward(t)).
+    TL_CUDA_TRY(cudaMemcpyAsync(m->d_token, m->d_prompt + n_prompt - 1, 4, cudaMemcpyDeviceToDevice, m->stream));
+    const size_t first = m->pos + n_prompt - 1;
+    for (size_t i = 0; i < n_new; i++) TL_TRY(run_step(m));
+    TL_CUDA_TRY(cudaMemcpyAsync(out, m->d_hist + first, n_new * 4, cudaMemcpyDeviceToHost, m->stream));
+    TL_TRY(sync(m));
+    m->pos += n_prompt - 1 + n_new;
+    return TL_OK;
+}
+
+tl_status tl_model_get_pos(const tl_model* m, size_t* pos) {
+    clear_error();
+    TL_REQUIRE(m && pos, "tl_model_get_pos: null argument");
+    *pos = m->pos;
+    return TL_OK;
+}
+
+tl_status tl_model_set_pos(tl_model* m, size_t pos) {
+    clear_error();
+    TL_REQUIRE(m, "tl_model_set_pos: null model");
+    if (pos > m->max_seq) return set_error(TL_ERR_CAPACITY, "pos %zu > max_seq %zu", pos, m->max_seq);
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    m->h_pinned[2] = static_cast<uint32_t>(pos);
+    TL_CUDA_TRY(cudaMemcpyAsync(m->d_pos, m->h_pinned + 2, 4, cudaMemcpyHostToDevice, m->stream));
+    TL_TRY(sync(m));
+    m->pos = pos;
+    return TL_OK;
+}
+
+tl_status tl_model_layer_forward(tl_model* m, int layer, float* hidden) {
+    clear_error();
+    TL_REQUIRE(m && hidden, "tl_model_layer_forward: null argument");
+    TL_REQUIRE(layer >= 0 && static_cast<size_t>(layer) < m->cfg.n_layers, "layer %d out of range", layer);
+    TL_TRY(check_capacity(m, 1));
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    const size_t D = m->cfg.hidden_size;
+    TL_CUDA_TRY(cudaMemcpyAsync(m->h, hidden, D * 4, cudaMemcpyHostToDevice, m->stream));
+    std::vector<Step> steps;
+    add_layer_steps(m, layer, steps);
+    for (auto& s : steps) TL_TRY(s.launch(m->stream, false));
+    TL_CUDA_TRY(cudaMemcpyAsync(hidden, m->h, D * 4, cudaMemcpyDeviceToHost, m->stream));
+    return sync(m);
+}
+
+tl_status tl_model_read_kv(const tl_model* m, int layer, size_t pos, float* k, float* v) {
+    clear_error();
+    TL_REQUIRE(m && k && v, "tl_model_read_kv: null argument");
+    TL_REQUIRE(layer >= 0 && static_cast<size_t>(layer) < m->cfg.n_layers && pos < m->max_seq,
+               "tl_model_read_kv: layer/pos out of range");
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    const size_t hd = m->cfg.head_dim;
+    for (size_t kh = 0; kh < m->cfg.n_kv_heads; kh++) {
+        const size_t off = layer * layer_kv_floats(m) + (kh * m->max_seq + pos) * hd;
+        TL_CUDA_TRY(cudaMemcpyAsync(k + kh * hd, m->kc + off, hd * 4, cudaMemcpyDeviceToHost, m->stream));
+        TL_CUDA_TRY(cudaMemcpyAsync(v + kh * hd, m->vc + off, hd * 4, cudaMemcpyDeviceToHost, m->stream));
+    }
+    return sync(const_cast<tl_model*>(m));
+}
+
+tl_status tl_model_time_decode(tl_model* m, uint32_t token, size_t n, uint32_t* out, float* ms) {
+    clear_error();
+    TL_REQUIRE(m && ms && n > 0, "tl_model_time_decode: bad arguments");
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    TL_TRY(check_capacity(m, n));
+    TL_TRY(set_token(m, token));
+    cudaEvent_t e0, e1;
+    TL_CUDA_TRY(cudaEventCreate(&e0));
+    TL_CUDA_TRY(cudaEventCreate(&e1));
+    const size_t first = m->pos;
+    tl_status st = TL_OK;
+    cudaEventRecord(e0, m->stream);
+    for (size_t i = 0; i < n && st == TL_OK; i++) st = run_step(m);
+    cudaEventRecord(e1, m->stream);
+    if (st == TL_OK) st = sync(m);
+    if (st == TL_OK) {
+        cudaEventElapsedTime(ms, e0, e1);
+        m->pos += n;
+        if (out) {
+            cudaMemcpy(out, m->d_hist + first, n * 4, cudaMemcpyDeviceToHost);
+        }
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    return st;
+}
+
+tl_status tl_model_profile(tl_model* m, uint32_t token, size_t n, tl_kernel_time* kinds, int max_kinds,
+                           int* n_kinds) {
+    clear_error();
+    TL_REQUIRE(m && kinds && n_kinds && n > 0 && max_kinds > 0, "tl_model_profile: bad arguments");
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    TL_TRY(check_capacity(m, n));
+    TL_TRY(set_token(m, token));
+    const size_t S = m->steps.size();
+    std::vector<cudaEvent_t> ev(S + 1);
+    for (auto& e : ev) TL_CUDA_TRY(cudaEventCreate(&e));
+    std::vector<std::string> names;
+    std::vector<double> total_ms, bytes;
+    std::vector<int> launches;
+    tl_status st = TL_OK;
+    for (size_t it = 0; it < n && st == TL_OK; it++) {
+        std::vector<double> step_bytes(S);
+        for (size_t i = 0; i < S; i++) step_bytes[i] = m->steps[i].bytes();
+        cudaEventRecord(ev[0], m->stream);
+        for (size_t i = 0; i < S && st == TL_OK; i++) {
+            st = m->steps[i].launch(m->stream, false);
+            cudaEventRecord(ev[i + 1], m->stream);
+        }
+        if (st == TL_OK) st = sync(m);
+        if (st != TL_OK) break;
+        m->pos++;
+        for (size_t i = 0; i < S; i++) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+            size_t k = 0;
+            while (k < names.size() && names[k] != m->steps[i].name) k++;
+            if (k == names.size()) {
+                names.push_back(m->steps[i].name);
+                total_ms.push_back(0);
+                bytes.push_back(0);
+                launches.push_back(0);
+            }
+            total_ms[k] += ms;
+            bytes[k] += step_bytes[i];
+            launches[k] += 1;
+        }
+    }
+    for (auto& e : ev) cudaEventDestroy(e);
+    if (st != TL_OK) return st;
+    *n_kinds = static_cast<int>(std::min<size_t>(names.size(), max_kinds));
+    for (int k = 0; k < *n_kinds; k++) {
+        std::snprintf(kinds[k].name, sizeof(kinds[k].name), "%s", names[k].c_str());
+        kinds[k].launches = launches[k];
+        kinds[k].total_ms = total_ms[k];
+        kinds[k].bytes_per_launch = bytes[k] / launches[k];
+    }
+    return TL_OK;
+}
+
+tl_status tl_model_launches_per_step(const tl_model* m, int* launches) {
+    clear_error();
+    TL_REQUIRE(m && launches, "tl_model_launches_per_step: null argument");
+    *launches = static_cast<int>(m->steps.size());
+    return TL_OK;
+}
+
+}  // extern "C"

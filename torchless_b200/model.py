@@ -1,0 +1,127 @@
+"""Model-level host API: Parameters + InferenceState + Model<int8_t> in one handle.
+
+Mirrors the reference's model loop (src/model/mistral/modules.cpp:154-171)
+and CLI loop (main.cpp:69-77) over the C ABI; all buffers handed to the
+library here are host numpy arrays.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+
+from . import check, lib, tl_config, tl_kernel_time, tl_model_options
+
+
+class Model:
+    """A device-resident int8 Mistral model (one GPU).
+
+    ``Model.load(path)`` reads the export_mistral.py binary from disk
+    (Parameters::load_parameters, parameters.cpp:95-129); ``Model.from_buffer``
+    takes the same bytes from host memory.
+    """
+
+    def __init__(self, handle: ctypes.c_void_p):
+        self._h = handle
+        cfg = tl_config()
+        check(lib().tl_model_config(self._h, ctypes.byref(cfg)))
+        self.config = {f: getattr(cfg, f) for f, _ in tl_config._fields_ if f != "quant"}
+        self.config["quant"] = cfg.quant.decode()
+
+    @staticmethod
+    def _opts(device: int, max_seq: int, use_graph: bool):
+        return tl_model_options(device=device, max_seq=max_seq, use_graph=1 if use_graph else 0)
+
+    @classmethod
+    def load(cls, path: str, device: int = 0, max_seq: int = 1024, use_graph: bool = True) -> "Model":
+        h = ctypes.c_void_p()
+        o = cls._opts(device, max_seq, use_graph)
+        check(lib().tl_model_load(path.encode(), ctypes.byref(o), ctypes.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def from_buffer(cls, buf: np.ndarray, device: int = 0, max_seq: int = 1024,
+                    use_graph: bool = True) -> "Model":
+        buf = np.ascontiguousarray(buf)
+        h = ctypes.c_void_p()
+        o = cls._opts(device, max_seq, use_graph)
+        check(lib().tl_model_load_buffer(buf.ctypes.data, buf.nbytes, ctypes.byref(o), ctypes.byref(h)))
+        return cls(h)
+
+    def close(self) -> None:
+        if self._h:
+            check(lib().tl_model_destroy(self._h))
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- InferenceState::pos ----
+    @property
+    def pos(self) -> int:
+        p = ctypes.c_size_t()
+        check(lib().tl_model_get_pos(self._h, ctypes.byref(p)))
+        return p.value
+
+    @pos.setter
+    def pos(self, value: int) -> None:
+        check(lib().tl_model_set_pos(self._h, int(value)))
+
+    # ---- Model<T>::forward + sample_max ----
+    def forward(self, token: int, logits: bool = True):
+        """One token at the current position; returns (logits or None, argmax)."""
+        out = np.empty(self.config["vocab_size"], dtype=np.float32) if logits else None
+        nxt = ctypes.c_uint32()
+        check(lib().tl_model_forward(self._h, int(token), out.ctypes.data if logits else None,
+                                     ctypes.byref(nxt)))
+        return out, nxt.value
+
+    def generate(self, prompt: Sequence[int], n_new: int) -> List[int]:
+        """main.cpp:69-77 on the device: returns the n_new greedy ids."""
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.empty(n_new, dtype=np.uint32)
+        check(lib().tl_model_generate(self._h, p.ctypes.data, p.size, n_new, out.ctypes.data))
+        return out.tolist()
+
+    def layer_forward(self, layer: int, hidden: np.ndarray) -> np.ndarray:
+        """Layer<T>::forward on a host hidden state at the current position."""
+        h = np.array(hidden, dtype=np.float32, copy=True)
+        check(lib().tl_model_layer_forward(self._h, int(layer), h.ctypes.data))
+        return h
+
+    def read_kv(self, layer: int, pos: int):
+        c = self.config
+        k = np.empty(c["n_kv_heads"] * c["head_dim"], dtype=np.float32)
+        v = np.empty_like(k)
+        check(lib().tl_model_read_kv(self._h, int(layer), int(pos), k.ctypes.data, v.ctypes.data))
+        return k.reshape(c["n_kv_heads"], c["head_dim"]), v.reshape(c["n_kv_heads"], c["head_dim"])
+
+    # ---- measurement ----
+    def time_decode(self, token: int, n: int):
+        """(device ms for n greedy steps, generated ids)."""
+        out = np.empty(n, dtype=np.uint32)
+        ms = ctypes.c_float()
+        check(lib().tl_model_time_decode(self._h, int(token), n, out.ctypes.data, ctypes.byref(ms)))
+        return ms.value, out.tolist()
+
+    def profile(self, token: int, n: int) -> List[Dict]:
+        kinds = (tl_kernel_time * 32)()
+        nk = ctypes.c_int()
+        check(lib().tl_model_profile(self._h, int(token), n, kinds, 32, ctypes.byref(nk)))
+        return [dict(name=k.name.decode(), launches=k.launches, total_ms=k.total_ms,
+                     bytes_per_launch=k.bytes_per_launch) for k in kinds[:nk.value]]
+
+    def launches_per_step(self) -> int:
+        n = ctypes.c_int()
+        check(lib().tl_model_launches_per_step(self._h, ctypes.byref(n)))
+        return n.value

@@ -1,0 +1,151 @@
+"""Seeded random-init Mistral-architecture models in the torchless binary format.
+
+Stands in for the Hugging Face checkpoint that export_mistral.py consumes:
+every ``*_proj`` matrix, the embedding and the lm_head are drawn from
+N(0, std) (std 0.02 by default) with a fixed seed; norm weights are 1.0
+(``norm="ones"``) or 1 + N(0, 0.1) (``norm="random"``, used by the parity
+tests so the norm gain is exercised).  Tensor names and shapes follow the HF
+Mistral checkpoint that the reference loads (src/model/mistral/modules.h:77-116).
+
+Two generators produce the same layout:
+  * ``numpy`` (PCG64): small models, and the HF directory that
+    tests/golden/make_golden.py feeds to the reference's own exporter;
+  * ``torch`` on a device (CUDA when present): Mistral-7B sized models in a few
+    seconds, quantised on the device by the library's own quantiser.
+"""
+from __future__ import annotations
+
+import json
+import os
+from typing import Dict, Iterator, List, Optional, Tuple
+
+import numpy as np
+
+from .binfmt import BinWriter, metadata_from_hf, quantize_i8
+
+# Mistral-7B-v0.1 architecture (the reference's target model).
+MISTRAL_7B = dict(
+    hidden_size=4096, intermediate_size=14336, num_hidden_layers=32, num_attention_heads=32,
+    num_key_value_heads=8, vocab_size=32000, max_position_embeddings=32768, sliding_window=4096,
+    rope_theta=10000.0, rms_norm_eps=1e-05, hidden_act="silu",
+)
+
+# Small models with the same structure for parity tests that the CPU oracle
+# finishes in well under a second per token.  The reference hard-codes the
+# GQA ratio n_heads / n_kv_heads = 4 (modules.cpp:70), so every config keeps it.
+SMALL = dict(
+    hidden_size=1024, intermediate_size=2048, num_hidden_layers=2, num_attention_heads=8,
+    num_key_value_heads=2, vocab_size=1000, max_position_embeddings=4096, sliding_window=4096,
+    rope_theta=10000.0, rms_norm_eps=1e-05, hidden_act="silu",
+)
+TINY = dict(
+    hidden_size=512, intermediate_size=1536, num_hidden_layers=2, num_attention_heads=4,
+    num_key_value_heads=1, vocab_size=777, max_position_embeddings=4096, sliding_window=4096,
+    rope_theta=10000.0, rms_norm_eps=1e-05, hidden_act="silu",
+)
+
+PLACEHOLDER_TOKENIZER = {"vocab": {"<unk>": 0, "<s>": 1, "</s>": 2}, "merges": []}
+
+
+def tensor_list(cfg: dict) -> List[Tuple[str, Tuple[int, ...]]]:
+    """HF Mistral tensor names and shapes, in the order written to the binary."""
+    D, F = cfg["hidden_size"], cfg["intermediate_size"]
+    H, KV = cfg["num_attention_heads"], cfg["num_key_value_heads"]
+    hd = D // H
+    out = [("model.embed_tokens.weight", (cfg["vocab_size"], D))]
+    for l in range(cfg["num_hidden_layers"]):
+        p = f"model.layers.{l}."
+        out += [
+            (p + "input_layernorm.weight", (D,)),
+            (p + "self_attn.q_proj.weight", (H * hd, D)),
+            (p + "self_attn.k_proj.weight", (KV * hd, D)),
+            (p + "self_attn.v_proj.weight", (KV * hd, D)),
+            (p + "self_attn.o_proj.weight", (D, H * hd)),
+            (p + "post_attention_layernorm.weight", (D,)),
+            (p + "mlp.gate_proj.weight", (F, D)),
+            (p + "mlp.up_proj.weight", (F, D)),
+            (p + "mlp.down_proj.weight", (D, F)),
+        ]
+    out += [("model.norm.weight", (D,)), ("lm_head.weight", (cfg["vocab_size"], D))]
+    return out
+
+
+def _is_norm(name: str) -> bool:
+    return name.endswith("norm.weight")
+
+
+def numpy_tensors(cfg: dict, seed: int, std: float = 0.02,
+                  norm: str = "ones") -> Iterator[Tuple[str, np.ndarray]]:
+    """fp32 source tensors from one PCG64 stream, in ``tensor_list`` order."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    for name, shape in tensor_list(cfg):
+        if _is_norm(name):
+            if norm == "ones":
+                x = np.ones(shape, dtype=np.float32)
+            else:
+                x = (1.0 + 0.1 * rng.standard_normal(shape, dtype=np.float32)).astype(np.float32)
+        else:
+            x = (rng.standard_normal(shape, dtype=np.float32) * np.float32(std)).astype(np.float32)
+        yield name, x
+
+
+def make_numpy_model(cfg: dict, seed: int, quant: str = "int8", std: float = 0.02,
+                     norm: str = "ones") -> BinWriter:
+    """A complete model binary built on the CPU (small configs)."""
+    w = BinWriter(metadata_from_hf(cfg, quant), tensor_list(cfg), quant, PLACEHOLDER_TOKENIZER)
+    for name, x in numpy_tensors(cfg, seed, std, norm):
+        w.put_fp32(name, x)
+    return w
+
+
+def make_torch_model(cfg: dict, seed: int, quant: str = "int8", std: float = 0.02,
+                     norm: str = "ones", device: str = "cuda", quantizer=None,
+                     buffer: Optional[np.ndarray] = None) -> BinWriter:
+    """A complete model binary whose random draws happen on ``device``.
+
+    ``quantizer(x_device) -> (q_device, scales_device)`` quantises on the
+    device (the CUDA quantiser of this library); without it the fp32 tensor
+    is copied to the host and quantised by ``quantize_i8``.
+    """
+    import torch
+
+    w = BinWriter(metadata_from_hf(cfg, quant), tensor_list(cfg), quant, PLACEHOLDER_TOKENIZER,
+                  buffer=buffer)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    for name, shape in tensor_list(cfg):
+        if _is_norm(name):
+            if norm == "ones":
+                x = torch.ones(shape, dtype=torch.float32, device=device)
+            else:
+                x = 1.0 + 0.1 * torch.randn(shape, generator=g, dtype=torch.float32, device=device)
+        else:
+            x = torch.randn(shape, generator=g, dtype=torch.float32, device=device) * std
+        d, s = w.view(name)
+        if s is None:
+            d[...] = x.cpu().numpy()
+        elif quantizer is not None:
+            q, sc = quantizer(x)
+            d[...] = q.cpu().numpy().reshape(d.shape)
+            s[...] = sc.cpu().numpy()
+        else:
+            q, sc = quantize_i8(x.cpu().numpy())
+            d[...] = q
+            s[...] = sc
+        del x
+    return w
+
+
+def write_hf_dir(path: str, cfg: dict, tensors: Dict[str, np.ndarray],
+                 tokenizer: dict = PLACEHOLDER_TOKENIZER) -> None:
+    """An HF-style model directory (fp32 safetensors) for export_mistral.py."""
+    from safetensors.numpy import save_file
+
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(cfg, f)
+    with open(os.path.join(path, "tokenizer.json"), "w") as f:
+        json.dump({"model": tokenizer}, f)
+    save_file(tensors, os.path.join(path, "model.safetensors"))
+    with open(os.path.join(path, "model.safetensors.index.json"), "w") as f:
+        json.dump({"weight_map": {k: "model.safetensors" for k in tensors}}, f)
