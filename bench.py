@@ -60,12 +60,13 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def make_model_bytes(device: str):
+def make_model_bytes(device: str, layers: int = 32):
     """Seeded Mistral-7B int8 binary, drawn and quantised on `device`."""
     from torchless_b200 import ops, synthetic as S
     t0 = time.time()
     quant = (lambda x: ops.quantize_i8(x)) if device.startswith("cuda") else None
-    w = S.make_torch_model(S.MISTRAL_7B, seed=SEED, device=device, quantizer=quant)
+    cfg = dict(S.MISTRAL_7B, num_hidden_layers=layers)
+    w = S.make_torch_model(cfg, seed=SEED, device=device, quantizer=quant)
     log(f"generated {w.size / 1e9:.2f} GB model on {device} in {time.time() - t0:.1f}s")
     return w.buf
 
@@ -196,7 +197,7 @@ def run_ours(args, rank, world, local):
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
-    buf = make_model_bytes(f"cuda:{local}")
+    buf = make_model_bytes(f"cuda:{local}", args.layers)
     max_seq = PROMPT_LEN + args.warmup + args.steps + 8
     m = Model.from_buffer(buf, device=local, max_seq=max_seq)
     prompt = prompt_ids()
@@ -255,7 +256,8 @@ def run_ours(args, rank, world, local):
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "Mistral-7B int8 bs1 greedy decode (16-token prompt, 128 tokens)",
+        "config": {"workload": "Mistral-7B int8 bs1 greedy decode (16-token prompt, 128 tokens)"
+                   + ("" if args.layers == 32 else f" [profiling case: {args.layers} of 32 layers]"),
                    "global_batch": world, "seq_len": max_seq,
                    "parallelism": "replicas" if world > 1 else "single",
                    "l2": "inputs larger than L2 (7.94 GB of weights per step)",
@@ -294,6 +296,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-layers", type=int, default=8)
+    ap.add_argument("--layers", type=int, default=32,
+                    help="transformer layers (32 = Mistral-7B; fewer only for small profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
