@@ -106,8 +106,9 @@ TL_API tl_status tl_rotary(float* cos_, float* sin_, const float* inv_freq, size
                            size_t head_dim, size_t pos, void* stream);
 
 /* sample_max (main.cpp:10-21): index of the first strict maximum of logits[n],
- * written to *out (device).  Uses a library-owned device workspace that is
- * allocated on the first call on each device. */
+ * written to *out (device).  Its per-block partials live in scratch that is
+ * allocated and freed stream-ordered (cudaMallocAsync / cudaFreeAsync) on
+ * `stream` by every call. */
 TL_API tl_status tl_argmax(uint32_t* out, const float* logits, size_t n, void* stream);
 
 /* MLP<T>::forward first half (modules.cpp:99-112), fused:
@@ -134,9 +135,11 @@ typedef struct tl_config {
 } tl_config;
 
 typedef struct tl_model_options {
-    int device;     /* CUDA device ordinal                                        */
-    size_t max_seq; /* KV cache capacity in positions; 0 -> 1024                  */
-    int use_graph;  /* 1: each decode step is one CUDA-graph replay (default)    */
+    int device;      /* CUDA device ordinal                                        */
+    size_t max_seq;  /* KV cache capacity in positions; 0 -> 1024                  */
+    int use_graph;   /* 1: each decode step is one CUDA-graph replay (default)    */
+    int kernel_mode; /* 0: one persistent kernel per decode step when the shape   */
+                     /*    fits (default), else per-op kernels; 1: per-op kernels */
 } tl_model_options;
 
 typedef struct tl_model tl_model;
@@ -194,6 +197,18 @@ typedef struct tl_kernel_time {
 } tl_kernel_time;
 TL_API tl_status tl_model_profile(tl_model* m, uint32_t token, size_t n, tl_kernel_time* kinds,
                                   int max_kinds, int* n_kinds);
+
+/* Phase trace of one persistent-kernel decode step (tracing aid; the step is a
+ * normal forward of `token` at the current position, launched without the
+ * graph).  out[0] = CTAs, out[1] = phases (5 per layer + lm_head), then
+ * %globaltimer ns stamps [cta][phase][8] = {phase begin, activation loads
+ * landed, activation staged, tiles done, epilogue done, grid barrier passed,
+ * producer's last issue, unused};
+ * stamps a CTA does not reach stay 0.  cap is the capacity of out in
+ * elements; *n_written receives the element count.  TL_ERR_UNSUPPORTED when
+ * the model runs per-op kernels. */
+TL_API tl_status tl_model_trace_step(tl_model* m, uint32_t token, uint64_t* out, size_t cap,
+                                     size_t* n_written);
 
 /* Number of kernel launches one decode step issues (all of them this library's). */
 TL_API tl_status tl_model_launches_per_step(const tl_model* m, int* launches);

@@ -26,6 +26,9 @@ def _cuda():
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
 
 
+MODES = {"persistent": 0, "per_op": 1}
+
+
 def load(buf, **kw):
     from torchless_b200 import Model
     return Model.from_buffer(buf, **kw)
@@ -54,12 +57,13 @@ def check_teacher_forced(model, prompt, ids, ref_logits):
     return worst, near_ties
 
 
+@pytest.mark.parametrize("mode", list(MODES))
 @pytest.mark.parametrize("name", ["tiny", "small"])
-def test_greedy_matches_reference(name, request):
+def test_greedy_matches_reference(name, mode, request):
     prompt, ids, logits = golden_greedy(name)
-    m = load(request.getfixturevalue(f"{name}_bin"), max_seq=64)
+    m = load(request.getfixturevalue(f"{name}_bin"), max_seq=64, kernel_mode=MODES[mode])
     worst, ties = check_teacher_forced(m, prompt, ids, logits)
-    print(f"{name}: worst logits rel err {worst:.2e}, near-ties {ties}")
+    print(f"{name}/{mode}: worst logits rel err {worst:.2e}, near-ties {ties}")
     assert worst < 1e-4  # the CUDA path is far inside the stated bound
     # the on-device greedy loop (main.cpp:69-77) reproduces the reference ids
     m.pos = 0
@@ -67,10 +71,11 @@ def test_greedy_matches_reference(name, request):
     m.close()
 
 
-def test_graph_and_eager_agree(small_bin):
+@pytest.mark.parametrize("mode", list(MODES))
+def test_graph_and_eager_agree(small_bin, mode):
     prompt, ids, logits = golden_greedy("small")
-    a = load(small_bin, max_seq=64, use_graph=True)
-    b = load(small_bin, max_seq=64, use_graph=False)
+    a = load(small_bin, max_seq=64, use_graph=True, kernel_mode=MODES[mode])
+    b = load(small_bin, max_seq=64, use_graph=False, kernel_mode=MODES[mode])
     for t in prompt + ids[:8]:
         la, na = a.forward(t)
         lb, nb = b.forward(t)
@@ -104,9 +109,10 @@ def test_layer_and_kv_push_match_oracle(small_bin):
     m.close()
 
 
-def test_capacity_and_token_errors(tiny_bin):
+@pytest.mark.parametrize("mode", list(MODES))
+def test_capacity_and_token_errors(tiny_bin, mode):
     from torchless_b200 import TLError
-    m = load(tiny_bin, max_seq=4)
+    m = load(tiny_bin, max_seq=4, kernel_mode=MODES[mode])
     for t in range(4):
         m.forward(t, logits=False)
     with pytest.raises(TLError) as e:
@@ -119,18 +125,23 @@ def test_capacity_and_token_errors(tiny_bin):
     m.close()
 
 
-def test_mistral7b_shapes_two_layers():
-    """Mistral-7B layer shapes (D 4096, F 14336, 32/8 heads, V 32000) with 2 layers:
-    every fast-path kernel at its real size, against the oracle, 6 steps."""
-    import oracle
+@pytest.fixture(scope="module")
+def m7b_two_layers():
+    """Mistral-7B layer shapes (D 4096, F 14336, 32/8 heads, V 32000) with 2 layers."""
     from torchless_b200 import synthetic as S
     from torchless_b200 import ops
-    from torchless_b200.binfmt import ModelFile
     cfg = dict(S.MISTRAL_7B, num_hidden_layers=2)
-    w = S.make_torch_model(cfg, seed=11, norm="random", device="cuda",
-                           quantizer=lambda x: ops.quantize_i8(x))
-    om = oracle.OracleModel(ModelFile(w.buf), max_seq=32)
-    m = load(w.buf, max_seq=32)
+    return S.make_torch_model(cfg, seed=11, norm="random", device="cuda",
+                              quantizer=lambda x: ops.quantize_i8(x)).buf
+
+
+@pytest.mark.parametrize("mode", list(MODES))
+def test_mistral7b_shapes_two_layers(m7b_two_layers, mode):
+    """Every kernel at its real size against the oracle, 6 steps."""
+    import oracle
+    from torchless_b200.binfmt import ModelFile
+    om = oracle.OracleModel(ModelFile(m7b_two_layers), max_seq=32)
+    m = load(m7b_two_layers, max_seq=32, kernel_mode=MODES[mode])
     rng = np.random.default_rng(1)
     toks = rng.integers(0, 32000, 6).tolist()
     for step, t in enumerate(toks):
@@ -142,3 +153,19 @@ def test_mistral7b_shapes_two_layers():
         if nxt != int(np.argmax(ref)):
             assert margin(ref) < TIE
     m.close()
+
+
+def test_persistent_and_per_op_agree_at_long_positions(small_bin):
+    """Both decode paths over 200 positions (attention spans many splits)."""
+    a = load(small_bin, max_seq=256, kernel_mode=0)
+    b = load(small_bin, max_seq=256, kernel_mode=1)
+    rng = np.random.default_rng(5)
+    toks = rng.integers(0, 1000, 200).tolist()
+    worst = 0.0
+    for t in toks:
+        la, _ = a.forward(t)
+        lb, _ = b.forward(t)
+        worst = max(worst, rel_err(la, lb))
+    assert worst < 1e-4, worst
+    a.close()
+    b.close()

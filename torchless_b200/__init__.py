@@ -50,7 +50,8 @@ class tl_config(ctypes.Structure):
 
 
 class tl_model_options(ctypes.Structure):
-    _fields_ = [("device", ctypes.c_int), ("max_seq", ctypes.c_size_t), ("use_graph", ctypes.c_int)]
+    _fields_ = [("device", ctypes.c_int), ("max_seq", ctypes.c_size_t), ("use_graph", ctypes.c_int),
+                ("kernel_mode", ctypes.c_int)]
 
 
 class tl_kernel_time(ctypes.Structure):
@@ -97,6 +98,7 @@ SIGNATURES = {
     "tl_model_time_decode": [_P, _U32, _S, _P, ctypes.POINTER(_F)],
     "tl_model_profile": [_P, _U32, _S, ctypes.POINTER(tl_kernel_time), _I, ctypes.POINTER(_I)],
     "tl_model_launches_per_step": [_P, ctypes.POINTER(_I)],
+    "tl_model_trace_step": [_P, _U32, _P, _S, ctypes.POINTER(_S)],
 }
 
 _lib: Optional[ctypes.CDLL] = None

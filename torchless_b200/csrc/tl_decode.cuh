@@ -1,0 +1,103 @@
+// tl_decode.cuh -- interface of the persistent decode-step kernel (tl_decode.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "torchless_b200.h"
+
+namespace tl {
+
+// Tiled weight layout streamed by the persistent kernel.
+//
+// int8 matrices ([n, d], row-major in the file) become tiles of 16 rows x 512
+// columns.  A tile is 8192 bytes of weights followed by 512 bytes of fp32
+// inverse scales; tiles are ordered row-block major ((rb, ks) -> rb*KS + ks),
+// so the rows a CTA owns are one contiguous byte range.  Inside a tile,
+// block w covers columns [64w, 64w+64) (one quantisation group):
+//   byte  w*1024 + half*512 + lane*16 + j   holds  W[16 rb + 8 half + lane/4]
+//                                                 [512 ks + 64 w + 16 (lane%4) + j]
+// stored as q + 128 (q ^ 0x80), the bias the int8 -> fp16 splice expects;
+//   float 2048 + rr*8 + w                    holds  1 / scale of row 16 rb + rr,
+//                                                 group 8 ks + w.
+// gate/up are interleaved: tile row rr < 8 is gate row 8 rb + rr, rr >= 8 is
+// up row 8 rb + rr - 8, so one tile yields 8 SwiGLU outputs.
+// The persistent kernel gives each tile to one consumer warp.
+// fp32 lm_head tiles are 4 rows x 512 columns (8192 bytes):
+//   float w*256 + (rr/2)*128 + lane*4 + (rr%2)*2 + e  holds
+//   W[4 rb + rr][512 ks + 64 w + 2 lane + e].
+constexpr int kTileCols = 512;
+constexpr int kTileRowsI8 = 16;
+constexpr int kTileBytesI8 = 8192 + 512;
+constexpr int kTileRowsF32 = 4;
+constexpr int kTileBytesF32 = 8192;
+
+struct DecodeLayer {
+    const uint8_t* qkv;  // tiles of [q; k; v]   ((H + 2 KV) hd rows, d = D)
+    const uint8_t* o;    // tiles of o_proj      (D rows, d = H hd)
+    const uint8_t* w13;  // tiles of gate/up     (2F rows interleaved, d = D)
+    const uint8_t* w2;   // tiles of down_proj   (D rows, d = F)
+    const float* g_in;
+    const float* g_post;
+    float* k_cache;      // [KV][max_seq][hd]
+    float* v_cache;
+};
+
+struct DecodeArgs {
+    const DecodeLayer* layers;  // device array [n_layers]
+    int n_layers;
+    const float* embed;         // [V, D]
+    const float* g_final;       // [D]
+    const uint8_t* lm_head;     // fp32 tiles
+    const float* cos_tab;       // [max_seq][hd/2]
+    const float* sin_tab;
+    float* h;                   // residual stream [D]
+    float* qkv;                 // [(H + 2 KV) hd]
+    float* attn_part;           // [H][S][hd + 2]
+    float* ctx;                 // [H hd] merged attention output (o_proj input)
+    unsigned* attn_cnt;         // [H] split tickets, zero between launches
+    float* act;                 // [F]
+    float* logits;              // [V]
+    float* am_v;                // [grid] argmax partials
+    uint32_t* am_i;
+    unsigned* ticket;           // zero between launches (last CTA resets it)
+    unsigned* bar;              // grid barrier counter, zeroed before each launch
+    int* err;                   // nonzero after a bounded wait gave up
+    uint32_t* token;            // in: this step's token; out: argmax
+    unsigned* pos;              // in: position; out: position + 1
+    uint32_t* history;          // history[pos] = argmax
+    int D, F, H, KV, HD, V, max_seq, splits;
+    int pbuf_floats;            // per-phase partial-sum buffer (decode_kernel_fits)
+    float attn_scale;
+    // Optional phase trace (nullptr = off): per CTA, kTraceEvents %globaltimer
+    // stamps for every phase, [cta][phase][event], phases = 5 per layer + lm_head.
+    unsigned long long* trace;
+};
+
+// Trace events per phase: 0 begin, 1 activation loads landed, 2 activation
+// staged, 3 tiles done, 4 epilogue done, 5 barrier passed, 6 producer's last
+// issue of the phase, 7 unused.
+constexpr int kTraceEvents = 8;
+
+// Shared-memory bytes, pipeline depth and partial-buffer size for a model
+// shape on `grid` CTAs; false when the shape cannot run in the persistent kernel.
+bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int grid, int max_smem, int* stages,
+                        size_t* smem_bytes, int* pbuf_floats);
+
+// Launch one decode step (cooperative: every CTA resident on its own SM).
+tl_status launch_decode_step(const DecodeArgs& a, int grid, int stages, size_t smem, cudaStream_t s);
+
+// Weight repacking into the tiled layout (run once at model load).
+tl_status repack_i8(uint8_t* dst, const int8_t* w, const float* s, int n, int d, cudaStream_t st);
+tl_status repack_i8_swiglu(uint8_t* dst, const int8_t* w1, const float* s1, const int8_t* w3,
+                           const float* s3, int n, int d, cudaStream_t st);
+tl_status repack_f32(uint8_t* dst, const float* w, int n, int d, cudaStream_t st);
+
+inline size_t tiles_i8_bytes(int n_rows, int d) {
+    return static_cast<size_t>((n_rows + kTileRowsI8 - 1) / kTileRowsI8) * (d / kTileCols) * kTileBytesI8;
+}
+inline size_t tiles_f32_bytes(int n_rows, int d) {
+    return static_cast<size_t>((n_rows + kTileRowsF32 - 1) / kTileRowsF32) * (d / kTileCols) * kTileBytesF32;
+}
+
+}  // namespace tl

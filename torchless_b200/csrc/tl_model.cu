@@ -38,6 +38,7 @@
 #include <vector>
 
 #include "tl_common.cuh"
+#include "tl_decode.cuh"
 #include "tl_gemv.cuh"
 #include "tl_json.h"
 #include "tl_kernels.h"
@@ -224,8 +225,19 @@ struct tl_model {
     uint32_t* h_pinned = nullptr;  // [2]: token in, token out
     size_t pos = 0;
     std::vector<Step> steps;
+    std::vector<DecodeLayer> layers_host_tmp;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
+    // persistent decode kernel (tl_decode.cu)
+    bool persistent = false;
+    DeviceArena tiles;
+    DecodeLayer* d_layers = nullptr;
+    DecodeArgs dargs = {};
+    int grid = 0, stages = 0, mega_splits = 0;
+    size_t mega_smem = 0;
+    unsigned *bar = nullptr, *ticket = nullptr;
+    int* err = nullptr;
+    double bytes_per_step = 0;
 };
 
 namespace tl {
@@ -385,13 +397,65 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         TL_TRY(check_launch("invert scales"));
     }
 
+    // ---- persistent decode kernel: tiled weight copies ----
+    const int kmode = opts ? opts->kernel_mode : 0;
+    if (kmode == 0) {
+        int max_smem = 0, dev_sms = 0, coop = 0;
+        TL_CUDA_TRY(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device));
+        TL_CUDA_TRY(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, m->device));
+        TL_CUDA_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->device));
+        int pbuf = 0;
+        if (coop && decode_kernel_fits(static_cast<int>(D), static_cast<int>(F), static_cast<int>(H),
+                                       static_cast<int>(KV), static_cast<int>(HD), static_cast<int>(V), dev_sms,
+                                       max_smem, &m->stages, &m->mega_smem, &pbuf)) {
+            m->persistent = true;
+            m->grid = dev_sms;
+            // Tuning knob: a shallower weight ring (fewer bytes in flight per SM).
+            if (const char* e = std::getenv("TL_DECODE_STAGES")) {
+                const int want = std::atoi(e);
+                if (want >= 8 && want < m->stages) {
+                    m->mega_smem -= static_cast<size_t>(m->stages - want) * (kTileBytesI8 + 16);
+                    m->stages = want;
+                }
+            }
+            m->mega_splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(dev_sms / H, 256 / H)));
+            m->dargs.pbuf_floats = pbuf;
+        }
+    }
+    if (m->persistent) {
+        const size_t per = tiles_i8_bytes(NQKV, D) + tiles_i8_bytes(D, H * HD) + tiles_i8_bytes(2 * F, D) +
+                           tiles_i8_bytes(D, F);
+        TL_TRY(m->tiles.reserve(per * L + tiles_f32_bytes(V, D) + 256 * (4 * L + 1)));
+        std::vector<DecodeLayer> dl(L);
+        for (int64_t l = 0; l < L; l++) {
+            const LayerW& w = m->layers[l];
+            uint8_t* tq = m->tiles.take<uint8_t>(tiles_i8_bytes(NQKV, D));
+            uint8_t* to = m->tiles.take<uint8_t>(tiles_i8_bytes(D, H * HD));
+            uint8_t* t13 = m->tiles.take<uint8_t>(tiles_i8_bytes(2 * F, D));
+            uint8_t* t2 = m->tiles.take<uint8_t>(tiles_i8_bytes(D, F));
+            TL_TRY(repack_i8(tq, w.wqkv, w.sqkv, NQKV, D, m->stream));
+            TL_TRY(repack_i8(to, w.wo, w.so, D, H * HD, m->stream));
+            TL_TRY(repack_i8_swiglu(t13, w.w1, w.s1, w.w3, w.s3, F, D, m->stream));
+            TL_TRY(repack_i8(t2, w.w2, w.s2, D, F, m->stream));
+            dl[l] = DecodeLayer{tq, to, t13, t2, w.g_in, w.g_post, nullptr, nullptr};
+        }
+        uint8_t* tl = m->tiles.take<uint8_t>(tiles_f32_bytes(V, D));
+        TL_TRY(repack_f32(tl, m->lm_head, V, D, m->stream));
+        m->dargs.lm_head = tl;
+        TL_CUDA_TRY(cudaMalloc(&m->d_layers, sizeof(DecodeLayer) * L));
+        // KV pointers are filled once the state arena exists (below).
+        m->dargs.layers = m->d_layers;
+        m->layers_host_tmp = dl;
+    }
+
     // ---- state arena: KV cache, RoPE tables, activations, scratch ----
     const size_t kv = L * layer_kv_floats(m.get());
     const size_t half = HD / 2;
-    const int am_grid = gemv_f32_grid(V, D, true, true);
+    const int am_grid = std::max(gemv_f32_grid(V, D, true, true), m->grid);
+    const int part_splits = std::max(m->splits, m->mega_splits);
     size_t sbytes = 2 * A::pad(kv * 4) + 2 * A::pad(m->max_seq * half * 4) + A::pad(D * 4) + A::pad(NQKV * 4) +
-                    A::pad(H * HD * 4) + A::pad(F * 4) + A::pad(V * 4) + A::pad(H * m->splits * (HD + 2) * 4) +
-                    A::pad(H * 4) + A::pad(am_grid * 4) * 2 + A::pad(4) * 3 + A::pad(m->max_seq * 4) * 2;
+                    A::pad(H * HD * 4) + A::pad(F * 4) + A::pad(V * 4) + A::pad(H * part_splits * (HD + 2) * 4) +
+                    A::pad(H * 4) + A::pad(am_grid * 4) * 2 + A::pad(4) * 6 + A::pad(m->max_seq * 4) * 2;
     TL_TRY(m->state.reserve(sbytes));
     TL_CUDA_TRY(cudaMemsetAsync(m->state.base, 0, sbytes, m->stream));
     m->kc = m->state.take<float>(kv);
@@ -403,7 +467,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     m->ctx = m->state.take<float>(H * HD);
     m->act = m->state.take<float>(F);
     m->logits = m->state.take<float>(V);
-    m->attn_part = m->state.take<float>(H * m->splits * (HD + 2));
+    m->attn_part = m->state.take<float>(H * part_splits * (HD + 2));
     m->attn_cnt = m->state.take<unsigned>(H);
     m->am_v = m->state.take<float>(am_grid);
     m->am_i = m->state.take<uint32_t>(am_grid);
@@ -412,7 +476,29 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     m->d_token = m->state.take<uint32_t>(1);
     m->d_hist = m->state.take<uint32_t>(m->max_seq);
     m->d_prompt = m->state.take<uint32_t>(m->max_seq);
-    if (!m->d_prompt) return set_error(TL_ERR_OUT_OF_MEMORY, "state arena too small (internal)");
+    m->bar = m->state.take<unsigned>(1);
+    m->ticket = m->state.take<unsigned>(1);
+    m->err = m->state.take<int>(1);
+    if (!m->err) return set_error(TL_ERR_OUT_OF_MEMORY, "state arena too small (internal)");
+    if (m->persistent) {
+        for (int64_t l = 0; l < L; l++) {
+            m->layers_host_tmp[l].k_cache = m->kc + static_cast<size_t>(l) * layer_kv_floats(m.get());
+            m->layers_host_tmp[l].v_cache = m->vc + static_cast<size_t>(l) * layer_kv_floats(m.get());
+        }
+        TL_CUDA_TRY(cudaMemcpy(m->d_layers, m->layers_host_tmp.data(), sizeof(DecodeLayer) * L,
+                               cudaMemcpyHostToDevice));
+        DecodeArgs& d = m->dargs;
+        d.n_layers = static_cast<int>(L);
+        d.embed = m->embed; d.g_final = m->norm; d.cos_tab = m->cos_tab; d.sin_tab = m->sin_tab;
+        d.h = m->h; d.qkv = m->qkv; d.attn_part = m->attn_part; d.act = m->act; d.logits = m->logits;
+        d.ctx = m->ctx; d.attn_cnt = m->attn_cnt;
+        d.am_v = m->am_v; d.am_i = m->am_i; d.ticket = m->ticket; d.bar = m->bar; d.err = m->err;
+        d.token = m->d_token; d.pos = m->d_pos; d.history = m->d_hist;
+        d.D = static_cast<int>(D); d.F = static_cast<int>(F); d.H = static_cast<int>(H);
+        d.KV = static_cast<int>(KV); d.HD = static_cast<int>(HD); d.V = static_cast<int>(V);
+        d.max_seq = static_cast<int>(m->max_seq); d.splits = m->mega_splits;
+        d.attn_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
+    }
 
     // RotaryEmbedding::init_freq + ::forward (modules.cpp:12-27) with the
     // reference's float arithmetic and libm, for every position up front.
@@ -504,6 +590,19 @@ tl_status build_steps(tl_model* m) {
     const tl_config& c = m->cfg;
     const int D = c.hidden_size, V = c.vocab_size;
     m->steps.clear();
+    if (m->persistent) {
+        const double F = c.intermediate_size, H = c.n_heads, KV = c.n_kv_heads, HD = c.head_dim, L = c.n_layers;
+        const double NQKV = (H + 2 * KV) * HD;
+        // int8 weights + fp32 scales of every projection, fp32 lm_head, norms, one embedding row
+        const double per_layer = (NQKV * D + D * H * HD + 3.0 * F * D) * (1 + 4.0 / 64) + 8.0 * D;
+        const double fixed = per_layer * L + double(V) * D * 4 + 8.0 * D;
+        m->steps.push_back({"decode_step",
+                            [=] { return fixed + 2.0 * L * KV * (double(m->pos) + 1) * HD * 4; },
+                            [=](cudaStream_t s, bool) {
+                                return launch_decode_step(m->dargs, m->grid, m->stages, m->mega_smem, s);
+                            }});
+        return TL_OK;
+    }
     m->steps.push_back({"embed", [=] { return 8.0 * D; },
                         [=](cudaStream_t s, bool pdl) {
                             return launch_embed(m->h, m->embed, m->d_token, D, s, pdl);
@@ -531,6 +630,13 @@ tl_status capture_graph(tl_model* m) {
     tl_status st = run_steps_eager(m);
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (m->persistent && (st != TL_OK || e != cudaSuccess)) {
+        // One cooperative launch per step needs no graph: launch it directly.
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        clear_error();
+        return TL_OK;
+    }
     if (st != TL_OK) {
         if (g) cudaGraphDestroy(g);
         return st;
@@ -569,8 +675,24 @@ tl_status check_capacity(const tl_model* m, size_t steps) {
 }
 
 tl_status sync(tl_model* m) {
+    if (m->persistent) {
+        cudaError_t e = cudaMemcpyAsync(m->h_pinned + 3, m->err, 4, cudaMemcpyDeviceToHost, m->stream);
+        if (e != cudaSuccess) return set_error(TL_ERR_CUDA, "error-flag read: %s", cudaGetErrorString(e));
+    }
     cudaError_t e = cudaStreamSynchronize(m->stream);
     if (e != cudaSuccess) return set_error(TL_ERR_CUDA, "decode step failed: %s", cudaGetErrorString(e));
+    if (m->persistent && m->h_pinned[3] != 0) {
+        const unsigned code = m->h_pinned[3];
+        // A bounded wait inside the kernel gave up: clear the barrier state so
+        // the next step starts clean, and report it.
+        cudaMemsetAsync(m->bar, 0, 4, m->stream);
+        cudaMemsetAsync(m->ticket, 0, 4, m->stream);
+        cudaMemsetAsync(m->err, 0, 4, m->stream);
+        cudaStreamSynchronize(m->stream);
+        m->h_pinned[3] = 0;
+        return set_error(TL_ERR_TIMEOUT, "decode kernel wait timed out (code %u: 1 grid barrier, 2 tile arrival, 3 ring slot)",
+                         code);
+    }
     return TL_OK;
 }
 
@@ -616,6 +738,8 @@ tl_status tl_model_destroy(tl_model* m) {
     if (m->graph) cudaGraphDestroy(m->graph);
     m->weights.release();
     m->state.release();
+    m->tiles.release();
+    if (m->d_layers) cudaFree(m->d_layers);
     if (m->h_pinned) cudaFreeHost(m->h_pinned);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -797,6 +921,39 @@ tl_status tl_model_profile(tl_model* m, uint32_t token, size_t n, tl_kernel_time
         kinds[k].bytes_per_launch = bytes[k] / launches[k];
     }
     return TL_OK;
+}
+
+tl_status tl_model_trace_step(tl_model* m, uint32_t token, uint64_t* out, size_t cap, size_t* n_written) {
+    clear_error();
+    TL_REQUIRE(m && out && n_written, "tl_model_trace_step: null argument");
+    if (!m->persistent) return set_error(TL_ERR_UNSUPPORTED, "tracing needs the persistent decode kernel");
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    TL_TRY(check_capacity(m, 1));
+    const size_t phases = 5 * m->cfg.n_layers + 1;
+    const size_t n = static_cast<size_t>(m->grid) * phases * kTraceEvents;
+    TL_REQUIRE(cap >= n + 2, "tl_model_trace_step: out holds %zu elements, %zu needed", cap, n + 2);
+    unsigned long long* d_trace = nullptr;
+    TL_CUDA_TRY(cudaMalloc(&d_trace, n * sizeof(unsigned long long)));
+    tl_status st = TL_OK;
+    if (cudaMemsetAsync(d_trace, 0, n * sizeof(unsigned long long), m->stream) != cudaSuccess)
+        st = set_error(TL_ERR_CUDA, "trace buffer clear failed");
+    if (st == TL_OK) st = set_token(m, token);
+    if (st == TL_OK) {
+        DecodeArgs a = m->dargs;
+        a.trace = d_trace;
+        st = launch_decode_step(a, m->grid, m->stages, m->mega_smem, m->stream);
+    }
+    if (st == TL_OK) st = sync(m);
+    if (st == TL_OK) {
+        m->pos++;
+        out[0] = static_cast<uint64_t>(m->grid);
+        out[1] = phases;
+        if (cudaMemcpy(out + 2, d_trace, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost) != cudaSuccess)
+            st = set_error(TL_ERR_CUDA, "trace copy failed");
+        *n_written = n + 2;
+    }
+    cudaFree(d_trace);
+    return st;
 }
 
 tl_status tl_model_launches_per_step(const tl_model* m, int* launches) {

@@ -268,7 +268,7 @@ tl_status tl_matmul_f32(float* xout, const float* w, const float* x, size_t n, s
         a.w = w; a.x = x; a.y = xout; a.n = static_cast<int>(n); a.d = static_cast<int>(d);
         return launch_gemv_f32(a, false, false, s, false);
     }
-    k_matmul_f32_rows<<<blocks_for(n, 8) , 256, 0, s>>>(xout, w, x, n, d);
+    k_matmul_f32_rows<<<static_cast<unsigned>((n + 7) / 8), 256, 0, s>>>(xout, w, x, n, d);
     return launched("matmul_f32");
 }
 

@@ -29,23 +29,28 @@ class Model:
         self.config = {f: getattr(cfg, f) for f, _ in tl_config._fields_ if f != "quant"}
         self.config["quant"] = cfg.quant.decode()
 
+    #: kernel_mode values: one persistent kernel per step, or one launch per op
+    PERSISTENT, PER_OP = 0, 1
+
     @staticmethod
-    def _opts(device: int, max_seq: int, use_graph: bool):
-        return tl_model_options(device=device, max_seq=max_seq, use_graph=1 if use_graph else 0)
+    def _opts(device: int, max_seq: int, use_graph: bool, kernel_mode: int):
+        return tl_model_options(device=device, max_seq=max_seq, use_graph=1 if use_graph else 0,
+                                kernel_mode=kernel_mode)
 
     @classmethod
-    def load(cls, path: str, device: int = 0, max_seq: int = 1024, use_graph: bool = True) -> "Model":
+    def load(cls, path: str, device: int = 0, max_seq: int = 1024, use_graph: bool = True,
+             kernel_mode: int = 0) -> "Model":
         h = ctypes.c_void_p()
-        o = cls._opts(device, max_seq, use_graph)
+        o = cls._opts(device, max_seq, use_graph, kernel_mode)
         check(lib().tl_model_load(path.encode(), ctypes.byref(o), ctypes.byref(h)))
         return cls(h)
 
     @classmethod
     def from_buffer(cls, buf: np.ndarray, device: int = 0, max_seq: int = 1024,
-                    use_graph: bool = True) -> "Model":
+                    use_graph: bool = True, kernel_mode: int = 0) -> "Model":
         buf = np.ascontiguousarray(buf)
         h = ctypes.c_void_p()
-        o = cls._opts(device, max_seq, use_graph)
+        o = cls._opts(device, max_seq, use_graph, kernel_mode)
         check(lib().tl_model_load_buffer(buf.ctypes.data, buf.nbytes, ctypes.byref(o), ctypes.byref(h)))
         return cls(h)
 
@@ -120,6 +125,17 @@ class Model:
         check(lib().tl_model_profile(self._h, int(token), n, kinds, 32, ctypes.byref(nk)))
         return [dict(name=k.name.decode(), launches=k.launches, total_ms=k.total_ms,
                      bytes_per_launch=k.bytes_per_launch) for k in kinds[:nk.value]]
+
+    def trace_step(self, token: int) -> np.ndarray:
+        """Phase trace of one persistent decode step: int64 [cta, phase, 8] ns stamps."""
+        c = self.config
+        n_phases = 5 * c["n_layers"] + 1
+        cap = 2 + 1024 * n_phases * 8
+        out = np.zeros(cap, dtype=np.uint64)
+        n = ctypes.c_size_t()
+        check(lib().tl_model_trace_step(self._h, int(token), out.ctypes.data, cap, ctypes.byref(n)))
+        grid, phases = int(out[0]), int(out[1])
+        return out[2:2 + grid * phases * 8].astype(np.int64).reshape(grid, phases, 8)
 
     def launches_per_step(self) -> int:
         n = ctypes.c_int()
