@@ -44,11 +44,16 @@ namespace tl {
 namespace {
 
 constexpr int kConsumerWarps = 8;
+// Ring slot = two consecutive tiles fetched by ONE bulk copy: a copy costs a
+// roughly fixed ~0.2 us per SM, so 17 KB copies stream at 7+ TB/s where
+// single 8.7 KB tiles top out near 6 (4 once consumers read them).
+constexpr int kTilesPerStage = 2;
+constexpr int kStageBytes = kTilesPerStage * kTileBytesI8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 
-enum ErrCode : int { kErrBarrier = 1, kErrFull = 2, kErrEmpty = 3, kErrFetch = 4 };
+enum ErrCode : int { kErrBarrier = 1, kErrFull = 2, kErrEmpty = 3, kErrFetch = 4, kErrInput = 5 };
 
 // ---------------------------------------------------------------------------
 // PTX helpers
@@ -78,10 +83,10 @@ __device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(b)), "r"(parity)
+        : "r"(smem_u32(b)), "r"(parity), "r"(20000u)  // sleep up to 20 us instead of spinning
         : "memory");
     return ok != 0;
 }
@@ -102,6 +107,11 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Orders this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (bulk copy) accesses to the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -134,11 +144,26 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Self-check build (TL_DECODE_CHECK): bounds/alignment checks that record the
+// first violation in DecodeArgs::dbg and let the caller skip the access.
+#ifdef TL_DECODE_CHECK
+__device__ __noinline__ void tld_report(int* dbg, int* err, int site, long long v0, long long v1) {
+    if (dbg && atomicCAS(dbg, 0, site) == 0) {
+        dbg[1] = static_cast<int>(v0);
+        dbg[2] = static_cast<int>(v1);
+    }
+    atomicCAS(err, 0, 1000 + site);
+}
+#define TLD_OK(cond, site, v0, v1) ((cond) ? true : (tld_report(a_dbg, a_err, (site), (v0), (v1)), false))
+#else
+#define TLD_OK(cond, site, v0, v1) true
+#endif
+
 // ---------------------------------------------------------------------------
 // Shared memory map
 // ---------------------------------------------------------------------------
 struct Shared {
-    uint8_t* ring;     // stages * kTileBytesI8
+    uint8_t* ring;     // stages * kStageBytes
     uint8_t* xbuf;     // activation staging (fp16 hi|lo, fp32 for lm_head, or attention scratch)
     float* pbuf;       // per-tile row partial sums of the current phase
     float* scratch;    // 64 floats for block reductions
@@ -170,7 +195,7 @@ __device__ Shared carve(uint8_t* base, int stages, const DecodeArgs& a) {
     Shared s;
     size_t off = 0;
     s.ring = base;
-    off += static_cast<size_t>(stages) * kTileBytesI8;
+    off += static_cast<size_t>(stages) * kStageBytes;
     s.xbuf = base + off;
     off += xbuf_bytes(a.D, a.F, a.HD);
     s.pbuf = reinterpret_cast<float*>(base + off);
@@ -203,8 +228,12 @@ __device__ __forceinline__ void split(int n, int& b0, int& b1) { split_of(n, blo
 struct Producer {
     const Shared& sh;
     int stages;
-    uint32_t it = 0;
+    uint32_t it = 0;  // ring slots used so far
+    int slot = 0;     // it % stages, kept incrementally
+    uint32_t rnd = 0; // it / stages
     bool ok = true;
+    int* a_dbg = nullptr;
+    int* a_err = nullptr;
     unsigned long long* trace = nullptr;
     int n_phases = 0;
 
@@ -215,14 +244,19 @@ struct Producer {
         if (trace) trace[(static_cast<size_t>(blockIdx.x) * n_phases + ph) * kTraceEvents + 6] = globaltimer();
     }
 
-    __device__ void range(const uint8_t* base, int n_rb, int ksn, uint32_t bytes, uint32_t stride) {
+    // This CTA's tiles of one phase, kTilesPerStage per bulk copy.
+    __device__ void range(const uint8_t* base, int n_rb, int ksn, uint32_t tile_bytes) {
         int b0, b1;
         split(n_rb, b0, b1);
-        const uint8_t* src = base + static_cast<size_t>(b0) * ksn * stride;
-        const int count = (b1 - b0) * ksn;
-        for (int i = 0; i < count && ok; i++, it++) {
-            const int s = it % stages;
-            const uint32_t round = it / stages;
+        const uint8_t* src = base + static_cast<size_t>(b0) * ksn * tile_bytes;
+        const int n = (b1 - b0) * ksn;
+        for (int i = 0; i < n && ok; i += kTilesPerStage, it++) {
+            const int s = slot;
+            const uint32_t round = rnd;
+            if (++slot == stages) {
+                slot = 0;
+                rnd++;
+            }
             if (round > 0 && !mbar_wait(&sh.empty[s], (round - 1) & 1)) {
                 ok = false;
                 break;
@@ -231,8 +265,18 @@ struct Producer {
                 ok = false;
                 break;
             }
+            const uint32_t bytes = static_cast<uint32_t>(min(kTilesPerStage, n - i)) * tile_bytes;
+            const uint8_t* gsrc = src + static_cast<size_t>(i) * tile_bytes;
+            if (!TLD_OK(s >= 0 && s < stages, 2, s, stages) ||
+                !TLD_OK(bytes > 0 && bytes <= kStageBytes && (bytes & 15) == 0, 3, bytes, i) ||
+                !TLD_OK(static_cast<size_t>(b0 * ksn + i) * tile_bytes + bytes <=
+                            static_cast<size_t>(n_rb) * ksn * tile_bytes, 4, b0 * ksn + i, n_rb * ksn) ||
+                !TLD_OK((reinterpret_cast<uintptr_t>(gsrc) & 15) == 0, 5, reinterpret_cast<uintptr_t>(gsrc) & 15, 0)) {
+                ok = false;
+                break;
+            }
             mbar_expect_tx(&sh.full[s], bytes);
-            bulk_load(sh.ring + static_cast<size_t>(s) * kTileBytesI8, src + static_cast<size_t>(i) * stride, bytes,
+            bulk_load(sh.ring + static_cast<size_t>(s) * kStageBytes, src + static_cast<size_t>(i) * tile_bytes, bytes,
                       &sh.full[s]);
         }
     }
@@ -259,11 +303,15 @@ struct Consumer {
     const Shared& sh;
     int stages;
     int t, lane, warp;
-    uint32_t it = 0;  // ring position of the current phase's first tile
+    int slot = 0;            // ring slot of the next tile pair
+    uint32_t phase_bit = 0;  // parity of its current round
     unsigned barriers = 0;
+    int* a_dbg;
+    int* a_err;
 
     __device__ Consumer(const DecodeArgs& args, const Shared& s, int st)
-        : a(args), sh(s), stages(st), t(threadIdx.x), lane(threadIdx.x & 31), warp(threadIdx.x >> 5) {}
+        : a(args), sh(s), stages(st), t(threadIdx.x), lane(threadIdx.x & 31), warp(threadIdx.x >> 5),
+          a_dbg(args.dbg), a_err(args.err) {}
 
     int phase = 0;  // trace slot of the current phase
     __device__ __forceinline__ void stamp(int ev) const {
@@ -306,8 +354,17 @@ struct Consumer {
     __device__ void fetch(const float* act, int n, const float* g) {
         if (t != 0) return;
         const uint32_t bytes = static_cast<uint32_t>(n) * 4u + (g ? static_cast<uint32_t>(a.D) * 4u : 0u);
-        // order this thread's acquire (generic proxy) before the async-proxy reads
+        if (!TLD_OK(static_cast<size_t>(n) * 4 <= (g ? 4 * static_cast<size_t>(a.D) : xbuf_bytes(a.D, a.F, a.HD)) &&
+                        bytes <= xbuf_bytes(a.D, a.F, a.HD), 20, n, bytes) ||
+            !TLD_OK(((reinterpret_cast<uintptr_t>(act) | reinterpret_cast<uintptr_t>(g)) & 15) == 0, 21,
+                    reinterpret_cast<uintptr_t>(act) & 15, reinterpret_cast<uintptr_t>(g) & 15))
+            return;
+        // order this thread's acquire (generic proxy) before the async-proxy
+        // reads of global memory, and the CTA's earlier generic accesses to
+        // xbuf (made visible to this thread by the preceding bar.sync) before
+        // the async-proxy writes into it
         asm volatile("fence.proxy.async.global;" ::: "memory");
+        fence_proxy_async_smem();
         mbar_expect_tx(sh.abar, bytes);
         bulk_load(sh.xbuf, act, static_cast<uint32_t>(n) * 4u, sh.abar);
         if (g) bulk_load(sh.xbuf + 4 * static_cast<size_t>(a.D), g, static_cast<uint32_t>(a.D) * 4u, sh.abar);
@@ -367,6 +424,8 @@ struct Consumer {
     // the vector is needed.
     enum { kHalf = 0, kFp32 = 1 };
     __device__ float stage(int d, bool norm, int mode) {
+        if (!TLD_OK(4 * static_cast<size_t>(d) <= xbuf_bytes(a.D, a.F, a.HD) && (!norm || d == a.D), 30, d, norm))
+            return 1.0f;
         float* xs = reinterpret_cast<float*>(sh.xbuf);
         const float* gs = xs + a.D;
         float ss = 0.f, m = 0.f;
@@ -383,6 +442,12 @@ struct Consumer {
         if (amax > 0.f) frexpf(amax, &e);
         const int k = ::min(::max(14 - e, -120), 120);
         const float sc = (mode == kHalf) ? ldexpf(1.0f, k) : 1.0f;
+        // kHalf layout: in each block of 16 columns [16 b, 16 b + 16), word
+        // 16 b + m (m < 8) holds {hi[16 b + 2m], hi[16 b + 2m + 1]} and word
+        // 16 b + 8 + m the lo pair: exactly the mma B-operand registers of the
+        // x_hi (lanes 0-3) and x_lo (lanes 4-7) columns.  A block lies in one
+        // warp (columns t + 256 i), so a warp sync separates reads from writes.
+        uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
         for (int col = t; col < d; col += kConsumers) {
             float x = xs[col];
             if (norm) x = (x * inv) * gs[col];
@@ -392,7 +457,14 @@ struct Consumer {
                 const float xsc = x * sc;
                 const __half hi = __float2half_rn(xsc);
                 const __half lo = __float2half_rn(xsc - __half2float(hi));
-                reinterpret_cast<__half2*>(xs)[col] = __halves2half2(hi, lo);
+                const unsigned short hb = __half_as_ushort(hi), lb = __half_as_ushort(lo);
+                const unsigned short hp = __shfl_xor_sync(FULL, hb, 1), lp = __shfl_xor_sync(FULL, lb, 1);
+                __syncwarp();
+                const int j = col & 15;
+                uint32_t* blk = xw + (col & ~15);
+                if ((j & 1) == 0) blk[j >> 1] = static_cast<uint32_t>(hb) | (static_cast<uint32_t>(hp) << 16);
+                else blk[8 + (j >> 1)] = static_cast<uint32_t>(lp) | (static_cast<uint32_t>(lb) << 16);
+                __syncwarp();
             }
         }
         consumer_sync();
@@ -410,10 +482,10 @@ struct Consumer {
         const float4 s8b = *reinterpret_cast<const float4*>(sc + (r + 8) * 8 + 4);
         const float sr[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
         const float sr8[8] = {s8a.x, s8a.y, s8a.z, s8a.w, s8b.x, s8b.y, s8b.z, s8b.w};
-        // x words {hi, lo} of columns 512 ks + 64 g + 16 c + [0, 16): lanes 0-3
-        // (B column 0) take the hi halves, lanes 4-7 (column 1) the lo halves.
-        const uint32_t* xw = reinterpret_cast<const uint32_t*>(sh.xbuf) + ks * kTileCols + c * 16;
-        const uint32_t sel = (lane < 4) ? 0x5410u : 0x7632u;
+        // B registers of columns 512 ks + 64 g + 16 c + [0, 16): lanes 0-3 the
+        // hi pairs (words 0-7 of the block), lanes 4-7 the lo pairs (8-15).
+        const uint32_t* xw =
+            reinterpret_cast<const uint32_t*>(sh.xbuf) + ks * kTileCols + c * 16 + (lane >= 4 ? 8 : 0);
         float yr = 0.f, yr8 = 0.f;
 #pragma unroll
         for (int g = 0; g < 8; g++) {
@@ -421,14 +493,8 @@ struct Consumer {
             const uint4 ar8 = lds128(st + g * 1024 + 512 + lane * 16);
             uint4 b0 = make_uint4(0, 0, 0, 0), b1 = make_uint4(0, 0, 0, 0);
             if (lane < 8) {
-                const uint4 w0 = lds128(xw + g * 64);
-                const uint4 w1 = lds128(xw + g * 64 + 4);
-                const uint4 w2 = lds128(xw + g * 64 + 8);
-                const uint4 w3 = lds128(xw + g * 64 + 12);
-                b0 = make_uint4(__byte_perm(w0.x, w0.y, sel), __byte_perm(w0.z, w0.w, sel),
-                                __byte_perm(w1.x, w1.y, sel), __byte_perm(w1.z, w1.w, sel));
-                b1 = make_uint4(__byte_perm(w2.x, w2.y, sel), __byte_perm(w2.z, w2.w, sel),
-                                __byte_perm(w3.x, w3.y, sel), __byte_perm(w3.z, w3.w, sel));
+                b0 = lds128(xw + g * 64);
+                b1 = lds128(xw + g * 64 + 4);
             }
             float dacc[4] = {0.f, 0.f, 0.f, 0.f};
             mma16816(dacc, u8x2_lo_to_h2(ar.x), u8x2_lo_to_h2(ar8.x), u8x2_hi_to_h2(ar.x), u8x2_hi_to_h2(ar8.x),
@@ -467,7 +533,12 @@ struct Consumer {
         if ((lane & 7) == 0) out[lane >> 3] = acc[0];
     }
 
-    // All tiles of one phase: warp w takes the CTA's tiles w, w + 8, ...
+    // All tiles of one phase: warp w computes the CTA's tiles w, w + 8, ...,
+    // but every warp waits on and releases EVERY ring slot in order (the
+    // empty barriers expect one arrival per consumer warp).  A warp therefore
+    // never waits on a slot more than one round ahead of what it has seen
+    // complete, which keeps the parity waits unambiguous even though bulk
+    // copies may land out of order.
     // Returns the CTA's first row block, or -1 on error (uniform over warps).
     template <bool F32>
     __device__ int run_tiles(int n_rb, int ksn, int& n_rb_local) {
@@ -475,29 +546,40 @@ struct Consumer {
         split(n_rb, rb0, rb1);
         n_rb_local = rb1 - rb0;
         const int n_tiles = n_rb_local * ksn;
+        const int n_slots = (n_tiles + kTilesPerStage - 1) / kTilesPerStage;
         constexpr int ROWS = F32 ? kTileRowsF32 : kTileRowsI8;
-        bool bad = false;
-        for (int i = warp; i < n_tiles && !bad; i += kConsumerWarps) {
-            const uint32_t g = it + i;
-            const int s = g % stages;
-            if (!mbar_wait(&sh.full[s], (g / stages) & 1)) {
+        constexpr int TB = F32 ? kTileBytesF32 : kTileBytesI8;
+        int my_i = warp;            // next tile of this warp
+        int my_ks = warp % ksn;     // its k-slice, kept incrementally
+        for (int j = 0; j < n_slots; j++) {
+            const int s = slot;
+            const uint32_t par = phase_bit;
+            if (++slot == stages) {
+                slot = 0;
+                phase_bit ^= 1u;
+            }
+            if (!mbar_wait(&sh.full[s], par)) {
                 fail(kErrFull);
-                bad = true;
                 break;
             }
-            const uint8_t* st = sh.ring + static_cast<size_t>(s) * kTileBytesI8;
-            float* out = sh.pbuf + static_cast<size_t>(i) * ROWS;
-            if (F32) tile_f32(st, i % ksn, out);
-            else tile_i8(st, i % ksn, out);
+            if (my_i < n_tiles && my_i / kTilesPerStage == j) {
+                if (TLD_OK((my_i + 1) * ROWS <= a.pbuf_floats, 12, my_i, a.pbuf_floats)) {
+                    const uint8_t* st = sh.ring + static_cast<size_t>(s) * kStageBytes + (my_i % kTilesPerStage) * TB;
+                    float* out = sh.pbuf + static_cast<size_t>(my_i) * ROWS;
+                    if (F32) tile_f32(st, my_ks, out);
+                    else tile_i8(st, my_ks, out);
+                }
+                my_i += kConsumerWarps;
+                my_ks += kConsumerWarps;
+                while (my_ks >= ksn) my_ks -= ksn;
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh.empty[s]);
         }
-        it += n_tiles;
         consumer_sync();
         stamp(3);
         return aborted() ? -1 : rb0;
     }
-
 
     // Row r (local) of the phase: sum of its ksn tile partials, fixed order.
     __device__ __forceinline__ float row_sum(int rbl, int rr, int ksn, int rows) const {
@@ -550,6 +632,9 @@ struct Consumer {
         const int u = blockIdx.x;
         if (u >= a.H * S) return;
         const int h = u / S, s = u % S, kh = h / 4;  // kv head h/4 (modules.cpp:70)
+        if (!TLD_OK(pos < static_cast<unsigned>(a.max_seq) && kh < a.KV && h < a.H, 40, pos, kh)) return;
+        if (!TLD_OK((3 * HD + kConsumerWarps * (HD + 2)) * 4 <= static_cast<int>(xbuf_bytes(a.D, a.F, a.HD)), 41, HD, 0))
+            return;
         float* q_s = reinterpret_cast<float*>(sh.xbuf);
         float* k_s = q_s + HD;
         float* v_s = k_s + HD;
@@ -687,10 +772,20 @@ template <int HD>
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, int stages) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Shared sh = carve(smem_raw, stages, a);
+#ifdef TL_DECODE_CHECK
+    {
+        unsigned dyn;
+        asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+        const size_t end = reinterpret_cast<uint8_t*>(sh.abar + 1) - smem_raw;
+        int* a_dbg = a.dbg;
+        int* a_err = a.err;
+        if (!TLD_OK(end <= dyn, 1, static_cast<long long>(end), dyn)) return;
+    }
+#endif
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; s++) {
             mbar_init(&sh.full[s], 1);
-            mbar_init(&sh.empty[s], 1);
+            mbar_init(&sh.empty[s], kConsumerWarps);
         }
         mbar_init(sh.abar, 1);
         sh.flags[0] = 0;
@@ -700,27 +795,34 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         fence_mbar_init();
     }
     __syncthreads();
+    // Never index with an out-of-range token or position: record and stop.
+    if (sh.info[0] >= static_cast<unsigned>(a.max_seq) || sh.info[1] >= static_cast<unsigned>(a.V)) {
+        if (threadIdx.x == 0) atomicCAS(a.err, 0, kErrInput);
+        return;
+    }
 
     const int D = a.D, F = a.F, NQKV = (a.H + 2 * a.KV) * a.HD;
     if (threadIdx.x >= kConsumers) {
         // ---------------- producer warp ----------------
         if (threadIdx.x != kConsumers) return;
         Producer p(sh, stages);
+        p.a_dbg = a.dbg;
+        p.a_err = a.err;
         p.trace = a.trace;
         p.n_phases = 5 * a.n_layers + 1;
         const int ksD = D / kTileCols, ksF = F / kTileCols;
         for (int l = 0; l < a.n_layers && p.ok; l++) {
             const DecodeLayer& L = a.layers[l];
-            p.range(L.qkv, (NQKV + 15) / 16, ksD, kTileBytesI8, kTileBytesI8);
+            p.range(L.qkv, (NQKV + 15) / 16, ksD, kTileBytesI8);
             p.stamp(5 * l);
-            p.range(L.o, (D + 15) / 16, (a.H * a.HD) / kTileCols, kTileBytesI8, kTileBytesI8);
+            p.range(L.o, (D + 15) / 16, (a.H * a.HD) / kTileCols, kTileBytesI8);
             p.stamp(5 * l + 2);
-            p.range(L.w13, (2 * F + 15) / 16, ksD, kTileBytesI8, kTileBytesI8);
+            p.range(L.w13, (2 * F + 15) / 16, ksD, kTileBytesI8);
             p.stamp(5 * l + 3);
-            p.range(L.w2, (D + 15) / 16, ksF, kTileBytesI8, kTileBytesI8);
+            p.range(L.w2, (D + 15) / 16, ksF, kTileBytesI8);
             p.stamp(5 * l + 4);
         }
-        if (p.ok) p.range(a.lm_head, (a.V + 3) / 4, ksD, kTileBytesF32, kTileBytesF32);
+        if (p.ok) p.range(a.lm_head, (a.V + 3) / 4, ksD, kTileBytesF32);
         p.stamp(5 * a.n_layers);
         p.drain();
         return;
@@ -944,12 +1046,12 @@ bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int grid, in
     pb = std::max(pb, need(V, kTileRowsF32, D));
     const size_t fixed = fixed_bytes(D, F, HD, pb);
     if (static_cast<size_t>(max_smem) <= fixed) return false;
-    int st = static_cast<int>((static_cast<size_t>(max_smem) - fixed - 16) / (kTileBytesI8 + 16));
+    int st = static_cast<int>((static_cast<size_t>(max_smem) - fixed - 16) / (kStageBytes + 16));
     st = st > 24 ? 24 : st;
-    if (st < 8) return false;
+    if (st < 4) return false;
     *stages = st;
     *pbuf_floats = pb;
-    *smem_bytes = static_cast<size_t>(st) * kTileBytesI8 + fixed + static_cast<size_t>(st) * 16 + 16;
+    *smem_bytes = static_cast<size_t>(st) * kStageBytes + fixed + static_cast<size_t>(st) * 16 + 16;
     return true;
 }
 

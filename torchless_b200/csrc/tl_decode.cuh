@@ -72,6 +72,9 @@ struct DecodeArgs {
     // Optional phase trace (nullptr = off): per CTA, kTraceEvents %globaltimer
     // stamps for every phase, [cta][phase][event], phases = 5 per layer + lm_head.
     unsigned long long* trace;
+    // Self-check build only (TL_DECODE_CHECK): first violated check as
+    // {site, value0, value1}; the checked access is skipped.
+    int* dbg;
 };
 
 // Trace events per phase: 0 begin, 1 activation loads landed, 2 activation

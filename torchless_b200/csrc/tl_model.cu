@@ -237,6 +237,7 @@ struct tl_model {
     size_t mega_smem = 0;
     unsigned *bar = nullptr, *ticket = nullptr;
     int* err = nullptr;
+    int* dbg = nullptr;  // self-check build: {site, v0, v1}
     double bytes_per_step = 0;
 };
 
@@ -413,8 +414,8 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
             // Tuning knob: a shallower weight ring (fewer bytes in flight per SM).
             if (const char* e = std::getenv("TL_DECODE_STAGES")) {
                 const int want = std::atoi(e);
-                if (want >= 8 && want < m->stages) {
-                    m->mega_smem -= static_cast<size_t>(m->stages - want) * (kTileBytesI8 + 16);
+                if (want >= 4 && want < m->stages) {
+                    m->mega_smem -= static_cast<size_t>(m->stages - want) * (2 * kTileBytesI8 + 16);
                     m->stages = want;
                 }
             }
@@ -455,7 +456,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     const int part_splits = std::max(m->splits, m->mega_splits);
     size_t sbytes = 2 * A::pad(kv * 4) + 2 * A::pad(m->max_seq * half * 4) + A::pad(D * 4) + A::pad(NQKV * 4) +
                     A::pad(H * HD * 4) + A::pad(F * 4) + A::pad(V * 4) + A::pad(H * part_splits * (HD + 2) * 4) +
-                    A::pad(H * 4) + A::pad(am_grid * 4) * 2 + A::pad(4) * 6 + A::pad(m->max_seq * 4) * 2;
+                    A::pad(H * 4) + A::pad(am_grid * 4) * 2 + A::pad(4) * 6 + A::pad(16) + A::pad(m->max_seq * 4) * 2;
     TL_TRY(m->state.reserve(sbytes));
     TL_CUDA_TRY(cudaMemsetAsync(m->state.base, 0, sbytes, m->stream));
     m->kc = m->state.take<float>(kv);
@@ -479,7 +480,8 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     m->bar = m->state.take<unsigned>(1);
     m->ticket = m->state.take<unsigned>(1);
     m->err = m->state.take<int>(1);
-    if (!m->err) return set_error(TL_ERR_OUT_OF_MEMORY, "state arena too small (internal)");
+    m->dbg = m->state.take<int>(4);
+    if (!m->dbg) return set_error(TL_ERR_OUT_OF_MEMORY, "state arena too small (internal)");
     if (m->persistent) {
         for (int64_t l = 0; l < L; l++) {
             m->layers_host_tmp[l].k_cache = m->kc + static_cast<size_t>(l) * layer_kv_floats(m.get());
@@ -492,6 +494,9 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         d.embed = m->embed; d.g_final = m->norm; d.cos_tab = m->cos_tab; d.sin_tab = m->sin_tab;
         d.h = m->h; d.qkv = m->qkv; d.attn_part = m->attn_part; d.act = m->act; d.logits = m->logits;
         d.ctx = m->ctx; d.attn_cnt = m->attn_cnt;
+#ifdef TL_DECODE_CHECK
+        d.dbg = m->dbg;
+#endif
         d.am_v = m->am_v; d.am_i = m->am_i; d.ticket = m->ticket; d.bar = m->bar; d.err = m->err;
         d.token = m->d_token; d.pos = m->d_pos; d.history = m->d_hist;
         d.D = static_cast<int>(D); d.F = static_cast<int>(F); d.H = static_cast<int>(H);
@@ -683,6 +688,16 @@ tl_status sync(tl_model* m) {
     if (e != cudaSuccess) return set_error(TL_ERR_CUDA, "decode step failed: %s", cudaGetErrorString(e));
     if (m->persistent && m->h_pinned[3] != 0) {
         const unsigned code = m->h_pinned[3];
+        if (code >= 1000) {
+            int dbg[4] = {0, 0, 0, 0};
+            cudaMemcpy(dbg, m->dbg, sizeof(dbg), cudaMemcpyDeviceToHost);
+            cudaMemsetAsync(m->err, 0, 4, m->stream);
+            cudaMemsetAsync(m->dbg, 0, 16, m->stream);
+            cudaStreamSynchronize(m->stream);
+            m->h_pinned[3] = 0;
+            return set_error(TL_ERR_INVALID_ARGUMENT, "decode kernel self-check: site %d values %d %d", dbg[0],
+                             dbg[1], dbg[2]);
+        }
         // A bounded wait inside the kernel gave up: clear the barrier state so
         // the next step starts clean, and report it.
         cudaMemsetAsync(m->bar, 0, 4, m->stream);
@@ -690,7 +705,9 @@ tl_status sync(tl_model* m) {
         cudaMemsetAsync(m->err, 0, 4, m->stream);
         cudaStreamSynchronize(m->stream);
         m->h_pinned[3] = 0;
-        return set_error(TL_ERR_TIMEOUT, "decode kernel wait timed out (code %u: 1 grid barrier, 2 tile arrival, 3 ring slot)",
+        if (code == 5) return set_error(TL_ERR_INVALID_ARGUMENT, "decode kernel: token or position out of range");
+        return set_error(TL_ERR_TIMEOUT,
+                         "decode kernel wait timed out (code %u: 1 grid barrier, 2 tile arrival, 3 ring slot, 4 activation fetch)",
                          code);
     }
     return TL_OK;
