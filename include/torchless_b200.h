@@ -111,6 +111,20 @@ TL_API tl_status tl_rotary(float* cos_, float* sin_, const float* inv_freq, size
  * `stream` by every call. */
 TL_API tl_status tl_argmax(uint32_t* out, const float* logits, size_t n, void* stream);
 
+/* tl_argmax without any device allocation.  No counterpart in the reference
+ * (its sample_max, main.cpp:10-21, is a host loop with no scratch); it exists
+ * for callers that cannot allocate device memory at call time, such as a
+ * serving loop that has given all free HBM to its KV-cache pool, where a
+ * per-call allocation could fail or wait mid-generation.  Same result as
+ * tl_argmax.  The partials live in a fixed 4 KB file-scope device array (512
+ * partials of 1024 logits), so n must be <= 524288; larger n returns
+ * TL_ERR_CAPACITY.  The first call on a device looks up that array's address
+ * (cudaGetSymbolAddress, with that device current) and caches it; make that
+ * first call before any stream capture begins.  The array is shared by all
+ * calls on a device: calls whose kernels overlap in time (other streams or
+ * host threads) race on it and must be serialised by the caller. */
+TL_API tl_status tl_argmax_noalloc(uint32_t* out, const float* logits, size_t n, void* stream);
+
 /* MLP<T>::forward first half (modules.cpp:99-112), fused:
  * out[i] = silu(W1[i,:] @ x) * (W3[i,:] @ x), int8 W1/W3 [n, d] with stored scales. */
 TL_API tl_status tl_mlp_gate_up(float* out, const int8_t* w1, const float* s1, const int8_t* w3,

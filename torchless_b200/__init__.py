@@ -83,6 +83,7 @@ SIGNATURES = {
     "tl_rmsnorm": [_P, _P, _P, _S, _F, _P],
     "tl_rotary": [_P, _P, _P, _S, _S, _S, _P],
     "tl_argmax": [_P, _P, _S, _P],
+    "tl_argmax_noalloc": [_P, _P, _S, _P],
     "tl_mlp_gate_up": [_P, _P, _P, _P, _P, _P, _S, _S, _P],
     "tl_quantize_i8": [_P, _P, _P, _S, _S, _P],
     "tl_model_load": [ctypes.c_char_p, ctypes.POINTER(tl_model_options), ctypes.POINTER(_P)],

@@ -10,10 +10,14 @@
 #include <math.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "tl_common.cuh"
 #include "tl_gemv.cuh"
 #include "tl_kernels.h"
+
+// Scratch of tl_argmax_noalloc: 512 (value, index) partials, 4 KB per device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[512 * 8];
 
 namespace tl {
 namespace {
@@ -414,6 +418,77 @@ tl_status tl_argmax(uint32_t* out, const float* logits, size_t n, void* stream) 
     if (st == TL_OK && e != cudaSuccess)
         return set_error(TL_ERR_CUDA, "cudaFreeAsync failed: %s", cudaGetErrorString(e));
     return st;
+}
+
+}  // extern "C"
+
+namespace tl {
+namespace {
+
+// ---- argmax without allocation ----
+// For callers that cannot allocate device memory at call time: a serving loop
+// that has handed all free HBM to its KV-cache pool at start-up has nothing
+// left for a per-call allocation, and an allocation that fails (or waits on
+// the pool) in the middle of a generation would end or stall the request.
+// The partials live in this fixed file-scope array instead: one (value,
+// index) pair per 1024 logits, so n is limited to kNoAllocMaxParts * 1024.
+// Pass 1 writes every partial that pass 2 reads, so nothing in the array has
+// to start at zero.  The array is shared by every call on a device: calls
+// whose kernels overlap (two streams, or two host threads) race on it.
+constexpr int kNoAllocMaxParts = 512;
+constexpr size_t kNoAllocMaxLogits = static_cast<size_t>(kNoAllocMaxParts) * 1024;
+constexpr int kNoAllocMaxDevices = 64;
+
+static_assert(sizeof(g_noalloc_scratch) == kNoAllocMaxParts * (sizeof(float) + sizeof(uint32_t)),
+              "scratch holds kNoAllocMaxParts (value, index) pairs");
+
+// Device address of g_noalloc_scratch, looked up once per device (with that
+// device current) on the first call made there.
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+tl_status noalloc_scratch(unsigned char** out) {
+    int dev = -1;
+    TL_CUDA_TRY(cudaGetDevice(&dev));
+    TL_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, "tl_argmax_noalloc: device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return set_error(TL_ERR_CUDA, "tl_argmax_noalloc: cudaGetSymbolAddress on device %d failed: %s", dev,
+                             cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return TL_OK;
+}
+
+}  // namespace
+}  // namespace tl
+
+using namespace tl;
+
+extern "C" {
+
+tl_status tl_argmax_noalloc(uint32_t* out, const float* logits, size_t n, void* stream) {
+    clear_error();
+    TL_REQUIRE(out && logits && n > 0, "tl_argmax_noalloc: bad arguments");
+    if (n > kNoAllocMaxLogits)
+        return set_error(TL_ERR_CAPACITY,
+                         "tl_argmax_noalloc: n = %zu exceeds the static scratch limit of %zu logits "
+                         "(%d partials of 1024); use tl_argmax",
+                         n, kNoAllocMaxLogits, kNoAllocMaxParts);
+    unsigned char* ws = nullptr;
+    TL_TRY(noalloc_scratch(&ws));
+    float* pv = reinterpret_cast<float*>(ws);
+    uint32_t* pi = reinterpret_cast<uint32_t*>(ws + kNoAllocMaxParts * sizeof(float));
+    cudaStream_t s = as_stream(stream);
+    const int parts = static_cast<int>((n + 1023) / 1024);
+    k_argmax_partial<<<parts, 1024, 0, s>>>(pv, pi, logits, n);
+    TL_TRY(launched("argmax_partial"));
+    k_argmax_final<<<1, 1024, 0, s>>>(out, pv, pi, parts, logits);
+    return launched("argmax_final");
 }
 
 tl_status tl_mlp_gate_up(float* out, const int8_t* w1, const float* s1, const int8_t* w3,
