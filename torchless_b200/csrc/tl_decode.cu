@@ -8,31 +8,33 @@
 // phase after phase and layer after layer, into a shared-memory ring of
 // `stages` slots with cp.async.bulk (non-multicast) completing on per-slot
 // mbarriers.  Weights never depend on activations, so the producer runs ahead
-// across phase boundaries and grid barriers; the ring (~160 KB per SM) keeps
-// HBM busy while consumers wait for the previous phase's activations.
+// across phase boundaries and grid barriers; it also prefetches the tiles a
+// few slots beyond the ring into L2, so HBM keeps streaming while consumers
+// wait at a barrier.
 //
-// Consumer warps: per phase, stage the activation vector as an fp16 hi/lo
-// pair in shared memory (x*2^k = hi + lo, ~22 significant bits); then each
-// warp takes whole tiles (round robin), converts the int8 weights to fp16
-// with a byte-permute splice and runs mma.m16n8k16 (f16 inputs, f32
-// accumulate) with B columns {x_hi, x_lo}: rows x (hi + lo) = W x to
-// near-fp32 accuracy.  Each 64-column group is accumulated separately and
-// scaled by its 1/s (tensor.cpp:101-104 dequantisation applied once per
-// group).  Tile row sums go to a shared buffer and, after the phase, each
-// row is summed over its tiles in a fixed order and the fused epilogue runs:
+// Consumer warps: per phase, stage the activation vector as three int8
+// digits of a 22-bit fixed-point value (x 2^k = 2^16 d0 + 2^8 d1 + d2); then
+// each warp takes whole tiles (round robin) and runs integer tensor-core
+// mma.m16n8k32 (s8 x s8 -> s32) with the raw int8 weights as A and the three
+// digit vectors as B columns: each 64-column group's three dot products are
+// exact integers, combined in fp32 and scaled by the group's 1/s
+// (tensor.cpp:101-104 dequantisation applied once per group).  Tile row sums
+// go to a shared buffer and, after the phase, each row is summed over its
+// tiles in a fixed order and the fused epilogue runs:
 //   q/k/v                       -> qkv buffer         (modules.cpp:53-55)
 //   o_proj + residual           -> h                  (modules.cpp:91, 128)
 //   SiLU(gate) * up             -> act                (modules.cpp:99-112)
 //   down_proj + residual        -> h                  (modules.cpp:113, 142)
 //   lm_head (fp32 tiles, FFMA)  -> logits + argmax    (modules.cpp:147-149)
-// RMSNorm (modules.cpp:31-46) is applied while staging x.  Attention
-// (modules.cpp:58-88) runs between q/k/v and o_proj on H x S CTAs
-// (flash-decoding partials; the o_proj phase merges them while staging x).
+// Epilogues that write a vector another phase stages also publish, per CTA,
+// its partial sum of squares and max magnitude, so that the stager gets the
+// RMSNorm factor (modules.cpp:31-46) and the digit scale without another
+// pass.  Attention (modules.cpp:58-88) runs between q/k/v and o_proj on
+// H x S CTAs (flash-decoding partials; the last split of a head merges).
 //
 // Phases are separated by a grid barrier (monotonic counter, acquire/release).
 // Every wait is bounded by ~2 s of %globaltimer; on expiry the kernel records
 // an error code, the producer drains its in-flight copies, and all CTAs exit.
-#include <cuda_fp16.h>
 #include <math.h>
 
 #include <algorithm>
@@ -46,14 +48,16 @@ namespace {
 constexpr int kConsumerWarps = 8;
 // Ring slot = two consecutive tiles fetched by ONE bulk copy: a copy costs a
 // roughly fixed ~0.2 us per SM, so 17 KB copies stream at 7+ TB/s where
-// single 8.7 KB tiles top out near 6 (4 once consumers read them).
+// single 8.7 KB tiles top out near 6.
 constexpr int kTilesPerStage = 2;
 constexpr int kStageBytes = kTilesPerStage * kTileBytesI8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
+// Staged digits of one 64-column group: d0 (x 2^16), d1 (x 2^8), d2 rows of 64 bytes.
+constexpr int kGroupDigitBytes = 192;
 
-enum ErrCode : int { kErrBarrier = 1, kErrFull = 2, kErrEmpty = 3, kErrFetch = 4, kErrInput = 5 };
+enum ErrCode : int { kErrBarrier = 1, kErrFull = 2, kErrEmpty = 3, kErrInput = 5 };
 
 // ---------------------------------------------------------------------------
 // PTX helpers
@@ -106,42 +110,34 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-// Orders this thread's earlier generic-proxy shared-memory accesses before
-// later async-proxy (bulk copy) accesses to the same bytes.
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+// Hint: bring [src, src + bytes) into L2 (no completion, no shared memory).
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
-
 __device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
-// int8 weights stored as q + 128: splice bytes into the mantissa of 1024.0h
-// (0x6400 | u == 1024 + u exactly) and subtract 1152 = 1024 + 128.
-__device__ __forceinline__ uint32_t u8x2_lo_to_h2(uint32_t w) {
-    uint32_t r = __byte_perm(w, 0x64646464u, 0x5140);
-    const __half2 h = __hsub2(*reinterpret_cast<__half2*>(&r), __half2(__float2half(1152.f), __float2half(1152.f)));
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
-__device__ __forceinline__ uint32_t u8x2_hi_to_h2(uint32_t w) {
-    uint32_t r = __byte_perm(w, 0x64646464u, 0x5342);
-    const __half2 h = __hsub2(*reinterpret_cast<__half2*>(&r), __half2(__float2half(1152.f), __float2half(1152.f)));
-    return *reinterpret_cast<const uint32_t*>(&h);
+// D = A(16x32 s8, row) * B(32x8 s8, col) + D (s32).
+__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// D = A(16x16 f16, row) * B(16x8 f16, col) + C (f32).
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+// Low bytes of four ints, packed little-endian.
+__device__ __forceinline__ uint32_t pack_lo_bytes(int x0, int x1, int x2, int x3) {
+    const uint32_t lo = __byte_perm(static_cast<uint32_t>(x0), static_cast<uint32_t>(x1), 0x0040);
+    const uint32_t hi = __byte_perm(static_cast<uint32_t>(x2), static_cast<uint32_t>(x3), 0x0040);
+    return __byte_perm(lo, hi, 0x5410);
 }
 
 // Self-check build (TL_DECODE_CHECK): bounds/alignment checks that record the
@@ -164,31 +160,29 @@ __device__ __noinline__ void tld_report(int* dbg, int* err, int site, long long 
 // ---------------------------------------------------------------------------
 struct Shared {
     uint8_t* ring;     // stages * kStageBytes
-    uint8_t* xbuf;     // activation staging (fp16 hi|lo, fp32 for lm_head, or attention scratch)
+    uint8_t* xbuf;     // staged activation (int8 digits, fp32 for lm_head) or attention scratch
     float* pbuf;       // per-tile row partial sums of the current phase
     float* scratch;    // 64 floats for block reductions
-    float* mw;         // [256] attention merge data
     uint64_t* full;    // [stages]
     uint64_t* empty;   // [stages]
-    uint64_t* abar;    // activation fetch (one bulk copy set per phase)
     int* flags;        // [0] abort, [1] last CTA (argmax), [2] last split (attention)
     uint32_t* info;    // [0] pos, [1] token
 };
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-// fp32 activation (later fp16 hi|lo in place) + RMSNorm gain right after a
-// length-D activation; or attention scratch.
+// Digits of the longest staged vector (3 bytes per column), the fp32 lm_head
+// input, or the attention scratch.
 __host__ __device__ inline size_t xbuf_bytes(int D, int F, int HD) {
-    size_t x = 4 * static_cast<size_t>(D > F ? D : F);
-    if (8 * static_cast<size_t>(D) > x) x = 8 * static_cast<size_t>(D);
+    size_t x = 3 * static_cast<size_t>(D > F ? D : F);
+    if (4 * static_cast<size_t>(D) > x) x = 4 * static_cast<size_t>(D);
     const size_t attn = (3 * HD + kConsumerWarps * (HD + 2)) * 4;  // q, k, v + warp partials
     if (attn > x) x = attn;
     return align_up(x, 128);
 }
 
 __host__ __device__ inline size_t fixed_bytes(int D, int F, int HD, int pbuf_floats) {
-    return xbuf_bytes(D, F, HD) + align_up(static_cast<size_t>(pbuf_floats) * 4, 128) + 64 * 4 + 256 * 4 + 64;
+    return xbuf_bytes(D, F, HD) + align_up(static_cast<size_t>(pbuf_floats) * 4, 128) + 64 * 4 + 64;
 }
 
 __device__ Shared carve(uint8_t* base, int stages, const DecodeArgs& a) {
@@ -202,14 +196,11 @@ __device__ Shared carve(uint8_t* base, int stages, const DecodeArgs& a) {
     off += align_up(static_cast<size_t>(a.pbuf_floats) * 4, 128);
     s.scratch = reinterpret_cast<float*>(base + off);
     off += 64 * 4;
-    s.mw = reinterpret_cast<float*>(base + off);
-    off += 256 * 4;
     s.flags = reinterpret_cast<int*>(base + off);
     s.info = reinterpret_cast<uint32_t*>(base + off + 16);
     off += 64;
     s.full = reinterpret_cast<uint64_t*>(base + off);
     s.empty = s.full + stages;
-    s.abar = s.empty + stages;
     return s;
 }
 
@@ -225,60 +216,120 @@ __device__ __forceinline__ void split(int n, int& b0, int& b1) { split_of(n, blo
 // ---------------------------------------------------------------------------
 // Producer
 // ---------------------------------------------------------------------------
+// This CTA's byte range of one tiled phase ("segment"): 4 per layer
+// (q/k/v, o, gate/up, down) and the lm_head.
+struct Seg {
+    const uint8_t* src;
+    int n;        // tiles
+    uint32_t tb;  // bytes per tile
+    int n_rb, ksn, b0;
+};
+
+__device__ Seg seg_info(const DecodeArgs& a, int s) {
+    const int NQKV = (a.H + 2 * a.KV) * a.HD;
+    const int ksD = a.D / kTileCols;
+    Seg g;
+    if (s >= 4 * a.n_layers) {
+        g.src = a.lm_head;
+        g.n_rb = (a.V + kTileRowsF32 - 1) / kTileRowsF32;
+        g.ksn = ksD;
+        g.tb = kTileBytesF32;
+    } else {
+        const DecodeLayer& L = a.layers[s >> 2];
+        g.tb = kTileBytesI8;
+        switch (s & 3) {
+            case 0: g.src = L.qkv; g.n_rb = (NQKV + 15) / 16; g.ksn = ksD; break;
+            case 1: g.src = L.o; g.n_rb = (a.D + 15) / 16; g.ksn = (a.H * a.HD) / kTileCols; break;
+            case 2: g.src = L.w13; g.n_rb = (2 * a.F + 15) / 16; g.ksn = ksD; break;
+            default: g.src = L.w2; g.n_rb = (a.D + 15) / 16; g.ksn = a.F / kTileCols; break;
+        }
+    }
+    int b1;
+    split(g.n_rb, g.b0, b1);
+    g.src += static_cast<size_t>(g.b0) * g.ksn * g.tb;
+    g.n = (b1 - g.b0) * g.ksn;
+    return g;
+}
+
 struct Producer {
+    const DecodeArgs& a;
     const Shared& sh;
     int stages;
-    uint32_t it = 0;  // ring slots used so far
-    int slot = 0;     // it % stages, kept incrementally
-    uint32_t rnd = 0; // it / stages
+    uint32_t it = 0;   // ring slots used so far
+    int slot = 0;      // it % stages, kept incrementally
+    uint32_t rnd = 0;  // it / stages
     bool ok = true;
-    int* a_dbg = nullptr;
-    int* a_err = nullptr;
-    unsigned long long* trace = nullptr;
-    int n_phases = 0;
+    int n_segs;
+    int* a_dbg;
+    int* a_err;
+    // L2 prefetch cursor, `a.prefetch` slots ahead of the copies
+    int pseg = 0, pi = 0;
+    Seg pg;
 
-    __device__ Producer(const Shared& s, int st) : sh(s), stages(st) {}
+    __device__ Producer(const DecodeArgs& args, const Shared& s, int st)
+        : a(args), sh(s), stages(st), n_segs(4 * args.n_layers + 1), a_dbg(args.dbg), a_err(args.err) {}
 
     // Trace: time of the last issue of tiled phase `ph`.
-    __device__ void stamp(int ph) const {
-        if (trace) trace[(static_cast<size_t>(blockIdx.x) * n_phases + ph) * kTraceEvents + 6] = globaltimer();
+    __device__ void stamp(int seg) const {
+        if (!a.trace) return;
+        const int n_phases = 5 * a.n_layers + 1;
+        const int ph = (seg >= 4 * a.n_layers) ? 5 * a.n_layers : 5 * (seg >> 2) + ((seg & 3) == 0 ? 0 : (seg & 3) + 1);
+        a.trace[(static_cast<size_t>(blockIdx.x) * n_phases + ph) * kTraceEvents + 6] = globaltimer();
     }
 
-    // This CTA's tiles of one phase, kTilesPerStage per bulk copy.
-    __device__ void range(const uint8_t* base, int n_rb, int ksn, uint32_t tile_bytes) {
-        int b0, b1;
-        split(n_rb, b0, b1);
-        const uint8_t* src = base + static_cast<size_t>(b0) * ksn * tile_bytes;
-        const int n = (b1 - b0) * ksn;
-        for (int i = 0; i < n && ok; i += kTilesPerStage, it++) {
-            const int s = slot;
-            const uint32_t round = rnd;
-            if (++slot == stages) {
-                slot = 0;
-                rnd++;
+    // Prefetch the next slot of the prefetch cursor into L2.
+    __device__ void prefetch_next() {
+        while (pseg < n_segs && pi >= pg.n) {
+            if (++pseg < n_segs) {
+                pg = seg_info(a, pseg);
+                pi = 0;
             }
-            if (round > 0 && !mbar_wait(&sh.empty[s], (round - 1) & 1)) {
-                ok = false;
-                break;
-            }
-            if (*reinterpret_cast<volatile int*>(&sh.flags[0])) {
-                ok = false;
-                break;
-            }
-            const uint32_t bytes = static_cast<uint32_t>(min(kTilesPerStage, n - i)) * tile_bytes;
-            const uint8_t* gsrc = src + static_cast<size_t>(i) * tile_bytes;
-            if (!TLD_OK(s >= 0 && s < stages, 2, s, stages) ||
-                !TLD_OK(bytes > 0 && bytes <= kStageBytes && (bytes & 15) == 0, 3, bytes, i) ||
-                !TLD_OK(static_cast<size_t>(b0 * ksn + i) * tile_bytes + bytes <=
-                            static_cast<size_t>(n_rb) * ksn * tile_bytes, 4, b0 * ksn + i, n_rb * ksn) ||
-                !TLD_OK((reinterpret_cast<uintptr_t>(gsrc) & 15) == 0, 5, reinterpret_cast<uintptr_t>(gsrc) & 15, 0)) {
-                ok = false;
-                break;
-            }
-            mbar_expect_tx(&sh.full[s], bytes);
-            bulk_load(sh.ring + static_cast<size_t>(s) * kStageBytes, src + static_cast<size_t>(i) * tile_bytes, bytes,
-                      &sh.full[s]);
         }
+        if (pseg >= n_segs) return;
+        const uint32_t bytes = static_cast<uint32_t>(min(kTilesPerStage, pg.n - pi)) * pg.tb;
+        prefetch_l2(pg.src + static_cast<size_t>(pi) * pg.tb, bytes);
+        pi += kTilesPerStage;
+    }
+
+    __device__ void run() {
+        if (a.prefetch > 0) {
+            pg = seg_info(a, 0);
+            for (int j = 0; j < a.prefetch; j++) prefetch_next();
+        }
+        for (int sg = 0; sg < n_segs && ok; sg++) {
+            const Seg g = seg_info(a, sg);
+            for (int i = 0; i < g.n && ok; i += kTilesPerStage, it++) {
+                const int s = slot;
+                const uint32_t round = rnd;
+                if (++slot == stages) {
+                    slot = 0;
+                    rnd++;
+                }
+                if (round > 0 && !mbar_wait(&sh.empty[s], (round - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                if (*reinterpret_cast<volatile int*>(&sh.flags[0])) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t bytes = static_cast<uint32_t>(min(kTilesPerStage, g.n - i)) * g.tb;
+                const uint8_t* gsrc = g.src + static_cast<size_t>(i) * g.tb;
+                if (!TLD_OK(bytes > 0 && bytes <= kStageBytes && (bytes & 15) == 0, 3, bytes, i) ||
+                    !TLD_OK(static_cast<size_t>(g.b0 * g.ksn + i) * g.tb + bytes <=
+                                static_cast<size_t>(g.n_rb) * g.ksn * g.tb, 4, g.b0 * g.ksn + i, g.n_rb * g.ksn) ||
+                    !TLD_OK((reinterpret_cast<uintptr_t>(gsrc) & 15) == 0, 5, reinterpret_cast<uintptr_t>(gsrc) & 15,
+                            0)) {
+                    ok = false;
+                    break;
+                }
+                mbar_expect_tx(&sh.full[s], bytes);
+                bulk_load(sh.ring + static_cast<size_t>(s) * kStageBytes, gsrc, bytes, &sh.full[s]);
+                if (a.prefetch > 0) prefetch_next();
+            }
+            stamp(sg);
+        }
+        drain();
     }
 
     // Every copy issued must land before the CTA exits.
@@ -305,7 +356,7 @@ struct Consumer {
     int t, lane, warp;
     int slot = 0;            // ring slot of the next tile pair
     uint32_t phase_bit = 0;  // parity of its current round
-    unsigned barriers = 0;
+    int phase = 0;           // current phase: 5 per layer (qkv, attention, o, gate/up, down), then lm_head
     int* a_dbg;
     int* a_err;
 
@@ -313,7 +364,6 @@ struct Consumer {
         : a(args), sh(s), stages(st), t(threadIdx.x), lane(threadIdx.x & 31), warp(threadIdx.x >> 5),
           a_dbg(args.dbg), a_err(args.err) {}
 
-    int phase = 0;  // trace slot of the current phase
     __device__ __forceinline__ void stamp(int ev) const {
         if (a.trace && t == 0) {
             const int n_phases = 5 * a.n_layers + 1;
@@ -347,132 +397,203 @@ struct Consumer {
         return make_float2(rs, rm);
     }
 
-    // Thread 0: bring the next phase's activation (fp32, n floats) and, for a
-    // normalised phase, its RMSNorm gain (D floats at byte 4 D) into xbuf
-    // with bulk copies completing on sh.abar.  Called only after every
-    // consumer warp is done with xbuf.
-    __device__ void fetch(const float* act, int n, const float* g) {
-        if (t != 0) return;
-        const uint32_t bytes = static_cast<uint32_t>(n) * 4u + (g ? static_cast<uint32_t>(a.D) * 4u : 0u);
-        if (!TLD_OK(static_cast<size_t>(n) * 4 <= (g ? 4 * static_cast<size_t>(a.D) : xbuf_bytes(a.D, a.F, a.HD)) &&
-                        bytes <= xbuf_bytes(a.D, a.F, a.HD), 20, n, bytes) ||
-            !TLD_OK(((reinterpret_cast<uintptr_t>(act) | reinterpret_cast<uintptr_t>(g)) & 15) == 0, 21,
-                    reinterpret_cast<uintptr_t>(act) & 15, reinterpret_cast<uintptr_t>(g) & 15))
-            return;
-        // order this thread's acquire (generic proxy) before the async-proxy
-        // reads of global memory, and the CTA's earlier generic accesses to
-        // xbuf (made visible to this thread by the preceding bar.sync) before
-        // the async-proxy writes into it
-        asm volatile("fence.proxy.async.global;" ::: "memory");
-        fence_proxy_async_smem();
-        mbar_expect_tx(sh.abar, bytes);
-        bulk_load(sh.xbuf, act, static_cast<uint32_t>(n) * 4u, sh.abar);
-        if (g) bulk_load(sh.xbuf + 4 * static_cast<size_t>(a.D), g, static_cast<uint32_t>(a.D) * 4u, sh.abar);
-    }
-    uint32_t fetches = 0;
+    // ---- phase hand-over -------------------------------------------------
+    // At the end of every phase each CTA publishes one entry {sum, max} of
+    // the vector it wrote (sum x^2, max |x g| for h; max |x| for act and ctx;
+    // zeros otherwise) into buffer phase % 2, then arrives at the grid
+    // barrier: a monotonic counter incremented with a release by one thread
+    // per CTA (after a CTA-wide bar.sync), polled with acquire loads.  Every
+    // CTA waits at every barrier, so the counter reaches G (p + 1) exactly
+    // when all G CTAs have finished phase p, and no CTA is ever more than one
+    // phase ahead of another: two statistics buffers suffice.
 
-    // Grid-wide barrier over all CTAs' consumers, then (thread 0) the fetch of
-    // the next phase's activation; false on error/abort.
-    __device__ bool grid_barrier(const float* act = nullptr, int n = 0, const float* g = nullptr) {
-        barriers++;
-        const unsigned target = barriers * gridDim.x;
-        consumer_sync();
-        stamp(4);
-        if (t == 0) {
-            __threadfence();
-            atomicAdd(a.bar, 1u);
-            const unsigned long long t0 = globaltimer();
-            bool ok = true;
-            for (unsigned i = 0;; i++) {
-                if (ld_acquire(a.bar) >= target) break;
-                if (ld_volatile(a.err)) {
-                    *reinterpret_cast<volatile int*>(&sh.flags[0]) = 1;
-                    ok = false;
-                    break;
-                }
-                if ((i & 63) == 63 && globaltimer() - t0 > kTimeoutNs) {
-                    fail(kErrBarrier);
-                    ok = false;
-                    break;
-                }
-                __nanosleep(32);
-            }
-            if (ok && act) fetch(act, n, g);
+    // Every thread: (sum vec^2, max |vec g|) computed by this CTA (layer 0's input).
+    __device__ float2 local_stats(const float* vec, int d, const float* g) {
+        float ss = 0.f, mx = 0.f;
+        for (int i = t; i < d; i += kConsumers) {
+            const float v = __ldg(vec + i);
+            ss += v * v;
+            mx = fmaxf(mx, fabsf(v * __ldg(g + i)));
         }
-        consumer_sync();
-        stamp(5);
+        return sum_max(ss, mx);
+    }
+
+    // Ends the current phase: publishes this CTA's partial and arrives (all
+    // consumer threads call).
+    __device__ void publish(float ss, float mx) {
+        const float2 r = sum_max(ss, mx);  // ends with a bar.sync after all writes of the phase
+        if (t == 0) {
+            a.stats[static_cast<size_t>(phase & 1) * kStatsCap + blockIdx.x] = r;
+            // release: the CTA's writes (ordered before by the bar.sync) become
+            // visible to every CTA that acquires the count past this arrival
+            asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.bar), "r"(1u) : "memory");
+        }
+        stamp(4);
         phase++;
         stamp(0);
-        return !aborted();
     }
 
-    // Waits for the fetched activation; false (uniform) on timeout.
-    __device__ bool wait_fetch() {
-        const bool ok = mbar_wait(sh.abar, fetches & 1);
-        fetches++;
-        if (!ok) fail(kErrFetch);
-        consumer_sync();
-        return !aborted();
-    }
-
-    // Stages the fetched activation in place (modules.cpp:31-46 RMSNorm with
-    // the fetched gain when `norm`, e = 1e-5f from modules.h:24).
-    //   kHalf: column c becomes the 4-byte word {hi, lo} (fp16) of x_c 2^k,
-    //          k chosen so that max|x| 2^k < 2^14; returns 2^-k.
-    //   kFp32: column c becomes the normalised fp32 x_c; returns 1.
-    // Each thread rewrites only the columns it read, so no register copy of
-    // the vector is needed.
-    enum { kHalf = 0, kFp32 = 1 };
-    __device__ float stage(int d, bool norm, int mode) {
-        if (!TLD_OK(4 * static_cast<size_t>(d) <= xbuf_bytes(a.D, a.F, a.HD) && (!norm || d == a.D), 30, d, norm))
-            return 1.0f;
-        float* xs = reinterpret_cast<float*>(sh.xbuf);
-        const float* gs = xs + a.D;
-        float ss = 0.f, m = 0.f;
-        for (int col = t; col < d; col += kConsumers) {
-            const float x = xs[col];
-            ss += x * x;
-            m = fmaxf(m, fabsf(norm ? x * gs[col] : x));
+    // Waits until every CTA has published the previous phase; false (uniform)
+    // on error or timeout.
+    __device__ bool wait_all() {
+        if (t == 0) {
+            const unsigned target = static_cast<unsigned>(phase) * gridDim.x;
+            const unsigned long long t0 = globaltimer();
+            for (unsigned i = 0;; i++) {
+                if (ld_acquire(a.bar) >= target) break;
+                if ((i & 63) == 63) {
+                    if (ld_volatile(a.err)) {
+                        *reinterpret_cast<volatile int*>(&sh.flags[0]) = 1;
+                        break;
+                    }
+                    if (globaltimer() - t0 > kTimeoutNs) {
+                        fail(kErrBarrier);
+                        break;
+                    }
+                }
+            }
         }
+        consumer_sync();
         stamp(1);
-        const float2 r = sum_max(ss, m);
-        const float inv = norm ? 1.0f / sqrtf(r.x / static_cast<float>(d) + 1e-5f) : 1.0f;
-        const float amax = norm ? r.y * inv * 1.0001f : r.y;  // bound on max|x|
+        return !aborted();
+    }
+
+    // Every thread: (sum of the sums, max of the maxima) of the previous
+    // phase's G entries, reduced in a fixed order (bit-identical in all CTAs);
+    // the first 256 are loaded together.  Call after wait_all().
+    __device__ float2 read_stats() const {
+        const float2* s = a.stats + static_cast<size_t>((phase - 1) & 1) * kStatsCap;
+        const int n = gridDim.x;
+        float2 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = (lane + 32 * j < n) ? __ldcg(s + lane + 32 * j) : make_float2(0.f, 0.f);
+        float ss = 0.f, mx = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            ss += v[j].x;
+            mx = fmaxf(mx, v[j].y);
+        }
+        for (int i = lane + 256; i < n; i += 32) {
+            const float2 w = __ldcg(s + i);
+            ss += w.x;
+            mx = fmaxf(mx, w.y);
+        }
+        return make_float2(warp_sum(ss), warp_max(mx));
+    }
+
+    // Converts 16 staged columns (block b) to digits and stores them.
+    __device__ __forceinline__ void put_digits(int b, const float (&v)[16], float sc) {
+        uint32_t w0[4], w1[4], w2[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            int x[4], y[4], z[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                x[j] = __float2int_rn(v[4 * q + j] * sc);
+                y[j] = (x[j] + 128) >> 8;  // (X - d2) / 256
+                z[j] = (y[j] + 128) >> 8;  // (X1 - d1) / 256 = d0
+            }
+            w2[q] = pack_lo_bytes(x[0], x[1], x[2], x[3]);
+            w1[q] = pack_lo_bytes(y[0], y[1], y[2], y[3]);
+            w0[q] = pack_lo_bytes(z[0], z[1], z[2], z[3]);
+        }
+        uint8_t* dst = sh.xbuf + (b >> 2) * kGroupDigitBytes + (b & 3) * 16;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+        *reinterpret_cast<uint4*>(dst + 64) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+        *reinterpret_cast<uint4*>(dst + 128) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
+    }
+
+    // Stages the phase input x into xbuf as int8 digits of X = rint(x 2^k):
+    //   X = 2^16 d0 + 2^8 d1 + d2, |X| <= 2^22, so |d0| <= 64 and d1, d2 are
+    //   the balanced base-256 digits in [-128, 127].
+    // x = vec, or RMSNorm(vec) = (vec * inv) * g (modules.cpp:31-46, eps 1e-5f
+    // from modules.h:24) when NORM; the whole vector's (sum vec^2, max |vec g|
+    // or max |vec|) is *local (layer 0) or the previous phase's published
+    // partials.  Column 64 j + i of digit n lands at byte 192 j + 64 n + i,
+    // the B-operand rows of tile_i8.  The statistics and the first NB blocks
+    // of 16 columns per thread are loaded together (one L2 round trip).
+    // Returns 2^-k.
+    template <bool NORM>
+    __device__ float stage_digits(const float* vec, int d, const float* g, const float2* local) {
+        constexpr int NB = NORM ? 2 : 4;
+        if (!TLD_OK(3 * static_cast<size_t>(d) <= xbuf_bytes(a.D, a.F, a.HD) && d % 64 == 0, 30, d, 0)) return 1.0f;
+        const int nb = d / 16;
+        const float4* v4 = reinterpret_cast<const float4*>(vec);
+        const float4* g4 = reinterpret_cast<const float4*>(g);
+        float4 vb[NB][4], gb[NB][4];
+#pragma unroll
+        for (int i = 0; i < NB; i++) {
+            const int b = t + i * kConsumers;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                vb[i][q] = (b < nb) ? __ldcg(v4 + 4 * b + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (NORM) gb[i][q] = (b < nb) ? __ldg(g4 + 4 * b + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        const float2 st = local ? *local : read_stats();
+        const float inv = NORM ? 1.0f / sqrtf(st.x / static_cast<float>(d) + 1e-5f) : 1.0f;
+        const float amax = NORM ? st.y * inv * 1.0001f : st.y;  // bound on max|x|
         int e = 0;
-        if (amax > 0.f) frexpf(amax, &e);
-        const int k = ::min(::max(14 - e, -120), 120);
-        const float sc = (mode == kHalf) ? ldexpf(1.0f, k) : 1.0f;
-        // kHalf layout: in each block of 16 columns [16 b, 16 b + 16), word
-        // 16 b + m (m < 8) holds {hi[16 b + 2m], hi[16 b + 2m + 1]} and word
-        // 16 b + 8 + m the lo pair: exactly the mma B-operand registers of the
-        // x_hi (lanes 0-3) and x_lo (lanes 4-7) columns.  A block lies in one
-        // warp (columns t + 256 i), so a warp sync separates reads from writes.
-        uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
-        for (int col = t; col < d; col += kConsumers) {
-            float x = xs[col];
-            if (norm) x = (x * inv) * gs[col];
-            if (mode == kFp32) {
-                xs[col] = x;
-            } else {
-                const float xsc = x * sc;
-                const __half hi = __float2half_rn(xsc);
-                const __half lo = __float2half_rn(xsc - __half2float(hi));
-                const unsigned short hb = __half_as_ushort(hi), lb = __half_as_ushort(lo);
-                const unsigned short hp = __shfl_xor_sync(FULL, hb, 1), lp = __shfl_xor_sync(FULL, lb, 1);
-                __syncwarp();
-                const int j = col & 15;
-                uint32_t* blk = xw + (col & ~15);
-                if ((j & 1) == 0) blk[j >> 1] = static_cast<uint32_t>(hb) | (static_cast<uint32_t>(hp) << 16);
-                else blk[8 + (j >> 1)] = static_cast<uint32_t>(lp) | (static_cast<uint32_t>(lb) << 16);
-                __syncwarp();
+        if (amax > 0.f) frexpf(amax, &e);  // amax < 2^e
+        const int k = ::min(::max(22 - e, -120), 120);
+        const float sc = ldexpf(1.0f, k);
+        for (int base = 0;; base += NB * kConsumers) {
+#pragma unroll
+            for (int i = 0; i < NB; i++) {
+                const int b = t + base + i * kConsumers;
+                if (b < nb) {
+                    float v[16];
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        float4 f = vb[i][q];
+                        if (NORM) {
+                            const float4 gg = gb[i][q];
+                            f = make_float4((f.x * inv) * gg.x, (f.y * inv) * gg.y, (f.z * inv) * gg.z,
+                                            (f.w * inv) * gg.w);
+                        }
+                        v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+                    }
+                    put_digits(b, v, sc);
+                }
+            }
+            if (base + NB * kConsumers >= nb) break;
+            // longer vectors: next batch
+#pragma unroll
+            for (int i = 0; i < NB; i++) {
+                const int b = t + base + NB * kConsumers + i * kConsumers;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    vb[i][q] = (b < nb) ? __ldcg(v4 + 4 * b + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (NORM) gb[i][q] = (b < nb) ? __ldg(g4 + 4 * b + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
             }
         }
         consumer_sync();
         stamp(2);
-        return (mode == kHalf) ? ldexpf(1.0f, -k) : 1.0f;
+        return ldexpf(1.0f, -k);
+    }
+
+    // Stages RMSNorm(vec) (modules.cpp:31-46) as fp32 for the fp32 lm_head tiles.
+    __device__ void stage_f32(const float* vec, int d, const float* g) {
+        if (!TLD_OK(4 * static_cast<size_t>(d) <= xbuf_bytes(a.D, a.F, a.HD) && d % 4 == 0, 31, d, 0)) return;
+        const float2 st = read_stats();
+        const float inv = 1.0f / sqrtf(st.x / static_cast<float>(d) + 1e-5f);
+        float4* xs = reinterpret_cast<float4*>(sh.xbuf);
+        for (int i = t; i < d / 4; i += kConsumers) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(vec) + i);
+            const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + i);
+            xs[i] = make_float4((v.x * inv) * gg.x, (v.y * inv) * gg.y, (v.z * inv) * gg.z, (v.w * inv) * gg.w);
+        }
+        consumer_sync();
+        stamp(2);
     }
 
     // One int8 tile (16 rows x 512 columns) into pbuf[tile][0..15].
+    // Lane (r, c) = (lane / 4, lane % 4).  Per 64-column group, two
+    // m16n8k32 integer MMAs: A = the raw weights (the lane's 16 bytes of rows
+    // r and r + 8 are its A registers), B column n < 3 = digit n of x (lanes
+    // with r = n load it), columns 3..7 zero.  The s32 results are exact;
+    // lane c = 0 holds columns 0, 1 (d0, d1), lane c = 1 column 2 (d2).
     __device__ __forceinline__ void tile_i8(const uint8_t* st, int ks, float* out) {
         const int r = lane >> 2, c = lane & 3;
         const float* sc = reinterpret_cast<const float*>(st + 8192);
@@ -480,35 +601,28 @@ struct Consumer {
         const float4 s1 = *reinterpret_cast<const float4*>(sc + r * 8 + 4);
         const float4 s8a = *reinterpret_cast<const float4*>(sc + (r + 8) * 8);
         const float4 s8b = *reinterpret_cast<const float4*>(sc + (r + 8) * 8 + 4);
-        const float sr[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-        const float sr8[8] = {s8a.x, s8a.y, s8a.z, s8a.w, s8b.x, s8b.y, s8b.z, s8b.w};
-        // B registers of columns 512 ks + 64 g + 16 c + [0, 16): lanes 0-3 the
-        // hi pairs (words 0-7 of the block), lanes 4-7 the lo pairs (8-15).
-        const uint32_t* xw =
-            reinterpret_cast<const uint32_t*>(sh.xbuf) + ks * kTileCols + c * 16 + (lane >= 4 ? 8 : 0);
+        // c = 0 lanes fold d0 in as (256 d0 + d1) * 256
+        const float w = (c == 0) ? 256.f : 1.f;
+        const int ms = (c == 0) ? 256 : 1;
+        const float sr[8] = {s0.x * w, s0.y * w, s0.z * w, s0.w * w, s1.x * w, s1.y * w, s1.z * w, s1.w * w};
+        const float sr8[8] = {s8a.x * w, s8a.y * w, s8a.z * w, s8a.w * w,
+                              s8b.x * w, s8b.y * w, s8b.z * w, s8b.w * w};
+        const uint8_t* xd = sh.xbuf + ks * (8 * kGroupDigitBytes) + (r < 3 ? r : 0) * 64 + c * 16;
         float yr = 0.f, yr8 = 0.f;
 #pragma unroll
         for (int g = 0; g < 8; g++) {
             const uint4 ar = lds128(st + g * 1024 + lane * 16);
             const uint4 ar8 = lds128(st + g * 1024 + 512 + lane * 16);
-            uint4 b0 = make_uint4(0, 0, 0, 0), b1 = make_uint4(0, 0, 0, 0);
-            if (lane < 8) {
-                b0 = lds128(xw + g * 64);
-                b1 = lds128(xw + g * 64 + 4);
-            }
-            float dacc[4] = {0.f, 0.f, 0.f, 0.f};
-            mma16816(dacc, u8x2_lo_to_h2(ar.x), u8x2_lo_to_h2(ar8.x), u8x2_hi_to_h2(ar.x), u8x2_hi_to_h2(ar8.x),
-                     b0.x, b0.y);
-            mma16816(dacc, u8x2_lo_to_h2(ar.y), u8x2_lo_to_h2(ar8.y), u8x2_hi_to_h2(ar.y), u8x2_hi_to_h2(ar8.y),
-                     b0.z, b0.w);
-            mma16816(dacc, u8x2_lo_to_h2(ar.z), u8x2_lo_to_h2(ar8.z), u8x2_hi_to_h2(ar.z), u8x2_hi_to_h2(ar8.z),
-                     b1.x, b1.y);
-            mma16816(dacc, u8x2_lo_to_h2(ar.w), u8x2_lo_to_h2(ar8.w), u8x2_hi_to_h2(ar.w), u8x2_hi_to_h2(ar8.w),
-                     b1.z, b1.w);
-            // column 0 holds W x_hi, column 1 W x_lo (lanes with c == 0)
-            yr = fmaf(dacc[0] + dacc[1], sr[g], yr);
-            yr8 = fmaf(dacc[2] + dacc[3], sr8[g], yr8);
+            uint4 b = make_uint4(0, 0, 0, 0);
+            if (r < 3) b = lds128(xd + g * kGroupDigitBytes);
+            int dd[4] = {0, 0, 0, 0};
+            imma16832(dd, ar.x, ar8.x, ar.y, ar8.y, b.x, b.y);
+            imma16832(dd, ar.z, ar8.z, ar.w, ar8.w, b.z, b.w);
+            yr = fmaf(static_cast<float>(dd[0] * ms + dd[1]), sr[g], yr);
+            yr8 = fmaf(static_cast<float>(dd[2] * ms + dd[3]), sr8[g], yr8);
         }
+        yr += __shfl_xor_sync(FULL, yr, 1);
+        yr8 += __shfl_xor_sync(FULL, yr8, 1);
         if (c == 0) {
             out[r] = yr;
             out[r + 8] = yr8;
@@ -549,8 +663,8 @@ struct Consumer {
         const int n_slots = (n_tiles + kTilesPerStage - 1) / kTilesPerStage;
         constexpr int ROWS = F32 ? kTileRowsF32 : kTileRowsI8;
         constexpr int TB = F32 ? kTileBytesF32 : kTileBytesI8;
-        int my_i = warp;            // next tile of this warp
-        int my_ks = warp % ksn;     // its k-slice, kept incrementally
+        int my_i = warp;         // next tile of this warp
+        int my_ks = warp % ksn;  // its k-slice, kept incrementally
         for (int j = 0; j < n_slots; j++) {
             const int s = slot;
             const uint32_t par = phase_bit;
@@ -590,13 +704,28 @@ struct Consumer {
     }
 
     // int8 phase; KIND 0 q/k/v, 1 o_proj (+res), 2 gate/up, 3 down (+res).
+    // Kinds 1 and 3 publish (sum h^2, max |h g_next|) of the rows they wrote,
+    // kind 2 (0, max |act|), kind 0 zeros.
     template <int KIND>
-    __device__ bool run_i8(int n_rows, int d, float unscale, const float* res) {
+    __device__ bool run_i8(int n_rows, int d, float unscale, const float* res, const float* g_next) {
         const int ksn = d / kTileCols;
         const int n_rb = (n_rows + kTileRowsI8 - 1) / kTileRowsI8;
+        // the first epilogue row's residual and next-norm gain, loaded before
+        // the tiles so the epilogue does not wait on them
+        float res0 = 0.f, g0 = 0.f;
+        if (KIND == 1 || KIND == 3) {
+            int b0, b1;
+            split(n_rb, b0, b1);
+            const int row = b0 * 16 + t;
+            if (t < (b1 - b0) * 16 && row < n_rows) {
+                res0 = __ldcg(res + row);
+                g0 = __ldg(g_next + row);
+            }
+        }
         int nrl = 0;
         const int rb0 = run_tiles<false>(n_rb, ksn, nrl);
         if (rb0 < 0) return false;
+        float ss = 0.f, mx = 0.f;
         if (KIND == 2) {
             for (int j = t; j < nrl * 8; j += kConsumers) {
                 const int rbl = j / 8, o = j % 8;
@@ -604,7 +733,9 @@ struct Consumer {
                 if (row < n_rows / 2) {
                     const float gate = row_sum(rbl, o, ksn, 16) * unscale;
                     const float up = row_sum(rbl, o + 8, ksn, 16) * unscale;
-                    a.act[row] = (gate / (1.0f + expf(-gate))) * up;  // silu * up, kernels.cpp:98-102, 127-131
+                    const float v = (gate / (1.0f + expf(-gate))) * up;  // silu * up, kernels.cpp:98-102, 127-131
+                    a.act[row] = v;
+                    mx = fmaxf(mx, fabsf(v));
                 }
             }
         } else {
@@ -613,28 +744,41 @@ struct Consumer {
                 const int row = (rb0 + rbl) * 16 + rr;
                 if (row < n_rows) {
                     const float v = row_sum(rbl, rr, ksn, 16) * unscale;
-                    if (KIND == 0) a.qkv[row] = v;
-                    else a.h[row] = v + __ldcg(res + row);
+                    if (KIND == 0) {
+                        a.qkv[row] = v;
+                    } else {
+                        const bool first = (j == t);
+                        const float hv = v + (first ? res0 : __ldcg(res + row));
+                        a.h[row] = hv;
+                        ss += hv * hv;
+                        mx = fmaxf(mx, fabsf(hv * (first ? g0 : __ldg(g_next + row))));
+                    }
                 }
             }
         }
+        publish(ss, mx);
         return true;
     }
 
     // Attention for (head, split) = divmod(blockIdx.x, S) (modules.cpp:58-88).
+    // The merging CTA of head h publishes (0, max |ctx_h|) at index h.
     template <int HD>
-    __device__ void attention(int layer, unsigned pos) {
+    // Returns max |ctx_h| on the CTA that wrote ctx_h, else 0 (uniform); -1 on
+    // error.
+    __device__ float attention(int layer, unsigned pos) {
         constexpr int VPL = HD / 32;
         constexpr int HALF = HD / 2;
         constexpr int PF = 4;  // positions per warp in flight
         const DecodeLayer& L = a.layers[layer];
-        const int S = a.splits;
+        // splits over positions: one per 64 cached positions, at most a.splits
+        const int S = ::min(a.splits, (static_cast<int>(pos) + 64) / 64);
         const int u = blockIdx.x;
-        if (u >= a.H * S) return;
+        if (!wait_all()) return -1.f;  // q/k/v of every head written
+        if (u >= a.H * S) return 0.f;
         const int h = u / S, s = u % S, kh = h / 4;  // kv head h/4 (modules.cpp:70)
-        if (!TLD_OK(pos < static_cast<unsigned>(a.max_seq) && kh < a.KV && h < a.H, 40, pos, kh)) return;
+        if (!TLD_OK(pos < static_cast<unsigned>(a.max_seq) && kh < a.KV && h < a.H, 40, pos, kh)) return 0.f;
         if (!TLD_OK((3 * HD + kConsumerWarps * (HD + 2)) * 4 <= static_cast<int>(xbuf_bytes(a.D, a.F, a.HD)), 41, HD, 0))
-            return;
+            return 0.f;
         float* q_s = reinterpret_cast<float*>(sh.xbuf);
         float* k_s = q_s + HD;
         float* v_s = k_s + HD;
@@ -720,6 +864,29 @@ struct Consumer {
 #pragma unroll
         for (int j = 0; j < VPL; j++) mine[2 + lane * VPL + j] = acc[j];
         consumer_sync();
+        if (S == 1) {  // one CTA per head: merge the warps straight into ctx
+            float mx = 0.f;
+            if (t < HD) {
+                float M = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; w++)
+                    if (wp[w * (HD + 2) + 1] > 0.f) M = fmaxf(M, wp[w * (HD + 2)]);
+                float GL = 0.f, acc_t = 0.f;
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; w++) {
+                    const float lw = wp[w * (HD + 2) + 1];
+                    if (lw > 0.f) {
+                        const float e = expf(wp[w * (HD + 2)] - M);
+                        GL += lw * e;
+                        acc_t += wp[w * (HD + 2) + 2 + t] * e;
+                    }
+                }
+                const float c = acc_t / GL;
+                a.ctx[h * HD + t] = c;
+                mx = fabsf(c);
+            }
+            return mx;
+        }
         float M = -INFINITY;
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; w++)
@@ -745,9 +912,10 @@ struct Consumer {
             sh.flags[2] = (atomicAdd(a.attn_cnt + h, 1u) == static_cast<unsigned>(S) - 1);
         }
         consumer_sync();
-        if (!sh.flags[2]) return;  // uniform; flags[2] is next written after a later sync
+        if (!sh.flags[2]) return 0.f;  // uniform; flags[2] is next written after a later sync
         __threadfence();
         const float* ph = a.attn_part + static_cast<size_t>(h) * S * (HD + 2);
+        float mx = 0.f;
         if (t < HD) {
             float GM = -INFINITY;
             for (int j = 0; j < S; j++)
@@ -761,11 +929,13 @@ struct Consumer {
                     acc_t += __ldcg(ph + j * (HD + 2) + 2 + t) * w;
                 }
             }
-            a.ctx[h * HD + t] = acc_t / GL;
+            const float c = acc_t / GL;
+            a.ctx[h * HD + t] = c;
+            mx = fabsf(c);
         }
         if (t == 0) a.attn_cnt[h] = 0;
+        return mx;
     }
-
 };
 
 template <int HD>
@@ -776,7 +946,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
     {
         unsigned dyn;
         asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
-        const size_t end = reinterpret_cast<uint8_t*>(sh.abar + 1) - smem_raw;
+        const size_t end = reinterpret_cast<uint8_t*>(sh.empty + stages) - smem_raw;
         int* a_dbg = a.dbg;
         int* a_err = a.err;
         if (!TLD_OK(end <= dyn, 1, static_cast<long long>(end), dyn)) return;
@@ -787,7 +957,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
             mbar_init(&sh.full[s], 1);
             mbar_init(&sh.empty[s], kConsumerWarps);
         }
-        mbar_init(sh.abar, 1);
         sh.flags[0] = 0;
         sh.flags[1] = 0;
         sh.info[0] = __ldcg(a.pos);
@@ -805,26 +974,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
     if (threadIdx.x >= kConsumers) {
         // ---------------- producer warp ----------------
         if (threadIdx.x != kConsumers) return;
-        Producer p(sh, stages);
-        p.a_dbg = a.dbg;
-        p.a_err = a.err;
-        p.trace = a.trace;
-        p.n_phases = 5 * a.n_layers + 1;
-        const int ksD = D / kTileCols, ksF = F / kTileCols;
-        for (int l = 0; l < a.n_layers && p.ok; l++) {
-            const DecodeLayer& L = a.layers[l];
-            p.range(L.qkv, (NQKV + 15) / 16, ksD, kTileBytesI8);
-            p.stamp(5 * l);
-            p.range(L.o, (D + 15) / 16, (a.H * a.HD) / kTileCols, kTileBytesI8);
-            p.stamp(5 * l + 2);
-            p.range(L.w13, (2 * F + 15) / 16, ksD, kTileBytesI8);
-            p.stamp(5 * l + 3);
-            p.range(L.w2, (D + 15) / 16, ksF, kTileBytesI8);
-            p.stamp(5 * l + 4);
-        }
-        if (p.ok) p.range(a.lm_head, (a.V + 3) / 4, ksD, kTileBytesF32);
-        p.stamp(5 * a.n_layers);
-        p.drain();
+        Producer p(a, sh, stages);
+        p.run();
         return;
     }
 
@@ -833,39 +984,36 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
     cw.stamp(0);
     const unsigned pos = sh.info[0];
     const uint32_t token = sh.info[1];
-    const float* emb = a.embed + static_cast<size_t>(token) * D;
-    cw.fetch(emb, D, a.layers[0].g_in);  // layer 0 reads the embedding row (modules.cpp:5-7)
+    const float* emb = a.embed + static_cast<size_t>(token) * D;  // Embedding::forward (modules.cpp:5-7)
+    const float2 st0 = cw.local_stats(emb, D, a.layers[0].g_in);
     for (int l = 0; l < a.n_layers; l++) {
         const DecodeLayer& L = a.layers[l];
         const float* hin = (l == 0) ? emb : a.h;
         // q/k/v = W_qkv rmsnorm(h)
-        if (!cw.wait_fetch()) return;
-        float un = cw.stage(D, true, Consumer::kHalf);
-        if (!cw.run_i8<0>(NQKV, D, un, nullptr)) return;
-        if (!cw.grid_barrier()) return;
-        // attention; the last split of each head writes ctx
-        cw.attention<HD>(l, pos);
-        if (!cw.grid_barrier(a.ctx, a.H * a.HD, nullptr)) return;
+        if (l > 0 && !cw.wait_all()) return;
+        float un = cw.stage_digits<true>(hin, D, L.g_in, l == 0 ? &st0 : nullptr);
+        if (!cw.run_i8<0>(NQKV, D, un, nullptr, nullptr)) return;
+        // attention; ctx written by one CTA per head
+        const float mx = cw.attention<HD>(l, pos);
+        if (mx < 0.f) return;
+        cw.publish(0.f, mx);
         // h = h + W_o ctx
-        if (!cw.wait_fetch()) return;
-        un = cw.stage(a.H * a.HD, false, Consumer::kHalf);
-        if (!cw.run_i8<1>(D, a.H * a.HD, un, hin)) return;
-        if (!cw.grid_barrier(a.h, D, L.g_post)) return;
+        if (!cw.wait_all()) return;
+        un = cw.stage_digits<false>(a.ctx, a.H * a.HD, nullptr, nullptr);
+        if (!cw.run_i8<1>(D, a.H * a.HD, un, hin, L.g_post)) return;
         // act = silu(W1 x) * (W3 x), x = rmsnorm(h)
-        if (!cw.wait_fetch()) return;
-        un = cw.stage(D, true, Consumer::kHalf);
-        if (!cw.run_i8<2>(2 * F, D, un, nullptr)) return;
-        if (!cw.grid_barrier(a.act, F, nullptr)) return;
+        if (!cw.wait_all()) return;
+        un = cw.stage_digits<true>(a.h, D, L.g_post, nullptr);
+        if (!cw.run_i8<2>(2 * F, D, un, nullptr, nullptr)) return;
         // h = h + W2 act
-        if (!cw.wait_fetch()) return;
-        un = cw.stage(F, false, Consumer::kHalf);
-        if (!cw.run_i8<3>(D, F, un, a.h)) return;
+        if (!cw.wait_all()) return;
+        un = cw.stage_digits<false>(a.act, F, nullptr, nullptr);
         const float* g_next = (l + 1 < a.n_layers) ? a.layers[l + 1].g_in : a.g_final;
-        if (!cw.grid_barrier(a.h, D, g_next)) return;
+        if (!cw.run_i8<3>(D, F, un, a.h, g_next)) return;
     }
     // logits = lm_head rmsnorm(h); token = argmax (main.cpp:10-21)
-    if (!cw.wait_fetch()) return;
-    cw.stage(D, true, Consumer::kFp32);
+    if (!cw.wait_all()) return;
+    cw.stage_f32(a.h, D, a.g_final);
     const int ksD = D / kTileCols;
     const int n_rb = (a.V + kTileRowsF32 - 1) / kTileRowsF32;
     int nrl = 0;
@@ -976,11 +1124,8 @@ __global__ void k_repack_i8(uint8_t* dst, const int8_t* w1, const float* s1, con
         const int w = cc / 64, c = (cc % 64) / 16, r = rr & 7, half = rr >> 3;
         const int lane = 4 * r + c;
         uint8_t* out = dst + (static_cast<size_t>(rb) * ksn + ks) * kTileBytesI8 + w * 1024 + half * 512 + lane * 16;
-        uint4 v = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
-        if (row < n) {
-            v = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(row) * d + col);
-            v.x ^= 0x80808080u; v.y ^= 0x80808080u; v.z ^= 0x80808080u; v.w ^= 0x80808080u;
-        }
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (row < n) v = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(row) * d + col);
         *reinterpret_cast<uint4*>(out) = v;
     }
     // scales (already 1/s): one per (logical row, group)
@@ -1028,17 +1173,19 @@ __global__ void k_repack_f32(uint8_t* dst, const float* w, int n, int d) {
 
 }  // namespace
 
-bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int grid, int max_smem, int* stages,
-                        size_t* smem_bytes, int* pbuf_floats) {
+bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers, int grid, int max_smem,
+                        int* stages, size_t* smem_bytes, int* pbuf_floats) {
     if (D % kTileCols || F % kTileCols) return false;
     if (!(HD == 64 || HD == 128 || HD == 256) || H * HD != D || grid < 1) return false;
+    // statistics entries; the barrier counter reaches grid x (5 L + 1)
+    if (grid > kStatsCap || static_cast<long long>(grid) * (5 * n_layers + 1) >= (1ll << 31)) return false;
     // partial-sum buffer: the most tiles x rows any CTA owns in one phase
     auto need = [&](int n_rows, int rows_per_tile, int d) {
         const int n_rb = (n_rows + rows_per_tile - 1) / rows_per_tile;
         const int per_cta = (n_rb + grid - 1) / grid;
         return per_cta * (d / kTileCols) * rows_per_tile;
     };
-    int pb = 512;  // also the attention-merge scratch (m and l of up to 256 heads x splits)
+    int pb = 512;
     pb = std::max(pb, need((H + 2 * KV) * HD, kTileRowsI8, D));
     pb = std::max(pb, need(D, kTileRowsI8, H * HD));
     pb = std::max(pb, need(2 * F, kTileRowsI8, D));
@@ -1046,12 +1193,12 @@ bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int grid, in
     pb = std::max(pb, need(V, kTileRowsF32, D));
     const size_t fixed = fixed_bytes(D, F, HD, pb);
     if (static_cast<size_t>(max_smem) <= fixed) return false;
-    int st = static_cast<int>((static_cast<size_t>(max_smem) - fixed - 16) / (kStageBytes + 16));
+    int st = static_cast<int>((static_cast<size_t>(max_smem) - fixed) / (kStageBytes + 16));
     st = st > 24 ? 24 : st;
     if (st < 4) return false;
     *stages = st;
     *pbuf_floats = pb;
-    *smem_bytes = static_cast<size_t>(st) * kStageBytes + fixed + static_cast<size_t>(st) * 16 + 16;
+    *smem_bytes = static_cast<size_t>(st) * kStageBytes + fixed + static_cast<size_t>(st) * 16;
     return true;
 }
 

@@ -17,7 +17,7 @@ namespace tl {
 // block w covers columns [64w, 64w+64) (one quantisation group):
 //   byte  w*1024 + half*512 + lane*16 + j   holds  W[16 rb + 8 half + lane/4]
 //                                                 [512 ks + 64 w + 16 (lane%4) + j]
-// stored as q + 128 (q ^ 0x80), the bias the int8 -> fp16 splice expects;
+// stored as the signed int8 q itself (the integer MMA's A operand);
 //   float 2048 + rr*8 + w                    holds  1 / scale of row 16 rb + rr,
 //                                                 group 8 ks + w.
 // gate/up are interleaved: tile row rr < 8 is gate row 8 rb + rr, rr >= 8 is
@@ -31,6 +31,7 @@ constexpr int kTileRowsI8 = 16;
 constexpr int kTileBytesI8 = 8192 + 512;
 constexpr int kTileRowsF32 = 4;
 constexpr int kTileBytesF32 = 8192;
+constexpr int kStatsCap = 1024;  // most CTAs / heads publishing statistics
 
 struct DecodeLayer {
     const uint8_t* qkv;  // tiles of [q; k; v]   ((H + 2 KV) hd rows, d = D)
@@ -61,7 +62,7 @@ struct DecodeArgs {
     float* am_v;                // [grid] argmax partials
     uint32_t* am_i;
     unsigned* ticket;           // zero between launches (last CTA resets it)
-    unsigned* bar;              // grid barrier counter, zeroed before each launch
+    unsigned* bar;              // grid barrier counter, zero between launches (last CTA resets it)
     int* err;                   // nonzero after a bounded wait gave up
     uint32_t* token;            // in: this step's token; out: argmax
     unsigned* pos;              // in: position; out: position + 1
@@ -69,6 +70,10 @@ struct DecodeArgs {
     int D, F, H, KV, HD, V, max_seq, splits;
     int pbuf_floats;            // per-phase partial-sum buffer (decode_kernel_fits)
     float attn_scale;
+    // Phase hand-over statistics: [2][kStatsCap] {sum x^2, max |x|} of what
+    // each CTA wrote in a phase, alternating buffers per phase.
+    float2* stats;
+    int prefetch;               // tile pairs prefetched into L2 ahead of the ring (0 = off)
     // Optional phase trace (nullptr = off): per CTA, kTraceEvents %globaltimer
     // stamps for every phase, [cta][phase][event], phases = 5 per layer + lm_head.
     unsigned long long* trace;
@@ -84,8 +89,8 @@ constexpr int kTraceEvents = 8;
 
 // Shared-memory bytes, pipeline depth and partial-buffer size for a model
 // shape on `grid` CTAs; false when the shape cannot run in the persistent kernel.
-bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int grid, int max_smem, int* stages,
-                        size_t* smem_bytes, int* pbuf_floats);
+bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers, int grid, int max_smem,
+                        int* stages, size_t* smem_bytes, int* pbuf_floats);
 
 // Launch one decode step (cooperative: every CTA resident on its own SM).
 tl_status launch_decode_step(const DecodeArgs& a, int grid, int stages, size_t smem, cudaStream_t s);

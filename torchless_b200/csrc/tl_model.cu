@@ -238,6 +238,7 @@ struct tl_model {
     unsigned *bar = nullptr, *ticket = nullptr;
     int* err = nullptr;
     int* dbg = nullptr;  // self-check build: {site, v0, v1}
+    float2* stats = nullptr;  // persistent kernel: phase hand-over statistics [2][kStatsCap]
     double bytes_per_step = 0;
 };
 
@@ -407,8 +408,8 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         TL_CUDA_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->device));
         int pbuf = 0;
         if (coop && decode_kernel_fits(static_cast<int>(D), static_cast<int>(F), static_cast<int>(H),
-                                       static_cast<int>(KV), static_cast<int>(HD), static_cast<int>(V), dev_sms,
-                                       max_smem, &m->stages, &m->mega_smem, &pbuf)) {
+                                       static_cast<int>(KV), static_cast<int>(HD), static_cast<int>(V),
+                                       static_cast<int>(L), dev_sms, max_smem, &m->stages, &m->mega_smem, &pbuf)) {
             m->persistent = true;
             m->grid = dev_sms;
             // Tuning knob: a shallower weight ring (fewer bytes in flight per SM).
@@ -456,7 +457,8 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     const int part_splits = std::max(m->splits, m->mega_splits);
     size_t sbytes = 2 * A::pad(kv * 4) + 2 * A::pad(m->max_seq * half * 4) + A::pad(D * 4) + A::pad(NQKV * 4) +
                     A::pad(H * HD * 4) + A::pad(F * 4) + A::pad(V * 4) + A::pad(H * part_splits * (HD + 2) * 4) +
-                    A::pad(H * 4) + A::pad(am_grid * 4) * 2 + A::pad(4) * 6 + A::pad(16) + A::pad(m->max_seq * 4) * 2;
+                    A::pad(H * 4) + A::pad(am_grid * 4) * 2 + A::pad(4) * 6 + A::pad(16) + A::pad(m->max_seq * 4) * 2 +
+                    A::pad(2 * kStatsCap * sizeof(float2));
     TL_TRY(m->state.reserve(sbytes));
     TL_CUDA_TRY(cudaMemsetAsync(m->state.base, 0, sbytes, m->stream));
     m->kc = m->state.take<float>(kv);
@@ -481,7 +483,8 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     m->ticket = m->state.take<unsigned>(1);
     m->err = m->state.take<int>(1);
     m->dbg = m->state.take<int>(4);
-    if (!m->dbg) return set_error(TL_ERR_OUT_OF_MEMORY, "state arena too small (internal)");
+    m->stats = m->state.take<float2>(2 * kStatsCap);
+    if (!m->stats) return set_error(TL_ERR_OUT_OF_MEMORY, "state arena too small (internal)");
     if (m->persistent) {
         for (int64_t l = 0; l < L; l++) {
             m->layers_host_tmp[l].k_cache = m->kc + static_cast<size_t>(l) * layer_kv_floats(m.get());
@@ -493,7 +496,10 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         d.n_layers = static_cast<int>(L);
         d.embed = m->embed; d.g_final = m->norm; d.cos_tab = m->cos_tab; d.sin_tab = m->sin_tab;
         d.h = m->h; d.qkv = m->qkv; d.attn_part = m->attn_part; d.act = m->act; d.logits = m->logits;
-        d.ctx = m->ctx; d.attn_cnt = m->attn_cnt;
+        d.ctx = m->ctx; d.attn_cnt = m->attn_cnt; d.stats = m->stats;
+        // Tuning knob: tile pairs prefetched into L2 ahead of the ring.
+        d.prefetch = 8;
+        if (const char* e = std::getenv("TL_DECODE_PREFETCH")) d.prefetch = std::max(0, std::min(64, std::atoi(e)));
 #ifdef TL_DECODE_CHECK
         d.dbg = m->dbg;
 #endif
@@ -698,16 +704,17 @@ tl_status sync(tl_model* m) {
             return set_error(TL_ERR_INVALID_ARGUMENT, "decode kernel self-check: site %d values %d %d", dbg[0],
                              dbg[1], dbg[2]);
         }
-        // A bounded wait inside the kernel gave up: clear the barrier state so
-        // the next step starts clean, and report it.
+        // A bounded wait inside the kernel gave up: clear the barrier and
+        // ticket state so the next step starts clean, and report it.
         cudaMemsetAsync(m->bar, 0, 4, m->stream);
         cudaMemsetAsync(m->ticket, 0, 4, m->stream);
+        cudaMemsetAsync(m->attn_cnt, 0, sizeof(unsigned) * m->cfg.n_heads, m->stream);
         cudaMemsetAsync(m->err, 0, 4, m->stream);
         cudaStreamSynchronize(m->stream);
         m->h_pinned[3] = 0;
         if (code == 5) return set_error(TL_ERR_INVALID_ARGUMENT, "decode kernel: token or position out of range");
         return set_error(TL_ERR_TIMEOUT,
-                         "decode kernel wait timed out (code %u: 1 grid barrier, 2 tile arrival, 3 ring slot, 4 activation fetch)",
+                         "decode kernel wait timed out (code %u: 1 grid barrier, 2 tile arrival, 3 ring slot)",
                          code);
     }
     return TL_OK;
