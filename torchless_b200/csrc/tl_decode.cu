@@ -357,6 +357,7 @@ struct Consumer {
     int slot = 0;            // ring slot of the next tile pair
     uint32_t phase_bit = 0;  // parity of its current round
     int phase = 0;           // current phase: 5 per layer (qkv, attention, o, gate/up, down), then lm_head
+    int arrivals = 0;        // grid barriers this CTA has arrived at (4 per layer)
     int* a_dbg;
     int* a_err;
 
@@ -398,14 +399,15 @@ struct Consumer {
     }
 
     // ---- phase hand-over -------------------------------------------------
-    // At the end of every phase each CTA publishes one entry {sum, max} of
-    // the vector it wrote (sum x^2, max |x g| for h; max |x| for act and ctx;
-    // zeros otherwise) into buffer phase % 2, then arrives at the grid
-    // barrier: a monotonic counter incremented with a release by one thread
-    // per CTA (after a CTA-wide bar.sync), polled with acquire loads.  Every
-    // CTA waits at every barrier, so the counter reaches G (p + 1) exactly
-    // when all G CTAs have finished phase p, and no CTA is ever more than one
-    // phase ahead of another: two statistics buffers suffice.
+    // At the end of the attention, o, gate/up and down phases each CTA
+    // publishes one entry {sum, max} of the vector it wrote (sum x^2,
+    // max |x g| for h; max |x| for act and ctx) into buffer (barrier % 2),
+    // then arrives at the grid barrier: a monotonic counter incremented with
+    // a release by one thread per CTA (after a CTA-wide bar.sync), polled
+    // with acquire loads.  Every CTA waits at every barrier, so the counter
+    // reaches G b exactly when all G CTAs have arrived at barrier b, and no
+    // CTA is ever more than one barrier ahead of another: two statistics
+    // buffers suffice.  (q/k/v hands over to attention per kv group instead.)
 
     // Every thread: (sum vec^2, max |vec g|) computed by this CTA (layer 0's input).
     __device__ float2 local_stats(const float* vec, int d, const float* g) {
@@ -423,21 +425,22 @@ struct Consumer {
     __device__ void publish(float ss, float mx) {
         const float2 r = sum_max(ss, mx);  // ends with a bar.sync after all writes of the phase
         if (t == 0) {
-            a.stats[static_cast<size_t>(phase & 1) * kStatsCap + blockIdx.x] = r;
+            a.stats[static_cast<size_t>(arrivals & 1) * kStatsCap + blockIdx.x] = r;
             // release: the CTA's writes (ordered before by the bar.sync) become
             // visible to every CTA that acquires the count past this arrival
             asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.bar), "r"(1u) : "memory");
         }
+        arrivals++;
         stamp(4);
         phase++;
         stamp(0);
     }
 
-    // Waits until every CTA has published the previous phase; false (uniform)
-    // on error or timeout.
+    // Waits until every CTA has arrived at this CTA's latest barrier; false
+    // (uniform) on error or timeout.
     __device__ bool wait_all() {
         if (t == 0) {
-            const unsigned target = static_cast<unsigned>(phase) * gridDim.x;
+            const unsigned target = static_cast<unsigned>(arrivals) * gridDim.x;
             const unsigned long long t0 = globaltimer();
             for (unsigned i = 0;; i++) {
                 if (ld_acquire(a.bar) >= target) break;
@@ -462,7 +465,7 @@ struct Consumer {
     // phase's G entries, reduced in a fixed order (bit-identical in all CTAs);
     // the first 256 are loaded together.  Call after wait_all().
     __device__ float2 read_stats() const {
-        const float2* s = a.stats + static_cast<size_t>((phase - 1) & 1) * kStatsCap;
+        const float2* s = a.stats + static_cast<size_t>((arrivals - 1) & 1) * kStatsCap;
         const int n = gridDim.x;
         float2 v[8];
 #pragma unroll
@@ -705,7 +708,8 @@ struct Consumer {
 
     // int8 phase; KIND 0 q/k/v, 1 o_proj (+res), 2 gate/up, 3 down (+res).
     // Kinds 1 and 3 publish (sum h^2, max |h g_next|) of the rows they wrote,
-    // kind 2 (0, max |act|), kind 0 zeros.
+    // kind 2 (0, max |act|); kind 0 instead adds its rows to each kv group's
+    // ready count (qkv_cnt), which attention waits on.
     template <int KIND>
     __device__ bool run_i8(int n_rows, int d, float unscale, const float* res, const float* g_next) {
         const int ksn = d / kTileCols;
@@ -746,6 +750,10 @@ struct Consumer {
                     const float v = row_sum(rbl, rr, ksn, 16) * unscale;
                     if (KIND == 0) {
                         a.qkv[row] = v;
+                        // kv group of the row: q head / 4, or the k / v head
+                        const int hh = row / a.HD;
+                        const int grp = hh < a.H ? hh / 4 : (hh < a.H + a.KV ? hh - a.H : hh - a.H - a.KV);
+                        atomicAdd(reinterpret_cast<unsigned*>(sh.scratch) + 32 + grp, 1u);
                     } else {
                         const bool first = (j == t);
                         const float hv = v + (first ? res0 : __ldcg(res + row));
@@ -756,15 +764,31 @@ struct Consumer {
                 }
             }
         }
-        publish(ss, mx);
+        if (KIND == 0) {
+            // release each touched group's row count (after the bar.sync, so
+            // every thread's rows are covered), then clear the counts
+            consumer_sync();
+            if (t < a.KV) {
+                unsigned* cnt = reinterpret_cast<unsigned*>(sh.scratch) + 32 + t;
+                if (*cnt) {
+                    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.qkv_cnt + t), "r"(*cnt) : "memory");
+                    *cnt = 0;
+                }
+            }
+            stamp(4);
+            phase++;
+            stamp(0);
+        } else {
+            publish(ss, mx);
+        }
         return true;
     }
 
     // Attention for (head, split) = divmod(blockIdx.x, S) (modules.cpp:58-88).
-    // The merging CTA of head h publishes (0, max |ctx_h|) at index h.
+    // Starts as soon as kv group h / 4's q, k and v rows are written
+    // (qkv_cnt, no grid barrier).  Returns max |ctx_h| on the CTA that wrote
+    // ctx_h, else 0 (uniform); -1 on error.
     template <int HD>
-    // Returns max |ctx_h| on the CTA that wrote ctx_h, else 0 (uniform); -1 on
-    // error.
     __device__ float attention(int layer, unsigned pos) {
         constexpr int VPL = HD / 32;
         constexpr int HALF = HD / 2;
@@ -773,12 +797,31 @@ struct Consumer {
         // splits over positions: one per 64 cached positions, at most a.splits
         const int S = ::min(a.splits, (static_cast<int>(pos) + 64) / 64);
         const int u = blockIdx.x;
-        if (!wait_all()) return -1.f;  // q/k/v of every head written
         if (u >= a.H * S) return 0.f;
         const int h = u / S, s = u % S, kh = h / 4;  // kv head h/4 (modules.cpp:70)
         if (!TLD_OK(pos < static_cast<unsigned>(a.max_seq) && kh < a.KV && h < a.H, 40, pos, kh)) return 0.f;
         if (!TLD_OK((3 * HD + kConsumerWarps * (HD + 2)) * 4 <= static_cast<int>(xbuf_bytes(a.D, a.F, a.HD)), 41, HD, 0))
             return 0.f;
+        // wait until kv group kh's q, k and v rows of this layer are written
+        if (t == 0) {
+            const unsigned target = static_cast<unsigned>(layer + 1) * 6 * HD;
+            const unsigned long long t0 = globaltimer();
+            for (unsigned i = 0;; i++) {
+                if (ld_acquire(a.qkv_cnt + kh) >= target) break;
+                if ((i & 63) == 63) {
+                    if (ld_volatile(a.err)) {
+                        *reinterpret_cast<volatile int*>(&sh.flags[0]) = 1;
+                        break;
+                    }
+                    if (globaltimer() - t0 > kTimeoutNs) {
+                        fail(kErrBarrier);
+                        break;
+                    }
+                }
+            }
+        }
+        consumer_sync();
+        if (aborted()) return -1.f;
         float* q_s = reinterpret_cast<float*>(sh.xbuf);
         float* k_s = q_s + HD;
         float* v_s = k_s + HD;
@@ -959,6 +1002,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         }
         sh.flags[0] = 0;
         sh.flags[1] = 0;
+        for (int i = 32; i < 64; i++) reinterpret_cast<unsigned*>(sh.scratch)[i] = 0u;  // kv group row counts
         sh.info[0] = __ldcg(a.pos);
         sh.info[1] = __ldcg(a.token);
         fence_mbar_init();
@@ -995,7 +1039,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         if (!cw.run_i8<0>(NQKV, D, un, nullptr, nullptr)) return;
         // attention; ctx written by one CTA per head
         const float mx = cw.attention<HD>(l, pos);
-        if (mx < 0.f) return;
+        if (mx < 0.f || cw.aborted()) return;
         cw.publish(0.f, mx);
         // h = h + W_o ctx
         if (!cw.wait_all()) return;
@@ -1092,9 +1136,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         *a.token = bi;
         a.history[pos] = bi;
         *a.pos = pos + 1;
-        // Every CTA has passed every barrier and taken its ticket: reset both.
+        // Every CTA has passed every barrier and taken its ticket: reset the
+        // counters for the next step.
         *a.ticket = 0;
         *a.bar = 0;
+        for (int g = 0; g < a.KV; g++) a.qkv_cnt[g] = 0;
         __threadfence();
     }
 }
@@ -1177,6 +1223,7 @@ bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers
                         int* stages, size_t* smem_bytes, int* pbuf_floats) {
     if (D % kTileCols || F % kTileCols) return false;
     if (!(HD == 64 || HD == 128 || HD == 256) || H * HD != D || grid < 1) return false;
+    if (H != 4 * KV || KV > 32) return false;  // kv head h / 4; group row counts in smem
     // statistics entries; the barrier counter reaches grid x (5 L + 1)
     if (grid > kStatsCap || static_cast<long long>(grid) * (5 * n_layers + 1) >= (1ll << 31)) return false;
     // partial-sum buffer: the most tiles x rows any CTA owns in one phase

@@ -54,9 +54,10 @@ struct DecodeArgs {
     const float* sin_tab;
     float* h;                   // residual stream [D]
     float* qkv;                 // [(H + 2 KV) hd]
-    float* attn_part;           // [H][S][hd + 2]
+    float* attn_part;           // [H][S][hd + 2] split partials {max, sum, acc}
     float* ctx;                 // [H hd] merged attention output (o_proj input)
-    unsigned* attn_cnt;         // [H] split tickets, zero between launches
+    unsigned* attn_cnt;         // [H] split tickets per head, zero between launches
+    unsigned* qkv_cnt;          // [KV] q/k/v rows written per kv group, zero between launches
     float* act;                 // [F]
     float* logits;              // [V]
     float* am_v;                // [grid] argmax partials

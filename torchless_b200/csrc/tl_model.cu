@@ -221,6 +221,7 @@ struct tl_model {
     float *h = nullptr, *qkv = nullptr, *ctx = nullptr, *act = nullptr, *logits = nullptr;
     float *attn_part = nullptr, *am_v = nullptr;
     unsigned *attn_cnt = nullptr, *am_cnt = nullptr, *d_pos = nullptr;
+    unsigned* qkv_cnt = nullptr;  // persistent kernel: q/k/v rows written per kv group
     uint32_t *am_i = nullptr, *d_token = nullptr, *d_hist = nullptr, *d_prompt = nullptr;
     uint32_t* h_pinned = nullptr;  // [2]: token in, token out
     size_t pos = 0;
@@ -457,7 +458,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     const int part_splits = std::max(m->splits, m->mega_splits);
     size_t sbytes = 2 * A::pad(kv * 4) + 2 * A::pad(m->max_seq * half * 4) + A::pad(D * 4) + A::pad(NQKV * 4) +
                     A::pad(H * HD * 4) + A::pad(F * 4) + A::pad(V * 4) + A::pad(H * part_splits * (HD + 2) * 4) +
-                    A::pad(H * 4) + A::pad(am_grid * 4) * 2 + A::pad(4) * 6 + A::pad(16) + A::pad(m->max_seq * 4) * 2 +
+                    A::pad(H * 4) * 2 + A::pad(am_grid * 4) * 2 + A::pad(4) * 6 + A::pad(16) + A::pad(m->max_seq * 4) * 2 +
                     A::pad(2 * kStatsCap * sizeof(float2));
     TL_TRY(m->state.reserve(sbytes));
     TL_CUDA_TRY(cudaMemsetAsync(m->state.base, 0, sbytes, m->stream));
@@ -472,6 +473,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     m->logits = m->state.take<float>(V);
     m->attn_part = m->state.take<float>(H * part_splits * (HD + 2));
     m->attn_cnt = m->state.take<unsigned>(H);
+    m->qkv_cnt = m->state.take<unsigned>(H);
     m->am_v = m->state.take<float>(am_grid);
     m->am_i = m->state.take<uint32_t>(am_grid);
     m->am_cnt = m->state.take<unsigned>(1);
@@ -496,7 +498,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         d.n_layers = static_cast<int>(L);
         d.embed = m->embed; d.g_final = m->norm; d.cos_tab = m->cos_tab; d.sin_tab = m->sin_tab;
         d.h = m->h; d.qkv = m->qkv; d.attn_part = m->attn_part; d.act = m->act; d.logits = m->logits;
-        d.ctx = m->ctx; d.attn_cnt = m->attn_cnt; d.stats = m->stats;
+        d.ctx = m->ctx; d.attn_cnt = m->attn_cnt; d.qkv_cnt = m->qkv_cnt; d.stats = m->stats;
         // Tuning knob: tile pairs prefetched into L2 ahead of the ring.
         d.prefetch = 8;
         if (const char* e = std::getenv("TL_DECODE_PREFETCH")) d.prefetch = std::max(0, std::min(64, std::atoi(e)));
@@ -709,6 +711,7 @@ tl_status sync(tl_model* m) {
         cudaMemsetAsync(m->bar, 0, 4, m->stream);
         cudaMemsetAsync(m->ticket, 0, 4, m->stream);
         cudaMemsetAsync(m->attn_cnt, 0, sizeof(unsigned) * m->cfg.n_heads, m->stream);
+        if (m->qkv_cnt) cudaMemsetAsync(m->qkv_cnt, 0, sizeof(unsigned) * m->cfg.n_heads, m->stream);
         cudaMemsetAsync(m->err, 0, 4, m->stream);
         cudaStreamSynchronize(m->stream);
         m->h_pinned[3] = 0;
