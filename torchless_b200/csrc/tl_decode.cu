@@ -784,24 +784,48 @@ struct Consumer {
         return true;
     }
 
-    // Attention for (head, split) = divmod(blockIdx.x, S) (modules.cpp:58-88).
-    // Starts as soon as kv group h / 4's q, k and v rows are written
-    // (qkv_cnt, no grid barrier).  Returns max |ctx_h| on the CTA that wrote
-    // ctx_h, else 0 (uniform); -1 on error.
+    // Splits over cached positions for attention at `pos`: one per 64, at most a.splits.
+    __device__ int attn_splits(unsigned pos) const {
+        return ::min(a.splits, (static_cast<int>(pos) + 64) / 64);
+    }
+
+    // Thread 0 of an attention CTA: hint its K and V position range of the
+    // layer into L2, ahead of the attention phase (cached rows are from
+    // earlier steps, so they can be fetched before q/k/v exist).
     template <int HD>
-    __device__ float attention(int layer, unsigned pos) {
+    __device__ void prefetch_kv(int layer, unsigned pos) const {
+        const int S = attn_splits(pos);
+        const int u = blockIdx.x;
+        if (t != 0 || u >= a.H * S || pos == 0) return;
+        const int h = u / S, s = u % S, kh = h / 4;
+        const int npos = static_cast<int>(pos);  // rows 0 .. pos - 1 are cached
+        const int chunk = (npos + 1 + S - 1) / S;
+        const int p0 = s * chunk, p1 = min(npos, p0 + chunk);
+        if (p1 <= p0) return;
+        const DecodeLayer& L = a.layers[layer];
+        const size_t off = (static_cast<size_t>(kh) * a.max_seq + p0) * HD;
+        const uint32_t bytes = static_cast<uint32_t>(p1 - p0) * HD * 4;
+        prefetch_l2(L.k_cache + off, bytes);
+        prefetch_l2(L.v_cache + off, bytes);
+    }
+
+    // Attention for (head, split) = divmod(blockIdx.x, S) (modules.cpp:58-88):
+    // writes the split's softmax partial {max, sum, acc}; the o_proj staging
+    // merges the splits.  Starts as soon as kv group h / 4's q, k and v rows
+    // are written (qkv_cnt, no grid barrier).  false (uniform) on error.
+    template <int HD>
+    __device__ bool attention(int layer, unsigned pos) {
         constexpr int VPL = HD / 32;
         constexpr int HALF = HD / 2;
         constexpr int PF = 4;  // positions per warp in flight
         const DecodeLayer& L = a.layers[layer];
-        // splits over positions: one per 64 cached positions, at most a.splits
-        const int S = ::min(a.splits, (static_cast<int>(pos) + 64) / 64);
+        const int S = attn_splits(pos);
         const int u = blockIdx.x;
-        if (u >= a.H * S) return 0.f;
+        if (u >= a.H * S) return true;
         const int h = u / S, s = u % S, kh = h / 4;  // kv head h/4 (modules.cpp:70)
-        if (!TLD_OK(pos < static_cast<unsigned>(a.max_seq) && kh < a.KV && h < a.H, 40, pos, kh)) return 0.f;
+        if (!TLD_OK(pos < static_cast<unsigned>(a.max_seq) && kh < a.KV && h < a.H, 40, pos, kh)) return true;
         if (!TLD_OK((3 * HD + kConsumerWarps * (HD + 2)) * 4 <= static_cast<int>(xbuf_bytes(a.D, a.F, a.HD)), 41, HD, 0))
-            return 0.f;
+            return true;
         // wait until kv group kh's q, k and v rows of this layer are written
         if (t == 0) {
             const unsigned target = static_cast<unsigned>(layer + 1) * 6 * HD;
@@ -821,7 +845,7 @@ struct Consumer {
             }
         }
         consumer_sync();
-        if (aborted()) return -1.f;
+        if (aborted()) return false;
         float* q_s = reinterpret_cast<float*>(sh.xbuf);
         float* k_s = q_s + HD;
         float* v_s = k_s + HD;
@@ -882,22 +906,33 @@ struct Consumer {
                     }
                 }
             }
+            // scores of the PF positions, then one online-softmax rescale for all of them
+            float sc[PF];
 #pragma unroll
             for (int f = 0; f < PF; f++) {
-                const int p = pb + f * kConsumerWarps;
-                if (p >= p1) break;
                 float dsum = 0.f;
 #pragma unroll
                 for (int j = 0; j < VPL; j++) dsum += kv[f][j] * q[j];
-                const float sc = warp_sum(dsum) * a.attn_scale;
-                const float mn = fmaxf(m, sc);
-                const float corr = expf(m - mn);
-                const float e = expf(sc - mn);
-                l = l * corr + e;
-#pragma unroll
-                for (int j = 0; j < VPL; j++) acc[j] = acc[j] * corr + e * vv[f][j];
-                m = mn;
+                sc[f] = warp_sum(dsum) * a.attn_scale;
             }
+            float mn = m;
+#pragma unroll
+            for (int f = 0; f < PF; f++)
+                if (pb + f * kConsumerWarps < p1) mn = fmaxf(mn, sc[f]);
+            const float corr = expf(m - mn);
+            l *= corr;
+#pragma unroll
+            for (int j = 0; j < VPL; j++) acc[j] *= corr;
+#pragma unroll
+            for (int f = 0; f < PF; f++) {
+                if (pb + f * kConsumerWarps < p1) {
+                    const float e = expf(sc[f] - mn);
+                    l += e;
+#pragma unroll
+                    for (int j = 0; j < VPL; j++) acc[j] = fmaf(e, vv[f][j], acc[j]);
+                }
+            }
+            m = mn;
         }
         float* mine = wp + warp * (HD + 2);
         if (lane == 0) {
@@ -907,77 +942,121 @@ struct Consumer {
 #pragma unroll
         for (int j = 0; j < VPL; j++) mine[2 + lane * VPL + j] = acc[j];
         consumer_sync();
-        if (S == 1) {  // one CTA per head: merge the warps straight into ctx
-            float mx = 0.f;
-            if (t < HD) {
-                float M = -INFINITY;
-#pragma unroll
-                for (int w = 0; w < kConsumerWarps; w++)
-                    if (wp[w * (HD + 2) + 1] > 0.f) M = fmaxf(M, wp[w * (HD + 2)]);
-                float GL = 0.f, acc_t = 0.f;
-#pragma unroll
-                for (int w = 0; w < kConsumerWarps; w++) {
-                    const float lw = wp[w * (HD + 2) + 1];
-                    if (lw > 0.f) {
-                        const float e = expf(wp[w * (HD + 2)] - M);
-                        GL += lw * e;
-                        acc_t += wp[w * (HD + 2) + 2 + t] * e;
-                    }
-                }
-                const float c = acc_t / GL;
-                a.ctx[h * HD + t] = c;
-                mx = fabsf(c);
-            }
-            return mx;
-        }
+        // this split's partial over the 8 warps: part[h S + s] = {M, L, 0, 0, acc[HD]}
         float M = -INFINITY;
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; w++)
             if (wp[w * (HD + 2) + 1] > 0.f) M = fmaxf(M, wp[w * (HD + 2)]);
-        float* part = a.attn_part + static_cast<size_t>(u) * (HD + 2);
-        for (int i = t; i < HD + 2; i += kConsumers) {
+        float* part = a.attn_part + static_cast<size_t>(h * S + s) * (HD + 4);
+        for (int i = t; i < HD + 4; i += kConsumers) {
             float v = 0.f;
             if (i == 0) {
                 v = M;
-            } else {
+            } else if (i == 1 || i >= 4) {
+                const int src = (i == 1) ? 1 : i - 2;  // l, or acc[i - 4] at warp offset 2 + (i - 4)
 #pragma unroll
                 for (int w = 0; w < kConsumerWarps; w++) {
-                    const float lw = wp[w * (HD + 2) + 1];
-                    if (lw > 0.f) v += wp[w * (HD + 2) + i] * expf(wp[w * (HD + 2)] - M);
+                    const float* pw = wp + w * (HD + 2);
+                    if (pw[1] > 0.f) v += pw[src] * expf(pw[0] - M);
                 }
             }
             part[i] = v;
         }
-        // The last split of head h to finish merges the S partials into ctx.
-        consumer_sync();
-        if (t == 0) {
-            __threadfence();
-            sh.flags[2] = (atomicAdd(a.attn_cnt + h, 1u) == static_cast<unsigned>(S) - 1);
+        return true;
+    }
+
+    // Stages ctx = attention output as int8 digits for o_proj: merges, for
+    // each head, the S split partials {M, L, acc} written by attention
+    // (softmax over all positions = sum_s acc_s e^(M_s - M) / sum_s L_s e^(M_s - M),
+    // M = max_s M_s), takes the CTA-wide max |ctx| for the digit scale and
+    // stores the digits as stage_digits does.  Returns 2^-k.
+    template <int HD>
+    __device__ float stage_ctx_digits(unsigned pos) {
+        const int S = attn_splits(pos);
+        const int d = a.H * HD;
+        const int nb = d / 16;
+        if (!TLD_OK(3 * static_cast<size_t>(d) <= xbuf_bytes(a.D, a.F, a.HD), 32, d, 0)) return 1.0f;
+        // first block of 16 columns per thread (the only one when H hd <= 4096)
+        float v[16];
+        float mx = 0.f;
+        const int b0 = t;
+        if (b0 < nb) {
+            merge_ctx_block<HD>(b0, S, v);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) mx = fmaxf(mx, fabsf(v[j]));
+        for (int b = b0 + kConsumers; b < nb; b += kConsumers) {  // longer ctx: not kept, recomputed below
+            float w[16];
+            merge_ctx_block<HD>(b, S, w);
+#pragma unroll
+            for (int j = 0; j < 16; j++) mx = fmaxf(mx, fabsf(w[j]));
+        }
+        const float amax = sum_max(0.f, mx).y;
+        int e = 0;
+        if (amax > 0.f) frexpf(amax, &e);
+        const int k = ::min(::max(22 - e, -120), 120);
+        const float sc = ldexpf(1.0f, k);
+        if (b0 < nb) put_digits(b0, v, sc);
+        for (int b = b0 + kConsumers; b < nb; b += kConsumers) {
+            float w[16];
+            merge_ctx_block<HD>(b, S, w);
+            put_digits(b, w, sc);
         }
         consumer_sync();
-        if (!sh.flags[2]) return 0.f;  // uniform; flags[2] is next written after a later sync
-        __threadfence();
-        const float* ph = a.attn_part + static_cast<size_t>(h) * S * (HD + 2);
-        float mx = 0.f;
-        if (t < HD) {
-            float GM = -INFINITY;
-            for (int j = 0; j < S; j++)
-                if (__ldcg(ph + j * (HD + 2) + 1) > 0.f) GM = fmaxf(GM, __ldcg(ph + j * (HD + 2)));
-            float GL = 0.f, acc_t = 0.f;
-            for (int j = 0; j < S; j++) {
-                const float lj = __ldcg(ph + j * (HD + 2) + 1);
-                if (lj > 0.f) {
-                    const float w = expf(__ldcg(ph + j * (HD + 2)) - GM);
-                    GL += lj * w;
-                    acc_t += __ldcg(ph + j * (HD + 2) + 2 + t) * w;
+        stamp(2);
+        return ldexpf(1.0f, -k);
+    }
+
+    // ctx columns [16 b, 16 b + 16) (one head): merge of the S split partials,
+    // all of a group of 4 splits loaded before any is used, combined with a
+    // running maximum in split order.
+    template <int HD>
+    __device__ __forceinline__ void merge_ctx_block(int b, int S, float (&v)[16]) const {
+        const int h = (16 * b) / HD, i0 = (16 * b) % HD;
+        const float* ph = a.attn_part + static_cast<size_t>(h) * S * (HD + 4);
+        float GM = -INFINITY, GL = 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; j++) v[j] = 0.f;
+        for (int s0 = 0; s0 < S; s0 += 4) {
+            float2 ml[4];
+            float4 ac[4][4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float* pp = ph + static_cast<size_t>(s0 + u) * (HD + 4);
+                const bool ok = s0 + u < S;
+                ml[u] = ok ? __ldcg(reinterpret_cast<const float2*>(pp)) : make_float2(-INFINITY, 0.f);
+#pragma unroll
+                for (int q = 0; q < 4; q++)
+                    ac[u][q] = ok ? __ldcg(reinterpret_cast<const float4*>(pp + 4 + i0) + q)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                if (!(ml[u].y > 0.f)) continue;
+                if (ml[u].x > GM) {  // rescale what was merged so far
+                    const float c = expf(GM - ml[u].x);
+                    GL *= c;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) v[j] *= c;
+                    GM = ml[u].x;
+                }
+                const float w = expf(ml[u].x - GM);
+                GL = fmaf(ml[u].y, w, GL);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    v[4 * q] = fmaf(ac[u][q].x, w, v[4 * q]);
+                    v[4 * q + 1] = fmaf(ac[u][q].y, w, v[4 * q + 1]);
+                    v[4 * q + 2] = fmaf(ac[u][q].z, w, v[4 * q + 2]);
+                    v[4 * q + 3] = fmaf(ac[u][q].w, w, v[4 * q + 3]);
                 }
             }
-            const float c = acc_t / GL;
-            a.ctx[h * HD + t] = c;
-            mx = fabsf(c);
         }
-        if (t == 0) a.attn_cnt[h] = 0;
-        return mx;
+        const float inv = 1.0f / GL;
+#pragma unroll
+        for (int j = 0; j < 16; j++) v[j] *= inv;
     }
 };
 
@@ -1036,14 +1115,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         // q/k/v = W_qkv rmsnorm(h)
         if (l > 0 && !cw.wait_all()) return;
         float un = cw.stage_digits<true>(hin, D, L.g_in, l == 0 ? &st0 : nullptr);
+        cw.prefetch_kv<HD>(l, pos);
         if (!cw.run_i8<0>(NQKV, D, un, nullptr, nullptr)) return;
         // attention; ctx written by one CTA per head
-        const float mx = cw.attention<HD>(l, pos);
-        if (mx < 0.f || cw.aborted()) return;
-        cw.publish(0.f, mx);
+        if (!cw.attention<HD>(l, pos) || cw.aborted()) return;
+        cw.publish(0.f, 0.f);
         // h = h + W_o ctx
         if (!cw.wait_all()) return;
-        un = cw.stage_digits<false>(a.ctx, a.H * a.HD, nullptr, nullptr);
+        un = cw.stage_ctx_digits<HD>(pos);
         if (!cw.run_i8<1>(D, a.H * a.HD, un, hin, L.g_post)) return;
         // act = silu(W1 x) * (W3 x), x = rmsnorm(h)
         if (!cw.wait_all()) return;

@@ -54,8 +54,8 @@ struct DecodeArgs {
     const float* sin_tab;
     float* h;                   // residual stream [D]
     float* qkv;                 // [(H + 2 KV) hd]
-    float* attn_part;           // [H][S][hd + 2] split partials {max, sum, acc}
-    float* ctx;                 // [H hd] merged attention output (o_proj input)
+    float* attn_part;           // [H][S][hd + 4] split partials {max, sum, 0, 0, acc}
+    float* ctx;                 // [H hd] (unused: the o_proj staging merges attn_part)
     unsigned* attn_cnt;         // [H] split tickets per head, zero between launches
     unsigned* qkv_cnt;          // [KV] q/k/v rows written per kv group, zero between launches
     float* act;                 // [F]

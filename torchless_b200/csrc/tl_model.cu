@@ -457,7 +457,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     const int am_grid = std::max(gemv_f32_grid(V, D, true, true), m->grid);
     const int part_splits = std::max(m->splits, m->mega_splits);
     size_t sbytes = 2 * A::pad(kv * 4) + 2 * A::pad(m->max_seq * half * 4) + A::pad(D * 4) + A::pad(NQKV * 4) +
-                    A::pad(H * HD * 4) + A::pad(F * 4) + A::pad(V * 4) + A::pad(H * part_splits * (HD + 2) * 4) +
+                    A::pad(H * HD * 4) + A::pad(F * 4) + A::pad(V * 4) + A::pad(H * part_splits * (HD + 4) * 4) +
                     A::pad(H * 4) * 2 + A::pad(am_grid * 4) * 2 + A::pad(4) * 6 + A::pad(16) + A::pad(m->max_seq * 4) * 2 +
                     A::pad(2 * kStatsCap * sizeof(float2));
     TL_TRY(m->state.reserve(sbytes));
@@ -471,7 +471,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     m->ctx = m->state.take<float>(H * HD);
     m->act = m->state.take<float>(F);
     m->logits = m->state.take<float>(V);
-    m->attn_part = m->state.take<float>(H * part_splits * (HD + 2));
+    m->attn_part = m->state.take<float>(H * part_splits * (HD + 4));
     m->attn_cnt = m->state.take<unsigned>(H);
     m->qkv_cnt = m->state.take<unsigned>(H);
     m->am_v = m->state.take<float>(am_grid);
