@@ -154,7 +154,12 @@ typedef struct tl_model_options {
     int use_graph;   /* 1: each decode step is one CUDA-graph replay (default)    */
     int kernel_mode; /* 0: one persistent kernel per decode step when the shape   */
                      /*    fits (default), else per-op kernels; 1: per-op kernels */
+    int tp_size;     /* tensor-parallel ranks (0 or 1: none; 2, 4, 8)              */
+    int tp_rank;     /* this process's rank in [0, tp_size)                        */
 } tl_model_options;
+
+/* Bytes of one rank's exchange-buffer handle (tl_model_tp_handle). */
+#define TL_TP_HANDLE_BYTES 64
 
 typedef struct tl_model tl_model;
 
@@ -223,6 +228,21 @@ TL_API tl_status tl_model_profile(tl_model* m, uint32_t token, size_t n, tl_kern
  * the model runs per-op kernels. */
 TL_API tl_status tl_model_trace_step(tl_model* m, uint32_t token, uint64_t* out, size_t cap,
                                      size_t* n_written);
+
+/* Tensor parallelism (Megatron-style split of the reference's layers,
+ * modules.cpp:49-143): with tp_size > 1 in tl_model_options, rank r keeps q
+ * heads, kv heads, gate/up rows, down_proj and o_proj columns and lm_head
+ * rows of its slice [r n / tp, (r + 1) n / tp); o_proj and down_proj partials
+ * are summed over the ranks inside the decode kernel through NVLink peer
+ * memory (no collective library), the argmax is merged across ranks, and
+ * every rank returns the same token.  logits arguments receive this rank's
+ * vocab_size / tp_size slice.  Each process loads its rank, publishes
+ * tl_model_tp_handle() (TL_TP_HANDLE_BYTES), gathers all ranks' handles in
+ * rank order and calls tl_model_tp_connect(); every rank then runs the same
+ * sequence of forward calls.  No reference counterpart (the reference is
+ * single-process CPU code). */
+TL_API tl_status tl_model_tp_handle(const tl_model* m, void* handle);
+TL_API tl_status tl_model_tp_connect(tl_model* m, const void* handles);
 
 /* Number of kernel launches one decode step issues (all of them this library's). */
 TL_API tl_status tl_model_launches_per_step(const tl_model* m, int* launches);

@@ -51,7 +51,10 @@ class tl_config(ctypes.Structure):
 
 class tl_model_options(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int), ("max_seq", ctypes.c_size_t), ("use_graph", ctypes.c_int),
-                ("kernel_mode", ctypes.c_int)]
+                ("kernel_mode", ctypes.c_int), ("tp_size", ctypes.c_int), ("tp_rank", ctypes.c_int)]
+
+
+TP_HANDLE_BYTES = 64
 
 
 class tl_kernel_time(ctypes.Structure):
@@ -100,6 +103,8 @@ SIGNATURES = {
     "tl_model_profile": [_P, _U32, _S, ctypes.POINTER(tl_kernel_time), _I, ctypes.POINTER(_I)],
     "tl_model_launches_per_step": [_P, ctypes.POINTER(_I)],
     "tl_model_trace_step": [_P, _U32, _P, _S, ctypes.POINTER(_S)],
+    "tl_model_tp_handle": [_P, _P],
+    "tl_model_tp_connect": [_P, _P],
 }
 
 _lib: Optional[ctypes.CDLL] = None

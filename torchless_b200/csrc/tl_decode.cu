@@ -121,6 +121,25 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     return v;
 }
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+// System scope (peer GPUs over NVLink): 64-bit counters and slots.
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void red_add_sys_u64(void* p, unsigned long long v) {
+    asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const void* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(void* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const void* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
 // D = A(16x32 s8, row) * B(32x8 s8, col) + D (s32).
@@ -174,7 +193,8 @@ __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + 
 // Digits of the longest staged vector (3 bytes per column), the fp32 lm_head
 // input, or the attention scratch.
 __host__ __device__ inline size_t xbuf_bytes(int D, int F, int HD) {
-    size_t x = 3 * static_cast<size_t>(D > F ? D : F);
+    const int Dp = tile_slices(D) * kTileCols, Fp = tile_slices(F) * kTileCols;
+    size_t x = 3 * static_cast<size_t>(Dp > Fp ? Dp : Fp);
     if (4 * static_cast<size_t>(D) > x) x = 4 * static_cast<size_t>(D);
     const size_t attn = (3 * HD + kConsumerWarps * (HD + 2)) * 4;  // q, k, v + warp partials
     if (attn > x) x = attn;
@@ -227,7 +247,7 @@ struct Seg {
 
 __device__ Seg seg_info(const DecodeArgs& a, int s) {
     const int NQKV = (a.H + 2 * a.KV) * a.HD;
-    const int ksD = a.D / kTileCols;
+    const int ksD = tile_slices(a.D);
     Seg g;
     if (s >= 4 * a.n_layers) {
         g.src = a.lm_head;
@@ -239,9 +259,9 @@ __device__ Seg seg_info(const DecodeArgs& a, int s) {
         g.tb = kTileBytesI8;
         switch (s & 3) {
             case 0: g.src = L.qkv; g.n_rb = (NQKV + 15) / 16; g.ksn = ksD; break;
-            case 1: g.src = L.o; g.n_rb = (a.D + 15) / 16; g.ksn = (a.H * a.HD) / kTileCols; break;
+            case 1: g.src = L.o; g.n_rb = (a.D + 15) / 16; g.ksn = tile_slices(a.H * a.HD); break;
             case 2: g.src = L.w13; g.n_rb = (2 * a.F + 15) / 16; g.ksn = ksD; break;
-            default: g.src = L.w2; g.n_rb = (a.D + 15) / 16; g.ksn = a.F / kTileCols; break;
+            default: g.src = L.w2; g.n_rb = (a.D + 15) / 16; g.ksn = tile_slices(a.F); break;
         }
     }
     int b1;
@@ -349,6 +369,7 @@ struct Producer {
 // the rows are reduced over their tiles in a fixed order, so results do not
 // depend on timing.
 // ---------------------------------------------------------------------------
+template <bool TP>  // TP: tensor-parallel exchange paths compiled in
 struct Consumer {
     const DecodeArgs& a;
     const Shared& sh;
@@ -519,8 +540,16 @@ struct Consumer {
     template <bool NORM>
     __device__ float stage_digits(const float* vec, int d, const float* g, const float2* local) {
         constexpr int NB = NORM ? 2 : 4;
-        if (!TLD_OK(3 * static_cast<size_t>(d) <= xbuf_bytes(a.D, a.F, a.HD) && d % 64 == 0, 30, d, 0)) return 1.0f;
+        const int dp = tile_slices(d) * kTileCols;  // padded to whole tiles
+        if (!TLD_OK(3 * static_cast<size_t>(dp) <= xbuf_bytes(a.D, a.F, a.HD) && d % 64 == 0, 30, d, dp)) return 1.0f;
         const int nb = d / 16;
+        // digits of the padding columns (zero weights) must be finite: zero them
+        for (int b = nb + t; b < dp / 16; b += kConsumers) {
+            uint8_t* dst = sh.xbuf + (b >> 2) * kGroupDigitBytes + (b & 3) * 16;
+            *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(dst + 64) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(dst + 128) = make_uint4(0, 0, 0, 0);
+        }
         const float4* v4 = reinterpret_cast<const float4*>(vec);
         const float4* g4 = reinterpret_cast<const float4*>(g);
         float4 vb[NB][4], gb[NB][4];
@@ -712,12 +741,13 @@ struct Consumer {
     // ready count (qkv_cnt), which attention waits on.
     template <int KIND>
     __device__ bool run_i8(int n_rows, int d, float unscale, const float* res, const float* g_next) {
-        const int ksn = d / kTileCols;
+        const int ksn = tile_slices(d);
+        constexpr bool xchg = (KIND == 1 || KIND == 3) && TP;  // partial rows go to every rank
         const int n_rb = (n_rows + kTileRowsI8 - 1) / kTileRowsI8;
         // the first epilogue row's residual and next-norm gain, loaded before
         // the tiles so the epilogue does not wait on them
         float res0 = 0.f, g0 = 0.f;
-        if (KIND == 1 || KIND == 3) {
+        if ((KIND == 1 || KIND == 3) && !xchg) {
             int b0, b1;
             split(n_rb, b0, b1);
             const int row = b0 * 16 + t;
@@ -754,6 +784,11 @@ struct Consumer {
                         const int hh = row / a.HD;
                         const int grp = hh < a.H ? hh / 4 : (hh < a.H + a.KV ? hh - a.H : hh - a.H - a.KV);
                         atomicAdd(reinterpret_cast<unsigned*>(sh.scratch) + 32 + grp, 1u);
+                    } else if (xchg) {
+                        // row of this rank's partial to every rank's receive buffer
+                        const size_t off = kXchgRecv + ((static_cast<size_t>(xk & 1) * a.tp_size + a.tp_rank) *
+                                                            a.D + row) * 4;
+                        for (int q = 0; q < a.tp_size; q++) *reinterpret_cast<float*>(a.xpeer[q] + off) = v;
                     } else {
                         const bool first = (j == t);
                         const float hv = v + (first ? res0 : __ldcg(res + row));
@@ -778,10 +813,148 @@ struct Consumer {
             stamp(4);
             phase++;
             stamp(0);
+        } else if (xchg) {
+            xchg_arrive();
         } else {
             publish(ss, mx);
         }
         return true;
+    }
+
+    // ---- tensor-parallel exchange (o_proj and down_proj partials) ----------
+    // Exchange xk of a step: every CTA of every rank stores its partial rows
+    // into buffer xk % 2 of every rank, then (one thread, after a CTA-wide
+    // bar.sync and a system-scope fence) adds 1 to every rank's arrival
+    // counter.  The counters are 64-bit and never reset, so exchange xk of
+    // step e is complete on a rank when its counter reaches
+    // (e * 2 L + xk + 1) * tp * G.  Every rank then sums the tp partials in
+    // rank order: the ranks hold bit-identical residuals.
+    int xk = 0;          // exchanges this CTA has arrived at in this step
+    unsigned epoch = 0;  // steps run before this one
+
+    __device__ void xchg_arrive() {
+        consumer_sync();
+        if (t == 0) {
+            fence_sys();
+            for (int q = 0; q < a.tp_size; q++) red_add_sys_u64(a.xpeer[q] + kXchgCnt, 1ull);
+        }
+        xk++;
+        stamp(4);
+        phase++;
+        stamp(0);
+    }
+
+    __device__ bool xchg_wait() {
+        if (t == 0) {
+            const unsigned long long target =
+                (static_cast<unsigned long long>(epoch) * 2 * a.n_layers + xk) * a.tp_size * gridDim.x;
+            const void* cnt = a.xpeer[a.tp_rank] + kXchgCnt;
+            const unsigned long long t0 = globaltimer();
+            for (unsigned i = 0;; i++) {
+                if (ld_acquire_sys_u64(cnt) >= target) break;
+                if ((i & 63) == 63) {
+                    if (ld_volatile(a.err)) {
+                        *reinterpret_cast<volatile int*>(&sh.flags[0]) = 1;
+                        break;
+                    }
+                    if (globaltimer() - t0 > kTimeoutNs) {
+                        fail(kErrBarrier);
+                        break;
+                    }
+                }
+            }
+        }
+        consumer_sync();
+        stamp(1);
+        return !aborted();
+    }
+
+    // After exchange xk - 1: h = hprev + sum over ranks (rank order) of the
+    // received partials; this CTA stores its share of h into hout; then
+    // RMSNorm(h) with gain g (modules.cpp:31-46) is staged as int8 digits
+    // (F32 false, returns 2^-k) or as fp32 (F32 true, lm_head; returns 1).
+    // The whole h is in registers (D <= 8192), so its statistics are local.
+    template <bool F32>
+    __device__ float stage_xchg(const float* hprev, float* hout, const float* g) {
+        const int D = a.D, nb = D / 16;
+        if (!TLD_OK(nb <= 2 * kConsumers && (F32 ? 4 : 3) * static_cast<size_t>(D) <= xbuf_bytes(a.D, a.F, a.HD),
+                    33, D, 0))
+            return 1.0f;
+        const float* recv = reinterpret_cast<const float*>(a.xpeer[a.tp_rank] + kXchgRecv) +
+                            static_cast<size_t>((xk - 1) & 1) * a.tp_size * D;
+        int B0, B1;  // this CTA's blocks of 16 rows of h
+        split(nb, B0, B1);
+        float v[2][16];
+        float ss = 0.f, mx = 0.f;
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const int b = t + r * kConsumers;
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[r][j] = 0.f;
+            if (b >= nb) continue;
+#pragma unroll
+            for (int qd = 0; qd < 4; qd++) {
+                float4 acc = __ldcg(reinterpret_cast<const float4*>(hprev) + 4 * b + qd);
+                for (int q = 0; q < a.tp_size; q++) {
+                    const float4 p = __ldcg(reinterpret_cast<const float4*>(recv + static_cast<size_t>(q) * D) + 4 * b + qd);
+                    acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+                }
+                v[r][4 * qd] = acc.x; v[r][4 * qd + 1] = acc.y; v[r][4 * qd + 2] = acc.z; v[r][4 * qd + 3] = acc.w;
+            }
+            if (b >= B0 && b < B1) {
+#pragma unroll
+                for (int qd = 0; qd < 4; qd++)
+                    reinterpret_cast<float4*>(hout)[4 * b + qd] =
+                        make_float4(v[r][4 * qd], v[r][4 * qd + 1], v[r][4 * qd + 2], v[r][4 * qd + 3]);
+            }
+#pragma unroll
+            for (int qd = 0; qd < 4; qd++) {
+                const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + 4 * b + qd);
+                const float gv[4] = {gg.x, gg.y, gg.z, gg.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const float x = v[r][4 * qd + j];
+                    ss += x * x;
+                    mx = fmaxf(mx, fabsf(x * gv[j]));
+                }
+            }
+        }
+        const float2 st = sum_max(ss, mx);
+        const float inv = 1.0f / sqrtf(st.x / static_cast<float>(D) + 1e-5f);
+        float sc = 1.0f;
+        int k = 0;
+        if (!F32) {
+            const float amax = st.y * inv * 1.0001f;
+            int e = 0;
+            if (amax > 0.f) frexpf(amax, &e);
+            k = ::min(::max(22 - e, -120), 120);
+            sc = ldexpf(1.0f, k);
+        }
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const int b = t + r * kConsumers;
+            if (b >= nb) continue;
+            float x[16];
+#pragma unroll
+            for (int qd = 0; qd < 4; qd++) {
+                const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + 4 * b + qd);
+                x[4 * qd] = (v[r][4 * qd] * inv) * gg.x;
+                x[4 * qd + 1] = (v[r][4 * qd + 1] * inv) * gg.y;
+                x[4 * qd + 2] = (v[r][4 * qd + 2] * inv) * gg.z;
+                x[4 * qd + 3] = (v[r][4 * qd + 3] * inv) * gg.w;
+            }
+            if (F32) {
+#pragma unroll
+                for (int qd = 0; qd < 4; qd++)
+                    reinterpret_cast<float4*>(sh.xbuf)[4 * b + qd] =
+                        make_float4(x[4 * qd], x[4 * qd + 1], x[4 * qd + 2], x[4 * qd + 3]);
+            } else {
+                put_digits(b, x, sc);
+            }
+        }
+        consumer_sync();
+        stamp(2);
+        return F32 ? 1.0f : ldexpf(1.0f, -k);
     }
 
     // Splits over cached positions for attention at `pos`: one per 64, at most a.splits.
@@ -1060,7 +1233,7 @@ struct Consumer {
     }
 };
 
-template <int HD>
+template <int HD, bool TP>
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, int stages) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Shared sh = carve(smem_raw, stages, a);
@@ -1084,11 +1257,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         for (int i = 32; i < 64; i++) reinterpret_cast<unsigned*>(sh.scratch)[i] = 0u;  // kv group row counts
         sh.info[0] = __ldcg(a.pos);
         sh.info[1] = __ldcg(a.token);
+        sh.info[2] = __ldcg(a.epoch);
         fence_mbar_init();
     }
     __syncthreads();
     // Never index with an out-of-range token or position: record and stop.
-    if (sh.info[0] >= static_cast<unsigned>(a.max_seq) || sh.info[1] >= static_cast<unsigned>(a.V)) {
+    // (a.V is this rank's vocabulary slice; tokens index the whole vocabulary)
+    if (sh.info[0] >= static_cast<unsigned>(a.max_seq) || sh.info[1] >= static_cast<unsigned>(a.V * a.tp_size)) {
         if (threadIdx.x == 0) atomicCAS(a.err, 0, kErrInput);
         return;
     }
@@ -1103,44 +1278,66 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
     }
 
     // ---------------- consumer warps ----------------
-    Consumer cw(a, sh, stages);
+    Consumer<TP> cw(a, sh, stages);
     cw.stamp(0);
     const unsigned pos = sh.info[0];
     const uint32_t token = sh.info[1];
     const float* emb = a.embed + static_cast<size_t>(token) * D;  // Embedding::forward (modules.cpp:5-7)
+    constexpr bool tp = TP;
+    cw.epoch = sh.info[2];
     const float2 st0 = cw.local_stats(emb, D, a.layers[0].g_in);
     for (int l = 0; l < a.n_layers; l++) {
         const DecodeLayer& L = a.layers[l];
         const float* hin = (l == 0) ? emb : a.h;
         // q/k/v = W_qkv rmsnorm(h)
-        if (l > 0 && !cw.wait_all()) return;
-        float un = cw.stage_digits<true>(hin, D, L.g_in, l == 0 ? &st0 : nullptr);
-        cw.prefetch_kv<HD>(l, pos);
-        if (!cw.run_i8<0>(NQKV, D, un, nullptr, nullptr)) return;
+        float un;
+        if (l == 0) {
+            un = cw.template stage_digits<true>(emb, D, L.g_in, &st0);
+        } else if (tp) {  // h = post-attention h + sum of the ranks' down_proj partials
+            if (!cw.xchg_wait()) return;
+            un = cw.template stage_xchg<false>(a.h, a.h2, L.g_in);
+        } else {
+            if (!cw.wait_all()) return;
+            un = cw.template stage_digits<true>(a.h, D, L.g_in, nullptr);
+        }
+        cw.template prefetch_kv<HD>(l, pos);
+        if (!cw.template run_i8<0>(NQKV, D, un, nullptr, nullptr)) return;
         // attention; ctx written by one CTA per head
-        if (!cw.attention<HD>(l, pos) || cw.aborted()) return;
+        if (!cw.template attention<HD>(l, pos) || cw.aborted()) return;
         cw.publish(0.f, 0.f);
         // h = h + W_o ctx
         if (!cw.wait_all()) return;
-        un = cw.stage_ctx_digits<HD>(pos);
-        if (!cw.run_i8<1>(D, a.H * a.HD, un, hin, L.g_post)) return;
+        un = cw.template stage_ctx_digits<HD>(pos);
+        if (cw.t == 0) prefetch_l2(L.g_post, static_cast<uint32_t>(D) * 4u);  // staged after this phase
+        if (!cw.template run_i8<1>(D, a.H * a.HD, un, hin, L.g_post)) return;
         // act = silu(W1 x) * (W3 x), x = rmsnorm(h)
-        if (!cw.wait_all()) return;
-        un = cw.stage_digits<true>(a.h, D, L.g_post, nullptr);
-        if (!cw.run_i8<2>(2 * F, D, un, nullptr, nullptr)) return;
+        if (tp) {  // h = residual + sum of the ranks' o_proj partials
+            if (!cw.xchg_wait()) return;
+            un = cw.template stage_xchg<false>(l == 0 ? emb : a.h2, a.h, L.g_post);
+        } else {
+            if (!cw.wait_all()) return;
+            un = cw.template stage_digits<true>(a.h, D, L.g_post, nullptr);
+        }
+        if (!cw.template run_i8<2>(2 * F, D, un, nullptr, nullptr)) return;
         // h = h + W2 act
         if (!cw.wait_all()) return;
-        un = cw.stage_digits<false>(a.act, F, nullptr, nullptr);
+        un = cw.template stage_digits<false>(a.act, F, nullptr, nullptr);
         const float* g_next = (l + 1 < a.n_layers) ? a.layers[l + 1].g_in : a.g_final;
-        if (!cw.run_i8<3>(D, F, un, a.h, g_next)) return;
+        if (cw.t == 0) prefetch_l2(g_next, static_cast<uint32_t>(D) * 4u);  // staged after this phase
+        if (!cw.template run_i8<3>(D, F, un, a.h, g_next)) return;
     }
     // logits = lm_head rmsnorm(h); token = argmax (main.cpp:10-21)
-    if (!cw.wait_all()) return;
-    cw.stage_f32(a.h, D, a.g_final);
-    const int ksD = D / kTileCols;
+    if (tp) {
+        if (!cw.xchg_wait()) return;
+        cw.template stage_xchg<true>(a.h, a.h2, a.g_final);
+    } else {
+        if (!cw.wait_all()) return;
+        cw.stage_f32(a.h, D, a.g_final);
+    }
+    const int ksD = tile_slices(D);
     const int n_rb = (a.V + kTileRowsF32 - 1) / kTileRowsF32;
     int nrl = 0;
-    const int rb0 = cw.run_tiles<true>(n_rb, ksD, nrl);
+    const int rb0 = cw.template run_tiles<true>(n_rb, ksD, nrl);
     if (rb0 < 0) return;
     float best_v = -INFINITY;
     uint32_t best_i = 0xffffffffu;
@@ -1211,10 +1408,50 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
             if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
         }
         const float l0 = __ldcg(a.logits);
-        if (l0 != l0 || bi == 0xffffffffu) bi = 0;  // sample_max keeps 0 (main.cpp:10-21)
+        if (TP) {
+            // Every rank sends its best {value, global index} (bit 31: this
+            // rank's logits[0] is NaN) to every rank, then merges all of them
+            // in rank order, i.e. in vocabulary order.
+            const unsigned ep = sh.info[2];
+            uint32_t gi = (bi == 0xffffffffu) ? 0xffffffffu : bi + static_cast<uint32_t>(a.vocab_off);
+            if (a.tp_rank == 0 && l0 != l0) gi = 0x80000000u;
+            const unsigned long long slot = (static_cast<unsigned long long>(gi) << 32) | __float_as_uint(bv);
+            const size_t off = kXchgAmSlot + (static_cast<size_t>(ep & 1) * kMaxTp + a.tp_rank) * 8;
+            for (int q = 0; q < a.tp_size; q++) st_relaxed_sys_u64(a.xpeer[q] + off, slot);
+            fence_sys();
+            for (int q = 0; q < a.tp_size; q++) red_add_sys_u64(a.xpeer[q] + kXchgAmCnt, 1ull);
+            const unsigned long long target = (static_cast<unsigned long long>(ep) + 1) * a.tp_size;
+            const unsigned long long t0 = globaltimer();
+            bool ok = true;
+            for (unsigned i = 0;; i++) {
+                if (ld_acquire_sys_u64(a.xpeer[a.tp_rank] + kXchgAmCnt) >= target) break;
+                if ((i & 63) == 63 && globaltimer() - t0 > kTimeoutNs) {
+                    atomicCAS(a.err, 0, static_cast<int>(kErrBarrier));
+                    ok = false;
+                    break;
+                }
+            }
+            bool nan0 = false;
+            bv = -INFINITY;
+            bi = 0xffffffffu;
+            for (int q = 0; ok && q < a.tp_size; q++) {
+                const unsigned long long v = ld_relaxed_sys_u64(
+                    a.xpeer[a.tp_rank] + kXchgAmSlot + (static_cast<size_t>(ep & 1) * kMaxTp + q) * 8);
+                const uint32_t vi = static_cast<uint32_t>(v >> 32);
+                if (vi == 0x80000000u) nan0 = true;
+                else if (better(__uint_as_float(static_cast<uint32_t>(v)), vi, bv, bi)) {
+                    bv = __uint_as_float(static_cast<uint32_t>(v));
+                    bi = vi;
+                }
+            }
+            if (nan0 || bi == 0xffffffffu) bi = 0;  // sample_max keeps 0 (main.cpp:10-21)
+        } else if (l0 != l0 || bi == 0xffffffffu) {
+            bi = 0;  // sample_max keeps 0 (main.cpp:10-21)
+        }
         *a.token = bi;
         a.history[pos] = bi;
         *a.pos = pos + 1;
+        *a.epoch = sh.info[2] + 1;
         // Every CTA has passed every barrier and taken its ticket: reset the
         // counters for the next step.
         *a.ticket = 0;
@@ -1229,12 +1466,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
 // ---------------------------------------------------------------------------
 __global__ void k_repack_i8(uint8_t* dst, const int8_t* w1, const float* s1, const int8_t* w3, const float* s3,
                             int n, int d, int swiglu) {
-    const int ksn = d / kTileCols;
+    const int ksn = tile_slices(d), dp = ksn * kTileCols;  // columns >= d: zero padding
     const int n_rb = swiglu ? (2 * n + 15) / 16 : (n + 15) / 16;
-    const size_t chunks = static_cast<size_t>(n_rb) * 16 * (d / 16);
+    const size_t chunks = static_cast<size_t>(n_rb) * 16 * (dp / 16);
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < chunks; idx += (size_t)gridDim.x * blockDim.x) {
-        const int ch = static_cast<int>(idx % (d / 16));
-        const int lrow = static_cast<int>(idx / (d / 16));
+        const int ch = static_cast<int>(idx % (dp / 16));
+        const int lrow = static_cast<int>(idx / (dp / 16));
         const int rb = lrow / 16, rr = lrow % 16;
         const int8_t* src;
         int row;
@@ -1250,15 +1487,15 @@ __global__ void k_repack_i8(uint8_t* dst, const int8_t* w1, const float* s1, con
         const int lane = 4 * r + c;
         uint8_t* out = dst + (static_cast<size_t>(rb) * ksn + ks) * kTileBytesI8 + w * 1024 + half * 512 + lane * 16;
         uint4 v = make_uint4(0, 0, 0, 0);
-        if (row < n) v = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(row) * d + col);
+        if (row < n && col < d) v = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(row) * d + col);
         *reinterpret_cast<uint4*>(out) = v;
     }
-    // scales (already 1/s): one per (logical row, group)
-    const int gpr = d / 64;
-    const size_t groups = static_cast<size_t>(n_rb) * 16 * gpr;
+    // scales (already 1/s): one per (logical row, group); padding groups 0
+    const int gpr = d / 64, gprp = dp / 64;
+    const size_t groups = static_cast<size_t>(n_rb) * 16 * gprp;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < groups; idx += (size_t)gridDim.x * blockDim.x) {
-        const int gi = static_cast<int>(idx % gpr);
-        const int lrow = static_cast<int>(idx / gpr);
+        const int gi = static_cast<int>(idx % gprp);
+        const int lrow = static_cast<int>(idx / gprp);
         const int rb = lrow / 16, rr = lrow % 16;
         const float* src;
         int row;
@@ -1271,7 +1508,7 @@ __global__ void k_repack_i8(uint8_t* dst, const int8_t* w1, const float* s1, con
         }
         const int ks = gi / 8, w = gi % 8;
         float* out = reinterpret_cast<float*>(dst + (static_cast<size_t>(rb) * ksn + ks) * kTileBytesI8 + 8192);
-        out[rr * 8 + w] = (row < n) ? src[static_cast<size_t>(row) * gpr + gi] : 0.f;
+        out[rr * 8 + w] = (row < n && gi < gpr) ? src[static_cast<size_t>(row) * gpr + gi] : 0.f;
     }
 }
 
@@ -1300,8 +1537,9 @@ __global__ void k_repack_f32(uint8_t* dst, const float* w, int n, int d) {
 
 bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers, int grid, int max_smem,
                         int* stages, size_t* smem_bytes, int* pbuf_floats) {
-    if (D % kTileCols || F % kTileCols) return false;
-    if (!(HD == 64 || HD == 128 || HD == 256) || H * HD != D || grid < 1) return false;
+    if (D % kTileCols || F % 64 || (H * HD) % 64) return false;
+    // H: this rank's q heads (H hd == D on one GPU, D / tp under tensor parallelism)
+    if (!(HD == 64 || HD == 128 || HD == 256) || H * HD > D || grid < 1) return false;
     if (H != 4 * KV || KV > 32) return false;  // kv head h / 4; group row counts in smem
     // statistics entries; the barrier counter reaches grid x (5 L + 1)
     if (grid > kStatsCap || static_cast<long long>(grid) * (5 * n_layers + 1) >= (1ll << 31)) return false;
@@ -1309,7 +1547,7 @@ bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers
     auto need = [&](int n_rows, int rows_per_tile, int d) {
         const int n_rb = (n_rows + rows_per_tile - 1) / rows_per_tile;
         const int per_cta = (n_rb + grid - 1) / grid;
-        return per_cta * (d / kTileCols) * rows_per_tile;
+        return per_cta * tile_slices(d) * rows_per_tile;
     };
     int pb = 512;
     pb = std::max(pb, need((H + 2 * KV) * HD, kTileRowsI8, D));
@@ -1332,10 +1570,14 @@ tl_status launch_decode_step(const DecodeArgs& a, int grid, int stages, size_t s
     DecodeArgs copy = a;
     void* args[] = {&copy, &stages};
     const void* fn = nullptr;
+    const bool tp = a.tp_size > 1;
     switch (a.HD) {
-        case 64: fn = reinterpret_cast<const void*>(decode_step_kernel<64>); break;
-        case 128: fn = reinterpret_cast<const void*>(decode_step_kernel<128>); break;
-        case 256: fn = reinterpret_cast<const void*>(decode_step_kernel<256>); break;
+        case 64: fn = tp ? reinterpret_cast<const void*>(decode_step_kernel<64, true>)
+                         : reinterpret_cast<const void*>(decode_step_kernel<64, false>); break;
+        case 128: fn = tp ? reinterpret_cast<const void*>(decode_step_kernel<128, true>)
+                          : reinterpret_cast<const void*>(decode_step_kernel<128, false>); break;
+        case 256: fn = tp ? reinterpret_cast<const void*>(decode_step_kernel<256, true>)
+                          : reinterpret_cast<const void*>(decode_step_kernel<256, false>); break;
         default: return set_error(TL_ERR_UNSUPPORTED, "persistent decode: head_dim %d", a.HD);
     }
     int have = 0;

@@ -11,7 +11,7 @@ namespace tl {
 // Tiled weight layout streamed by the persistent kernel.
 //
 // int8 matrices ([n, d], row-major in the file) become tiles of 16 rows x 512
-// columns.  A tile is 8192 bytes of weights followed by 512 bytes of fp32
+// columns (d a multiple of 64; the last tile of a row block is zero-padded).  A tile is 8192 bytes of weights followed by 512 bytes of fp32
 // inverse scales; tiles are ordered row-block major ((rb, ks) -> rb*KS + ks),
 // so the rows a CTA owns are one contiguous byte range.  Inside a tile,
 // block w covers columns [64w, 64w+64) (one quantisation group):
@@ -32,6 +32,15 @@ constexpr int kTileBytesI8 = 8192 + 512;
 constexpr int kTileRowsF32 = 4;
 constexpr int kTileBytesF32 = 8192;
 constexpr int kStatsCap = 1024;  // most CTAs / heads publishing statistics
+
+// Tensor-parallel exchange buffer (one per rank, mapped into every rank's
+// process over CUDA IPC), byte offsets:
+constexpr size_t kXchgCnt = 0;       // u64: o / down partial-row arrivals from all ranks' CTAs
+constexpr size_t kXchgAmCnt = 8;     // u64: argmax candidate arrivals from all ranks
+constexpr size_t kXchgAmSlot = 256;  // u64 [2][8]: {value bits | rank-local best index << 32}
+constexpr size_t kXchgRecv = 512;    // f32 [2][tp][D]: partial rows of o_proj / down_proj per sender
+constexpr int kMaxTp = 8;
+inline size_t xchg_bytes(int tp, int D) { return kXchgRecv + 2 * static_cast<size_t>(tp) * D * 4; }
 
 struct DecodeLayer {
     const uint8_t* qkv;  // tiles of [q; k; v]   ((H + 2 KV) hd rows, d = D)
@@ -75,6 +84,16 @@ struct DecodeArgs {
     // each CTA wrote in a phase, alternating buffers per phase.
     float2* stats;
     int prefetch;               // tile pairs prefetched into L2 ahead of the ring (0 = off)
+    // Tensor parallelism (tp_size > 1, modules.cpp layers split Megatron
+    // style): this rank holds q heads and kv heads [rank H, (rank + 1) H)
+    // (H, KV local), gate/up rows and down columns of its F slice, o_proj
+    // columns of its heads, and lm_head rows [vocab_off, vocab_off + V).
+    // o_proj and down_proj produce full-D partials that every rank sums in
+    // rank order; xpeer[q] is rank q's exchange buffer (own at q = tp_rank).
+    int tp_size, tp_rank, vocab_off;
+    uint8_t* xpeer[kMaxTp];
+    float* h2;                  // tp: post-MLP residual (h holds post-attention)
+    unsigned* epoch;            // steps run so far (tp exchange counters never reset)
     // Optional phase trace (nullptr = off): per CTA, kTraceEvents %globaltimer
     // stamps for every phase, [cta][phase][event], phases = 5 per layer + lm_head.
     unsigned long long* trace;
@@ -102,11 +121,13 @@ tl_status repack_i8_swiglu(uint8_t* dst, const int8_t* w1, const float* s1, cons
                            const float* s3, int n, int d, cudaStream_t st);
 tl_status repack_f32(uint8_t* dst, const float* w, int n, int d, cudaStream_t st);
 
+// Tiles per row block: columns rounded up to whole tiles (padding is zero).
+__host__ __device__ inline int tile_slices(int d) { return (d + kTileCols - 1) / kTileCols; }
 inline size_t tiles_i8_bytes(int n_rows, int d) {
-    return static_cast<size_t>((n_rows + kTileRowsI8 - 1) / kTileRowsI8) * (d / kTileCols) * kTileBytesI8;
+    return static_cast<size_t>((n_rows + kTileRowsI8 - 1) / kTileRowsI8) * tile_slices(d) * kTileBytesI8;
 }
 inline size_t tiles_f32_bytes(int n_rows, int d) {
-    return static_cast<size_t>((n_rows + kTileRowsF32 - 1) / kTileRowsF32) * (d / kTileCols) * kTileBytesF32;
+    return static_cast<size_t>((n_rows + kTileRowsF32 - 1) / kTileRowsF32) * tile_slices(d) * kTileBytesF32;
 }
 
 }  // namespace tl

@@ -240,13 +240,22 @@ struct tl_model {
     int* err = nullptr;
     int* dbg = nullptr;  // self-check build: {site, v0, v1}
     float2* stats = nullptr;  // persistent kernel: phase hand-over statistics [2][kStatsCap]
+    // tensor parallelism: rank `rank` of `tp`; local head / kv head / F / vocab counts
+    int tp = 1, rank = 0;
+    int64_t lH = 0, lKV = 0, lF = 0, lV = 0;
+    float* h2 = nullptr;          // second residual buffer (tp)
+    unsigned* epoch = nullptr;    // steps run (tp exchange counters)
+    uint8_t* xbuf = nullptr;      // this rank's exchange buffer (tp), cudaMalloc'd for IPC
+    uint8_t* xpeer_open[kMaxTp] = {};  // peer buffers opened with cudaIpcOpenMemHandle
+    bool connected = false;
+    bool broken = false;  // tp: a device-side wait gave up; the ranks' exchange state is lost
     double bytes_per_step = 0;
 };
 
 namespace tl {
 namespace {
 
-size_t layer_kv_floats(const tl_model* m) { return m->cfg.n_kv_heads * m->max_seq * m->cfg.head_dim; }
+size_t layer_kv_floats(const tl_model* m) { return m->lKV * m->max_seq * m->cfg.head_dim; }
 
 tl_status check_shapes(const Header& h) {
     const tl_config& c = h.cfg;
@@ -297,6 +306,13 @@ tl_status upload(void* dst, const Header& h, uint64_t offset, size_t bytes) {
     return TL_OK;
 }
 
+// Columns [col0, col0 + width) (in bytes) of every row of a row-major tensor.
+tl_status upload_cols(void* dst, const Header& h, uint64_t offset, size_t rows, size_t row_bytes, size_t col0,
+                      size_t width) {
+    TL_CUDA_TRY(cudaMemcpy2D(dst, width, h.payload + offset + col0, row_bytes, width, rows, cudaMemcpyHostToDevice));
+    return TL_OK;
+}
+
 tl_status build_steps(tl_model* m);
 tl_status capture_graph(tl_model* m);
 
@@ -335,6 +351,29 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     m->device = opts ? opts->device : 0;
     m->max_seq = (opts && opts->max_seq) ? opts->max_seq : 1024;
     m->use_graph = opts ? opts->use_graph != 0 : true;
+    // Tensor parallelism (Megatron split of modules.cpp's layers): this rank
+    // keeps q heads / kv heads / F rows / vocab rows [rank n / tp, (rank + 1) n / tp).
+    const int tp = (opts && opts->tp_size > 0) ? opts->tp_size : 1;
+    const int rank = opts ? opts->tp_rank : 0;
+    if (tp > 1) {
+        if (!(tp == 2 || tp == 4 || tp == 8) || rank < 0 || rank >= tp)
+            return set_error(TL_ERR_INVALID_ARGUMENT, "tp_size %d / tp_rank %d: tp_size must be 2, 4 or 8", tp, rank);
+        if (KV % tp || V % tp || F % tp || (F / tp) % 64)
+            return set_error(TL_ERR_UNSUPPORTED,
+                             "tp_size %d must divide n_kv_heads (%lld) and vocab_size (%lld), and "
+                             "intermediate_size (%lld) into multiples of 64",
+                             tp, static_cast<long long>(KV), static_cast<long long>(V), static_cast<long long>(F));
+        if (opts->kernel_mode != 0)
+            return set_error(TL_ERR_UNSUPPORTED, "tensor parallelism runs the persistent decode kernel (kernel_mode 0)");
+    }
+    m->tp = tp;
+    m->rank = rank;
+    const int64_t Hl = H / tp, KVl = KV / tp, Fl = F / tp, Vl = V / tp;
+    const int64_t NQKVl = (Hl + 2 * KVl) * HD;
+    m->lH = Hl;
+    m->lKV = KVl;
+    m->lF = Fl;
+    m->lV = Vl;
     if (const char* e = std::getenv("TL_NO_PDL")) m->pdl = (e[0] == '0');
     if (m->max_seq > (1u << 24))
         return set_error(TL_ERR_INVALID_ARGUMENT, "max_seq %zu too large (positions are exact in fp32 up to 2^24)",
@@ -343,58 +382,62 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     TL_CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
     m->splits = static_cast<int>(std::min<size_t>(32, std::max<size_t>(4, m->max_seq / 256)));
 
-    // ---- weights arena ----
+    // ---- weights arena (this rank's slices) ----
     using A = DeviceArena;
-    size_t wbytes = A::pad(V * D * 4) * 2 + A::pad(D * 4);
-    const size_t per_layer = A::pad(NQKV * D) + A::pad(D * H * HD) + 2 * A::pad(F * D) + A::pad(D * F) +
-                             A::pad(NQKV * D / 64 * 4) + A::pad(D * H * HD / 64 * 4) + 2 * A::pad(F * D / 64 * 4) +
-                             A::pad(D * F / 64 * 4) + 2 * A::pad(D * 4);
+    size_t wbytes = A::pad(V * D * 4) + A::pad(Vl * D * 4) + A::pad(D * 4);
+    const size_t per_layer = A::pad(NQKVl * D) + A::pad(D * Hl * HD) + 2 * A::pad(Fl * D) + A::pad(D * Fl) +
+                             A::pad(NQKVl * D / 64 * 4) + A::pad(D * Hl * HD / 64 * 4) + 2 * A::pad(Fl * D / 64 * 4) +
+                             A::pad(D * Fl / 64 * 4) + 2 * A::pad(D * 4);
     wbytes += per_layer * L;
     TL_TRY(m->weights.reserve(wbytes));
     m->embed = m->weights.take<float>(V * D);
-    m->lm_head = m->weights.take<float>(V * D);
+    m->lm_head = m->weights.take<float>(Vl * D);
     m->norm = m->weights.take<float>(D);
     TL_TRY(upload(m->embed, h, emb->offset, V * D * 4));
-    TL_TRY(upload(m->lm_head, h, lmh->offset, V * D * 4));
+    TL_TRY(upload(m->lm_head, h, lmh->offset + static_cast<uint64_t>(rank) * Vl * D * 4, Vl * D * 4));
     TL_TRY(upload(m->norm, h, nrm->offset, D * 4));
     m->layers.resize(L);
+    const int64_t G = D / 64;  // scale groups per row of a [*, D] tensor
     for (int64_t l = 0; l < L; l++) {
         LayerW& w = m->layers[l];
         const LayerRecs& r = recs[l];
-        w.wqkv = m->weights.take<int8_t>(NQKV * D);
-        w.wo = m->weights.take<int8_t>(D * H * HD);
-        w.w1 = m->weights.take<int8_t>(F * D);
-        w.w3 = m->weights.take<int8_t>(F * D);
-        w.w2 = m->weights.take<int8_t>(D * F);
-        w.sqkv = m->weights.take<float>(NQKV * D / 64);
-        w.so = m->weights.take<float>(D * H * HD / 64);
-        w.s1 = m->weights.take<float>(F * D / 64);
-        w.s3 = m->weights.take<float>(F * D / 64);
-        w.s2 = m->weights.take<float>(D * F / 64);
+        w.wqkv = m->weights.take<int8_t>(NQKVl * D);
+        w.wo = m->weights.take<int8_t>(D * Hl * HD);
+        w.w1 = m->weights.take<int8_t>(Fl * D);
+        w.w3 = m->weights.take<int8_t>(Fl * D);
+        w.w2 = m->weights.take<int8_t>(D * Fl);
+        w.sqkv = m->weights.take<float>(NQKVl * D / 64);
+        w.so = m->weights.take<float>(D * Hl * HD / 64);
+        w.s1 = m->weights.take<float>(Fl * D / 64);
+        w.s3 = m->weights.take<float>(Fl * D / 64);
+        w.s2 = m->weights.take<float>(D * Fl / 64);
         w.g_in = m->weights.take<float>(D);
         w.g_post = m->weights.take<float>(D);
         if (!w.g_post) return set_error(TL_ERR_OUT_OF_MEMORY, "weights arena too small (internal)");
-        // q, k, v rows back to back: one GEMV produces [q | k | v].
-        TL_TRY(upload(w.wqkv, h, r.q->offset, H * HD * D));
-        TL_TRY(upload(w.wqkv + H * HD * D, h, r.k->offset, KV * HD * D));
-        TL_TRY(upload(w.wqkv + (H + KV) * HD * D, h, r.v->offset, KV * HD * D));
-        TL_TRY(upload(w.sqkv, h, r.q->scale_offset, H * HD * D / 64 * 4));
-        TL_TRY(upload(w.sqkv + H * HD * D / 64, h, r.k->scale_offset, KV * HD * D / 64 * 4));
-        TL_TRY(upload(w.sqkv + (H + KV) * HD * D / 64, h, r.v->scale_offset, KV * HD * D / 64 * 4));
-        TL_TRY(upload(w.wo, h, r.o->offset, D * H * HD));
-        TL_TRY(upload(w.so, h, r.o->scale_offset, D * H * HD / 64 * 4));
-        TL_TRY(upload(w.w1, h, r.g->offset, F * D));
-        TL_TRY(upload(w.s1, h, r.g->scale_offset, F * D / 64 * 4));
-        TL_TRY(upload(w.w3, h, r.u->offset, F * D));
-        TL_TRY(upload(w.s3, h, r.u->scale_offset, F * D / 64 * 4));
-        TL_TRY(upload(w.w2, h, r.d->offset, D * F));
-        TL_TRY(upload(w.s2, h, r.d->scale_offset, D * F / 64 * 4));
+        // q rows of this rank's heads, then its k and v rows: one GEMV produces [q | k | v].
+        const int64_t q0 = rank * Hl * HD, k0 = rank * KVl * HD;
+        TL_TRY(upload(w.wqkv, h, r.q->offset + q0 * D, Hl * HD * D));
+        TL_TRY(upload(w.wqkv + Hl * HD * D, h, r.k->offset + k0 * D, KVl * HD * D));
+        TL_TRY(upload(w.wqkv + (Hl + KVl) * HD * D, h, r.v->offset + k0 * D, KVl * HD * D));
+        TL_TRY(upload(w.sqkv, h, r.q->scale_offset + q0 * G * 4, Hl * HD * G * 4));
+        TL_TRY(upload(w.sqkv + Hl * HD * G, h, r.k->scale_offset + k0 * G * 4, KVl * HD * G * 4));
+        TL_TRY(upload(w.sqkv + (Hl + KVl) * HD * G, h, r.v->scale_offset + k0 * G * 4, KVl * HD * G * 4));
+        // o_proj: this rank's head columns of [D, H hd] (row-parallel)
+        TL_TRY(upload_cols(w.wo, h, r.o->offset, D, H * HD, q0, Hl * HD));
+        TL_TRY(upload_cols(w.so, h, r.o->scale_offset, D, H * HD / 64 * 4, q0 / 64 * 4, Hl * HD / 64 * 4));
+        // gate/up: this rank's F rows; down_proj: its F columns (row-parallel)
+        TL_TRY(upload(w.w1, h, r.g->offset + rank * Fl * D, Fl * D));
+        TL_TRY(upload(w.s1, h, r.g->scale_offset + rank * Fl * G * 4, Fl * G * 4));
+        TL_TRY(upload(w.w3, h, r.u->offset + rank * Fl * D, Fl * D));
+        TL_TRY(upload(w.s3, h, r.u->scale_offset + rank * Fl * G * 4, Fl * G * 4));
+        TL_TRY(upload_cols(w.w2, h, r.d->offset, D, F, rank * Fl, Fl));
+        TL_TRY(upload_cols(w.s2, h, r.d->scale_offset, D, F / 64 * 4, rank * Fl / 64 * 4, Fl / 64 * 4));
         TL_TRY(upload(w.g_in, h, r.ni->offset, D * 4));
         TL_TRY(upload(w.g_post, h, r.np->offset, D * 4));
         // Stored scales s = 127/absmax become 1/s: the GEMV multiplies.
-        const size_t ns[5] = {static_cast<size_t>(NQKV * D / 64), static_cast<size_t>(D * H * HD / 64),
-                              static_cast<size_t>(F * D / 64), static_cast<size_t>(F * D / 64),
-                              static_cast<size_t>(D * F / 64)};
+        const size_t ns[5] = {static_cast<size_t>(NQKVl * D / 64), static_cast<size_t>(D * Hl * HD / 64),
+                              static_cast<size_t>(Fl * D / 64), static_cast<size_t>(Fl * D / 64),
+                              static_cast<size_t>(D * Fl / 64)};
         float* sp[5] = {w.sqkv, w.so, w.s1, w.s3, w.s2};
         for (int k = 0; k < 5; k++) k_invert<<<256, 256, 0, m->stream>>>(sp[k], ns[k]);
         TL_TRY(check_launch("invert scales"));
@@ -408,8 +451,8 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         TL_CUDA_TRY(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, m->device));
         TL_CUDA_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->device));
         int pbuf = 0;
-        if (coop && decode_kernel_fits(static_cast<int>(D), static_cast<int>(F), static_cast<int>(H),
-                                       static_cast<int>(KV), static_cast<int>(HD), static_cast<int>(V),
+        if (coop && decode_kernel_fits(static_cast<int>(D), static_cast<int>(Fl), static_cast<int>(Hl),
+                                       static_cast<int>(KVl), static_cast<int>(HD), static_cast<int>(Vl),
                                        static_cast<int>(L), dev_sms, max_smem, &m->stages, &m->mega_smem, &pbuf)) {
             m->persistent = true;
             m->grid = dev_sms;
@@ -421,29 +464,31 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
                     m->stages = want;
                 }
             }
-            m->mega_splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(dev_sms / H, 256 / H)));
+            m->mega_splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(dev_sms / Hl, 256 / Hl)));
             m->dargs.pbuf_floats = pbuf;
         }
     }
+    if (tp > 1 && !m->persistent)
+        return set_error(TL_ERR_UNSUPPORTED, "tensor parallelism needs the persistent decode kernel (shape or device)");
     if (m->persistent) {
-        const size_t per = tiles_i8_bytes(NQKV, D) + tiles_i8_bytes(D, H * HD) + tiles_i8_bytes(2 * F, D) +
-                           tiles_i8_bytes(D, F);
-        TL_TRY(m->tiles.reserve(per * L + tiles_f32_bytes(V, D) + 256 * (4 * L + 1)));
+        const size_t per = tiles_i8_bytes(NQKVl, D) + tiles_i8_bytes(D, Hl * HD) + tiles_i8_bytes(2 * Fl, D) +
+                           tiles_i8_bytes(D, Fl);
+        TL_TRY(m->tiles.reserve(per * L + tiles_f32_bytes(Vl, D) + 256 * (4 * L + 1)));
         std::vector<DecodeLayer> dl(L);
         for (int64_t l = 0; l < L; l++) {
             const LayerW& w = m->layers[l];
-            uint8_t* tq = m->tiles.take<uint8_t>(tiles_i8_bytes(NQKV, D));
-            uint8_t* to = m->tiles.take<uint8_t>(tiles_i8_bytes(D, H * HD));
-            uint8_t* t13 = m->tiles.take<uint8_t>(tiles_i8_bytes(2 * F, D));
-            uint8_t* t2 = m->tiles.take<uint8_t>(tiles_i8_bytes(D, F));
-            TL_TRY(repack_i8(tq, w.wqkv, w.sqkv, NQKV, D, m->stream));
-            TL_TRY(repack_i8(to, w.wo, w.so, D, H * HD, m->stream));
-            TL_TRY(repack_i8_swiglu(t13, w.w1, w.s1, w.w3, w.s3, F, D, m->stream));
-            TL_TRY(repack_i8(t2, w.w2, w.s2, D, F, m->stream));
+            uint8_t* tq = m->tiles.take<uint8_t>(tiles_i8_bytes(NQKVl, D));
+            uint8_t* to = m->tiles.take<uint8_t>(tiles_i8_bytes(D, Hl * HD));
+            uint8_t* t13 = m->tiles.take<uint8_t>(tiles_i8_bytes(2 * Fl, D));
+            uint8_t* t2 = m->tiles.take<uint8_t>(tiles_i8_bytes(D, Fl));
+            TL_TRY(repack_i8(tq, w.wqkv, w.sqkv, NQKVl, D, m->stream));
+            TL_TRY(repack_i8(to, w.wo, w.so, D, Hl * HD, m->stream));
+            TL_TRY(repack_i8_swiglu(t13, w.w1, w.s1, w.w3, w.s3, Fl, D, m->stream));
+            TL_TRY(repack_i8(t2, w.w2, w.s2, D, Fl, m->stream));
             dl[l] = DecodeLayer{tq, to, t13, t2, w.g_in, w.g_post, nullptr, nullptr};
         }
-        uint8_t* tl = m->tiles.take<uint8_t>(tiles_f32_bytes(V, D));
-        TL_TRY(repack_f32(tl, m->lm_head, V, D, m->stream));
+        uint8_t* tl = m->tiles.take<uint8_t>(tiles_f32_bytes(Vl, D));
+        TL_TRY(repack_f32(tl, m->lm_head, Vl, D, m->stream));
         m->dargs.lm_head = tl;
         TL_CUDA_TRY(cudaMalloc(&m->d_layers, sizeof(DecodeLayer) * L));
         // KV pointers are filled once the state arena exists (below).
@@ -456,10 +501,10 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     const size_t half = HD / 2;
     const int am_grid = std::max(gemv_f32_grid(V, D, true, true), m->grid);
     const int part_splits = std::max(m->splits, m->mega_splits);
-    size_t sbytes = 2 * A::pad(kv * 4) + 2 * A::pad(m->max_seq * half * 4) + A::pad(D * 4) + A::pad(NQKV * 4) +
-                    A::pad(H * HD * 4) + A::pad(F * 4) + A::pad(V * 4) + A::pad(H * part_splits * (HD + 4) * 4) +
-                    A::pad(H * 4) * 2 + A::pad(am_grid * 4) * 2 + A::pad(4) * 6 + A::pad(16) + A::pad(m->max_seq * 4) * 2 +
-                    A::pad(2 * kStatsCap * sizeof(float2));
+    size_t sbytes = 2 * A::pad(kv * 4) + 2 * A::pad(m->max_seq * half * 4) + A::pad(D * 4) + A::pad(NQKVl * 4) +
+                    A::pad(Hl * HD * 4) + A::pad(Fl * 4) + A::pad(Vl * 4) + A::pad(Hl * part_splits * (HD + 4) * 4) +
+                    A::pad(Hl * 4) * 2 + A::pad(am_grid * 4) * 2 + A::pad(4) * 6 + A::pad(16) + A::pad(m->max_seq * 4) * 2 +
+                    A::pad(2 * kStatsCap * sizeof(float2)) + A::pad(D * 4) + A::pad(4);
     TL_TRY(m->state.reserve(sbytes));
     TL_CUDA_TRY(cudaMemsetAsync(m->state.base, 0, sbytes, m->stream));
     m->kc = m->state.take<float>(kv);
@@ -467,13 +512,13 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     m->cos_tab = m->state.take<float>(m->max_seq * half);
     m->sin_tab = m->state.take<float>(m->max_seq * half);
     m->h = m->state.take<float>(D);
-    m->qkv = m->state.take<float>(NQKV);
-    m->ctx = m->state.take<float>(H * HD);
-    m->act = m->state.take<float>(F);
-    m->logits = m->state.take<float>(V);
-    m->attn_part = m->state.take<float>(H * part_splits * (HD + 4));
-    m->attn_cnt = m->state.take<unsigned>(H);
-    m->qkv_cnt = m->state.take<unsigned>(H);
+    m->qkv = m->state.take<float>(NQKVl);
+    m->ctx = m->state.take<float>(Hl * HD);
+    m->act = m->state.take<float>(Fl);
+    m->logits = m->state.take<float>(Vl);
+    m->attn_part = m->state.take<float>(Hl * part_splits * (HD + 4));
+    m->attn_cnt = m->state.take<unsigned>(Hl);
+    m->qkv_cnt = m->state.take<unsigned>(Hl);
     m->am_v = m->state.take<float>(am_grid);
     m->am_i = m->state.take<uint32_t>(am_grid);
     m->am_cnt = m->state.take<unsigned>(1);
@@ -486,7 +531,9 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     m->err = m->state.take<int>(1);
     m->dbg = m->state.take<int>(4);
     m->stats = m->state.take<float2>(2 * kStatsCap);
-    if (!m->stats) return set_error(TL_ERR_OUT_OF_MEMORY, "state arena too small (internal)");
+    m->h2 = m->state.take<float>(D);
+    m->epoch = m->state.take<unsigned>(1);
+    if (!m->epoch) return set_error(TL_ERR_OUT_OF_MEMORY, "state arena too small (internal)");
     if (m->persistent) {
         for (int64_t l = 0; l < L; l++) {
             m->layers_host_tmp[l].k_cache = m->kc + static_cast<size_t>(l) * layer_kv_floats(m.get());
@@ -507,8 +554,16 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
 #endif
         d.am_v = m->am_v; d.am_i = m->am_i; d.ticket = m->ticket; d.bar = m->bar; d.err = m->err;
         d.token = m->d_token; d.pos = m->d_pos; d.history = m->d_hist;
-        d.D = static_cast<int>(D); d.F = static_cast<int>(F); d.H = static_cast<int>(H);
-        d.KV = static_cast<int>(KV); d.HD = static_cast<int>(HD); d.V = static_cast<int>(V);
+        d.D = static_cast<int>(D); d.F = static_cast<int>(Fl); d.H = static_cast<int>(Hl);
+        d.KV = static_cast<int>(KVl); d.HD = static_cast<int>(HD); d.V = static_cast<int>(Vl);
+        d.tp_size = tp; d.tp_rank = rank; d.vocab_off = static_cast<int>(rank * Vl);
+        d.h2 = m->h2; d.epoch = m->epoch;
+        if (tp > 1) {  // this rank's exchange buffer; peers are mapped by tl_model_tp_connect
+            const size_t xb = xchg_bytes(tp, static_cast<int>(D));
+            TL_CUDA_TRY(cudaMalloc(&m->xbuf, xb));
+            TL_CUDA_TRY(cudaMemset(m->xbuf, 0, xb));
+            d.xpeer[rank] = m->xbuf;
+        }
         d.max_seq = static_cast<int>(m->max_seq); d.splits = m->mega_splits;
         d.attn_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
     }
@@ -604,11 +659,13 @@ tl_status build_steps(tl_model* m) {
     const int D = c.hidden_size, V = c.vocab_size;
     m->steps.clear();
     if (m->persistent) {
-        const double F = c.intermediate_size, H = c.n_heads, KV = c.n_kv_heads, HD = c.head_dim, L = c.n_layers;
+        // this rank's bytes (all of them when tp = 1)
+        const double F = m->lF, H = m->lH, KV = m->lKV, HD = c.head_dim, L = c.n_layers;
         const double NQKV = (H + 2 * KV) * HD;
+        const double Vr = double(m->lV);
         // int8 weights + fp32 scales of every projection, fp32 lm_head, norms, one embedding row
         const double per_layer = (NQKV * D + D * H * HD + 3.0 * F * D) * (1 + 4.0 / 64) + 8.0 * D;
-        const double fixed = per_layer * L + double(V) * D * 4 + 8.0 * D;
+        const double fixed = per_layer * L + Vr * D * 4 + 8.0 * D;
         m->steps.push_back({"decode_step",
                             [=] { return fixed + 2.0 * L * KV * (double(m->pos) + 1) * HD * 4; },
                             [=](cudaStream_t s, bool) {
@@ -680,6 +737,16 @@ tl_status set_token(tl_model* m, uint32_t token) {
     return TL_OK;
 }
 
+// A tensor-parallel model runs only once every rank's exchange buffer is mapped.
+tl_status check_tp_ready(const tl_model* m) {
+    if (m->tp > 1 && !m->connected)
+        return set_error(TL_ERR_INVALID_ARGUMENT, "tensor-parallel model: call tl_model_tp_connect on every rank first");
+    if (m->broken)
+        return set_error(TL_ERR_TIMEOUT, "tensor-parallel exchange state was lost after a device-side timeout; "
+                                         "reload the model on every rank");
+    return TL_OK;
+}
+
 tl_status check_capacity(const tl_model* m, size_t steps) {
     if (m->pos + steps > m->max_seq)
         return set_error(TL_ERR_CAPACITY, "KV cache full: pos %zu + %zu steps > max_seq %zu", m->pos, steps,
@@ -716,6 +783,7 @@ tl_status sync(tl_model* m) {
         cudaStreamSynchronize(m->stream);
         m->h_pinned[3] = 0;
         if (code == 5) return set_error(TL_ERR_INVALID_ARGUMENT, "decode kernel: token or position out of range");
+        if (m->tp > 1) m->broken = true;
         return set_error(TL_ERR_TIMEOUT,
                          "decode kernel wait timed out (code %u: 1 grid barrier, 2 tile arrival, 3 ring slot)",
                          code);
@@ -768,6 +836,9 @@ tl_status tl_model_destroy(tl_model* m) {
     m->tiles.release();
     if (m->d_layers) cudaFree(m->d_layers);
     if (m->h_pinned) cudaFreeHost(m->h_pinned);
+    for (int q = 0; q < kMaxTp; q++)
+        if (m->xpeer_open[q]) cudaIpcCloseMemHandle(m->xpeer_open[q]);
+    if (m->xbuf) cudaFree(m->xbuf);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
     return TL_OK;
@@ -780,15 +851,61 @@ tl_status tl_model_config(const tl_model* m, tl_config* out) {
     return TL_OK;
 }
 
+tl_status tl_model_tp_handle(const tl_model* m, void* handle) {
+    clear_error();
+    TL_REQUIRE(m && handle, "tl_model_tp_handle: null argument");
+    if (m->tp < 2) return set_error(TL_ERR_INVALID_ARGUMENT, "tl_model_tp_handle: model was not loaded with tp_size > 1");
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    cudaIpcMemHandle_t h;
+    TL_CUDA_TRY(cudaIpcGetMemHandle(&h, m->xbuf));
+    static_assert(sizeof(h) == TL_TP_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle, &h, sizeof(h));
+    return TL_OK;
+}
+
+tl_status tl_model_tp_connect(tl_model* m, const void* handles) {
+    clear_error();
+    TL_REQUIRE(m && handles, "tl_model_tp_connect: null argument");
+    if (m->tp < 2) return set_error(TL_ERR_INVALID_ARGUMENT, "tl_model_tp_connect: model was not loaded with tp_size > 1");
+    if (m->connected) return set_error(TL_ERR_INVALID_ARGUMENT, "tl_model_tp_connect: already connected");
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    for (int q = 0; q < m->tp; q++) {
+        if (q == m->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t*>(handles) + static_cast<size_t>(q) * TL_TP_HANDLE_BYTES, sizeof(h));
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            return set_error(TL_ERR_CUDA, "tl_model_tp_connect: opening rank %d's exchange buffer failed: %s", q,
+                             cudaGetErrorString(e));
+        m->xpeer_open[q] = static_cast<uint8_t*>(p);
+        m->dargs.xpeer[q] = static_cast<uint8_t*>(p);
+    }
+    m->connected = true;
+    // the step launch (and its graph) captured the arguments before the peers were known
+    if (m->graph_exec) {
+        cudaGraphExecDestroy(m->graph_exec);
+        m->graph_exec = nullptr;
+    }
+    if (m->graph) {
+        cudaGraphDestroy(m->graph);
+        m->graph = nullptr;
+    }
+    TL_TRY(build_steps(m));
+    if (m->use_graph) TL_TRY(capture_graph(m));
+    return TL_OK;
+}
+
 tl_status tl_model_forward(tl_model* m, uint32_t token, float* logits, uint32_t* next_token) {
     clear_error();
     TL_REQUIRE(m, "tl_model_forward: null model");
+    TL_TRY(check_tp_ready(m));
     TL_CUDA_TRY(cudaSetDevice(m->device));
     TL_TRY(check_capacity(m, 1));
     TL_TRY(set_token(m, token));
     TL_TRY(run_step(m));
     if (logits)
-        TL_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, m->stream));
+        TL_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, m->lV * 4, cudaMemcpyDeviceToHost, m->stream));
     if (next_token)
         TL_CUDA_TRY(cudaMemcpyAsync(m->h_pinned + 1, m->d_token, 4, cudaMemcpyDeviceToHost, m->stream));
     TL_TRY(sync(m));
@@ -801,6 +918,7 @@ tl_status tl_model_generate(tl_model* m, const uint32_t* prompt, size_t n_prompt
     clear_error();
     TL_REQUIRE(m && prompt && n_prompt > 0 && (out || n_new == 0), "tl_model_generate: bad arguments");
     TL_REQUIRE(n_new > 0, "tl_model_generate: n_new must be positive (the last prompt token is forwarded by it)");
+    TL_TRY(check_tp_ready(m));
     TL_CUDA_TRY(cudaSetDevice(m->device));
     TL_TRY(check_capacity(m, n_prompt - 1 + n_new));
     for (size_t i = 0; i < n_prompt; i++)
@@ -844,6 +962,7 @@ tl_status tl_model_layer_forward(tl_model* m, int layer, float* hidden) {
     clear_error();
     TL_REQUIRE(m && hidden, "tl_model_layer_forward: null argument");
     TL_REQUIRE(layer >= 0 && static_cast<size_t>(layer) < m->cfg.n_layers, "layer %d out of range", layer);
+    if (m->tp > 1) return set_error(TL_ERR_UNSUPPORTED, "tl_model_layer_forward: not available under tensor parallelism");
     TL_TRY(check_capacity(m, 1));
     TL_CUDA_TRY(cudaSetDevice(m->device));
     const size_t D = m->cfg.hidden_size;
@@ -862,7 +981,7 @@ tl_status tl_model_read_kv(const tl_model* m, int layer, size_t pos, float* k, f
                "tl_model_read_kv: layer/pos out of range");
     TL_CUDA_TRY(cudaSetDevice(m->device));
     const size_t hd = m->cfg.head_dim;
-    for (size_t kh = 0; kh < m->cfg.n_kv_heads; kh++) {
+    for (size_t kh = 0; kh < static_cast<size_t>(m->lKV); kh++) {
         const size_t off = layer * layer_kv_floats(m) + (kh * m->max_seq + pos) * hd;
         TL_CUDA_TRY(cudaMemcpyAsync(k + kh * hd, m->kc + off, hd * 4, cudaMemcpyDeviceToHost, m->stream));
         TL_CUDA_TRY(cudaMemcpyAsync(v + kh * hd, m->vc + off, hd * 4, cudaMemcpyDeviceToHost, m->stream));
@@ -873,6 +992,7 @@ tl_status tl_model_read_kv(const tl_model* m, int layer, size_t pos, float* k, f
 tl_status tl_model_time_decode(tl_model* m, uint32_t token, size_t n, uint32_t* out, float* ms) {
     clear_error();
     TL_REQUIRE(m && ms && n > 0, "tl_model_time_decode: bad arguments");
+    TL_TRY(check_tp_ready(m));
     TL_CUDA_TRY(cudaSetDevice(m->device));
     TL_TRY(check_capacity(m, n));
     TL_TRY(set_token(m, token));
@@ -901,6 +1021,7 @@ tl_status tl_model_profile(tl_model* m, uint32_t token, size_t n, tl_kernel_time
                            int* n_kinds) {
     clear_error();
     TL_REQUIRE(m && kinds && n_kinds && n > 0 && max_kinds > 0, "tl_model_profile: bad arguments");
+    TL_TRY(check_tp_ready(m));
     TL_CUDA_TRY(cudaSetDevice(m->device));
     TL_TRY(check_capacity(m, n));
     TL_TRY(set_token(m, token));
@@ -954,6 +1075,7 @@ tl_status tl_model_trace_step(tl_model* m, uint32_t token, uint64_t* out, size_t
     clear_error();
     TL_REQUIRE(m && out && n_written, "tl_model_trace_step: null argument");
     if (!m->persistent) return set_error(TL_ERR_UNSUPPORTED, "tracing needs the persistent decode kernel");
+    TL_TRY(check_tp_ready(m));
     TL_CUDA_TRY(cudaSetDevice(m->device));
     TL_TRY(check_capacity(m, 1));
     const size_t phases = 5 * m->cfg.n_layers + 1;

@@ -11,7 +11,7 @@ from typing import Dict, List, Optional, Sequence
 
 import numpy as np
 
-from . import check, lib, tl_config, tl_kernel_time, tl_model_options
+from . import TP_HANDLE_BYTES, check, lib, tl_config, tl_kernel_time, tl_model_options
 
 
 class Model:
@@ -22,8 +22,9 @@ class Model:
     takes the same bytes from host memory.
     """
 
-    def __init__(self, handle: ctypes.c_void_p):
+    def __init__(self, handle: ctypes.c_void_p, tp_size: int = 1, tp_rank: int = 0):
         self._h = handle
+        self.tp_size, self.tp_rank = max(1, tp_size), tp_rank
         cfg = tl_config()
         check(lib().tl_model_config(self._h, ctypes.byref(cfg)))
         self.config = {f: getattr(cfg, f) for f, _ in tl_config._fields_ if f != "quant"}
@@ -33,26 +34,43 @@ class Model:
     PERSISTENT, PER_OP = 0, 1
 
     @staticmethod
-    def _opts(device: int, max_seq: int, use_graph: bool, kernel_mode: int):
+    def _opts(device: int, max_seq: int, use_graph: bool, kernel_mode: int, tp_size: int = 1,
+              tp_rank: int = 0):
         return tl_model_options(device=device, max_seq=max_seq, use_graph=1 if use_graph else 0,
-                                kernel_mode=kernel_mode)
+                                kernel_mode=kernel_mode, tp_size=tp_size, tp_rank=tp_rank)
 
     @classmethod
     def load(cls, path: str, device: int = 0, max_seq: int = 1024, use_graph: bool = True,
-             kernel_mode: int = 0) -> "Model":
+             kernel_mode: int = 0, tp_size: int = 1, tp_rank: int = 0) -> "Model":
         h = ctypes.c_void_p()
-        o = cls._opts(device, max_seq, use_graph, kernel_mode)
+        o = cls._opts(device, max_seq, use_graph, kernel_mode, tp_size, tp_rank)
         check(lib().tl_model_load(path.encode(), ctypes.byref(o), ctypes.byref(h)))
-        return cls(h)
+        return cls(h, tp_size, tp_rank)
 
     @classmethod
     def from_buffer(cls, buf: np.ndarray, device: int = 0, max_seq: int = 1024,
-                    use_graph: bool = True, kernel_mode: int = 0) -> "Model":
+                    use_graph: bool = True, kernel_mode: int = 0, tp_size: int = 1,
+                    tp_rank: int = 0) -> "Model":
         buf = np.ascontiguousarray(buf)
         h = ctypes.c_void_p()
-        o = cls._opts(device, max_seq, use_graph, kernel_mode)
+        o = cls._opts(device, max_seq, use_graph, kernel_mode, tp_size, tp_rank)
         check(lib().tl_model_load_buffer(buf.ctypes.data, buf.nbytes, ctypes.byref(o), ctypes.byref(h)))
-        return cls(h)
+        return cls(h, tp_size, tp_rank)
+
+    # ---- tensor parallelism ----
+    def tp_handle(self) -> bytes:
+        """This rank's exchange-buffer handle (to be gathered by every rank)."""
+        buf = (ctypes.c_uint8 * TP_HANDLE_BYTES)()
+        check(lib().tl_model_tp_handle(self._h, buf))
+        return bytes(buf)
+
+    def tp_connect(self, handles: Sequence[bytes]) -> None:
+        """Map every rank's exchange buffer; `handles` in rank order."""
+        blob = b"".join(handles)
+        if len(handles) != self.tp_size or len(blob) != self.tp_size * TP_HANDLE_BYTES:
+            raise ValueError(f"need {self.tp_size} handles of {TP_HANDLE_BYTES} bytes")
+        arr = (ctypes.c_uint8 * len(blob)).from_buffer_copy(blob)
+        check(lib().tl_model_tp_connect(self._h, arr))
 
     def close(self) -> None:
         if self._h:
@@ -84,8 +102,9 @@ class Model:
 
     # ---- Model<T>::forward + sample_max ----
     def forward(self, token: int, logits: bool = True):
-        """One token at the current position; returns (logits or None, argmax)."""
-        out = np.empty(self.config["vocab_size"], dtype=np.float32) if logits else None
+        """One token at the current position; returns (logits or None, argmax).
+        Under tensor parallelism the logits are this rank's vocabulary slice."""
+        out = np.empty(self.config["vocab_size"] // self.tp_size, dtype=np.float32) if logits else None
         nxt = ctypes.c_uint32()
         check(lib().tl_model_forward(self._h, int(token), out.ctypes.data if logits else None,
                                      ctypes.byref(nxt)))
@@ -105,11 +124,13 @@ class Model:
         return h
 
     def read_kv(self, layer: int, pos: int):
+        """K and V rows at `pos` (this rank's kv heads under tensor parallelism)."""
         c = self.config
-        k = np.empty(c["n_kv_heads"] * c["head_dim"], dtype=np.float32)
+        kv = c["n_kv_heads"] // self.tp_size
+        k = np.empty(kv * c["head_dim"], dtype=np.float32)
         v = np.empty_like(k)
         check(lib().tl_model_read_kv(self._h, int(layer), int(pos), k.ctypes.data, v.ctypes.data))
-        return k.reshape(c["n_kv_heads"], c["head_dim"]), v.reshape(c["n_kv_heads"], c["head_dim"])
+        return k.reshape(kv, c["head_dim"]), v.reshape(kv, c["head_dim"])
 
     # ---- measurement ----
     def time_decode(self, token: int, n: int):
