@@ -13,9 +13,11 @@ flush is needed between steps.
 Prints one JSON line (rank 0).  `value` is device time (CUDA events around
 K back-to-back CUDA-graph replays); `e2e` is the same K steps through the
 public C ABI call tl_model_forward with the token copied in from and the
-argmax copied back to host memory each step.  For N > 1 every rank decodes
-its own sequence on its own GPU (independent replicas, weak scaling), the
-timed region is bracketed by barriers and the slowest rank's time counts.
+argmax copied back to host memory each step.  For N > 1 the one sequence is
+tensor-parallel over the N GPUs (each rank holds 1/N of every projection and
+of the lm_head; o_proj and down_proj partials are summed inside the decode
+kernel over NVLink): strong scaling, the timed region is bracketed by
+barriers and the slowest rank's time counts.
 
 --impl reference times the reference's own CPU code (oracle/_ref, built from
 the reference sources) on this host: each step is one decode token at
@@ -192,14 +194,30 @@ def load_traffic():
 def run_ours(args, rank, world, local):
     import torch
     import torch.distributed as dist
-    from torchless_b200 import Model
+    from torchless_b200 import Model, tp
 
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
-    buf = make_model_bytes(f"cuda:{local}", args.layers)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600),
+                                device_id=torch.device(f"cuda:{local}"))
     max_seq = PROMPT_LEN + args.warmup + args.steps + 8
-    m = Model.from_buffer(buf, device=local, max_seq=max_seq)
+    if world == 1:
+        buf = make_model_bytes(f"cuda:{local}", args.layers)
+        m = Model.from_buffer(buf, device=local, max_seq=max_seq)
+    else:
+        # N > 1: one sequence, tensor-parallel over the N GPUs.  Rank 0 writes
+        # the model file once; every rank maps it and loads its slice.
+        import tempfile
+        path = os.path.join(tempfile.gettempdir(), f"tl_bench_model_{os.environ.get('MASTER_PORT', '0')}.bin")
+        if rank == 0:
+            make_model_bytes(f"cuda:{local}", args.layers).tofile(path)
+        dist.barrier()
+        m = Model.load(path, device=local, max_seq=max_seq, tp_size=world, tp_rank=rank)
+        dist.barrier()
+        if rank == 0:
+            os.remove(path)
+        tp.connect(m)
+        buf = None
     prompt = prompt_ids()
     for t in prompt[:-1]:
         m.forward(t, logits=False)
@@ -231,15 +249,19 @@ def run_ours(args, rank, world, local):
         t = torch.tensor([ms, e2e_s], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_s = float(t[0]), float(t[1])
-    value = world * args.steps / (ms / 1000.0)
-    e2e = world * args.steps / e2e_s
+    # one sequence on all N GPUs: tokens of that sequence per second
+    value = args.steps / (ms / 1000.0)
+    e2e = args.steps / e2e_s
 
     # Per-kernel device times (eager launches with an event pair around each)
     m.pos = start_pos
     prof = m.profile(prompt[-1], 4)
     launches = m.launches_per_step()
+    if world > 1:
+        dist.barrier()  # no rank unmaps its exchange buffer while a peer kernel runs
     m.close()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -248,17 +270,19 @@ def run_ours(args, rank, world, local):
     avg_ms = top["total_ms"] / top["launches"]
     achieved = top["bytes_per_launch"] / (avg_ms / 1000.0) / 1e9
     peak, peak_kind = peaks()
-    traffic = load_traffic().get(top["name"])
+    # ncu traffic of the 1-GPU launch; a rank's launch under tensor parallelism is not captured
+    traffic = load_traffic().get(top["name"]) if world == 1 else None
     total_prof = sum(k["total_ms"] for k in prof)
 
     out = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
         "config": {"workload": "Mistral-7B int8 bs1 greedy decode (16-token prompt, 128 tokens)"
                    + ("" if args.layers == 32 else f" [profiling case: {args.layers} of 32 layers]"),
-                   "global_batch": world, "seq_len": max_seq,
-                   "parallelism": "replicas" if world > 1 else "single",
+                   "global_batch": 1, "seq_len": max_seq,
+                   "parallelism": f"tp{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (7.94 GB of weights per step)",
                    "weights_bytes_per_token": 7940898816},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
@@ -266,13 +290,14 @@ def run_ours(args, rank, world, local):
         "roofline": {"bound": "hbm", "kernel": top["name"], "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "algorithmic_bytes": top["bytes_per_launch"]},
-        "model_roofline": {"bytes_per_token": 7940898816, "tok_s_at_peak": peak * 1e9 / 7940898816,
-                           "frac": value / world / (peak * 1e9 / 7940898816)},
+        # N GPUs share the bytes of a token: the roofline is N x peak / bytes
+        "model_roofline": {"bytes_per_token": 7940898816, "tok_s_at_peak": world * peak * 1e9 / 7940898816,
+                           "frac": value / (world * peak * 1e9 / 7940898816)},
         "kernel_shares": {k["name"]: round(k["total_ms"] / total_prof, 4) for k in prof},
         "clocks": clocks.summary(),
         "ids_head": ids[:8],
     }
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:
         try:
             v, secs, cores = cpu_reference_sample(buf, args.cpu_layers)
             out["cpu_baseline"] = {
