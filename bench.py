@@ -312,6 +312,108 @@ def run_ours(args, rank, world, local):
     print(json.dumps(out))
 
 
+# ---------------------------------------------------------------------------
+# Isolated int8 GEMV sweep at Mistral-7B shapes (batch 1), through the op-level
+# C ABI (tl_matmul_i8 = kernels.h matmul(int8); tl_mlp_gate_up = w1|w3 fused
+# with SiLU * up).  Weights int8 uniform in [-127, 127], stored scales
+# |N(0, 0.01)| (divisors, tensor.cpp:101-104), x ~ N(0, 1).  Enough weight
+# copies rotate that every launch streams its weights from HBM (> L2).
+# ---------------------------------------------------------------------------
+SWEEP = [("wq/wo 4096->4096", 4096, 4096, "matmul"), ("wk/wv 4096->1024", 1024, 4096, "matmul"),
+         ("w1|w3 4096->14336 fused SiLU*up", 14336, 4096, "gate_up"), ("w2 14336->4096", 4096, 14336, "matmul"),
+         ("lm_head int8 4096->32000", 32000, 4096, "matmul")]
+
+
+def run_gemv_sweep(args):
+    import torch
+    from torchless_b200 import ops
+    torch.cuda.set_device(0)
+    peak, peak_kind = peaks()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED)
+    for name, n, d, kind in SWEEP:
+        mats = 2 if kind == "gate_up" else 1
+        wbytes = mats * (n * d + 4 * n * d // 64)
+        copies = max(2, -(-(256 << 20) // wbytes))  # > 256 MB in rotation: no L2 reuse
+        ws = []
+        for _ in range(copies):
+            one = []
+            for _ in range(mats):
+                w = torch.randint(-127, 128, (n, d), dtype=torch.int8, device="cuda", generator=g)
+                sc = torch.randn(n * d // 64, device="cuda", generator=g).abs_() * 0.01 + 1e-6
+                one.append((w, sc))
+            ws.append(one)
+        x = torch.randn(d, device="cuda", generator=g)
+        y = torch.empty(n, device="cuda")
+
+        def launch(i):
+            one = ws[i % copies]
+            if kind == "gate_up":
+                ops.mlp_gate_up(y, one[0][0], one[0][1], one[1][0], one[1][1], x)
+            else:
+                ops.matmul(y, one[0][0], x, scales=one[0][1])
+
+        # parity against a torch fp32 restatement (w / scale per 64-group)
+        launch(0)
+        torch.cuda.synchronize()
+
+        def deq(w, sc):
+            return (w.float().view(n, d // 64, 64) / sc.view(n, d // 64, 1)).view(n, d)
+        if kind == "gate_up":
+            gate = deq(*ws[0][0]) @ x
+            ref = gate / (1.0 + torch.exp(-gate)) * (deq(*ws[0][1]) @ x)
+        else:
+            ref = deq(*ws[0][0]) @ x
+        err = float((y - ref).abs().max() / ref.abs().max())
+        for i in range(args.warmup):
+            launch(i)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(args.steps):
+            launch(args.warmup + i)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / args.steps
+        algo = wbytes + 4 * d + 4 * n
+        gbs = algo / (us * 1e-6) / 1e9
+        line = {"metric": "int8 GEMV HBM GB/s (bs1)", "shape": name, "n": n, "d": d,
+                "value": gbs, "unit": "GB/s", "us_per_launch": us, "algorithmic_bytes": algo,
+                "peak": peak, "peak_kind": peak_kind, "frac": gbs / peak, "rel_err_vs_fp32": err,
+                "launches": args.steps, "copies_rotated": copies}
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_gemv_sample(ws[0][0][0], ws[0][0][1], x, mats)
+        print(json.dumps(line), flush=True)
+        del ws
+
+
+def cpu_gemv_sample(w, sc, x, mats, rows=256):
+    """The reference's matmul(int8) (kernels.cpp:21-33, oracle/_ref) on the first
+    `rows` rows of the same weights; GB/s of weight + scale bytes (single thread,
+    as the reference's int8 matmul is)."""
+    import ctypes
+    import oracle
+    if not oracle.ref_available():
+        return {"value": None, "unit": "GB/s", "cores": 1, "kind": "reference", "sample": "oracle/_ref not built"}
+    n, d = w.shape
+    r = min(rows, n)
+    wh = np.ascontiguousarray(w[:r].cpu().numpy())
+    sh = np.ascontiguousarray(sc[: r * d // 64].cpu().numpy())
+    xh = np.ascontiguousarray(x.cpu().numpy())
+    yh = np.empty(r, dtype=np.float32)
+    L = oracle.ref_lib()
+    P = ctypes.c_void_p
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < 3 or time.perf_counter() - t0 < 1.0:
+        L.ref_matmul_i8(P(yh.ctypes.data), P(wh.ctypes.data), P(sh.ctypes.data), sh.size, P(xh.ctypes.data), r, d)
+        reps += 1
+    secs = (time.perf_counter() - t0) / reps
+    return {"value": (r * d + 4 * r * d // 64) / secs / 1e9, "unit": "GB/s", "cores": 1, "kind": "reference",
+            "sample": f"first {r} rows of the same weights, x{mats} matrices for the fused shape not included, "
+                      f"{reps} repetitions"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -320,12 +422,17 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-layers", type=int, default=8)
+    ap.add_argument("--gemv-sweep", action="store_true",
+                    help="isolated int8 GEMV sweep at Mistral-7B shapes (one JSON line per shape)")
     ap.add_argument("--layers", type=int, default=32,
                     help="transformer layers (32 = Mistral-7B; fewer only for small profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank, world, local = dist_env()
+    if args.gemv_sweep:
+        run_gemv_sweep(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
     else:
