@@ -131,6 +131,18 @@ TL_API tl_status tl_mlp_gate_up(float* out, const int8_t* w1, const float* s1, c
                                 const float* s3, const float* x, size_t n, size_t d,
                                 void* stream);
 
+/* Tensor-core GEMM of the batched paths (prefill, batched decode): no
+ * counterpart in the reference, which runs one token at a time through
+ * matmul (kernels.cpp:21-33).  c = a[m, k] b[n, k]^T with fp16 a and b
+ * (row-major, k contiguous; the weights dequantised from int8), fp32
+ * accumulation on the sm_100a tensor cores (tcgen05).  epilogue 0: c fp32
+ * [m, ldc] = result; 1: c fp32 += result; 2: b rows come in blocks of 256 =
+ * [128 gate rows | 128 up rows] and c is fp16 [m, ldc] with column
+ * 128 block + j = silu(gate_j) * up_j (modules.cpp:99-112).  k must be a
+ * multiple of 64; device pointers 16-byte aligned. */
+TL_API tl_status tl_gemm_f16(void* c, const void* a, const void* b, size_t m, size_t n, size_t k, size_t ldc,
+                             int epilogue, void* stream);
+
 /* quantize (export_mistral.py:53-68): per group of `group` elements
  * scales[g] = fl(fl(1/max|x|) * 127), q = round_half_even(x * scales[g]). */
 TL_API tl_status tl_quantize_i8(int8_t* q, float* scales, const float* x, size_t numel,

@@ -1,0 +1,367 @@
+// tl_gemm.cu -- tcgen05 GEMM (sm_100a): C = A B^T, fp16 operands, fp32
+// accumulation in tensor memory, fused epilogues.
+//
+// One CTA computes a 128 x BN tile of C.  Warp roles (192 threads):
+//   warp 0      TMA producer: 128-row A and BN-row B boxes of 64 K-elements
+//               (128 bytes, SWIZZLE_128B) into a ring of shared-memory stages,
+//               completing on per-stage `full` mbarriers;
+//   warp 1      allocates the BN tensor-memory columns of the accumulator and
+//               issues tcgen05.mma (kind::f16, M 128, N BN, K 16; 4 per stage)
+//               from one thread; tcgen05.commit frees each stage (`empty`) and
+//               finally signals the accumulator (`accum`);
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator rows (warp w reads
+//               tensor-memory lanes 32 (w % 4) ..), fused op, global stores.
+// Every mbarrier wait is bounded by ~2 s of %globaltimer; on expiry the
+// kernel records an error code, stops issuing, lets the work in flight drain
+// (bounded), frees its tensor memory and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include <mutex>
+
+#include "tl_common.cuh"
+#include "tl_gemm.cuh"
+
+namespace tl {
+namespace {
+
+constexpr int kBM = 128, kBK = 64;
+constexpr int kGemmThreads = 192;
+constexpr unsigned long long kGemmTimeoutNs = 2000000000ull;
+
+template <int BN>
+struct GemmCfg {
+    static constexpr int kStages = BN == 256 ? 4 : 6;
+    static constexpr int kABytes = kBM * kBK * 2;
+    static constexpr int kBBytes = BN * kBK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    // 1024-byte alignment slack (SWIZZLE_128B destinations) + stages + barriers
+    static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256;
+};
+
+struct GemmArgs {
+    int M, N, K;
+    void* C;
+    int ldc;
+    int* err;
+};
+
+__device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool bar_test(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity), "r"(10000u)
+        : "memory");
+    return ok != 0;
+}
+// false after ~2 s
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity) {
+    if (bar_test(b, parity)) return true;
+    const unsigned long long t0 = gtime();
+    for (unsigned i = 1;; i++) {
+        if (bar_test(b, parity)) return true;
+        if ((i & 63) == 0 && gtime() - t0 > kGemmTimeoutNs) return false;
+    }
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            su32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(su32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, SWIZZLE_128B (rows of 64
+// fp16 = 128 bytes, 8-row atoms 1024 bytes apart), descriptor version 1.
+__device__ __forceinline__ uint64_t sdesc_k128(uint32_t addr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>(16 >> 4) << 16;    // leading byte offset (unused for this layout)
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;  // stride byte offset: next 8-row atom
+    d |= static_cast<uint64_t>(1) << 46;          // version
+    d |= static_cast<uint64_t>(2) << 61;          // SWIZZLE_128B
+    return d;
+}
+// Instruction descriptor, kind::f16: D fp32, A/B fp16, both K-major, M 128, N.
+template <int BN>
+__host__ __device__ constexpr uint32_t idesc_f16() {
+    return (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, GemmArgs g) {
+    using Cfg = GemmCfg<BN>;
+    constexpr int S = Cfg::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + S * Cfg::kStageBytes);
+    uint64_t* empty = full + S;
+    uint64_t* accum = empty + S;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
+    const int nk = g.K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            bar_init(&full[s], 1);
+            bar_init(&empty[s], 1);
+        }
+        bar_init(accum, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {  // accumulator: BN fp32 columns x 128 lanes
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                     "r"(BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    auto fail = [&](int code) {
+        *abort_flag = 1;
+        if (g.err) atomicCAS(g.err, 0, code);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % S;
+                if (kb >= S && !bar_wait(&empty[s], ((kb / S) - 1) & 1)) {
+                    fail(1);
+                    break;
+                }
+                if (*abort_flag) break;
+                uint8_t* sa = base + s * Cfg::kStageBytes;
+                bar_expect_tx(&full[s], Cfg::kStageBytes);
+                tma_load_2d(sa, &tma_a, kb * kBK, m0, &full[s]);
+                tma_load_2d(sa + Cfg::kABytes, &tma_b, kb * kBK, n0, &full[s]);
+                issued++;
+            }
+            // every copy issued lands before the CTA exits (the consumer may have stopped)
+            for (int kb = (issued > S ? issued - S : 0); kb < issued; kb++) bar_wait(&full[kb % S], (kb / S) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16<BN>();
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % S;
+                if (!bar_wait(&full[s], (kb / S) & 1)) {
+                    fail(2);
+                    break;
+                }
+                if (*abort_flag) break;
+                tc_fence_after();
+                const uint32_t sa = su32(base + s * Cfg::kStageBytes);
+                const uint64_t da = sdesc_k128(sa), db = sdesc_k128(sa + Cfg::kABytes);
+#pragma unroll
+                for (int k = 0; k < kBK / 16; k++)  // K 16 per MMA = 32 bytes along the swizzled row
+                    umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+                umma_commit(&empty[s]);  // stage free once these MMAs have read it
+            }
+            umma_commit(accum);  // all MMAs issued so far complete -> accumulator ready
+        }
+    } else {
+        // epilogue warps 2..5: tensor-memory lanes 32 (warp % 4) + lane = tile rows
+        const int sub = warp & 3;
+        const int row = m0 + sub * 32 + lane;
+        const bool ok = bar_wait(accum, 0);
+        if (!ok) fail(3);
+        tc_fence_after();
+        if (ok && !*abort_flag) {
+            const uint32_t tl = tmem + (static_cast<uint32_t>(sub * 32) << 16);
+            if (EPI == kEpiSwiGluF16) {
+                __half* out = static_cast<__half*>(g.C);
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN / 2; c0 += 32) {
+                    float gv[32], uv[32];
+                    tmem_ld32(tl + c0, gv);
+                    tmem_ld32(tl + BN / 2 + c0, uv);
+                    const int col = n0 / 2 + c0;
+                    if (row < g.M) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 2) {
+                            if (col + j + 1 < g.N / 2 + 1) {
+                                const float a0 = (gv[j] / (1.0f + expf(-gv[j]))) * uv[j];
+                                const float a1 = (gv[j + 1] / (1.0f + expf(-gv[j + 1]))) * uv[j + 1];
+                                *reinterpret_cast<__half2*>(out + static_cast<size_t>(row) * g.ldc + col + j) =
+                                    __floats2half2_rn(a0, a1);
+                            }
+                        }
+                    }
+                }
+            } else {
+                float* out = static_cast<float*>(g.C);
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(tl + c0, v);
+                    if (row < g.M) {
+                        float* dst = out + static_cast<size_t>(row) * g.ldc + n0 + c0;
+                        const int rem = g.N - (n0 + c0);
+                        if (rem >= 32) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4) {
+                                float4 x = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                                if (EPI == kEpiAddF32) {
+                                    const float4 r = *reinterpret_cast<const float4*>(dst + j);
+                                    x.x += r.x; x.y += r.y; x.z += r.z; x.w += r.w;
+                                }
+                                *reinterpret_cast<float4*>(dst + j) = x;
+                            }
+                        } else {
+                            for (int j = 0; j < rem; j++) dst[j] = (EPI == kEpiAddF32) ? dst[j] + v[j] : v[j];
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+    }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point.
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// [rows, K] fp16 row-major, box {64, box_rows}, SWIZZLE_128B, zero fill outside.
+tl_status encode_kmajor(CUtensorMap* map, const __half* ptr, int rows, int K, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return set_error(TL_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(ptr), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(TL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return TL_OK;
+}
+
+template <int BN, int EPI>
+tl_status launch_gemm(const __half* A, int M, int K, const __half* B, int N, void* C, int ldc, int* err,
+                      cudaStream_t s) {
+    CUtensorMap ta, tb;
+    TL_TRY(encode_kmajor(&ta, A, M, K, kBM));
+    TL_TRY(encode_kmajor(&tb, B, N, K, BN));
+    auto kern = gemm_tc_kernel<BN, EPI>;
+    static std::once_flag once;  // per instantiation
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [&] {
+        attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(GemmCfg<BN>::kSmem));
+    });
+    if (attr_err != cudaSuccess)
+        return set_error(TL_ERR_CUDA, "gemm smem attribute: %s", cudaGetErrorString(attr_err));
+    const dim3 grid((N + BN - 1) / BN, (M + kBM - 1) / kBM);
+    GemmArgs g{M, N, K, C, ldc, err};
+    kern<<<grid, kGemmThreads, GemmCfg<BN>::kSmem, s>>>(ta, tb, g);
+    return check_launch("gemm_tc");
+}
+
+}  // namespace
+
+tl_status gemm_f16(int epi, const __half* A, int M, int K, const __half* B, int N, void* C, int ldc, int* err,
+                   cudaStream_t s) {
+    TL_REQUIRE(A && B && C && M > 0 && N > 0 && K > 0, "gemm: bad arguments");
+    TL_REQUIRE(K % kBK == 0, "gemm: K = %d must be a multiple of %d", K, kBK);
+    TL_REQUIRE(((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) &
+                15) == 0,
+               "gemm: operands must be 16-byte aligned");
+    switch (epi) {
+        case kEpiStoreF32:
+            TL_REQUIRE(ldc >= N && ldc % 4 == 0, "gemm: ldc");
+            return launch_gemm<256, kEpiStoreF32>(A, M, K, B, N, C, ldc, err, s);
+        case kEpiAddF32:
+            TL_REQUIRE(ldc >= N && ldc % 4 == 0, "gemm: ldc");
+            return launch_gemm<256, kEpiAddF32>(A, M, K, B, N, C, ldc, err, s);
+        case kEpiSwiGluF16:
+            TL_REQUIRE(N % 256 == 0 && ldc >= N / 2 && ldc % 2 == 0, "gemm swiglu: N %% 256, ldc");
+            return launch_gemm<256, kEpiSwiGluF16>(A, M, K, B, N, C, ldc, err, s);
+        default:
+            return set_error(TL_ERR_INVALID_ARGUMENT, "gemm: unknown epilogue %d", epi);
+    }
+}
+
+}  // namespace tl
+
+using namespace tl;
+
+extern "C" {
+
+tl_status tl_gemm_f16(void* c, const void* a, const void* b, size_t m, size_t n, size_t k, size_t ldc, int epilogue,
+                      void* stream) {
+    clear_error();
+    TL_REQUIRE(m < (1u << 30) && n < (1u << 30) && k < (1u << 30) && ldc < (1u << 30), "tl_gemm_f16: sizes");
+    return gemm_f16(epilogue, static_cast<const __half*>(a), static_cast<int>(m), static_cast<int>(k),
+                    static_cast<const __half*>(b), static_cast<int>(n), c, static_cast<int>(ldc), nullptr,
+                    as_stream(stream));
+}
+
+}  // extern "C"

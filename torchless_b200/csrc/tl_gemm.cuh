@@ -1,0 +1,27 @@
+// tl_gemm.cuh -- tcgen05 tensor-core GEMM for the batched paths (prefill,
+// batched decode): C[M, N] = A[M, K] B[N, K]^T, A and B fp16 row-major
+// (both K-contiguous), fp32 accumulation in tensor memory (tl_gemm.cu).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "torchless_b200.h"
+
+namespace tl {
+
+enum GemmEpilogue : int {
+    kEpiStoreF32 = 0,  // C (fp32, row stride ldc) = A B^T
+    kEpiAddF32 = 1,    // C += A B^T (residual add, modules.cpp:128, 142)
+    kEpiSwiGluF16 = 2, // B rows in blocks of 256 = [128 gate rows | 128 up rows]; C (fp16, row stride
+                       // ldc) column n0 / 2 + j = silu(gate_j) * up_j (modules.cpp:99-112)
+};
+
+// Shapes: K % 64 == 0, A / B / C 16-byte aligned; any M, N (tails masked).
+// `err` (device int, may be null) receives a nonzero code if a bounded
+// device-side wait gave up.
+tl_status gemm_f16(int epilogue, const __half* A, int M, int K, const __half* B, int N, void* C, int ldc, int* err,
+                   cudaStream_t s);
+
+}  // namespace tl
