@@ -193,6 +193,18 @@ TL_API tl_status tl_model_config(const tl_model* m, tl_config* out);
  * (host; sample_max of the logits, main.cpp:10-21) are optional outputs. */
 TL_API tl_status tl_model_forward(tl_model* m, uint32_t token, float* logits, uint32_t* next_token);
 
+/* The prompt loop of main.cpp:69-71 (Model<T>::forward once per token) as
+ * one batched pass over tokens[0..n) at positions pos .. pos + n - 1: every
+ * layer runs as tensor-core GEMMs over all n rows (fp16 weights dequantised
+ * from int8 once, fp32 accumulation) with causal attention over the KV cache,
+ * which receives the n new positions exactly as n forwards would write them.
+ * logits (host, may be NULL) / *next_token (may be NULL) are those of the
+ * last token (sample_max, main.cpp:10-21); pos advances by n and decoding
+ * continues with tl_model_forward.  The first call allocates the fp16
+ * weights (2 bytes per parameter).  Not available under tensor parallelism. */
+TL_API tl_status tl_model_prefill(tl_model* m, const uint32_t* tokens, size_t n, float* logits,
+                                  uint32_t* next_token);
+
 /* The greedy loop of main.cpp:69-77 on the device: forwards prompt[0..n_prompt-1]
  * then n_new times forwards the last argmax; writes the n_new generated ids
  * to out (host).  Only the ids cross the PCIe bus. */

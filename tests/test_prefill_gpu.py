@@ -1,0 +1,113 @@
+"""Batched prompt pass (tl_model_prefill) through the C ABI.
+
+The reference forwards a prompt one token at a time (main.cpp:69-71); the
+prefill runs the same tokens as one pass of tensor-core GEMMs (fp16 operands
+dequantised from int8, fp32 accumulation).  Checks:
+  * the last prompt token's logits against the reference's own logits
+    (parity rule: max rel err <= 1e-2; greedy token identical unless the
+    reference's top-2 margin is a near-tie, < 1e-3 max|logit|), then decoding
+    continues token by token and keeps matching the reference;
+  * the KV cache rows the prefill wrote against the oracle's;
+  * at Mistral-7B shapes, against token-by-token decoding of the same
+    prompt, in one pass and in two chunks (p0 > 0).
+"""
+import numpy as np
+import pytest
+
+from conftest import golden_greedy, rel_err
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+TOL = 1e-2
+TIE = 1e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+
+
+def margin(logits):
+    top = np.sort(logits)[-2:]
+    return float(top[1] - top[0]) / max(float(np.max(np.abs(logits))), 1e-30)
+
+
+@pytest.mark.parametrize("name", ["tiny", "small"])
+def test_prefill_then_decode_matches_reference(name, request):
+    import oracle
+    from torchless_b200 import Model
+    from torchless_b200.binfmt import ModelFile
+    buf = request.getfixturevalue(f"{name}_bin")
+    prompt, ids, ref_logits = golden_greedy(name)
+    m = Model.from_buffer(buf, max_seq=64)
+    lg, nxt = m.prefill(prompt)
+    assert m.pos == len(prompt)
+    worst = rel_err(lg, ref_logits[0])
+    assert worst <= TOL
+    assert nxt == ids[0] or margin(ref_logits[0]) < TIE
+    # KV rows written by the prefill against the oracle's sequential pass
+    om = oracle.OracleModel(ModelFile(buf), max_seq=64)
+    for t in prompt:
+        om.forward(t)
+    kv_worst = 0.0
+    for layer in range(m.config["n_layers"]):
+        for pos in range(len(prompt)):
+            k, v = m.read_kv(layer, pos)
+            ko, vo = om.read_kv(layer, pos)
+            kv_worst = max(kv_worst, rel_err(k, ko), rel_err(v, vo))
+    assert kv_worst <= TOL
+    # decoding continues from the prefilled cache (teacher-forced on the reference's ids)
+    for step in range(1, len(ids)):
+        lg, nxt = m.forward(ids[step - 1])
+        e = rel_err(lg, ref_logits[step])
+        worst = max(worst, e)
+        assert e <= TOL, (step, e)
+        if nxt != ids[step]:
+            assert margin(ref_logits[step]) < TIE, step
+    print(f"{name}: prefill+decode worst logits rel err {worst:.2e}, KV {kv_worst:.2e}")
+    m.close()
+
+
+@pytest.fixture(scope="module")
+def m7b_two_layers():
+    from torchless_b200 import ops, synthetic as S
+    cfg = dict(S.MISTRAL_7B, num_hidden_layers=2)
+    return S.make_torch_model(cfg, seed=13, norm="random", device="cuda",
+                              quantizer=lambda x: ops.quantize_i8(x)).buf
+
+
+def test_prefill_matches_token_by_token_7b_shapes(m7b_two_layers):
+    from torchless_b200 import Model
+    rng = np.random.default_rng(4)
+    prompt = rng.integers(0, 32000, 150).tolist()
+    seq = Model.from_buffer(m7b_two_layers, max_seq=256)
+    for t in prompt[:-1]:
+        seq.forward(t, logits=False)
+    ref, ref_tok = seq.forward(prompt[-1])
+    one = Model.from_buffer(m7b_two_layers, max_seq=256)
+    lg, tok = one.prefill(prompt)
+    e = rel_err(lg, ref)
+    assert e <= TOL, e
+    assert tok == ref_tok or margin(ref) < TIE
+    # two chunks: the second attends over the first's cache rows (p0 > 0)
+    two = Model.from_buffer(m7b_two_layers, max_seq=256)
+    two.prefill(prompt[:61], logits=False)
+    lg2, tok2 = two.prefill(prompt[61:])
+    e2 = rel_err(lg2, ref)
+    assert e2 <= TOL, e2
+    kv = 0.0
+    for layer in (0, 1):
+        for pos in (0, 60, 61, 149):
+            k, v = one.read_kv(layer, pos)
+            k2, v2 = two.read_kv(layer, pos)
+            ks, vs = seq.read_kv(layer, pos)
+            kv = max(kv, rel_err(k, ks), rel_err(v, vs), rel_err(k2, ks), rel_err(v2, vs))
+    assert kv <= TOL, kv
+    # decoding after the prefill agrees with decoding after the sequential pass
+    for t in rng.integers(0, 32000, 4).tolist():
+        a, _ = seq.forward(t)
+        b, _ = one.forward(t)
+        assert rel_err(b, a) <= TOL
+    print(f"7b-shapes prefill: logits rel err {e:.2e} (chunked {e2:.2e}), KV {kv:.2e}")
+    for mm in (seq, one, two):
+        mm.close()

@@ -30,6 +30,7 @@
 #include <cerrno>
 #include <cmath>
 #include <cstdio>
+#include <array>
 #include <cstring>
 #include <functional>
 #include <map>
@@ -39,6 +40,8 @@
 
 #include "tl_common.cuh"
 #include "tl_decode.cuh"
+#include "tl_gemm.cuh"
+#include "tl_prefill.cuh"
 #include "tl_gemv.cuh"
 #include "tl_json.h"
 #include "tl_kernels.h"
@@ -249,6 +252,14 @@ struct tl_model {
     uint8_t* xpeer_open[kMaxTp] = {};  // peer buffers opened with cudaIpcOpenMemHandle
     bool connected = false;
     bool broken = false;  // tp: a device-side wait gave up; the ranks' exchange state is lost
+    // batched prompt pass (tl_model_prefill): fp16 weights dequantised on first
+    // use (per layer q|k|v, o, gate|up in SwiGLU blocks, down) and row buffers
+    DeviceArena w16, rows;
+    std::vector<std::array<__half*, 4>> lw16;
+    size_t rows_cap = 0;
+    float *p_h = nullptr, *p_qkv = nullptr;
+    __half *p_x16 = nullptr, *p_q16 = nullptr, *p_ctx16 = nullptr, *p_act16 = nullptr;
+    uint32_t* p_tok = nullptr;
     double bytes_per_step = 0;
 };
 
@@ -754,6 +765,51 @@ tl_status check_capacity(const tl_model* m, size_t steps) {
     return TL_OK;
 }
 
+// fp16 weights and row buffers of the batched prompt pass (first use / growth).
+tl_status ensure_prefill(tl_model* m, size_t n) {
+    const int64_t D = m->cfg.hidden_size, HD = m->cfg.head_dim, H = m->lH, KV = m->lKV, F = m->lF;
+    const int64_t NQKV = (H + 2 * KV) * HD, L = m->cfg.n_layers;
+    if (m->lw16.empty()) {
+        if (F % 128) return set_error(TL_ERR_UNSUPPORTED, "prefill: intermediate_size %lld not a multiple of 128",
+                                      static_cast<long long>(F));
+        using A = DeviceArena;
+        const size_t per = A::pad(NQKV * D * 2) + A::pad(D * H * HD * 2) + A::pad(2 * F * D * 2) + A::pad(D * F * 2);
+        TL_TRY(m->w16.reserve(per * L));
+        m->lw16.resize(L);
+        for (int64_t l = 0; l < L; l++) {
+            const LayerW& w = m->layers[l];
+            auto& W = m->lw16[l];
+            W[0] = m->w16.take<__half>(NQKV * D);
+            W[1] = m->w16.take<__half>(D * H * HD);
+            W[2] = m->w16.take<__half>(2 * F * D);
+            W[3] = m->w16.take<__half>(D * F);
+            // the arena's scales are already 1/s
+            TL_TRY(dequant_f16(W[0], w.wqkv, w.sqkv, nullptr, nullptr, NQKV, D, false, m->stream));
+            TL_TRY(dequant_f16(W[1], w.wo, w.so, nullptr, nullptr, D, H * HD, false, m->stream));
+            TL_TRY(dequant_f16(W[2], w.w1, w.s1, w.w3, w.s3, F, D, true, m->stream));
+            TL_TRY(dequant_f16(W[3], w.w2, w.s2, nullptr, nullptr, D, F, false, m->stream));
+        }
+    }
+    if (n > m->rows_cap) {
+        m->rows.release();
+        m->rows = DeviceArena();
+        const size_t cap = std::max<size_t>(n, 64);
+        using A = DeviceArena;
+        TL_TRY(m->rows.reserve(A::pad(cap * D * 4) + A::pad(cap * NQKV * 4) + A::pad(cap * D * 2) +
+                               2 * A::pad(cap * H * HD * 2) + A::pad(cap * F * 2) + A::pad(cap * 4)));
+        m->p_h = m->rows.take<float>(cap * D);
+        m->p_qkv = m->rows.take<float>(cap * NQKV);
+        m->p_x16 = m->rows.take<__half>(cap * D);
+        m->p_q16 = m->rows.take<__half>(cap * H * HD);
+        m->p_ctx16 = m->rows.take<__half>(cap * H * HD);
+        m->p_act16 = m->rows.take<__half>(cap * F);
+        m->p_tok = m->rows.take<uint32_t>(cap);
+        if (!m->p_tok) return set_error(TL_ERR_OUT_OF_MEMORY, "prefill row arena (internal)");
+        m->rows_cap = cap;
+    }
+    return TL_OK;
+}
+
 tl_status sync(tl_model* m) {
     if (m->persistent) {
         cudaError_t e = cudaMemcpyAsync(m->h_pinned + 3, m->err, 4, cudaMemcpyDeviceToHost, m->stream);
@@ -834,6 +890,8 @@ tl_status tl_model_destroy(tl_model* m) {
     m->weights.release();
     m->state.release();
     m->tiles.release();
+    m->w16.release();
+    m->rows.release();
     if (m->d_layers) cudaFree(m->d_layers);
     if (m->h_pinned) cudaFreeHost(m->h_pinned);
     for (int q = 0; q < kMaxTp; q++)
@@ -910,6 +968,57 @@ tl_status tl_model_forward(tl_model* m, uint32_t token, float* logits, uint32_t*
         TL_CUDA_TRY(cudaMemcpyAsync(m->h_pinned + 1, m->d_token, 4, cudaMemcpyDeviceToHost, m->stream));
     TL_TRY(sync(m));
     m->pos++;
+    if (next_token) *next_token = m->h_pinned[1];
+    return TL_OK;
+}
+
+tl_status tl_model_prefill(tl_model* m, const uint32_t* tokens, size_t n, float* logits, uint32_t* next_token) {
+    clear_error();
+    TL_REQUIRE(m && tokens && n > 0, "tl_model_prefill: bad arguments");
+    if (m->tp > 1) return set_error(TL_ERR_UNSUPPORTED, "tl_model_prefill: not available under tensor parallelism");
+    TL_REQUIRE(n < (1u << 30), "tl_model_prefill: n too large");
+    for (size_t i = 0; i < n; i++)
+        TL_REQUIRE(tokens[i] < m->cfg.vocab_size, "token %u >= vocab_size %zu", tokens[i], m->cfg.vocab_size);
+    TL_TRY(check_capacity(m, n));
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    TL_TRY(ensure_prefill(m, n));
+    const int M = static_cast<int>(n), p0 = static_cast<int>(m->pos);
+    const int D = static_cast<int>(m->cfg.hidden_size), HD = static_cast<int>(m->cfg.head_dim);
+    const int H = static_cast<int>(m->lH), KV = static_cast<int>(m->lKV), F = static_cast<int>(m->lF);
+    const int NQKV = (H + 2 * KV) * HD, V = static_cast<int>(m->lV);
+    const int ms = static_cast<int>(m->max_seq);
+    const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));  // modules.cpp:79-80
+    cudaStream_t s = m->stream;
+    TL_CUDA_TRY(cudaMemcpyAsync(m->p_tok, tokens, n * 4, cudaMemcpyHostToDevice, s));
+    TL_TRY(embed_rows(m->p_h, m->embed, m->p_tok, M, D, s));
+    for (size_t l = 0; l < m->cfg.n_layers; l++) {
+        const LayerW& w = m->layers[l];
+        const auto& W = m->lw16[l];
+        float* kc = m->kc + l * layer_kv_floats(m);
+        float* vc = m->vc + l * layer_kv_floats(m);
+        TL_TRY(rmsnorm_rows_f16(m->p_x16, m->p_h, w.g_in, M, D, s));
+        TL_TRY(gemm_f16(kEpiStoreF32, m->p_x16, M, D, W[0], NQKV, m->p_qkv, NQKV, m->err, s));
+        TL_TRY(rope_cache_rows(m->p_q16, m->p_qkv, kc, vc, m->cos_tab, m->sin_tab, M, p0, H, KV, HD, ms, s));
+        TL_TRY(attention_prefill(m->p_ctx16, m->p_q16, kc, vc, M, p0, H, KV, HD, ms, scale, s));
+        TL_TRY(gemm_f16(kEpiAddF32, m->p_ctx16, M, H * HD, W[1], D, m->p_h, D, m->err, s));
+        TL_TRY(rmsnorm_rows_f16(m->p_x16, m->p_h, w.g_post, M, D, s));
+        TL_TRY(gemm_f16(kEpiSwiGluF16, m->p_x16, M, D, W[2], 2 * F, m->p_act16, F, m->err, s));
+        TL_TRY(gemm_f16(kEpiAddF32, m->p_act16, M, F, W[3], D, m->p_h, D, m->err, s));
+    }
+    // the last token's hidden state: final norm, lm_head, sample_max (modules.cpp:147-171, main.cpp:10-21)
+    TL_CUDA_TRY(cudaMemcpyAsync(m->h, m->p_h + static_cast<size_t>(M - 1) * D, D * 4, cudaMemcpyDeviceToDevice, s));
+    m->h_pinned[2] = static_cast<uint32_t>(p0 + M - 1);
+    TL_CUDA_TRY(cudaMemcpyAsync(m->d_pos, m->h_pinned + 2, 4, cudaMemcpyHostToDevice, s));
+    GemvF32Args a = {};
+    a.w = m->lm_head; a.x = m->h; a.g = m->norm; a.eps = 1e-5f; a.y = m->logits;
+    a.n = V; a.d = D;
+    a.part_v = m->am_v; a.part_i = m->am_i; a.counter = m->am_cnt;
+    a.out_token = m->d_token; a.history = m->d_hist; a.pos = m->d_pos;
+    TL_TRY(launch_gemv_f32(a, true, true, s, false));
+    if (logits) TL_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, static_cast<size_t>(V) * 4, cudaMemcpyDeviceToHost, s));
+    TL_CUDA_TRY(cudaMemcpyAsync(m->h_pinned + 1, m->d_token, 4, cudaMemcpyDeviceToHost, s));
+    TL_TRY(sync(m));
+    m->pos = p0 + n;
     if (next_token) *next_token = m->h_pinned[1];
     return TL_OK;
 }

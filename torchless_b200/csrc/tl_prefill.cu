@@ -1,0 +1,287 @@
+// tl_prefill.cu -- row-wise kernels and causal attention of the batched
+// prompt pass (interface and data flow in tl_prefill.cuh).
+#include <math.h>
+
+#include <algorithm>
+
+#include "tl_common.cuh"
+#include "tl_prefill.cuh"
+
+namespace tl {
+namespace {
+
+__global__ void k_dequant_f16(__half* w16, const int8_t* q1, const float* inv1, const int8_t* q3, const float* inv3,
+                              int n, int d, int swiglu) {
+    const size_t rows = swiglu ? 2 * static_cast<size_t>(n) : n;
+    const size_t chunks = rows * (d / 8);
+    for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < chunks; idx += (size_t)gridDim.x * blockDim.x) {
+        const size_t R = idx / (d / 8);
+        const int c = static_cast<int>(idx % (d / 8)) * 8;
+        const int8_t* q = q1;
+        const float* inv = inv1;
+        size_t r = R;
+        if (swiglu) {  // block of 256 output rows = 128 gate rows, then the same 128 up rows
+            const size_t b = R / 256, w = R % 256;
+            if (w < 128) {
+                r = b * 128 + w;
+            } else {
+                r = b * 128 + (w - 128);
+                q = q3;
+                inv = inv3;
+            }
+        }
+        const int2 raw = *reinterpret_cast<const int2*>(q + r * d + c);
+        const float s = inv[(r * d + c) / 64];
+        const int8_t* b8 = reinterpret_cast<const int8_t*>(&raw);
+        __half2 out[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            out[j] = __floats2half2_rn(static_cast<float>(b8[2 * j]) * s, static_cast<float>(b8[2 * j + 1]) * s);
+        *reinterpret_cast<uint4*>(w16 + R * d + c) = *reinterpret_cast<const uint4*>(out);
+    }
+}
+
+__global__ void k_embed_rows(float* h, const float* embed, const uint32_t* tokens, int M, int D) {
+    const size_t n4 = static_cast<size_t>(M) * D / 4;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t row = i / (D / 4), c = i % (D / 4);
+        reinterpret_cast<float4*>(h)[i] = reinterpret_cast<const float4*>(embed + static_cast<size_t>(tokens[row]) * D)[c];
+    }
+}
+
+__global__ void k_rmsnorm_rows_f16(__half* x16, const float* h, const float* g, int D) {
+    __shared__ float red[32];
+    const float* x = h + static_cast<size_t>(blockIdx.x) * D;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) ss += x[i] * x[i];
+    ss = block_sum(ss, red);
+    const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + 1e-5f);
+    __half* y = x16 + static_cast<size_t>(blockIdx.x) * D;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) y[i] = __float2half_rn((x[i] * inv) * g[i]);
+}
+
+__global__ void k_rope_cache_rows(__half* q16, const float* qkv, float* kc, float* vc, const float* cos_tab,
+                                  const float* sin_tab, int p0, int H, int KV, int HD, int max_seq) {
+    const int i = blockIdx.x, pos = p0 + i, half = HD / 2;
+    const float* row = qkv + static_cast<size_t>(i) * (H + 2 * KV) * HD;
+    const float* ct = cos_tab + static_cast<size_t>(pos) * half;
+    const float* st = sin_tab + static_cast<size_t>(pos) * half;
+    for (int k = threadIdx.x; k < (H + KV) * half; k += blockDim.x) {
+        const int hh = k / half, c = k % half;
+        const float x = row[hh * HD + c], y = row[hh * HD + c + half];
+        const float cc = ct[c], sn = st[c];
+        const float xr = x * cc - y * sn, yr = x * sn + y * cc;
+        if (hh < H) {
+            __half* q = q16 + static_cast<size_t>(i) * H * HD + hh * HD;
+            q[c] = __float2half_rn(xr);
+            q[c + half] = __float2half_rn(yr);
+        } else {
+            float* k = kc + (static_cast<size_t>(hh - H) * max_seq + pos) * HD;
+            k[c] = xr;
+            k[c + half] = yr;
+        }
+    }
+    for (int k = threadIdx.x; k < KV * HD; k += blockDim.x) {
+        const int kh = k / HD, c = k % HD;
+        vc[(static_cast<size_t>(kh) * max_seq + pos) * HD + c] = row[(H + KV) * HD + k];
+    }
+}
+
+// mma.m16n8k16 f16 x f16 -> f32 (A row-major 16x16, B col-major 16x8).
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Flash attention, one CTA per (64 queries, head), 4 warps x 16 query rows.
+// K block [64 keys][HD] and V block transposed [HD][64 keys] staged as fp16.
+constexpr int kAQ = 64, kAK = 64;
+template <int HD>
+__global__ void __launch_bounds__(128) k_attention_prefill(__half* ctx16, const __half* q16, const float* kc,
+                                                           const float* vc, int M, int p0, int H, int max_seq,
+                                                           float scale) {
+    constexpr int KP = HD + 8, VP = kAK + 8;  // padded rows (halves)
+    __shared__ __align__(16) __half Ks[kAK * KP];
+    __shared__ __align__(16) __half Vt[HD * VP];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int h = blockIdx.y, kh = h / 4;  // kv head h / 4 (modules.cpp:70)
+    const int q0 = blockIdx.x * kAQ, qend = min(M, q0 + kAQ);
+    const int r0 = q0 + warp * 16;  // this warp's first query row
+    const float* kbase = kc + static_cast<size_t>(kh) * max_seq * HD;
+    const float* vbase = vc + static_cast<size_t>(kh) * max_seq * HD;
+
+    // Q fragments (A operand) for the HD / 16 k-steps
+    uint32_t qa[HD / 16][4];
+    {
+        const int ra = r0 + g, rb = r0 + g + 8;
+        const __half* qa_row = q16 + (static_cast<size_t>(ra) * H + h) * HD;
+        const __half* qb_row = q16 + (static_cast<size_t>(rb) * H + h) * HD;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ks++) {
+            const int c = ks * 16 + 2 * t;
+            qa[ks][0] = ra < M ? *reinterpret_cast<const uint32_t*>(qa_row + c) : 0u;
+            qa[ks][1] = rb < M ? *reinterpret_cast<const uint32_t*>(qb_row + c) : 0u;
+            qa[ks][2] = ra < M ? *reinterpret_cast<const uint32_t*>(qa_row + c + 8) : 0u;
+            qa[ks][3] = rb < M ? *reinterpret_cast<const uint32_t*>(qb_row + c + 8) : 0u;
+        }
+    }
+    float o[HD / 8][4];
+#pragma unroll
+    for (int j = 0; j < HD / 8; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;  // rows g and g + 8
+    const int pos_a = p0 + r0 + g, pos_b = pos_a + 8;
+    const bool row_a = (r0 + g) < M, row_b = (r0 + g + 8) < M;
+    const int kmax = p0 + qend;  // keys [0, kmax) exist for this CTA
+    const int nkb = (kmax + kAK - 1) / kAK;
+
+    for (int kb = 0; kb < nkb; kb++) {
+        const int k0 = kb * kAK;
+        __syncthreads();
+        // stage K (row-major) and V (transposed) as fp16; keys >= kmax are zero
+        for (int e = threadIdx.x; e < kAK * HD / 4; e += blockDim.x) {
+            const int key = e / (HD / 4), c = (e % (HD / 4)) * 4;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (k0 + key < kmax) {
+                kv = *reinterpret_cast<const float4*>(kbase + static_cast<size_t>(k0 + key) * HD + c);
+                vv = *reinterpret_cast<const float4*>(vbase + static_cast<size_t>(k0 + key) * HD + c);
+            }
+            *reinterpret_cast<uint32_t*>(&Ks[key * KP + c]) = pack_h2(kv.x, kv.y);
+            *reinterpret_cast<uint32_t*>(&Ks[key * KP + c + 2]) = pack_h2(kv.z, kv.w);
+            Vt[(c + 0) * VP + key] = __float2half_rn(vv.x);
+            Vt[(c + 1) * VP + key] = __float2half_rn(vv.y);
+            Vt[(c + 2) * VP + key] = __float2half_rn(vv.z);
+            Vt[(c + 3) * VP + key] = __float2half_rn(vv.w);
+        }
+        __syncthreads();
+        // S = Q K^T (16 x 64 per warp)
+        float s[kAK / 8][4];
+#pragma unroll
+        for (int j = 0; j < kAK / 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ks++) {
+#pragma unroll
+            for (int j = 0; j < kAK / 8; j++) {
+                const __half* kr = &Ks[(j * 8 + g) * KP + ks * 16 + 2 * t];
+                mma_f16(s[j], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], *reinterpret_cast<const uint32_t*>(kr),
+                        *reinterpret_cast<const uint32_t*>(kr + 8));
+            }
+        }
+        // scale, causal mask (key position <= query position), row max over the quad
+        float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kAK / 8; j++) {
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int key = k0 + j * 8 + 2 * t + e;
+                s[j][e] = (row_a && key <= pos_a) ? s[j][e] * scale : -INFINITY;
+                s[j][2 + e] = (row_b && key <= pos_b) ? s[j][2 + e] * scale : -INFINITY;
+                mx_a = fmaxf(mx_a, s[j][e]);
+                mx_b = fmaxf(mx_b, s[j][2 + e]);
+            }
+        }
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(FULL, mx_a, 1));
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(FULL, mx_a, 2));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(FULL, mx_b, 1));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(FULL, mx_b, 2));
+        const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+        const float c_a = (mn_a == -INFINITY) ? 1.f : expf(m_a - mn_a);
+        const float c_b = (mn_b == -INFINITY) ? 1.f : expf(m_b - mn_b);
+        m_a = mn_a;
+        m_b = mn_b;
+        l_a *= c_a;
+        l_b *= c_b;
+#pragma unroll
+        for (int j = 0; j < HD / 8; j++) {
+            o[j][0] *= c_a;
+            o[j][1] *= c_a;
+            o[j][2] *= c_b;
+            o[j][3] *= c_b;
+        }
+        // P = exp(S - m) as fp16 A fragments; O += P V
+#pragma unroll
+        for (int kk = 0; kk < kAK / 16; kk++) {
+            float p[2][4];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int j = 2 * kk + u;
+                p[u][0] = (s[j][0] == -INFINITY) ? 0.f : expf(s[j][0] - mn_a);
+                p[u][1] = (s[j][1] == -INFINITY) ? 0.f : expf(s[j][1] - mn_a);
+                p[u][2] = (s[j][2] == -INFINITY) ? 0.f : expf(s[j][2] - mn_b);
+                p[u][3] = (s[j][3] == -INFINITY) ? 0.f : expf(s[j][3] - mn_b);
+                l_a += p[u][0] + p[u][1];
+                l_b += p[u][2] + p[u][3];
+            }
+            const uint32_t a0 = pack_h2(p[0][0], p[0][1]), a1 = pack_h2(p[0][2], p[0][3]);
+            const uint32_t a2 = pack_h2(p[1][0], p[1][1]), a3 = pack_h2(p[1][2], p[1][3]);
+#pragma unroll
+            for (int j = 0; j < HD / 8; j++) {
+                const __half* vr = &Vt[(j * 8 + g) * VP + kk * 16 + 2 * t];
+                mma_f16(o[j], a0, a1, a2, a3, *reinterpret_cast<const uint32_t*>(vr),
+                        *reinterpret_cast<const uint32_t*>(vr + 8));
+            }
+        }
+    }
+    // row sums over the quad, normalise, store fp16 ctx
+    l_a += __shfl_xor_sync(FULL, l_a, 1);
+    l_a += __shfl_xor_sync(FULL, l_a, 2);
+    l_b += __shfl_xor_sync(FULL, l_b, 1);
+    l_b += __shfl_xor_sync(FULL, l_b, 2);
+    const float ia = l_a > 0.f ? 1.0f / l_a : 0.f, ib = l_b > 0.f ? 1.0f / l_b : 0.f;
+    __half* ya = ctx16 + (static_cast<size_t>(r0 + g) * H + h) * HD;
+    __half* yb = ctx16 + (static_cast<size_t>(r0 + g + 8) * H + h) * HD;
+#pragma unroll
+    for (int j = 0; j < HD / 8; j++) {
+        const int c = j * 8 + 2 * t;
+        if (row_a) *reinterpret_cast<uint32_t*>(ya + c) = pack_h2(o[j][0] * ia, o[j][1] * ia);
+        if (row_b) *reinterpret_cast<uint32_t*>(yb + c) = pack_h2(o[j][2] * ib, o[j][3] * ib);
+    }
+}
+
+int grid_for(size_t n, int per) { return static_cast<int>(std::min<size_t>((n + per - 1) / per, 148 * 16)); }
+
+}  // namespace
+
+tl_status dequant_f16(__half* w16, const int8_t* q1, const float* inv1, const int8_t* q3, const float* inv3, int n,
+                      int d, bool swiglu, cudaStream_t s) {
+    TL_REQUIRE(d % 64 == 0 && (!swiglu || n % 128 == 0), "dequant_f16: shape");
+    const size_t chunks = (swiglu ? 2 * static_cast<size_t>(n) : n) * (d / 8);
+    k_dequant_f16<<<grid_for(chunks, 256), 256, 0, s>>>(w16, q1, inv1, q3, inv3, n, d, swiglu ? 1 : 0);
+    return check_launch("dequant_f16");
+}
+
+tl_status embed_rows(float* h, const float* embed, const uint32_t* tokens, int M, int D, cudaStream_t s) {
+    k_embed_rows<<<grid_for(static_cast<size_t>(M) * D / 4, 256), 256, 0, s>>>(h, embed, tokens, M, D);
+    return check_launch("embed_rows");
+}
+
+tl_status rmsnorm_rows_f16(__half* x16, const float* h, const float* g, int M, int D, cudaStream_t s) {
+    k_rmsnorm_rows_f16<<<M, 256, 0, s>>>(x16, h, g, D);
+    return check_launch("rmsnorm_rows_f16");
+}
+
+tl_status rope_cache_rows(__half* q16, const float* qkv, float* k_cache, float* v_cache, const float* cos_tab,
+                          const float* sin_tab, int M, int p0, int H, int KV, int HD, int max_seq, cudaStream_t s) {
+    k_rope_cache_rows<<<M, 128, 0, s>>>(q16, qkv, k_cache, v_cache, cos_tab, sin_tab, p0, H, KV, HD, max_seq);
+    return check_launch("rope_cache_rows");
+}
+
+tl_status attention_prefill(__half* ctx16, const __half* q16, const float* k_cache, const float* v_cache, int M,
+                            int p0, int H, int KV, int HD, int max_seq, float scale, cudaStream_t s) {
+    TL_REQUIRE(H == 4 * KV, "attention_prefill: kv head h / 4 needs H == 4 KV");
+    const dim3 grid((M + kAQ - 1) / kAQ, H);
+    switch (HD) {
+        case 64: k_attention_prefill<64><<<grid, 128, 0, s>>>(ctx16, q16, k_cache, v_cache, M, p0, H, max_seq, scale); break;
+        case 128: k_attention_prefill<128><<<grid, 128, 0, s>>>(ctx16, q16, k_cache, v_cache, M, p0, H, max_seq, scale); break;
+        default: return set_error(TL_ERR_UNSUPPORTED, "attention_prefill: head_dim %d", HD);
+    }
+    return check_launch("attention_prefill");
+}
+
+}  // namespace tl

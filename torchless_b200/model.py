@@ -110,6 +110,16 @@ class Model:
                                      ctypes.byref(nxt)))
         return out, nxt.value
 
+    def prefill(self, tokens: Sequence[int], logits: bool = True):
+        """All of `tokens` in one batched pass at the current position (the
+        prompt loop of main.cpp:69-71); returns (last token's logits or None, argmax)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.empty(self.config["vocab_size"] // self.tp_size, dtype=np.float32) if logits else None
+        nxt = ctypes.c_uint32()
+        check(lib().tl_model_prefill(self._h, t.ctypes.data, t.size, out.ctypes.data if logits else None,
+                                     ctypes.byref(nxt)))
+        return out, nxt.value
+
     def generate(self, prompt: Sequence[int], n_new: int) -> List[int]:
         """main.cpp:69-77 on the device: returns the n_new greedy ids."""
         p = np.ascontiguousarray(prompt, dtype=np.uint32)
