@@ -414,6 +414,53 @@ def cpu_gemv_sample(w, sc, x, mats, rows=256):
                       f"{reps} repetitions"}
 
 
+# ---------------------------------------------------------------------------
+# Prefill: Mistral-7B, 2048-token random prompt in one batched pass (tensor
+# cores), then 32 greedy decode steps from the filled KV cache.
+# ---------------------------------------------------------------------------
+def run_prefill(args):
+    import torch
+    from torchless_b200 import Model
+    torch.cuda.set_device(0)
+    T, N_DEC = args.prefill_tokens, 32
+    buf = make_model_bytes("cuda:0", args.layers)
+    m = Model.from_buffer(buf, max_seq=T + N_DEC + 8)
+    rng = np.random.default_rng(SEED)
+    prompt = rng.integers(0, 32000, T).tolist()
+    times = []
+    for i in range(args.warmup + args.steps):  # each step: the whole prompt from position 0
+        m.pos = 0
+        ms, first = m.time_prefill(prompt)
+        if i >= args.warmup:
+            times.append(ms)
+    ms_prefill = float(np.mean(times))
+    # decode continues from the cache
+    m.pos = 0
+    _, first = m.prefill(prompt, logits=False)
+    ms_dec, ids = m.time_decode(first, N_DEC)
+    m.close()
+    L, D, F, H, KV, HD = args.layers, 4096, 14336, 32, 8, 128
+    lin = 2.0 * T * L * ((H + 2 * KV) * HD * D + D * H * HD + 3 * F * D)
+    attn = 4.0 * HD * H * L * T * (T + 1) / 2
+    flops = lin + attn + 2.0 * 32000 * D
+    tflops = flops / (ms_prefill * 1e-3) / 1e12
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak = json.load(open(pk))["bf16_tflops"] if os.path.exists(pk) else 1590.0
+    out = {"metric": "int8 Mistral-7B prefill tok/s (2048-token prompt)", "value": T / (ms_prefill * 1e-3),
+           "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_prefill,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 operands, f32 accumulate",
+           "data": "synthetic",
+           "config": {"workload": f"Mistral-7B int8 ({L} layers), prefill of {T} random token ids, "
+                                  f"then {N_DEC} greedy decode steps", "prompt": T, "decode": N_DEC},
+           "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                        "frac": tflops / peak, "flops_per_step": flops,
+                        "note": "whole prefill (GEMMs + attention + row kernels) against the dense fp16 peak"},
+           "decode_after_prefill": {"tok_s": N_DEC / (ms_dec * 1e-3), "ms_per_token": ms_dec / N_DEC,
+                                    "ids_head": ids[:8]},
+           "first_token": first}
+    print(json.dumps(out))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -422,6 +469,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-layers", type=int, default=8)
+    ap.add_argument("--prefill", action="store_true",
+                    help="batched prefill of a --prefill-tokens prompt, then 32 decode steps")
+    ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--gemv-sweep", action="store_true",
                     help="isolated int8 GEMV sweep at Mistral-7B shapes (one JSON line per shape)")
     ap.add_argument("--layers", type=int, default=32,
@@ -432,6 +482,9 @@ def main():
     rank, world, local = dist_env()
     if args.gemv_sweep:
         run_gemv_sweep(args)
+        return
+    if args.prefill:
+        run_prefill(args)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)

@@ -205,6 +205,11 @@ TL_API tl_status tl_model_forward(tl_model* m, uint32_t token, float* logits, ui
 TL_API tl_status tl_model_prefill(tl_model* m, const uint32_t* tokens, size_t n, float* logits,
                                   uint32_t* next_token);
 
+/* tl_model_prefill with the device time of the pass (token ids resident,
+ * CUDA events on the model's stream) in *ms (measurement aid). */
+TL_API tl_status tl_model_time_prefill(tl_model* m, const uint32_t* tokens, size_t n, uint32_t* next_token,
+                                       float* ms);
+
 /* The greedy loop of main.cpp:69-77 on the device: forwards prompt[0..n_prompt-1]
  * then n_new times forwards the last argmax; writes the n_new generated ids
  * to out (host).  Only the ids cross the PCIe bus. */

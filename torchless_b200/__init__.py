@@ -97,6 +97,7 @@ SIGNATURES = {
     "tl_model_forward": [_P, _U32, _P, _P],
     "tl_model_generate": [_P, _P, _S, _S, _P],
     "tl_model_prefill": [_P, _P, _S, _P, _P],
+    "tl_model_time_prefill": [_P, _P, _S, _P, ctypes.POINTER(_F)],
     "tl_model_get_pos": [_P, ctypes.POINTER(_S)],
     "tl_model_set_pos": [_P, _S],
     "tl_model_layer_forward": [_P, _I, _P],

@@ -972,8 +972,22 @@ tl_status tl_model_forward(tl_model* m, uint32_t token, float* logits, uint32_t*
     return TL_OK;
 }
 
+tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* logits, uint32_t* next_token,
+                       float* ms);
+
 tl_status tl_model_prefill(tl_model* m, const uint32_t* tokens, size_t n, float* logits, uint32_t* next_token) {
     clear_error();
+    return prefill_impl(m, tokens, n, logits, next_token, nullptr);
+}
+
+tl_status tl_model_time_prefill(tl_model* m, const uint32_t* tokens, size_t n, uint32_t* next_token, float* ms) {
+    clear_error();
+    TL_REQUIRE(ms, "tl_model_time_prefill: null ms");
+    return prefill_impl(m, tokens, n, nullptr, next_token, ms);
+}
+
+tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* logits, uint32_t* next_token,
+                       float* ms_out) {
     TL_REQUIRE(m && tokens && n > 0, "tl_model_prefill: bad arguments");
     if (m->tp > 1) return set_error(TL_ERR_UNSUPPORTED, "tl_model_prefill: not available under tensor parallelism");
     TL_REQUIRE(n < (1u << 30), "tl_model_prefill: n too large");
@@ -990,6 +1004,12 @@ tl_status tl_model_prefill(tl_model* m, const uint32_t* tokens, size_t n, float*
     const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));  // modules.cpp:79-80
     cudaStream_t s = m->stream;
     TL_CUDA_TRY(cudaMemcpyAsync(m->p_tok, tokens, n * 4, cudaMemcpyHostToDevice, s));
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (ms_out) {  // device time of the whole pass, token ids resident
+        TL_CUDA_TRY(cudaEventCreate(&e0));
+        TL_CUDA_TRY(cudaEventCreate(&e1));
+        TL_CUDA_TRY(cudaEventRecord(e0, s));
+    }
     TL_TRY(embed_rows(m->p_h, m->embed, m->p_tok, M, D, s));
     for (size_t l = 0; l < m->cfg.n_layers; l++) {
         const LayerW& w = m->layers[l];
@@ -1015,9 +1035,15 @@ tl_status tl_model_prefill(tl_model* m, const uint32_t* tokens, size_t n, float*
     a.part_v = m->am_v; a.part_i = m->am_i; a.counter = m->am_cnt;
     a.out_token = m->d_token; a.history = m->d_hist; a.pos = m->d_pos;
     TL_TRY(launch_gemv_f32(a, true, true, s, false));
+    if (ms_out) TL_CUDA_TRY(cudaEventRecord(e1, s));
     if (logits) TL_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, static_cast<size_t>(V) * 4, cudaMemcpyDeviceToHost, s));
     TL_CUDA_TRY(cudaMemcpyAsync(m->h_pinned + 1, m->d_token, 4, cudaMemcpyDeviceToHost, s));
     TL_TRY(sync(m));
+    if (ms_out) {
+        TL_CUDA_TRY(cudaEventElapsedTime(ms_out, e0, e1));
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
     m->pos = p0 + n;
     if (next_token) *next_token = m->h_pinned[1];
     return TL_OK;

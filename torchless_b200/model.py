@@ -120,6 +120,14 @@ class Model:
                                      ctypes.byref(nxt)))
         return out, nxt.value
 
+    def time_prefill(self, tokens: Sequence[int]):
+        """(device ms of a prefill of `tokens`, argmax of the last token)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        ms = ctypes.c_float()
+        nxt = ctypes.c_uint32()
+        check(lib().tl_model_time_prefill(self._h, t.ctypes.data, t.size, ctypes.byref(nxt), ctypes.byref(ms)))
+        return ms.value, nxt.value
+
     def generate(self, prompt: Sequence[int], n_new: int) -> List[int]:
         """main.cpp:69-77 on the device: returns the n_new greedy ids."""
         p = np.ascontiguousarray(prompt, dtype=np.uint32)
