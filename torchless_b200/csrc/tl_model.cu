@@ -259,6 +259,7 @@ struct tl_model {
     size_t rows_cap = 0;
     float *p_h = nullptr, *p_qkv = nullptr;
     __half *p_x16 = nullptr, *p_q16 = nullptr, *p_ctx16 = nullptr, *p_act16 = nullptr;
+    __half *p_k16 = nullptr, *p_v16 = nullptr;  // fp16 copies of one layer's cache rows
     uint32_t* p_tok = nullptr;
     double bytes_per_step = 0;
 };
@@ -795,8 +796,10 @@ tl_status ensure_prefill(tl_model* m, size_t n) {
         m->rows = DeviceArena();
         const size_t cap = std::max<size_t>(n, 64);
         using A = DeviceArena;
+        const size_t kvh = static_cast<size_t>(KV) * m->max_seq * HD;
         TL_TRY(m->rows.reserve(A::pad(cap * D * 4) + A::pad(cap * NQKV * 4) + A::pad(cap * D * 2) +
-                               2 * A::pad(cap * H * HD * 2) + A::pad(cap * F * 2) + A::pad(cap * 4)));
+                               2 * A::pad(cap * H * HD * 2) + A::pad(cap * F * 2) + A::pad(cap * 4) +
+                               2 * A::pad(kvh * 2)));
         m->p_h = m->rows.take<float>(cap * D);
         m->p_qkv = m->rows.take<float>(cap * NQKV);
         m->p_x16 = m->rows.take<__half>(cap * D);
@@ -804,7 +807,9 @@ tl_status ensure_prefill(tl_model* m, size_t n) {
         m->p_ctx16 = m->rows.take<__half>(cap * H * HD);
         m->p_act16 = m->rows.take<__half>(cap * F);
         m->p_tok = m->rows.take<uint32_t>(cap);
-        if (!m->p_tok) return set_error(TL_ERR_OUT_OF_MEMORY, "prefill row arena (internal)");
+        m->p_k16 = m->rows.take<__half>(kvh);
+        m->p_v16 = m->rows.take<__half>(kvh);
+        if (!m->p_v16) return set_error(TL_ERR_OUT_OF_MEMORY, "prefill row arena (internal)");
         m->rows_cap = cap;
     }
     return TL_OK;
@@ -1019,7 +1024,7 @@ tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* log
         TL_TRY(rmsnorm_rows_f16(m->p_x16, m->p_h, w.g_in, M, D, s));
         TL_TRY(gemm_f16(kEpiStoreF32, m->p_x16, M, D, W[0], NQKV, m->p_qkv, NQKV, m->err, s));
         TL_TRY(rope_cache_rows(m->p_q16, m->p_qkv, kc, vc, m->cos_tab, m->sin_tab, M, p0, H, KV, HD, ms, s));
-        TL_TRY(attention_prefill(m->p_ctx16, m->p_q16, kc, vc, M, p0, H, KV, HD, ms, scale, s));
+        TL_TRY(attention_prefill(m->p_ctx16, m->p_q16, m->p_k16, m->p_v16, kc, vc, M, p0, H, KV, HD, ms, scale, s));
         TL_TRY(gemm_f16(kEpiAddF32, m->p_ctx16, M, H * HD, W[1], D, m->p_h, D, m->err, s));
         TL_TRY(rmsnorm_rows_f16(m->p_x16, m->p_h, w.g_post, M, D, s));
         TL_TRY(gemm_f16(kEpiSwiGluF16, m->p_x16, M, D, W[2], 2 * F, m->p_act16, F, m->err, s));

@@ -100,24 +100,60 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+__device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+// Four 8x8 b16 matrices; lanes 8 i .. 8 i + 7 give the row addresses of matrix i.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(su32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(su32(p)));
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__global__ void k_kv_to_f16(__half* k16, __half* v16, const float* kc, const float* vc, int KV, int T, int HD,
+                            int max_seq) {
+    const size_t n4 = static_cast<size_t>(KV) * T * HD / 4;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t e = i * 4, kh = e / (static_cast<size_t>(T) * HD), rest = e % (static_cast<size_t>(T) * HD);
+        const size_t src = kh * max_seq * HD + rest;
+        const float4 a = *reinterpret_cast<const float4*>(kc + src);
+        const float4 b = *reinterpret_cast<const float4*>(vc + src);
+        const __half2 ka[2] = {__floats2half2_rn(a.x, a.y), __floats2half2_rn(a.z, a.w)};
+        const __half2 vb[2] = {__floats2half2_rn(b.x, b.y), __floats2half2_rn(b.z, b.w)};
+        *reinterpret_cast<uint2*>(k16 + e) = *reinterpret_cast<const uint2*>(ka);
+        *reinterpret_cast<uint2*>(v16 + e) = *reinterpret_cast<const uint2*>(vb);
+    }
+}
+
 // Flash attention, one CTA per (64 queries, head), 4 warps x 16 query rows.
-// K block [64 keys][HD] and V block transposed [HD][64 keys] staged as fp16.
+// fp16 K and V blocks of 64 keys ([key][HD], rows padded) double-buffered with
+// cp.async; S = Q K^T B fragments by ldmatrix, O += P V B fragments by
+// ldmatrix.trans of the row-major V block.
 constexpr int kAQ = 64, kAK = 64;
 template <int HD>
-__global__ void __launch_bounds__(128) k_attention_prefill(__half* ctx16, const __half* q16, const float* kc,
-                                                           const float* vc, int M, int p0, int H, int max_seq,
+__global__ void __launch_bounds__(128) k_attention_prefill(__half* ctx16, const __half* q16, const __half* k16,
+                                                           const __half* v16, int M, int p0, int H, int T,
                                                            float scale) {
-    constexpr int KP = HD + 8, VP = kAK + 8;  // padded rows (halves)
-    __shared__ __align__(16) __half Ks[kAK * KP];
-    __shared__ __align__(16) __half Vt[HD * VP];
+    constexpr int KP = HD + 8;  // padded row (halves): 16-byte aligned, conflict-free ldmatrix
+    extern __shared__ __align__(16) __half smem_h[];
+    __half* Ks = smem_h;                 // [2][kAK][KP]
+    __half* Vs = smem_h + 2 * kAK * KP;  // [2][kAK][KP]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int h = blockIdx.y, kh = h / 4;  // kv head h / 4 (modules.cpp:70)
     const int q0 = blockIdx.x * kAQ, qend = min(M, q0 + kAQ);
-    const int r0 = q0 + warp * 16;  // this warp's first query row
-    const float* kbase = kc + static_cast<size_t>(kh) * max_seq * HD;
-    const float* vbase = vc + static_cast<size_t>(kh) * max_seq * HD;
+    const int r0 = q0 + warp * 16;
+    const __half* kbase = k16 + static_cast<size_t>(kh) * T * HD;
+    const __half* vbase = v16 + static_cast<size_t>(kh) * T * HD;
 
-    // Q fragments (A operand) for the HD / 16 k-steps
     uint32_t qa[HD / 16][4];
     {
         const int ra = r0 + g, rb = r0 + g + 8;
@@ -141,25 +177,35 @@ __global__ void __launch_bounds__(128) k_attention_prefill(__half* ctx16, const 
     const int kmax = p0 + qend;  // keys [0, kmax) exist for this CTA
     const int nkb = (kmax + kAK - 1) / kAK;
 
-    for (int kb = 0; kb < nkb; kb++) {
+    auto stage = [&](int kb, int buf) {  // keys >= kmax are zero rows
         const int k0 = kb * kAK;
-        __syncthreads();
-        // stage K (row-major) and V (transposed) as fp16; keys >= kmax are zero
-        for (int e = threadIdx.x; e < kAK * HD / 4; e += blockDim.x) {
-            const int key = e / (HD / 4), c = (e % (HD / 4)) * 4;
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+        __half* kd = Ks + buf * kAK * KP;
+        __half* vd = Vs + buf * kAK * KP;
+        for (int e = threadIdx.x; e < kAK * HD / 8; e += blockDim.x) {
+            const int key = e / (HD / 8), c = (e % (HD / 8)) * 8;
             if (k0 + key < kmax) {
-                kv = *reinterpret_cast<const float4*>(kbase + static_cast<size_t>(k0 + key) * HD + c);
-                vv = *reinterpret_cast<const float4*>(vbase + static_cast<size_t>(k0 + key) * HD + c);
+                cp_async16(kd + key * KP + c, kbase + static_cast<size_t>(k0 + key) * HD + c);
+                cp_async16(vd + key * KP + c, vbase + static_cast<size_t>(k0 + key) * HD + c);
+            } else {
+                *reinterpret_cast<uint4*>(kd + key * KP + c) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4*>(vd + key * KP + c) = make_uint4(0, 0, 0, 0);
             }
-            *reinterpret_cast<uint32_t*>(&Ks[key * KP + c]) = pack_h2(kv.x, kv.y);
-            *reinterpret_cast<uint32_t*>(&Ks[key * KP + c + 2]) = pack_h2(kv.z, kv.w);
-            Vt[(c + 0) * VP + key] = __float2half_rn(vv.x);
-            Vt[(c + 1) * VP + key] = __float2half_rn(vv.y);
-            Vt[(c + 2) * VP + key] = __float2half_rn(vv.z);
-            Vt[(c + 3) * VP + key] = __float2half_rn(vv.w);
+        }
+        cp_async_commit();
+    };
+    stage(0, 0);
+    const int mi = lane >> 3, mr = lane & 7;  // ldmatrix: matrix index, row within it
+    for (int kb = 0; kb < nkb; kb++) {
+        const int buf = kb & 1, k0 = kb * kAK;
+        if (kb + 1 < nkb) {
+            stage(kb + 1, buf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
         __syncthreads();
+        const __half* kd = Ks + buf * kAK * KP;
+        const __half* vd = Vs + buf * kAK * KP;
         // S = Q K^T (16 x 64 per warp)
         float s[kAK / 8][4];
 #pragma unroll
@@ -167,10 +213,11 @@ __global__ void __launch_bounds__(128) k_attention_prefill(__half* ctx16, const 
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ks++) {
 #pragma unroll
-            for (int j = 0; j < kAK / 8; j++) {
-                const __half* kr = &Ks[(j * 8 + g) * KP + ks * 16 + 2 * t];
-                mma_f16(s[j], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], *reinterpret_cast<const uint32_t*>(kr),
-                        *reinterpret_cast<const uint32_t*>(kr + 8));
+            for (int j = 0; j < kAK / 8; j += 2) {
+                uint32_t b[4];  // b0, b1 of key tiles j and j + 1
+                ldsm_x4(b, kd + (8 * j + 8 * (mi >> 1) + mr) * KP + 16 * ks + 8 * (mi & 1));
+                mma_f16(s[j], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b[0], b[1]);
+                mma_f16(s[j + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b[2], b[3]);
             }
         }
         // scale, causal mask (key position <= query position), row max over the quad
@@ -221,12 +268,14 @@ __global__ void __launch_bounds__(128) k_attention_prefill(__half* ctx16, const 
             const uint32_t a0 = pack_h2(p[0][0], p[0][1]), a1 = pack_h2(p[0][2], p[0][3]);
             const uint32_t a2 = pack_h2(p[1][0], p[1][1]), a3 = pack_h2(p[1][2], p[1][3]);
 #pragma unroll
-            for (int j = 0; j < HD / 8; j++) {
-                const __half* vr = &Vt[(j * 8 + g) * VP + kk * 16 + 2 * t];
-                mma_f16(o[j], a0, a1, a2, a3, *reinterpret_cast<const uint32_t*>(vr),
-                        *reinterpret_cast<const uint32_t*>(vr + 8));
+            for (int j = 0; j < HD / 8; j += 2) {
+                uint32_t b[4];  // b0, b1 of dim tiles j and j + 1 (V transposed by ldmatrix)
+                ldsm_x4_t(b, vd + (16 * kk + 8 * (mi & 1) + mr) * KP + 8 * j + 8 * (mi >> 1));
+                mma_f16(o[j], a0, a1, a2, a3, b[0], b[1]);
+                mma_f16(o[j + 1], a0, a1, a2, a3, b[2], b[3]);
             }
         }
+        __syncthreads();  // everyone is done with `buf` before it is refilled
     }
     // row sums over the quad, normalise, store fp16 ctx
     l_a += __shfl_xor_sync(FULL, l_a, 1);
@@ -272,13 +321,32 @@ tl_status rope_cache_rows(__half* q16, const float* qkv, float* k_cache, float* 
     return check_launch("rope_cache_rows");
 }
 
-tl_status attention_prefill(__half* ctx16, const __half* q16, const float* k_cache, const float* v_cache, int M,
-                            int p0, int H, int KV, int HD, int max_seq, float scale, cudaStream_t s) {
+tl_status attention_prefill(__half* ctx16, const __half* q16, __half* k16, __half* v16, const float* k_cache,
+                            const float* v_cache, int M, int p0, int H, int KV, int HD, int max_seq, float scale,
+                            cudaStream_t s) {
     TL_REQUIRE(H == 4 * KV, "attention_prefill: kv head h / 4 needs H == 4 KV");
+    const int T = p0 + M;  // cached positions the queries can see
+    const size_t n4 = static_cast<size_t>(KV) * T * HD / 4;
+    k_kv_to_f16<<<grid_for(n4, 256), 256, 0, s>>>(k16, v16, k_cache, v_cache, KV, T, HD, max_seq);
+    TL_TRY(check_launch("kv_to_f16"));
     const dim3 grid((M + kAQ - 1) / kAQ, H);
     switch (HD) {
-        case 64: k_attention_prefill<64><<<grid, 128, 0, s>>>(ctx16, q16, k_cache, v_cache, M, p0, H, max_seq, scale); break;
-        case 128: k_attention_prefill<128><<<grid, 128, 0, s>>>(ctx16, q16, k_cache, v_cache, M, p0, H, max_seq, scale); break;
+        case 64: {
+            const size_t smem = 4 * kAK * (64 + 8) * 2;
+            k_attention_prefill<64><<<grid, 128, smem, s>>>(ctx16, q16, k16, v16, M, p0, H, T, scale);
+            break;
+        }
+        case 128: {
+            const size_t smem = 4 * kAK * (128 + 8) * 2;  // 69632 bytes
+            static bool attr = false;
+            if (!attr) {
+                TL_CUDA_TRY(cudaFuncSetAttribute(k_attention_prefill<128>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+                attr = true;
+            }
+            k_attention_prefill<128><<<grid, 128, smem, s>>>(ctx16, q16, k16, v16, M, p0, H, T, scale);
+            break;
+        }
         default: return set_error(TL_ERR_UNSUPPORTED, "attention_prefill: head_dim %d", HD);
     }
     return check_launch("attention_prefill");
