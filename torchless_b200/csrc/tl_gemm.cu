@@ -1,16 +1,18 @@
 // tl_gemm.cu -- tcgen05 GEMM (sm_100a): C = A B^T, fp16 operands, fp32
 // accumulation in tensor memory, fused epilogues.
 //
-// One CTA computes a 128 x BN tile of C.  Warp roles (192 threads):
+// Persistent: one CTA per SM walks 128 x BN tiles of C.  Warp roles (192 threads):
 //   warp 0      TMA producer: 128-row A and BN-row B boxes of 64 K-elements
 //               (128 bytes, SWIZZLE_128B) into a ring of shared-memory stages,
 //               completing on per-stage `full` mbarriers;
-//   warp 1      allocates the BN tensor-memory columns of the accumulator and
+//   warp 1      allocates 2 x BN tensor-memory columns (two accumulators) and
 //               issues tcgen05.mma (kind::f16, M 128, N BN, K 16; 4 per stage)
 //               from one thread; tcgen05.commit frees each stage (`empty`) and
-//               finally signals the accumulator (`accum`);
+//               signals a finished accumulator (`tfull`);
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator rows (warp w reads
-//               tensor-memory lanes 32 (w % 4) ..), fused op, global stores.
+//               tensor-memory lanes 32 (w % 4) ..), fused op, global stores,
+//               then hand the accumulator back (`tempty`) while the next
+//               tile's MMAs already run in the other one.
 // Every mbarrier wait is bounded by ~2 s of %globaltimer; on expiry the
 // kernel records an error code, stops issuing, lets the work in flight drain
 // (bounded), frees its tensor memory and returns.
@@ -18,6 +20,7 @@
 #include <cudaTypedefs.h>
 #include <math.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "tl_common.cuh"
@@ -38,6 +41,7 @@ struct GemmCfg {
     static constexpr int kStageBytes = kABytes + kBBytes;
     // 1024-byte alignment slack (SWIZZLE_128B destinations) + stages + barriers
     static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256;
+    static_assert(2 * BN <= 512, "two accumulators must fit the 512 tensor-memory columns");
 };
 
 struct GemmArgs {
@@ -131,6 +135,74 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
 }
 
+// Waits like bar_wait but also gives up as soon as the CTA has aborted.
+__device__ __forceinline__ bool bar_wait_ab(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
+    if (bar_test(b, parity)) return true;
+    const unsigned long long t0 = gtime();
+    for (unsigned i = 1;; i++) {
+        if (bar_test(b, parity)) return true;
+        if ((i & 15) == 0 && (*abort_flag || gtime() - t0 > kGemmTimeoutNs)) return false;
+    }
+}
+
+// The epilogue of one 128 x BN accumulator (tensor-memory columns tcol ..)
+// for tile rows m0 .., columns n0 ..; called by the 4 epilogue warps.
+template <int BN, int EPI>
+__device__ __forceinline__ void gemm_epilogue(const GemmArgs& g, uint32_t tcol, int m0, int n0, int sub, int lane) {
+    const int row = m0 + sub * 32 + lane;
+    const uint32_t tl = tcol + (static_cast<uint32_t>(sub * 32) << 16);
+    if (EPI == kEpiSwiGluF16) {
+        __half* out = static_cast<__half*>(g.C);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN / 2; c0 += 32) {
+            float gv[32], uv[32];
+            tmem_ld32(tl + c0, gv);
+            tmem_ld32(tl + BN / 2 + c0, uv);
+            const int col = n0 / 2 + c0;
+            if (row < g.M && col < g.N / 2) {
+                __half2 h[16];
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float a0 = (gv[j] / (1.0f + expf(-gv[j]))) * uv[j];  // silu * up (kernels.cpp:98-102)
+                    const float a1 = (gv[j + 1] / (1.0f + expf(-gv[j + 1]))) * uv[j + 1];
+                    h[j / 2] = __floats2half2_rn(a0, a1);
+                }
+                uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * g.ldc + col);
+#pragma unroll
+                for (int q = 0; q < 4; q++) dst[q] = reinterpret_cast<const uint4*>(h)[q];
+            }
+        }
+    } else {
+        float* out = static_cast<float*>(g.C);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            float v[32];
+            tmem_ld32(tl + c0, v);
+            if (row < g.M) {
+                float* dst = out + static_cast<size_t>(row) * g.ldc + n0 + c0;
+                const int rem = g.N - (n0 + c0);
+                if (rem >= 32) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        float4 x = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        if (EPI == kEpiAddF32) {
+                            const float4 r = *reinterpret_cast<const float4*>(dst + j);
+                            x.x += r.x; x.y += r.y; x.z += r.z; x.w += r.w;
+                        }
+                        *reinterpret_cast<float4*>(dst + j) = x;
+                    }
+                } else {
+                    for (int j = 0; j < rem; j++) dst[j] = (EPI == kEpiAddF32) ? dst[j] + v[j] : v[j];
+                }
+            }
+        }
+    }
+}
+
+// Persistent: CTA c takes tiles c, c + G, ... (m fastest, so the CTAs that
+// run together share B blocks: each weight block is read from HBM once).
+// Two accumulators (2 x BN tensor-memory columns) let the epilogue of tile i
+// run while the MMAs of tile i + 1 accumulate.
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, GemmArgs g) {
@@ -140,12 +212,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(base + S * Cfg::kStageBytes);
     uint64_t* empty = full + S;
-    uint64_t* accum = empty + S;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+    uint64_t* tfull = empty + S;   // [2] accumulator ready
+    uint64_t* tempty = tfull + 2;  // [2] accumulator drained by the epilogue
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
+    const int tm = (g.M + kBM - 1) / kBM, tn = (g.N + BN - 1) / BN, n_tiles = tm * tn;
     const int nk = g.K / kBK;
 
     if (threadIdx.x == 0) {
@@ -153,13 +226,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             bar_init(&full[s], 1);
             bar_init(&empty[s], 1);
         }
-        bar_init(accum, 1);
+        for (int b = 0; b < 2; b++) {
+            bar_init(&tfull[b], 1);
+            bar_init(&tempty[b], 4);  // one arrival per epilogue warp
+        }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) {  // accumulator: BN fp32 columns x 128 lanes
+    if (warp == 1) {  // two accumulators: 2 BN fp32 columns x 128 lanes
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
-                     "r"(BN));
+                     "r"(2 * BN));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -168,110 +244,87 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     auto fail = [&](int code) {
+        if (!*abort_flag && g.err) atomicCAS(g.err, 0, code);
         *abort_flag = 1;
-        if (g.err) atomicCAS(g.err, 0, code);
     };
 
     if (warp == 0) {
         if (lane == 0) {
-            int issued = 0;
-            for (int kb = 0; kb < nk; kb++) {
-                const int s = kb % S;
-                if (kb >= S && !bar_wait(&empty[s], ((kb / S) - 1) & 1)) {
-                    fail(1);
-                    break;
+            uint32_t it = 0;
+            for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x) {
+                const int m0 = (tile % tm) * kBM, n0 = (tile / tm) * BN;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % S;
+                    if (it >= S && !bar_wait_ab(&empty[s], ((it / S) - 1) & 1, abort_flag)) {
+                        fail(1);
+                        break;
+                    }
+                    uint8_t* sa = base + s * Cfg::kStageBytes;
+                    bar_expect_tx(&full[s], Cfg::kStageBytes);
+                    tma_load_2d(sa, &tma_a, kb * kBK, m0, &full[s]);
+                    tma_load_2d(sa + Cfg::kABytes, &tma_b, kb * kBK, n0, &full[s]);
                 }
-                if (*abort_flag) break;
-                uint8_t* sa = base + s * Cfg::kStageBytes;
-                bar_expect_tx(&full[s], Cfg::kStageBytes);
-                tma_load_2d(sa, &tma_a, kb * kBK, m0, &full[s]);
-                tma_load_2d(sa + Cfg::kABytes, &tma_b, kb * kBK, n0, &full[s]);
-                issued++;
             }
-            // every copy issued lands before the CTA exits (the consumer may have stopped)
-            for (int kb = (issued > S ? issued - S : 0); kb < issued; kb++) bar_wait(&full[kb % S], (kb / S) & 1);
+            // every copy issued lands before the CTA exits
+            const uint32_t first = it > static_cast<uint32_t>(S) ? it - S : 0;
+            for (uint32_t k = first; k < it; k++) bar_wait(&full[k % S], (k / S) & 1);
         }
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t idesc = idesc_f16<BN>();
-            for (int kb = 0; kb < nk; kb++) {
-                const int s = kb % S;
-                if (!bar_wait(&full[s], (kb / S) & 1)) {
-                    fail(2);
+            uint32_t it = 0;
+            int i = 0;
+            for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x, i++) {
+                const int buf = i & 1;
+                if (i >= 2 && !bar_wait_ab(&tempty[buf], ((i / 2) - 1) & 1, abort_flag)) {
+                    fail(4);
                     break;
                 }
-                if (*abort_flag) break;
                 tc_fence_after();
-                const uint32_t sa = su32(base + s * Cfg::kStageBytes);
-                const uint64_t da = sdesc_k128(sa), db = sdesc_k128(sa + Cfg::kABytes);
+                const uint32_t dt = tmem + static_cast<uint32_t>(buf * BN);
+                bool ok = true;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % S;
+                    if (!bar_wait_ab(&full[s], (it / S) & 1, abort_flag)) {
+                        fail(2);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = su32(base + s * Cfg::kStageBytes);
+                    const uint64_t da = sdesc_k128(sa), db = sdesc_k128(sa + Cfg::kABytes);
 #pragma unroll
-                for (int k = 0; k < kBK / 16; k++)  // K 16 per MMA = 32 bytes along the swizzled row
-                    umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
-                umma_commit(&empty[s]);  // stage free once these MMAs have read it
+                    for (int k = 0; k < kBK / 16; k++)  // K 16 per MMA = 32 bytes along the swizzled row
+                        umma_f16(dt, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+                    umma_commit(&empty[s]);  // stage free once these MMAs have read it
+                }
+                umma_commit(&tfull[buf]);  // accumulator ready (also on abort: frees the epilogue)
+                if (!ok) break;
             }
-            umma_commit(accum);  // all MMAs issued so far complete -> accumulator ready
         }
     } else {
-        // epilogue warps 2..5: tensor-memory lanes 32 (warp % 4) + lane = tile rows
-        const int sub = warp & 3;
-        const int row = m0 + sub * 32 + lane;
-        const bool ok = bar_wait(accum, 0);
-        if (!ok) fail(3);
-        tc_fence_after();
-        if (ok && !*abort_flag) {
-            const uint32_t tl = tmem + (static_cast<uint32_t>(sub * 32) << 16);
-            if (EPI == kEpiSwiGluF16) {
-                __half* out = static_cast<__half*>(g.C);
-#pragma unroll 1
-                for (int c0 = 0; c0 < BN / 2; c0 += 32) {
-                    float gv[32], uv[32];
-                    tmem_ld32(tl + c0, gv);
-                    tmem_ld32(tl + BN / 2 + c0, uv);
-                    const int col = n0 / 2 + c0;
-                    if (row < g.M) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 2) {
-                            if (col + j + 1 < g.N / 2 + 1) {
-                                const float a0 = (gv[j] / (1.0f + expf(-gv[j]))) * uv[j];
-                                const float a1 = (gv[j + 1] / (1.0f + expf(-gv[j + 1]))) * uv[j + 1];
-                                *reinterpret_cast<__half2*>(out + static_cast<size_t>(row) * g.ldc + col + j) =
-                                    __floats2half2_rn(a0, a1);
-                            }
-                        }
-                    }
-                }
-            } else {
-                float* out = static_cast<float*>(g.C);
-#pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 32) {
-                    float v[32];
-                    tmem_ld32(tl + c0, v);
-                    if (row < g.M) {
-                        float* dst = out + static_cast<size_t>(row) * g.ldc + n0 + c0;
-                        const int rem = g.N - (n0 + c0);
-                        if (rem >= 32) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4) {
-                                float4 x = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                                if (EPI == kEpiAddF32) {
-                                    const float4 r = *reinterpret_cast<const float4*>(dst + j);
-                                    x.x += r.x; x.y += r.y; x.z += r.z; x.w += r.w;
-                                }
-                                *reinterpret_cast<float4*>(dst + j) = x;
-                            }
-                        } else {
-                            for (int j = 0; j < rem; j++) dst[j] = (EPI == kEpiAddF32) ? dst[j] + v[j] : v[j];
-                        }
-                    }
-                }
+        const int sub = warp & 3;  // tensor-memory lanes 32 sub .. (tcgen05.ld lane quarter of this warp)
+        int i = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, i++) {
+            const int buf = i & 1;
+            if (!bar_wait_ab(&tfull[buf], (i / 2) & 1, abort_flag)) {
+                fail(3);
+                break;
             }
+            tc_fence_after();
+            if (*abort_flag) break;
+            gemm_epilogue<BN, EPI>(g, tmem + static_cast<uint32_t>(buf * BN), (tile % tm) * kBM, (tile / tm) * BN,
+                                   sub, lane);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&tempty[buf])) : "memory");
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
     }
 }
 
@@ -319,7 +372,8 @@ tl_status launch_gemm(const __half* A, int M, int K, const __half* B, int N, voi
     });
     if (attr_err != cudaSuccess)
         return set_error(TL_ERR_CUDA, "gemm smem attribute: %s", cudaGetErrorString(attr_err));
-    const dim3 grid((N + BN - 1) / BN, (M + kBM - 1) / kBM);
+    const int tiles = ((N + BN - 1) / BN) * ((M + kBM - 1) / kBM);
+    const int grid = std::min(tiles, sm_count());
     GemmArgs g{M, N, K, C, ldc, err};
     kern<<<grid, kGemmThreads, GemmCfg<BN>::kSmem, s>>>(ta, tb, g);
     return check_launch("gemm_tc");
@@ -342,7 +396,7 @@ tl_status gemm_f16(int epi, const __half* A, int M, int K, const __half* B, int 
             TL_REQUIRE(ldc >= N && ldc % 4 == 0, "gemm: ldc");
             return launch_gemm<256, kEpiAddF32>(A, M, K, B, N, C, ldc, err, s);
         case kEpiSwiGluF16:
-            TL_REQUIRE(N % 256 == 0 && ldc >= N / 2 && ldc % 2 == 0, "gemm swiglu: N %% 256, ldc");
+            TL_REQUIRE(N % 256 == 0 && ldc >= N / 2 && ldc % 8 == 0, "gemm swiglu: N %% 256, ldc %% 8");
             return launch_gemm<256, kEpiSwiGluF16>(A, M, K, B, N, C, ldc, err, s);
         default:
             return set_error(TL_ERR_INVALID_ARGUMENT, "gemm: unknown epilogue %d", epi);
