@@ -273,6 +273,33 @@ TL_API tl_status tl_model_trace_step(tl_model* m, uint32_t token, uint64_t* out,
 TL_API tl_status tl_model_tp_handle(const tl_model* m, void* handle);
 TL_API tl_status tl_model_tp_connect(tl_model* m, const void* handles);
 
+/* Batched decoding: B independent sequences, each with its own fp32 KV
+ * cache [L][KV][max_seq][hd] and position, one token per sequence per step.
+ * No reference counterpart (the reference's InferenceState holds one
+ * sequence); a step equals Model<int8_t>::forward (modules.cpp:118-171) plus
+ * sample_max (main.cpp:10-21) run for every sequence, with the linear layers
+ * as tensor-core GEMMs over the B rows (fp16 weights dequantised from int8,
+ * fp32 accumulation, fp16 lm_head) and each sequence's attention over its own
+ * cache.  The batch shares the model's weights and stream; max_seq (0: the
+ * model's) must not exceed the model's.  Not available under tensor
+ * parallelism. */
+typedef struct tl_batch tl_batch;
+TL_API tl_status tl_batch_create(tl_model* m, int n_seq, size_t max_seq, tl_batch** out);
+TL_API tl_status tl_batch_destroy(tl_batch* b);
+/* Cache rows [0, n_pos) of every sequence and layer = N(0, 1) draws of a
+ * counter-based generator keyed (seed, sequence, layer, k/v, head, position,
+ * dim), so any one sequence can be regenerated alone; every position := n_pos. */
+TL_API tl_status tl_batch_fill_kv_random(tl_batch* b, uint64_t seed, size_t n_pos);
+/* One step: tokens[B] (host) at each sequence's position; logits (host
+ * [B][vocab_size], may be NULL) and next_tokens[B] (host, may be NULL). */
+TL_API tl_status tl_batch_step(tl_batch* b, const uint32_t* tokens, float* logits, uint32_t* next_tokens);
+/* n_steps greedy steps from tokens[B], each step feeding its argmaxes to the
+ * next; out [n_steps][B] (host, may be NULL); *ms = device time (CUDA events). */
+TL_API tl_status tl_batch_time_decode(tl_batch* b, const uint32_t* tokens, size_t n_steps, uint32_t* out,
+                                      float* ms);
+/* K and V rows of sequence `seq` at (layer, pos) into host k, v [n_kv_heads * head_dim]. */
+TL_API tl_status tl_batch_read_kv(const tl_batch* b, int seq, int layer, size_t pos, float* k, float* v);
+
 /* Number of kernel launches one decode step issues (all of them this library's). */
 TL_API tl_status tl_model_launches_per_step(const tl_model* m, int* launches);
 

@@ -202,6 +202,14 @@ class OracleModel:
         v = np.ctypeslib.as_array(oracle_lib().tlo_model_v_cache(self._h), (n,)).reshape(self.kv_shape)
         return k[layer, :, pos].copy(), v[layer, :, pos].copy()
 
+    def write_kv(self, layer: int, pos: int, k: np.ndarray, v: np.ndarray) -> None:
+        """Sets the cache rows at (layer, pos) (test set-up of a pre-filled cache)."""
+        n = int(np.prod(self.kv_shape))
+        kc = np.ctypeslib.as_array(oracle_lib().tlo_model_k_cache(self._h), (n,)).reshape(self.kv_shape)
+        vc = np.ctypeslib.as_array(oracle_lib().tlo_model_v_cache(self._h), (n,)).reshape(self.kv_shape)
+        kc[layer, :, pos] = k
+        vc[layer, :, pos] = v
+
     def layer_forward(self, layer: int, h: np.ndarray) -> np.ndarray:
         hid = np.ctypeslib.as_array(oracle_lib().tlo_model_hidden(self._h), (self.hidden,))
         hid[:] = h
@@ -246,6 +254,14 @@ class RefModel:
 
     def sample_max(self) -> int:
         return ref_lib().ref_sample_max(self._h)
+
+    def write_kv(self, layer: int, pos: int, k: np.ndarray, v: np.ndarray) -> None:
+        """Sets the cache rows at (layer, pos) (test set-up of a pre-filled cache)."""
+        n = int(np.prod(self.kv_shape))
+        kc = np.ctypeslib.as_array(oracle_lib().tlo_model_k_cache(self._h), (n,)).reshape(self.kv_shape)
+        vc = np.ctypeslib.as_array(oracle_lib().tlo_model_v_cache(self._h), (n,)).reshape(self.kv_shape)
+        kc[layer, :, pos] = k
+        vc[layer, :, pos] = v
 
     def layer_forward(self, layer: int, h: np.ndarray) -> np.ndarray:
         x = np.array(h, dtype=np.float32, copy=True)

@@ -106,6 +106,12 @@ SIGNATURES = {
     "tl_model_profile": [_P, _U32, _S, ctypes.POINTER(tl_kernel_time), _I, ctypes.POINTER(_I)],
     "tl_model_launches_per_step": [_P, ctypes.POINTER(_I)],
     "tl_model_trace_step": [_P, _U32, _P, _S, ctypes.POINTER(_S)],
+    "tl_batch_create": [_P, _I, _S, ctypes.POINTER(_P)],
+    "tl_batch_destroy": [_P],
+    "tl_batch_fill_kv_random": [_P, ctypes.c_uint64, _S],
+    "tl_batch_step": [_P, _P, _P, _P],
+    "tl_batch_time_decode": [_P, _P, _S, _P, ctypes.POINTER(_F)],
+    "tl_batch_read_kv": [_P, _I, _I, _S, _P, _P],
     "tl_model_tp_handle": [_P, _P],
     "tl_model_tp_connect": [_P, _P],
 }
@@ -137,6 +143,6 @@ def check(status: int) -> None:
 
 
 from . import ops  # noqa: E402  (needs lib/check)
-from .model import Model  # noqa: E402
+from .model import Batch, Model  # noqa: E402
 
-__all__ = ["lib", "check", "TLError", "ops", "Model", "LIB_PATH", "SIGNATURES"]
+__all__ = ["lib", "check", "TLError", "ops", "Model", "Batch", "LIB_PATH", "SIGNATURES"]

@@ -42,6 +42,7 @@
 #include "tl_decode.cuh"
 #include "tl_gemm.cuh"
 #include "tl_prefill.cuh"
+#include "tl_batch.cuh"
 #include "tl_gemv.cuh"
 #include "tl_json.h"
 #include "tl_kernels.h"
@@ -261,6 +262,8 @@ struct tl_model {
     __half *p_x16 = nullptr, *p_q16 = nullptr, *p_ctx16 = nullptr, *p_act16 = nullptr;
     __half *p_k16 = nullptr, *p_v16 = nullptr;  // fp16 copies of one layer's cache rows
     uint32_t* p_tok = nullptr;
+    __half* lm16 = nullptr;  // fp16 lm_head for the batched logits GEMM (first batch use)
+    DeviceArena lm16_arena;
     double bytes_per_step = 0;
 };
 
@@ -897,6 +900,7 @@ tl_status tl_model_destroy(tl_model* m) {
     m->tiles.release();
     m->w16.release();
     m->rows.release();
+    m->lm16_arena.release();
     if (m->d_layers) cudaFree(m->d_layers);
     if (m->h_pinned) cudaFreeHost(m->h_pinned);
     for (int q = 0; q < kMaxTp; q++)
@@ -1243,6 +1247,219 @@ tl_status tl_model_trace_step(tl_model* m, uint32_t token, uint64_t* out, size_t
     }
     cudaFree(d_trace);
     return st;
+}
+
+// ---------------------------------------------------------------------------
+// Batched decoding: B sequences with their own KV caches and positions.
+// ---------------------------------------------------------------------------
+}  // extern "C"
+
+struct tl_batch {
+    tl_model* m = nullptr;
+    int B = 0, S = 1;
+    size_t max_seq = 0;
+    DeviceArena kv, rows;
+    BatchKV bkv = {};
+    float *hres = nullptr, *qkv = nullptr, *qf = nullptr, *part = nullptr, *logits = nullptr;
+    __half *x16 = nullptr, *ctx16 = nullptr, *act16 = nullptr;
+    uint32_t *tok = nullptr, *pos = nullptr, *next = nullptr;
+    uint32_t* h_pinned = nullptr;       // [B]
+    std::vector<size_t> pos_host;
+};
+
+namespace tl {
+namespace {
+
+// One step of every sequence: token ids already in b->tok.
+tl_status batch_step(tl_batch* b) {
+    tl_model* m = b->m;
+    cudaStream_t s = m->stream;
+    const int B = b->B, D = static_cast<int>(m->cfg.hidden_size), HD = static_cast<int>(m->cfg.head_dim);
+    const int H = static_cast<int>(m->lH), KV = static_cast<int>(m->lKV), F = static_cast<int>(m->lF);
+    const int NQKV = (H + 2 * KV) * HD, V = static_cast<int>(m->lV);
+    const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));  // modules.cpp:79-80
+    size_t maxp = 0;
+    for (size_t p : b->pos_host) maxp = std::max(maxp, p);
+    const int S = std::max(1, std::min(b->S, static_cast<int>((maxp + 1 + 511) / 512)));  // >= 512 positions a split
+    TL_TRY(embed_rows(b->hres, m->embed, b->tok, B, D, s));
+    for (size_t l = 0; l < m->cfg.n_layers; l++) {
+        const LayerW& w = m->layers[l];
+        const auto& W = m->lw16[l];
+        TL_TRY(rmsnorm_rows_f16(b->x16, b->hres, w.g_in, B, D, s));
+        TL_TRY(gemm_f16(kEpiStoreF32, b->x16, B, D, W[0], NQKV, b->qkv, NQKV, m->err, s));
+        TL_TRY(rope_cache_batch(b->qf, b->qkv, b->bkv, static_cast<int>(l), b->pos, m->cos_tab, m->sin_tab, B, H, KV,
+                                HD, s));
+        TL_TRY(attention_decode_batch(b->part, b->qf, b->bkv, static_cast<int>(l), b->pos, B, H, KV, HD, S, scale, s));
+        TL_TRY(attention_merge_batch(b->ctx16, b->part, B, H, HD, S, s));
+        TL_TRY(gemm_f16(kEpiAddF32, b->ctx16, B, H * HD, W[1], D, b->hres, D, m->err, s));
+        TL_TRY(rmsnorm_rows_f16(b->x16, b->hres, w.g_post, B, D, s));
+        TL_TRY(gemm_f16(kEpiSwiGluF16, b->x16, B, D, W[2], 2 * F, b->act16, F, m->err, s));
+        TL_TRY(gemm_f16(kEpiAddF32, b->act16, B, F, W[3], D, b->hres, D, m->err, s));
+    }
+    TL_TRY(rmsnorm_rows_f16(b->x16, b->hres, m->norm, B, D, s));
+    TL_TRY(gemm_f16(kEpiStoreF32, b->x16, B, D, m->lm16, V, b->logits, V, m->err, s));
+    TL_TRY(argmax_rows(b->next, b->logits, B, V, b->pos, s));
+    for (auto& p : b->pos_host) p++;
+    return TL_OK;
+}
+
+tl_status batch_ready(const tl_batch* b, size_t steps) {
+    TL_REQUIRE(b, "tl_batch: null batch");
+    for (size_t p : b->pos_host)
+        if (p + steps > b->max_seq)
+            return set_error(TL_ERR_CAPACITY, "tl_batch: position %zu + %zu steps > max_seq %zu", p, steps, b->max_seq);
+    return TL_OK;
+}
+
+}  // namespace
+}  // namespace tl
+
+extern "C" {
+
+tl_status tl_batch_create(tl_model* m, int n_seq, size_t max_seq, tl_batch** out) {
+    clear_error();
+    TL_REQUIRE(m && out && n_seq > 0 && n_seq <= 4096, "tl_batch_create: bad arguments");
+    *out = nullptr;
+    if (m->tp > 1) return set_error(TL_ERR_UNSUPPORTED, "tl_batch_create: not available under tensor parallelism");
+    if (max_seq == 0) max_seq = m->max_seq;
+    TL_REQUIRE(max_seq <= m->max_seq, "tl_batch_create: max_seq %zu > the model's %zu (RoPE tables)", max_seq,
+               m->max_seq);
+    TL_REQUIRE(m->cfg.head_dim == 128, "tl_batch_create: head_dim 128 is built");
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    TL_TRY(ensure_prefill(m, 1));  // fp16 weights
+    const int64_t D = m->cfg.hidden_size, HD = m->cfg.head_dim, H = m->lH, KV = m->lKV, F = m->lF, V = m->lV;
+    const int64_t L = m->cfg.n_layers, NQKV = (H + 2 * KV) * HD;
+    if (!m->lm16) {
+        TL_TRY(m->lm16_arena.reserve(DeviceArena::pad(V * D * 2)));
+        m->lm16 = m->lm16_arena.take<__half>(V * D);
+        TL_TRY(f32_to_f16(m->lm16, m->lm_head, static_cast<size_t>(V) * D, m->stream));
+    }
+    std::unique_ptr<tl_batch> b(new tl_batch());
+    b->m = m;
+    b->B = n_seq;
+    b->max_seq = max_seq;
+    // most attention splits: about 16 CTAs per SM over the B x KV (sequence, kv head) pairs
+    b->S = std::max(1, std::min(64, 16 * sm_count() / static_cast<int>(std::max<int64_t>(1, KV * n_seq))));
+    const size_t layer = static_cast<size_t>(KV) * max_seq * HD;
+    const size_t seq = layer * L;
+    using A = DeviceArena;
+    TL_TRY(b->kv.reserve(2 * A::pad(seq * n_seq * 4)));
+    b->bkv.k = b->kv.take<float>(seq * n_seq);
+    b->bkv.v = b->kv.take<float>(seq * n_seq);
+    b->bkv.seq_stride = seq;
+    b->bkv.layer_stride = layer;
+    b->bkv.max_seq = static_cast<int>(max_seq);
+    const size_t Bn = n_seq;
+    TL_TRY(b->rows.reserve(A::pad(Bn * D * 4) + A::pad(Bn * NQKV * 4) + A::pad(Bn * H * HD * 4) +
+                           A::pad(Bn * H * b->S * (HD + 4) * 4) + A::pad(Bn * V * 4) + A::pad(Bn * D * 2) +
+                           A::pad(Bn * H * HD * 2) + A::pad(Bn * F * 2) + 3 * A::pad(Bn * 4)));
+    b->hres = b->rows.take<float>(Bn * D);
+    b->qkv = b->rows.take<float>(Bn * NQKV);
+    b->qf = b->rows.take<float>(Bn * H * HD);
+    b->part = b->rows.take<float>(Bn * H * b->S * (HD + 4));
+    b->logits = b->rows.take<float>(Bn * V);
+    b->x16 = b->rows.take<__half>(Bn * D);
+    b->ctx16 = b->rows.take<__half>(Bn * H * HD);
+    b->act16 = b->rows.take<__half>(Bn * F);
+    b->tok = b->rows.take<uint32_t>(Bn);
+    b->pos = b->rows.take<uint32_t>(Bn);
+    b->next = b->rows.take<uint32_t>(Bn);
+    if (!b->next) return set_error(TL_ERR_OUT_OF_MEMORY, "tl_batch rows (internal)");
+    TL_CUDA_TRY(cudaMemsetAsync(b->pos, 0, Bn * 4, m->stream));
+    TL_CUDA_TRY(cudaMallocHost(&b->h_pinned, Bn * 4));
+    b->pos_host.assign(Bn, 0);
+    TL_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    *out = b.release();
+    return TL_OK;
+}
+
+tl_status tl_batch_destroy(tl_batch* b) {
+    clear_error();
+    if (!b) return TL_OK;
+    cudaSetDevice(b->m->device);
+    cudaStreamSynchronize(b->m->stream);
+    b->kv.release();
+    b->rows.release();
+    if (b->h_pinned) cudaFreeHost(b->h_pinned);
+    delete b;
+    return TL_OK;
+}
+
+tl_status tl_batch_fill_kv_random(tl_batch* b, uint64_t seed, size_t n_pos) {
+    clear_error();
+    TL_REQUIRE(b && n_pos < b->max_seq && n_pos < (1u << 20), "tl_batch_fill_kv_random: bad arguments");
+    tl_model* m = b->m;
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    TL_TRY(fill_kv_random(b->bkv, seed, b->B, static_cast<int>(m->cfg.n_layers), static_cast<int>(m->lKV),
+                          static_cast<int>(m->cfg.head_dim), static_cast<int>(n_pos), m->stream));
+    for (int i = 0; i < b->B; i++) b->h_pinned[i] = static_cast<uint32_t>(n_pos);
+    TL_CUDA_TRY(cudaMemcpyAsync(b->pos, b->h_pinned, b->B * 4, cudaMemcpyHostToDevice, m->stream));
+    TL_TRY(sync(m));
+    b->pos_host.assign(b->B, n_pos);
+    return TL_OK;
+}
+
+tl_status tl_batch_step(tl_batch* b, const uint32_t* tokens, float* logits, uint32_t* next_tokens) {
+    clear_error();
+    TL_TRY(batch_ready(b, 1));
+    tl_model* m = b->m;
+    TL_REQUIRE(tokens, "tl_batch_step: null tokens");
+    for (int i = 0; i < b->B; i++)
+        TL_REQUIRE(tokens[i] < m->cfg.vocab_size, "tl_batch_step: token %u >= vocab_size", tokens[i]);
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    std::memcpy(b->h_pinned, tokens, b->B * 4);
+    TL_CUDA_TRY(cudaMemcpyAsync(b->tok, b->h_pinned, b->B * 4, cudaMemcpyHostToDevice, m->stream));
+    TL_TRY(batch_step(b));
+    if (logits)
+        TL_CUDA_TRY(cudaMemcpyAsync(logits, b->logits, static_cast<size_t>(b->B) * m->lV * 4, cudaMemcpyDeviceToHost,
+                                    m->stream));
+    TL_CUDA_TRY(cudaMemcpyAsync(b->h_pinned, b->next, b->B * 4, cudaMemcpyDeviceToHost, m->stream));
+    TL_TRY(sync(m));
+    if (next_tokens) std::memcpy(next_tokens, b->h_pinned, b->B * 4);
+    return TL_OK;
+}
+
+tl_status tl_batch_time_decode(tl_batch* b, const uint32_t* tokens, size_t n_steps, uint32_t* out, float* ms) {
+    clear_error();
+    TL_TRY(batch_ready(b, n_steps));
+    TL_REQUIRE(tokens && ms && n_steps > 0, "tl_batch_time_decode: bad arguments");
+    tl_model* m = b->m;
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    std::memcpy(b->h_pinned, tokens, b->B * 4);
+    TL_CUDA_TRY(cudaMemcpyAsync(b->tok, b->h_pinned, b->B * 4, cudaMemcpyHostToDevice, m->stream));
+    cudaEvent_t e0, e1;
+    TL_CUDA_TRY(cudaEventCreate(&e0));
+    TL_CUDA_TRY(cudaEventCreate(&e1));
+    TL_CUDA_TRY(cudaEventRecord(e0, m->stream));
+    for (size_t i = 0; i < n_steps; i++) {
+        TL_TRY(batch_step(b));
+        // the argmax of this step is the next step's token (main.cpp:72-77 per sequence)
+        TL_CUDA_TRY(cudaMemcpyAsync(b->tok, b->next, b->B * 4, cudaMemcpyDeviceToDevice, m->stream));
+        if (out)
+            TL_CUDA_TRY(cudaMemcpyAsync(out + i * b->B, b->next, b->B * 4, cudaMemcpyDeviceToHost, m->stream));
+    }
+    TL_CUDA_TRY(cudaEventRecord(e1, m->stream));
+    TL_TRY(sync(m));
+    TL_CUDA_TRY(cudaEventElapsedTime(ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    return TL_OK;
+}
+
+tl_status tl_batch_read_kv(const tl_batch* b, int seq, int layer, size_t pos, float* k, float* v) {
+    clear_error();
+    TL_REQUIRE(b && k && v && seq >= 0 && seq < b->B && layer >= 0 &&
+                   static_cast<size_t>(layer) < b->m->cfg.n_layers && pos < b->max_seq,
+               "tl_batch_read_kv: bad arguments");
+    const tl_model* m = b->m;
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    const size_t hd = m->cfg.head_dim;
+    for (size_t kh = 0; kh < static_cast<size_t>(m->lKV); kh++) {
+        const size_t off = seq * b->bkv.seq_stride + layer * b->bkv.layer_stride + (kh * b->max_seq + pos) * hd;
+        TL_CUDA_TRY(cudaMemcpy(k + kh * hd, b->bkv.k + off, hd * 4, cudaMemcpyDeviceToHost));
+        TL_CUDA_TRY(cudaMemcpy(v + kh * hd, b->bkv.v + off, hd * 4, cudaMemcpyDeviceToHost));
+    }
+    return TL_OK;
 }
 
 tl_status tl_model_launches_per_step(const tl_model* m, int* launches) {

@@ -180,3 +180,51 @@ class Model:
         n = ctypes.c_int()
         check(lib().tl_model_launches_per_step(self._h, ctypes.byref(n)))
         return n.value
+
+
+class Batch:
+    """B independent sequences decoded together on one model's weights
+    (tl_batch_*): each sequence has its own KV cache and position."""
+
+    def __init__(self, model: Model, n_seq: int, max_seq: int = 0):
+        self.model, self.n_seq = model, n_seq
+        h = ctypes.c_void_p()
+        check(lib().tl_batch_create(model._h, n_seq, max_seq, ctypes.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if self._h:
+            check(lib().tl_batch_destroy(self._h))
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def fill_kv_random(self, seed: int, n_pos: int) -> None:
+        check(lib().tl_batch_fill_kv_random(self._h, seed, n_pos))
+
+    def step(self, tokens: Sequence[int], logits: bool = True):
+        """One token per sequence; returns (logits [B, V] or None, next tokens [B])."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.empty((self.n_seq, self.model.config["vocab_size"]), dtype=np.float32) if logits else None
+        nxt = np.empty(self.n_seq, dtype=np.uint32)
+        check(lib().tl_batch_step(self._h, t.ctypes.data, out.ctypes.data if logits else None, nxt.ctypes.data))
+        return out, nxt
+
+    def time_decode(self, tokens: Sequence[int], n_steps: int):
+        """(device ms for n_steps greedy steps of every sequence, ids [n_steps, B])."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.empty((n_steps, self.n_seq), dtype=np.uint32)
+        ms = ctypes.c_float()
+        check(lib().tl_batch_time_decode(self._h, t.ctypes.data, n_steps, out.ctypes.data, ctypes.byref(ms)))
+        return ms.value, out
+
+    def read_kv(self, seq: int, layer: int, pos: int):
+        c = self.model.config
+        k = np.empty(c["n_kv_heads"] * c["head_dim"], dtype=np.float32)
+        v = np.empty_like(k)
+        check(lib().tl_batch_read_kv(self._h, seq, layer, pos, k.ctypes.data, v.ctypes.data))
+        return k.reshape(c["n_kv_heads"], c["head_dim"]), v.reshape(c["n_kv_heads"], c["head_dim"])
