@@ -35,90 +35,96 @@ __global__ void k_rope_cache_batch(float* qf, const float* qkv, BatchKV kv, int 
 }
 
 constexpr int kBW = 8;  // warps per attention CTA
-constexpr int kPF = 4;  // positions per warp in flight
 
+// Warp w takes groups of 8 positions; lane l holds dims 4 l .. 4 l + 3 of q,
+// K, V and of the accumulators of the 4 heads.  The 32 partial dot products
+// of a group (4 heads x 8 positions) are reduced together (transposed
+// reduction, 31 shuffles); lane l then holds score(head l / 8, position l % 8),
+// and the online softmax runs per 8-lane group.
 template <int HD>
 __global__ void __launch_bounds__(kBW * 32) k_attention_decode_batch(float* part, const float* qf, BatchKV kv,
                                                                      int layer, const uint32_t* pos, int H, int S,
                                                                      float scale) {
-    constexpr int VPL = HD / 32, QPG = 4, W = HD + 2;
-    __shared__ float q_s[QPG * HD];
+    static_assert(HD == 128, "lane owns 4 of 128 dims");
+    constexpr int QPG = 4, W = HD + 2, G = 8;  // heads per kv head, partial row, positions per group
     __shared__ float wp[kBW * QPG * W];
     const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int npos = static_cast<int>(pos[b]) + 1;
     const int chunk = (npos + S - 1) / S;
     const int p0 = s * chunk, p1 = min(npos, p0 + chunk);
-    for (int i = threadIdx.x; i < QPG * HD; i += blockDim.x)
-        q_s[i] = qf[(static_cast<size_t>(b) * H + g * QPG) * HD + i];
-    __syncthreads();
     const float* kc = kv.k + b * kv.seq_stride + layer * kv.layer_stride + static_cast<size_t>(g) * kv.max_seq * HD;
     const float* vc = kv.v + b * kv.seq_stride + layer * kv.layer_stride + static_cast<size_t>(g) * kv.max_seq * HD;
-    float q[QPG][VPL], acc[QPG][VPL], m[QPG], l[QPG];
+    float4 q[QPG], acc[QPG];
+    float m[QPG];
 #pragma unroll
     for (int h = 0; h < QPG; h++) {
+        q[h] = reinterpret_cast<const float4*>(qf + (static_cast<size_t>(b) * H + g * QPG + h) * HD)[lane];
+        acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
         m[h] = -INFINITY;
-        l[h] = 0.f;
-#pragma unroll
-        for (int j = 0; j < VPL; j++) {
-            q[h][j] = q_s[h * HD + lane * VPL + j];
-            acc[h][j] = 0.f;
-        }
     }
-    for (int pb = p0 + warp; pb < p1; pb += kBW * kPF) {
-        float kr[kPF][VPL], vr[kPF][VPL];
+    const int my_h = lane >> 3, my_f = lane & 7;
+    float l_lane = 0.f;  // softmax denominator share of (head my_h, position slot my_f)
+    for (int pb = p0 + warp * G; pb < p1; pb += kBW * G) {
+        float4 kr[G], vr[G];
 #pragma unroll
-        for (int f = 0; f < kPF; f++) {
-            const int p = pb + f * kBW;
-            if (p < p1) {
-                const float4 k4 = __ldcs(reinterpret_cast<const float4*>(kc + static_cast<size_t>(p) * HD) + lane);
-                const float4 v4 = __ldcs(reinterpret_cast<const float4*>(vc + static_cast<size_t>(p) * HD) + lane);
-                kr[f][0] = k4.x; kr[f][1] = k4.y; kr[f][2] = k4.z; kr[f][3] = k4.w;
-                vr[f][0] = v4.x; vr[f][1] = v4.y; vr[f][2] = v4.z; vr[f][3] = v4.w;
+        for (int f = 0; f < G; f++) {
+            if (pb + f < p1) {
+                kr[f] = __ldcs(reinterpret_cast<const float4*>(kc + static_cast<size_t>(pb + f) * HD) + lane);
+                vr[f] = __ldcs(reinterpret_cast<const float4*>(vc + static_cast<size_t>(pb + f) * HD) + lane);
             } else {
-#pragma unroll
-                for (int j = 0; j < VPL; j++) kr[f][j] = vr[f][j] = 0.f;
+                kr[f] = vr[f] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
+        float v[QPG * G];
+#pragma unroll
+        for (int h = 0; h < QPG; h++)
+#pragma unroll
+            for (int f = 0; f < G; f++)
+                v[h * G + f] = q[h].x * kr[f].x + q[h].y * kr[f].y + q[h].z * kr[f].z + q[h].w * kr[f].w;
+        warp_reduce_multi<QPG * G>(v);  // lane l: full dot of (head l / 8, position l % 8)
+        const bool valid = pb + my_f < p1;
+        const float sc = valid ? v[0] * scale : -INFINITY;
+        float gm = sc;
+        gm = fmaxf(gm, __shfl_xor_sync(FULL, gm, 1));
+        gm = fmaxf(gm, __shfl_xor_sync(FULL, gm, 2));
+        gm = fmaxf(gm, __shfl_xor_sync(FULL, gm, 4));
+        float corr[QPG];
 #pragma unroll
         for (int h = 0; h < QPG; h++) {
-            float sc[kPF];
-#pragma unroll
-            for (int f = 0; f < kPF; f++) {
-                float d = 0.f;
-#pragma unroll
-                for (int j = 0; j < VPL; j++) d += kr[f][j] * q[h][j];
-                sc[f] = warp_sum(d) * scale;
-            }
-            float mn = m[h];
-#pragma unroll
-            for (int f = 0; f < kPF; f++)
-                if (pb + f * kBW < p1) mn = fmaxf(mn, sc[f]);
-            const float corr = expf(m[h] - mn);  // m = -inf first: exp(-inf) = 0
-            l[h] *= corr;
-#pragma unroll
-            for (int j = 0; j < VPL; j++) acc[h][j] *= corr;
-#pragma unroll
-            for (int f = 0; f < kPF; f++) {
-                if (pb + f * kBW < p1) {
-                    const float e = expf(sc[f] - mn);
-                    l[h] += e;
-#pragma unroll
-                    for (int j = 0; j < VPL; j++) acc[h][j] = fmaf(e, vr[f][j], acc[h][j]);
-                }
-            }
+            const float mn = fmaxf(m[h], __shfl_sync(FULL, gm, h * G));  // position pb is valid: mn finite
+            corr[h] = expf(m[h] - mn);  // first group: exp(-inf) = 0
             m[h] = mn;
+            acc[h].x *= corr[h]; acc[h].y *= corr[h]; acc[h].z *= corr[h]; acc[h].w *= corr[h];
+        }
+        const float p = valid ? expf(sc - m[my_h]) : 0.f;
+        l_lane = l_lane * corr[my_h] + p;
+#pragma unroll
+        for (int f = 0; f < G; f++) {
+#pragma unroll
+            for (int h = 0; h < QPG; h++) {
+                const float ph = __shfl_sync(FULL, p, h * G + f);
+                acc[h].x = fmaf(ph, vr[f].x, acc[h].x);
+                acc[h].y = fmaf(ph, vr[f].y, acc[h].y);
+                acc[h].z = fmaf(ph, vr[f].z, acc[h].z);
+                acc[h].w = fmaf(ph, vr[f].w, acc[h].w);
+            }
         }
     }
+    // denominators: sum over each head's 8 lanes
+    l_lane += __shfl_xor_sync(FULL, l_lane, 1);
+    l_lane += __shfl_xor_sync(FULL, l_lane, 2);
+    l_lane += __shfl_xor_sync(FULL, l_lane, 4);
 #pragma unroll
     for (int h = 0; h < QPG; h++) {
+        const float lh = __shfl_sync(FULL, l_lane, h * G);
         float* mine = wp + (warp * QPG + h) * W;
         if (lane == 0) {
             mine[0] = m[h];
-            mine[1] = l[h];
+            mine[1] = lh;
         }
-#pragma unroll
-        for (int j = 0; j < VPL; j++) mine[2 + lane * VPL + j] = acc[h][j];
+        *reinterpret_cast<float2*>(mine + 2 + 4 * lane) = make_float2(acc[h].x, acc[h].y);
+        *reinterpret_cast<float2*>(mine + 4 + 4 * lane) = make_float2(acc[h].z, acc[h].w);
     }
     __syncthreads();
     // this split's partial for each of the 4 heads: {M, L, 0, 0, acc[HD]}
@@ -128,18 +134,18 @@ __global__ void __launch_bounds__(kBW * 32) k_attention_decode_batch(float* part
 #pragma unroll
         for (int w = 0; w < kBW; w++)
             if (wp[(w * QPG + h) * W + 1] > 0.f) M = fmaxf(M, wp[(w * QPG + h) * W]);
-        float v = 0.f;
+        float val = 0.f;
         if (i == 0) {
-            v = M;
+            val = M;
         } else if (i == 1 || i >= 4) {
             const int src = (i == 1) ? 1 : i - 2;
 #pragma unroll
             for (int w = 0; w < kBW; w++) {
                 const float* pw = wp + (w * QPG + h) * W;
-                if (pw[1] > 0.f) v += pw[src] * expf(pw[0] - M);
+                if (pw[1] > 0.f) val += pw[src] * expf(pw[0] - M);
             }
         }
-        part[((static_cast<size_t>(b) * H + g * QPG + h) * S + s) * (HD + 4) + i] = v;
+        part[((static_cast<size_t>(b) * H + g * QPG + h) * S + s) * (HD + 4) + i] = val;
     }
 }
 
