@@ -49,6 +49,7 @@ struct GemmArgs {
     void* C;
     int ldc;
     int* err;
+    int ksplit;  // K-block ranges per output tile (1: none); split s stores into C + s * M * ldc
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -218,8 +219,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tm = (g.M + kBM - 1) / kBM, tn = (g.N + BN - 1) / BN, n_tiles = tm * tn;
-    const int nk = g.K / kBK;
+    const int tm = (g.M + kBM - 1) / kBM, tn = (g.N + BN - 1) / BN, n_tiles = tm * tn * g.ksplit;
+    const int nk_all = g.K / kBK, nk_per = (nk_all + g.ksplit - 1) / g.ksplit;
+    // tile -> (m tile fastest, n tile, K split); its K-block range [kb0, kb0 + nk)
+    auto tile_of = [&](int t, int& m0, int& n0, int& kb0, int& nk) {
+        m0 = (t % tm) * kBM;
+        const int r = t / tm;
+        n0 = (r % tn) * BN;
+        kb0 = (r / tn) * nk_per;
+        nk = max(0, min(nk_all, kb0 + nk_per) - kb0);
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
@@ -252,8 +261,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) {
             uint32_t it = 0;
             for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x) {
-                const int m0 = (tile % tm) * kBM, n0 = (tile / tm) * BN;
-                for (int kb = 0; kb < nk; kb++, it++) {
+                int m0, n0, kb0, nk;
+                tile_of(tile, m0, n0, kb0, nk);
+                for (int kb = kb0; kb < kb0 + nk; kb++, it++) {
                     const int s = it % S;
                     if (it >= S && !bar_wait_ab(&empty[s], ((it / S) - 1) & 1, abort_flag)) {
                         fail(1);
@@ -282,6 +292,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t dt = tmem + static_cast<uint32_t>(buf * BN);
+                int m0, n0, kb0, nk;
+                tile_of(tile, m0, n0, kb0, nk);
                 bool ok = true;
                 for (int kb = 0; kb < nk; kb++, it++) {
                     const int s = it % S;
@@ -313,8 +325,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             tc_fence_after();
             if (*abort_flag) break;
-            gemm_epilogue<BN, EPI>(g, tmem + static_cast<uint32_t>(buf * BN), (tile % tm) * kBM, (tile / tm) * BN,
-                                   sub, lane);
+            int m0, n0, kb0, nk;
+            tile_of(tile, m0, n0, kb0, nk);
+            GemmArgs gs = g;  // a K split stores into its own slice
+            if (g.ksplit > 1)
+                gs.C = static_cast<float*>(g.C) + static_cast<size_t>(kb0 / nk_per) * g.M * g.ldc;
+            gemm_epilogue<BN, EPI>(gs, tmem + static_cast<uint32_t>(buf * BN), m0, n0, sub, lane);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&tempty[buf])) : "memory");
@@ -325,6 +341,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+    }
+}
+
+// c[m, n] (+)= sum over the K splits, in split order (deterministic).
+__global__ void k_splitk_reduce(float* c, int ldc, const float* part, int M, int N, int ksplit, int add) {
+    const size_t total = static_cast<size_t>(M) * N;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        float v = 0.f;
+        for (int s = 0; s < ksplit; s++) v += part[s * total + i];
+        const size_t m = i / N, n = i % N;
+        float* dst = c + m * ldc + n;
+        *dst = add ? *dst + v : v;
     }
 }
 
@@ -359,7 +387,7 @@ tl_status encode_kmajor(CUtensorMap* map, const __half* ptr, int rows, int K, in
 
 template <int BN, int EPI>
 tl_status launch_gemm(const __half* A, int M, int K, const __half* B, int N, void* C, int ldc, int* err,
-                      cudaStream_t s) {
+                      cudaStream_t s, int ksplit = 1) {
     CUtensorMap ta, tb;
     TL_TRY(encode_kmajor(&ta, A, M, K, kBM));
     TL_TRY(encode_kmajor(&tb, B, N, K, BN));
@@ -372,9 +400,9 @@ tl_status launch_gemm(const __half* A, int M, int K, const __half* B, int N, voi
     });
     if (attr_err != cudaSuccess)
         return set_error(TL_ERR_CUDA, "gemm smem attribute: %s", cudaGetErrorString(attr_err));
-    const int tiles = ((N + BN - 1) / BN) * ((M + kBM - 1) / kBM);
+    const int tiles = ((N + BN - 1) / BN) * ((M + kBM - 1) / kBM) * ksplit;
     const int grid = std::min(tiles, sm_count());
-    GemmArgs g{M, N, K, C, ldc, err};
+    GemmArgs g{M, N, K, C, ldc, err, ksplit};
     kern<<<grid, kGemmThreads, GemmCfg<BN>::kSmem, s>>>(ta, tb, g);
     return check_launch("gemm_tc");
 }
@@ -382,12 +410,28 @@ tl_status launch_gemm(const __half* A, int M, int K, const __half* B, int N, voi
 }  // namespace
 
 tl_status gemm_f16(int epi, const __half* A, int M, int K, const __half* B, int N, void* C, int ldc, int* err,
-                   cudaStream_t s) {
+                   cudaStream_t s, float* scratch, size_t scratch_floats) {
     TL_REQUIRE(A && B && C && M > 0 && N > 0 && K > 0, "gemm: bad arguments");
     TL_REQUIRE(K % kBK == 0, "gemm: K = %d must be a multiple of %d", K, kBK);
     TL_REQUIRE(((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) &
                 15) == 0,
                "gemm: operands must be 16-byte aligned");
+    if ((epi == kEpiStoreF32 || epi == kEpiAddF32) && scratch) {
+        // few output tiles (small M): split K so that every SM streams weights
+        const int tiles = ((N + 255) / 256) * ((M + kBM - 1) / kBM);
+        const int nk = K / kBK;
+        int ks = std::min({8, sm_count() / std::max(1, tiles), nk / 4});
+        while (ks > 1 && static_cast<size_t>(ks) * M * N > scratch_floats) ks--;
+        if (ks > 1) ks = (nk + (nk + ks - 1) / ks - 1) / ((nk + ks - 1) / ks);  // no empty K range
+        if (ks > 1) {
+            TL_REQUIRE(ldc >= N && ldc % 4 == 0, "gemm: ldc");
+            TL_TRY((launch_gemm<256, kEpiStoreF32>(A, M, K, B, N, scratch, N, err, s, ks)));
+            const size_t total = static_cast<size_t>(M) * N;
+            k_splitk_reduce<<<static_cast<int>(std::min<size_t>((total + 255) / 256, 2048)), 256, 0, s>>>(
+                static_cast<float*>(C), ldc, scratch, M, N, ks, epi == kEpiAddF32 ? 1 : 0);
+            return check_launch("splitk_reduce");
+        }
+    }
     switch (epi) {
         case kEpiStoreF32:
             TL_REQUIRE(ldc >= N && ldc % 4 == 0, "gemm: ldc");
@@ -415,7 +459,7 @@ tl_status tl_gemm_f16(void* c, const void* a, const void* b, size_t m, size_t n,
     TL_REQUIRE(m < (1u << 30) && n < (1u << 30) && k < (1u << 30) && ldc < (1u << 30), "tl_gemm_f16: sizes");
     return gemm_f16(epilogue, static_cast<const __half*>(a), static_cast<int>(m), static_cast<int>(k),
                     static_cast<const __half*>(b), static_cast<int>(n), c, static_cast<int>(ldc), nullptr,
-                    as_stream(stream));
+                    as_stream(stream), nullptr, 0);
 }
 
 }  // extern "C"

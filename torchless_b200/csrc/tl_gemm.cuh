@@ -20,8 +20,10 @@ enum GemmEpilogue : int {
 
 // Shapes: K % 64 == 0, A / B / C 16-byte aligned; any M, N (tails masked).
 // `err` (device int, may be null) receives a nonzero code if a bounded
-// device-side wait gave up.
+// device-side wait gave up.  With `scratch` (fp32, scratch_floats of it), a
+// store / add GEMM with too few output tiles to fill the GPU (small M) splits
+// K and reduces the splits in a fixed order.
 tl_status gemm_f16(int epilogue, const __half* A, int M, int K, const __half* B, int N, void* C, int ldc, int* err,
-                   cudaStream_t s);
+                   cudaStream_t s, float* scratch = nullptr, size_t scratch_floats = 0);
 
 }  // namespace tl

@@ -1263,6 +1263,8 @@ struct tl_batch {
     float *hres = nullptr, *qkv = nullptr, *qf = nullptr, *part = nullptr, *logits = nullptr;
     __half *x16 = nullptr, *ctx16 = nullptr, *act16 = nullptr;
     uint32_t *tok = nullptr, *pos = nullptr, *next = nullptr;
+    float* split = nullptr;  // split-K partials of the small-M GEMMs
+    size_t split_floats = 0;
     uint32_t* h_pinned = nullptr;       // [B]
     std::vector<size_t> pos_host;
 };
@@ -1286,15 +1288,15 @@ tl_status batch_step(tl_batch* b) {
         const LayerW& w = m->layers[l];
         const auto& W = m->lw16[l];
         TL_TRY(rmsnorm_rows_f16(b->x16, b->hres, w.g_in, B, D, s));
-        TL_TRY(gemm_f16(kEpiStoreF32, b->x16, B, D, W[0], NQKV, b->qkv, NQKV, m->err, s));
+        TL_TRY(gemm_f16(kEpiStoreF32, b->x16, B, D, W[0], NQKV, b->qkv, NQKV, m->err, s, b->split, b->split_floats));
         TL_TRY(rope_cache_batch(b->qf, b->qkv, b->bkv, static_cast<int>(l), b->pos, m->cos_tab, m->sin_tab, B, H, KV,
                                 HD, s));
         TL_TRY(attention_decode_batch(b->part, b->qf, b->bkv, static_cast<int>(l), b->pos, B, H, KV, HD, S, scale, s));
         TL_TRY(attention_merge_batch(b->ctx16, b->part, B, H, HD, S, s));
-        TL_TRY(gemm_f16(kEpiAddF32, b->ctx16, B, H * HD, W[1], D, b->hres, D, m->err, s));
+        TL_TRY(gemm_f16(kEpiAddF32, b->ctx16, B, H * HD, W[1], D, b->hres, D, m->err, s, b->split, b->split_floats));
         TL_TRY(rmsnorm_rows_f16(b->x16, b->hres, w.g_post, B, D, s));
         TL_TRY(gemm_f16(kEpiSwiGluF16, b->x16, B, D, W[2], 2 * F, b->act16, F, m->err, s));
-        TL_TRY(gemm_f16(kEpiAddF32, b->act16, B, F, W[3], D, b->hres, D, m->err, s));
+        TL_TRY(gemm_f16(kEpiAddF32, b->act16, B, F, W[3], D, b->hres, D, m->err, s, b->split, b->split_floats));
     }
     TL_TRY(rmsnorm_rows_f16(b->x16, b->hres, m->norm, B, D, s));
     TL_TRY(gemm_f16(kEpiStoreF32, b->x16, B, D, m->lm16, V, b->logits, V, m->err, s));
@@ -1350,9 +1352,11 @@ tl_status tl_batch_create(tl_model* m, int n_seq, size_t max_seq, tl_batch** out
     b->bkv.layer_stride = layer;
     b->bkv.max_seq = static_cast<int>(max_seq);
     const size_t Bn = n_seq;
+    b->split_floats = 8 * Bn * static_cast<size_t>(std::max<int64_t>(NQKV, D));
     TL_TRY(b->rows.reserve(A::pad(Bn * D * 4) + A::pad(Bn * NQKV * 4) + A::pad(Bn * H * HD * 4) +
                            A::pad(Bn * H * b->S * (HD + 4) * 4) + A::pad(Bn * V * 4) + A::pad(Bn * D * 2) +
-                           A::pad(Bn * H * HD * 2) + A::pad(Bn * F * 2) + 3 * A::pad(Bn * 4)));
+                           A::pad(Bn * H * HD * 2) + A::pad(Bn * F * 2) + 3 * A::pad(Bn * 4) +
+                           A::pad(b->split_floats * 4)));
     b->hres = b->rows.take<float>(Bn * D);
     b->qkv = b->rows.take<float>(Bn * NQKV);
     b->qf = b->rows.take<float>(Bn * H * HD);
@@ -1364,7 +1368,8 @@ tl_status tl_batch_create(tl_model* m, int n_seq, size_t max_seq, tl_batch** out
     b->tok = b->rows.take<uint32_t>(Bn);
     b->pos = b->rows.take<uint32_t>(Bn);
     b->next = b->rows.take<uint32_t>(Bn);
-    if (!b->next) return set_error(TL_ERR_OUT_OF_MEMORY, "tl_batch rows (internal)");
+    b->split = b->rows.take<float>(b->split_floats);
+    if (!b->split) return set_error(TL_ERR_OUT_OF_MEMORY, "tl_batch rows (internal)");
     TL_CUDA_TRY(cudaMemsetAsync(b->pos, 0, Bn * 4, m->stream));
     TL_CUDA_TRY(cudaMallocHost(&b->h_pinned, Bn * 4));
     b->pos_host.assign(Bn, 0);
