@@ -9,28 +9,31 @@
 namespace tl {
 namespace {
 
-__global__ void k_rope_cache_batch(float* qf, const float* qkv, BatchKV kv, int layer, const uint32_t* pos,
-                                   const float* cos_tab, const float* sin_tab, int H, int KV, int HD) {
-    const int b = blockIdx.x, half = HD / 2;
+// Block (b, head slot hh), thread c < hd / 2: element pair (c, c + hd / 2) of
+// q|k|v slot hh of row b, summed over the K-split partials in order.
+__global__ void k_rope_cache_batch(float* qf, const float* part, int ks, size_t part_stride, BatchKV kv, int layer,
+                                   const uint32_t* pos, const float* cos_tab, const float* sin_tab, int H, int KV,
+                                   int HD) {
+    const int b = blockIdx.x, hh = blockIdx.y, c = threadIdx.x, half = HD / 2;
     const int p = static_cast<int>(pos[b]);
-    const float* row = qkv + static_cast<size_t>(b) * (H + 2 * KV) * HD;
-    const float* ct = cos_tab + static_cast<size_t>(p) * half;
-    const float* st = sin_tab + static_cast<size_t>(p) * half;
-    float* kc = kv.k + b * kv.seq_stride + layer * kv.layer_stride;
-    float* vc = kv.v + b * kv.seq_stride + layer * kv.layer_stride;
-    for (int k = threadIdx.x; k < (H + KV) * half; k += blockDim.x) {
-        const int hh = k / half, c = k % half;
-        const float x = row[hh * HD + c], y = row[hh * HD + c + half];
-        const float cc = ct[c], sn = st[c];
+    const float* row = part + static_cast<size_t>(b) * (H + 2 * KV) * HD + hh * HD;
+    float x = 0.f, y = 0.f;
+    for (int r = 0; r < ks; r++) {
+        x += row[r * part_stride + c];
+        y += row[r * part_stride + c + half];
+    }
+    const size_t cache = b * kv.seq_stride + layer * kv.layer_stride;
+    if (hh < H + KV) {
+        const float cc = cos_tab[static_cast<size_t>(p) * half + c], sn = sin_tab[static_cast<size_t>(p) * half + c];
         const float xr = x * cc - y * sn, yr = x * sn + y * cc;
         float* dst = (hh < H) ? qf + (static_cast<size_t>(b) * H + hh) * HD
-                              : kc + (static_cast<size_t>(hh - H) * kv.max_seq + p) * HD;
+                              : kv.k + cache + (static_cast<size_t>(hh - H) * kv.max_seq + p) * HD;
         dst[c] = xr;
         dst[c + half] = yr;
-    }
-    for (int k = threadIdx.x; k < KV * HD; k += blockDim.x) {
-        const int kh = k / HD, c = k % HD;
-        vc[(static_cast<size_t>(kh) * kv.max_seq + p) * HD + c] = row[(H + KV) * HD + k];
+    } else {
+        float* dst = kv.v + cache + (static_cast<size_t>(hh - H - KV) * kv.max_seq + p) * HD;
+        dst[c] = x;
+        dst[c + half] = y;
     }
 }
 
@@ -246,9 +249,12 @@ int grid_of(size_t n, int per) { return static_cast<int>(std::min<size_t>((n + p
 
 }  // namespace
 
-tl_status rope_cache_batch(float* qf, const float* qkv, const BatchKV& kv, int layer, const uint32_t* pos,
-                           const float* cos_tab, const float* sin_tab, int B, int H, int KV, int HD, cudaStream_t s) {
-    k_rope_cache_batch<<<B, 128, 0, s>>>(qf, qkv, kv, layer, pos, cos_tab, sin_tab, H, KV, HD);
+tl_status rope_cache_batch(float* qf, const float* part, int ks, size_t part_stride, const BatchKV& kv, int layer,
+                           const uint32_t* pos, const float* cos_tab, const float* sin_tab, int B, int H, int KV,
+                           int HD, cudaStream_t s) {
+    TL_REQUIRE(ks >= 1 && HD % 2 == 0 && HD <= 2048, "rope_cache_batch: ks %d, head_dim %d", ks, HD);
+    k_rope_cache_batch<<<dim3(B, H + 2 * KV), HD / 2, 0, s>>>(qf, part, ks, part_stride, kv, layer, pos, cos_tab,
+                                                               sin_tab, H, KV, HD);
     return check_launch("rope_cache_batch");
 }
 

@@ -21,11 +21,14 @@ struct BatchKV {
     int max_seq;
 };
 
-// Row b of qkv [B, (H + 2 KV) hd] at position pos[b]: RoPE (kernels.cpp:78-95)
-// on its q and k heads; k and v pushed into sequence b's cache of `layer`
-// (inference_state.h:38-43); rotated q as fp32 qf [B, H hd].
-tl_status rope_cache_batch(float* qf, const float* qkv, const BatchKV& kv, int layer, const uint32_t* pos,
-                           const float* cos_tab, const float* sin_tab, int B, int H, int KV, int HD, cudaStream_t s);
+// Row b of qkv [B, (H + 2 KV) hd] = part_0 + ... + part_{ks-1} (the q|k|v
+// GEMM's split-K partials, part_r = part + r part_stride, summed in order) at
+// position pos[b]: RoPE (kernels.cpp:78-95) on its q and k heads; k and v
+// pushed into sequence b's cache of `layer` (inference_state.h:38-43); rotated
+// q as fp32 qf [B, H hd].
+tl_status rope_cache_batch(float* qf, const float* part, int ks, size_t part_stride, const BatchKV& kv, int layer,
+                           const uint32_t* pos, const float* cos_tab, const float* sin_tab, int B, int H, int KV,
+                           int HD, cudaStream_t s);
 
 // Attention (modules.cpp:58-88) of each sequence's new query over its cache
 // positions [0, pos[b]] in S splits; CTA (b, kv head g, split) serves the 4 q

@@ -344,18 +344,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
 }
 
-// c[m, n] (+)= sum over the K splits, in split order (deterministic).
-__global__ void k_splitk_reduce(float* c, int ldc, const float* part, int M, int N, int ksplit, int add) {
-    const size_t total = static_cast<size_t>(M) * N;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        float v = 0.f;
-        for (int s = 0; s < ksplit; s++) v += part[s * total + i];
-        const size_t m = i / N, n = i % N;
-        float* dst = c + m * ldc + n;
-        *dst = add ? *dst + v : v;
-    }
-}
-
 // cuTensorMapEncodeTiled through the runtime's driver entry point.
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -410,28 +398,12 @@ tl_status launch_gemm(const __half* A, int M, int K, const __half* B, int N, voi
 }  // namespace
 
 tl_status gemm_f16(int epi, const __half* A, int M, int K, const __half* B, int N, void* C, int ldc, int* err,
-                   cudaStream_t s, float* scratch, size_t scratch_floats) {
+                   cudaStream_t s) {
     TL_REQUIRE(A && B && C && M > 0 && N > 0 && K > 0, "gemm: bad arguments");
     TL_REQUIRE(K % kBK == 0, "gemm: K = %d must be a multiple of %d", K, kBK);
     TL_REQUIRE(((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) &
                 15) == 0,
                "gemm: operands must be 16-byte aligned");
-    if ((epi == kEpiStoreF32 || epi == kEpiAddF32) && scratch) {
-        // few output tiles (small M): split K so that every SM streams weights
-        const int tiles = ((N + 255) / 256) * ((M + kBM - 1) / kBM);
-        const int nk = K / kBK;
-        int ks = std::min({8, sm_count() / std::max(1, tiles), nk / 4});
-        while (ks > 1 && static_cast<size_t>(ks) * M * N > scratch_floats) ks--;
-        if (ks > 1) ks = (nk + (nk + ks - 1) / ks - 1) / ((nk + ks - 1) / ks);  // no empty K range
-        if (ks > 1) {
-            TL_REQUIRE(ldc >= N && ldc % 4 == 0, "gemm: ldc");
-            TL_TRY((launch_gemm<256, kEpiStoreF32>(A, M, K, B, N, scratch, N, err, s, ks)));
-            const size_t total = static_cast<size_t>(M) * N;
-            k_splitk_reduce<<<static_cast<int>(std::min<size_t>((total + 255) / 256, 2048)), 256, 0, s>>>(
-                static_cast<float*>(C), ldc, scratch, M, N, ks, epi == kEpiAddF32 ? 1 : 0);
-            return check_launch("splitk_reduce");
-        }
-    }
     switch (epi) {
         case kEpiStoreF32:
             TL_REQUIRE(ldc >= N && ldc % 4 == 0, "gemm: ldc");
@@ -447,6 +419,26 @@ tl_status gemm_f16(int epi, const __half* A, int M, int K, const __half* B, int 
     }
 }
 
+tl_status gemm_f16_splitk(const __half* A, int M, int K, const __half* B, int N, float* part, size_t part_floats,
+                          int* ksplit, int* err, cudaStream_t s) {
+    TL_REQUIRE(A && B && part && ksplit && M > 0 && N > 0 && K > 0, "gemm splitk: bad arguments");
+    TL_REQUIRE(K % kBK == 0 && N % 4 == 0, "gemm splitk: K = %d (multiple of %d), N = %d (multiple of 4)", K, kBK, N);
+    TL_REQUIRE(((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(part)) &
+                15) == 0,
+               "gemm splitk: operands must be 16-byte aligned");
+    TL_REQUIRE(static_cast<size_t>(M) * N <= part_floats, "gemm splitk: part holds %zu floats, %zu needed",
+               part_floats, static_cast<size_t>(M) * N);
+    // enough (output tile, K range) pairs for every SM; each range >= 4 K blocks and none empty
+    const int tiles = ((N + 255) / 256) * ((M + kBM - 1) / kBM);
+    const int nk = K / kBK;
+    int ks = std::max(1, std::min({8, sm_count() / std::max(1, tiles), nk / 4}));
+    while (ks > 1 && static_cast<size_t>(ks) * M * N > part_floats) ks--;
+    const int per = (nk + ks - 1) / ks;
+    ks = (nk + per - 1) / per;
+    *ksplit = ks;
+    return launch_gemm<256, kEpiStoreF32>(A, M, K, B, N, part, N, err, s, ks);
+}
+
 }  // namespace tl
 
 using namespace tl;
@@ -459,7 +451,7 @@ tl_status tl_gemm_f16(void* c, const void* a, const void* b, size_t m, size_t n,
     TL_REQUIRE(m < (1u << 30) && n < (1u << 30) && k < (1u << 30) && ldc < (1u << 30), "tl_gemm_f16: sizes");
     return gemm_f16(epilogue, static_cast<const __half*>(a), static_cast<int>(m), static_cast<int>(k),
                     static_cast<const __half*>(b), static_cast<int>(n), c, static_cast<int>(ldc), nullptr,
-                    as_stream(stream), nullptr, 0);
+                    as_stream(stream));
 }
 
 }  // extern "C"

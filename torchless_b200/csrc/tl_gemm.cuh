@@ -20,10 +20,15 @@ enum GemmEpilogue : int {
 
 // Shapes: K % 64 == 0, A / B / C 16-byte aligned; any M, N (tails masked).
 // `err` (device int, may be null) receives a nonzero code if a bounded
-// device-side wait gave up.  With `scratch` (fp32, scratch_floats of it), a
-// store / add GEMM with too few output tiles to fill the GPU (small M) splits
-// K and reduces the splits in a fixed order.
+// device-side wait gave up.
 tl_status gemm_f16(int epilogue, const __half* A, int M, int K, const __half* B, int N, void* C, int ldc, int* err,
-                   cudaStream_t s, float* scratch = nullptr, size_t scratch_floats = 0);
+                   cudaStream_t s);
+
+// Split-K for few output tiles (small M): K is cut into *ksplit ranges (chosen
+// here, 1..8, so that the (tile, range) pairs fill the SMs) and range r stores
+// its product into part + r M N ([M, N] row-major fp32).  The consumer sums
+// the ranges in order r = 0, 1, ... (fused into its own kernel).
+tl_status gemm_f16_splitk(const __half* A, int M, int K, const __half* B, int N, float* part, size_t part_floats,
+                          int* ksplit, int* err, cudaStream_t s);
 
 }  // namespace tl

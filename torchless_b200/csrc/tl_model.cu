@@ -1260,7 +1260,7 @@ struct tl_batch {
     size_t max_seq = 0;
     DeviceArena kv, rows;
     BatchKV bkv = {};
-    float *hres = nullptr, *qkv = nullptr, *qf = nullptr, *part = nullptr, *logits = nullptr;
+    float *hres = nullptr, *qf = nullptr, *part = nullptr, *logits = nullptr;
     __half *x16 = nullptr, *ctx16 = nullptr, *act16 = nullptr;
     uint32_t *tok = nullptr, *pos = nullptr, *next = nullptr;
     float* split = nullptr;  // split-K partials of the small-M GEMMs
@@ -1283,22 +1283,27 @@ tl_status batch_step(tl_batch* b) {
     size_t maxp = 0;
     for (size_t p : b->pos_host) maxp = std::max(maxp, p);
     const int S = std::max(1, std::min(b->S, static_cast<int>((maxp + 1 + 511) / 512)));  // >= 512 positions a split
+    // q|k|v, o and down run split-K (B rows fill few output tiles); their
+    // consumers (RoPE, residual + RMSNorm) sum the partials
+    const size_t qkv_stride = static_cast<size_t>(B) * NQKV, d_stride = static_cast<size_t>(B) * D;
+    int ks = 0;
     TL_TRY(embed_rows(b->hres, m->embed, b->tok, B, D, s));
+    TL_TRY(residual_rmsnorm_rows(b->x16, b->hres, nullptr, 0, 0, m->layers[0].g_in, B, D, s));
     for (size_t l = 0; l < m->cfg.n_layers; l++) {
         const LayerW& w = m->layers[l];
         const auto& W = m->lw16[l];
-        TL_TRY(rmsnorm_rows_f16(b->x16, b->hres, w.g_in, B, D, s));
-        TL_TRY(gemm_f16(kEpiStoreF32, b->x16, B, D, W[0], NQKV, b->qkv, NQKV, m->err, s, b->split, b->split_floats));
-        TL_TRY(rope_cache_batch(b->qf, b->qkv, b->bkv, static_cast<int>(l), b->pos, m->cos_tab, m->sin_tab, B, H, KV,
-                                HD, s));
+        TL_TRY(gemm_f16_splitk(b->x16, B, D, W[0], NQKV, b->split, b->split_floats, &ks, m->err, s));
+        TL_TRY(rope_cache_batch(b->qf, b->split, ks, qkv_stride, b->bkv, static_cast<int>(l), b->pos, m->cos_tab,
+                                m->sin_tab, B, H, KV, HD, s));
         TL_TRY(attention_decode_batch(b->part, b->qf, b->bkv, static_cast<int>(l), b->pos, B, H, KV, HD, S, scale, s));
         TL_TRY(attention_merge_batch(b->ctx16, b->part, B, H, HD, S, s));
-        TL_TRY(gemm_f16(kEpiAddF32, b->ctx16, B, H * HD, W[1], D, b->hres, D, m->err, s, b->split, b->split_floats));
-        TL_TRY(rmsnorm_rows_f16(b->x16, b->hres, w.g_post, B, D, s));
+        TL_TRY(gemm_f16_splitk(b->ctx16, B, H * HD, W[1], D, b->split, b->split_floats, &ks, m->err, s));
+        TL_TRY(residual_rmsnorm_rows(b->x16, b->hres, b->split, ks, d_stride, w.g_post, B, D, s));
         TL_TRY(gemm_f16(kEpiSwiGluF16, b->x16, B, D, W[2], 2 * F, b->act16, F, m->err, s));
-        TL_TRY(gemm_f16(kEpiAddF32, b->act16, B, F, W[3], D, b->hres, D, m->err, s, b->split, b->split_floats));
+        TL_TRY(gemm_f16_splitk(b->act16, B, F, W[3], D, b->split, b->split_floats, &ks, m->err, s));
+        const float* g_next = l + 1 < m->cfg.n_layers ? m->layers[l + 1].g_in : m->norm;
+        TL_TRY(residual_rmsnorm_rows(b->x16, b->hres, b->split, ks, d_stride, g_next, B, D, s));
     }
-    TL_TRY(rmsnorm_rows_f16(b->x16, b->hres, m->norm, B, D, s));
     TL_TRY(gemm_f16(kEpiStoreF32, b->x16, B, D, m->lm16, V, b->logits, V, m->err, s));
     TL_TRY(argmax_rows(b->next, b->logits, B, V, b->pos, s));
     for (auto& p : b->pos_host) p++;
@@ -1353,12 +1358,11 @@ tl_status tl_batch_create(tl_model* m, int n_seq, size_t max_seq, tl_batch** out
     b->bkv.max_seq = static_cast<int>(max_seq);
     const size_t Bn = n_seq;
     b->split_floats = 8 * Bn * static_cast<size_t>(std::max<int64_t>(NQKV, D));
-    TL_TRY(b->rows.reserve(A::pad(Bn * D * 4) + A::pad(Bn * NQKV * 4) + A::pad(Bn * H * HD * 4) +
+    TL_TRY(b->rows.reserve(A::pad(Bn * D * 4) + A::pad(Bn * H * HD * 4) +
                            A::pad(Bn * H * b->S * (HD + 4) * 4) + A::pad(Bn * V * 4) + A::pad(Bn * D * 2) +
                            A::pad(Bn * H * HD * 2) + A::pad(Bn * F * 2) + 3 * A::pad(Bn * 4) +
                            A::pad(b->split_floats * 4)));
     b->hres = b->rows.take<float>(Bn * D);
-    b->qkv = b->rows.take<float>(Bn * NQKV);
     b->qf = b->rows.take<float>(Bn * H * HD);
     b->part = b->rows.take<float>(Bn * H * b->S * (HD + 4));
     b->logits = b->rows.take<float>(Bn * V);

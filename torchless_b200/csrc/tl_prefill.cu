@@ -49,15 +49,47 @@ __global__ void k_embed_rows(float* h, const float* embed, const uint32_t* token
     }
 }
 
-__global__ void k_rmsnorm_rows_f16(__half* x16, const float* h, const float* g, int D) {
+constexpr int kNormVec = 4;  // float4 columns a thread holds: rows up to 4 x 4 x 1024 = 16384 wide
+
+// One CTA per row; thread t owns float4 columns t, t + blockDim, ...  With
+// ks > 0 the row first takes its residual add: h += (part_0 + part_1 + ...).
+__global__ void k_residual_rmsnorm_rows(__half* x16, float* h, const float* part, int ks, size_t part_stride,
+                                        const float* g, int D) {
     __shared__ float red[32];
-    const float* x = h + static_cast<size_t>(blockIdx.x) * D;
+    const int n4 = D / 4;
+    float4* hr = reinterpret_cast<float4*>(h + static_cast<size_t>(blockIdx.x) * D);
+    const float4* pr = reinterpret_cast<const float4*>(part + static_cast<size_t>(blockIdx.x) * D);
+    float4 v[kNormVec];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < D; i += blockDim.x) ss += x[i] * x[i];
+#pragma unroll
+    for (int j = 0; j < kNormVec; j++) {
+        const int c = threadIdx.x + j * blockDim.x;
+        if (c >= n4) break;
+        float4 x = hr[c];
+        if (ks > 0) {
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = 0; r < ks; r++) {
+                const float4 p = pr[r * (part_stride / 4) + c];
+                a.x += p.x; a.y += p.y; a.z += p.z; a.w += p.w;
+            }
+            x.x += a.x; x.y += a.y; x.z += a.z; x.w += a.w;
+            hr[c] = x;
+        }
+        v[j] = x;
+        ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+    }
     ss = block_sum(ss, red);
     const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + 1e-5f);
-    __half* y = x16 + static_cast<size_t>(blockIdx.x) * D;
-    for (int i = threadIdx.x; i < D; i += blockDim.x) y[i] = __float2half_rn((x[i] * inv) * g[i]);
+    uint2* y = reinterpret_cast<uint2*>(x16 + static_cast<size_t>(blockIdx.x) * D);
+#pragma unroll
+    for (int j = 0; j < kNormVec; j++) {
+        const int c = threadIdx.x + j * blockDim.x;
+        if (c >= n4) break;
+        const float* gc = g + 4 * c;
+        __half2 o[2] = {__floats2half2_rn((v[j].x * inv) * gc[0], (v[j].y * inv) * gc[1]),
+                        __floats2half2_rn((v[j].z * inv) * gc[2], (v[j].w * inv) * gc[3])};
+        y[c] = *reinterpret_cast<const uint2*>(o);
+    }
 }
 
 __global__ void k_rope_cache_rows(__half* q16, const float* qkv, float* kc, float* vc, const float* cos_tab,
@@ -311,8 +343,20 @@ tl_status embed_rows(float* h, const float* embed, const uint32_t* tokens, int M
 }
 
 tl_status rmsnorm_rows_f16(__half* x16, const float* h, const float* g, int M, int D, cudaStream_t s) {
-    k_rmsnorm_rows_f16<<<M, 256, 0, s>>>(x16, h, g, D);
-    return check_launch("rmsnorm_rows_f16");
+    return residual_rmsnorm_rows(x16, const_cast<float*>(h), nullptr, 0, 0, g, M, D, s);
+}
+
+tl_status residual_rmsnorm_rows(__half* x16, float* h, const float* part, int ks, size_t part_stride, const float* g,
+                                int M, int D, cudaStream_t s) {
+    const int n4 = D / 4;
+    const int threads = std::min(1024, (n4 + 31) / 32 * 32);
+    TL_REQUIRE(D % 4 == 0 && n4 <= kNormVec * threads, "rmsnorm rows: width %d (multiple of 4, at most %d)", D,
+               kNormVec * 4 * 1024);
+    TL_REQUIRE(((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(part)) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(x16) & 7) == 0 && part_stride % 4 == 0 && (ks == 0 || part),
+               "rmsnorm rows: alignment");
+    k_residual_rmsnorm_rows<<<M, threads, 0, s>>>(x16, h, part, ks, part_stride, g, D);
+    return check_launch("residual_rmsnorm_rows");
 }
 
 tl_status rope_cache_rows(__half* q16, const float* qkv, float* k_cache, float* v_cache, const float* cos_tab,

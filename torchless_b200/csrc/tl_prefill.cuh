@@ -27,6 +27,13 @@ tl_status embed_rows(float* h, const float* embed, const uint32_t* tokens, int M
 // x16[i, :] = fp16(h[i, :] * (1 / sqrt(sum h^2 / D + 1e-5)) * g)   (RMSNorm, modules.cpp:31-46)
 tl_status rmsnorm_rows_f16(__half* x16, const float* h, const float* g, int M, int D, cudaStream_t s);
 
+// Residual add fused with the next RMSNorm: h[i, :] += part_0[i, :] + ... +
+// part_{ks-1}[i, :] (split-K partials of the producing GEMM, part_r = part +
+// r part_stride, summed in order; modules.cpp:128, 142), then x16 as in
+// rmsnorm_rows_f16.  ks = 0 leaves h as it is.  D % 4 == 0, D <= 16384.
+tl_status residual_rmsnorm_rows(__half* x16, float* h, const float* part, int ks, size_t part_stride, const float* g,
+                                int M, int D, cudaStream_t s);
+
 // Row i (position p0 + i) of qkv [M, (H + 2 KV) hd]: RoPE on its q and k heads
 // (kernels.cpp:78-95, tables at the position), k and v rows pushed into the
 // layer's cache (inference_state.h:38-43), rotated q written as fp16 q16 [M, H hd].
