@@ -155,14 +155,46 @@ def test_mistral7b_shapes_two_layers(m7b_two_layers, mode):
     m.close()
 
 
-def test_persistent_and_per_op_agree_at_long_positions(small_bin):
+# Persistent-kernel attention variants: per-head CTAs (the default below
+# 1024 positions), and GQA CTAs (one per kv group and split) from the first
+# position with 16 positions per split, so 200 positions run up to 13 splits
+# merged by the last split of each group.
+ATTN_ENV = {"per_head": {}, "gqa": {"TL_DECODE_GQA_FROM": "0", "TL_DECODE_GQA_ROWS": "16"}}
+
+
+@pytest.mark.parametrize("attn", list(ATTN_ENV))
+def test_persistent_and_per_op_agree_at_long_positions(small_bin, attn, monkeypatch):
     """Both decode paths over 200 positions (attention spans many splits)."""
+    for k, v in ATTN_ENV[attn].items():
+        monkeypatch.setenv(k, v)
     a = load(small_bin, max_seq=256, kernel_mode=0)
     b = load(small_bin, max_seq=256, kernel_mode=1)
     rng = np.random.default_rng(5)
     toks = rng.integers(0, 1000, 200).tolist()
     worst = 0.0
     for t in toks:
+        la, _ = a.forward(t)
+        lb, _ = b.forward(t)
+        worst = max(worst, rel_err(la, lb))
+    assert worst < 1e-4, worst
+    for layer, pos in [(0, 0), (1, 99), (1, 199)]:  # KV pushed by both paths
+        ka, va = a.read_kv(layer, pos)
+        kb, vb = b.read_kv(layer, pos)
+        assert rel_err(ka, kb) < 1e-5 and rel_err(va, vb) < 1e-5, (layer, pos)
+    a.close()
+    b.close()
+
+
+def test_gqa_attention_mistral7b_shapes(m7b_two_layers, monkeypatch):
+    """GQA attention at Mistral-7B head counts (8 kv groups x 4 q heads) with
+    up to 5 splits per group, against the per-op path, 40 steps."""
+    monkeypatch.setenv("TL_DECODE_GQA_FROM", "0")
+    monkeypatch.setenv("TL_DECODE_GQA_ROWS", "8")
+    a = load(m7b_two_layers, max_seq=64, kernel_mode=0)
+    b = load(m7b_two_layers, max_seq=64, kernel_mode=1)
+    rng = np.random.default_rng(9)
+    worst = 0.0
+    for t in rng.integers(0, 32000, 40).tolist():
         la, _ = a.forward(t)
         lb, _ = b.forward(t)
         worst = max(worst, rel_err(la, lb))

@@ -198,6 +198,8 @@ __host__ __device__ inline size_t xbuf_bytes(int D, int F, int HD) {
     if (4 * static_cast<size_t>(D) > x) x = 4 * static_cast<size_t>(D);
     const size_t attn = (3 * HD + kConsumerWarps * (HD + 2)) * 4;  // q, k, v + warp partials
     if (attn > x) x = attn;
+    const size_t gqa = (6 * HD + kConsumerWarps * 4 * (HD + 2)) * 4;  // 4 q, k, v + 4 heads' warp partials
+    if (HD == 128 && gqa > x) x = gqa;
     return align_up(x, 128);
 }
 
@@ -957,9 +959,39 @@ struct Consumer {
         return F32 ? 1.0f : ldexpf(1.0f, -k);
     }
 
-    // Splits over cached positions for attention at `pos`: one per 64, at most a.splits.
+    // GQA attention (attention_gqa) at this position?
+    __device__ bool gqa(unsigned pos) const {
+        return a.HD == 128 && a.gqa_splits > 0 && static_cast<int>(pos) + 1 >= a.gqa_from;
+    }
+    // Splits over cached positions for attention at `pos`: one per a.gqa_rows
+    // (GQA, at most a.gqa_splits) or per 64 (per head, at most a.splits).
     __device__ int attn_splits(unsigned pos) const {
+        if (gqa(pos)) return ::min(a.gqa_splits, (static_cast<int>(pos) + a.gqa_rows) / a.gqa_rows);
         return ::min(a.splits, (static_cast<int>(pos) + 64) / 64);
+    }
+
+    // Thread 0 polls until kv group g's q, k and v rows of this layer are
+    // written (qkv_cnt); every consumer thread returns false on error.
+    __device__ bool wait_qkv(int g, int layer) {
+        if (t == 0) {
+            const unsigned target = static_cast<unsigned>(layer + 1) * 6 * a.HD;
+            const unsigned long long t0 = globaltimer();
+            for (unsigned i = 0;; i++) {
+                if (ld_acquire(a.qkv_cnt + g) >= target) break;
+                if ((i & 63) == 63) {
+                    if (ld_volatile(a.err)) {
+                        *reinterpret_cast<volatile int*>(&sh.flags[0]) = 1;
+                        break;
+                    }
+                    if (globaltimer() - t0 > kTimeoutNs) {
+                        fail(kErrBarrier);
+                        break;
+                    }
+                }
+            }
+        }
+        consumer_sync();
+        return !aborted();
     }
 
     // Thread 0 of an attention CTA: hint its K and V position range of the
@@ -969,17 +1001,224 @@ struct Consumer {
     __device__ void prefetch_kv(int layer, unsigned pos) const {
         const int S = attn_splits(pos);
         const int u = blockIdx.x;
-        if (t != 0 || u >= a.H * S || pos == 0) return;
-        const int h = u / S, s = u % S, kh = h / 4;
+        const int units = gqa(pos) ? a.KV * S : a.H * S;
+        if (t != 0 || u >= units || pos == 0) return;
+        const int s = u % S, kh = gqa(pos) ? u / S : (u / S) / 4;
         const int npos = static_cast<int>(pos);  // rows 0 .. pos - 1 are cached
         const int chunk = (npos + 1 + S - 1) / S;
         const int p0 = s * chunk, p1 = min(npos, p0 + chunk);
         if (p1 <= p0) return;
         const DecodeLayer& L = a.layers[layer];
         const size_t off = (static_cast<size_t>(kh) * a.max_seq + p0) * HD;
-        const uint32_t bytes = static_cast<uint32_t>(p1 - p0) * HD * 4;
+        const uint32_t bytes = static_cast<uint32_t>(::min(p1 - p0, a.kv_prefetch_rows)) * HD * 4;
         prefetch_l2(L.k_cache + off, bytes);
         prefetch_l2(L.v_cache + off, bytes);
+    }
+
+    // GQA attention (hd 128, H = 4 KV; modules.cpp:58-88, kv head h / 4):
+    // CTA u < KV S takes kv group g = u / S and position split s = u % S for
+    // the group's 4 query heads, so each K / V row is read once.  Warp w takes
+    // groups of 8 positions; lane l holds dims 4 l .. 4 l + 3 of q, K, V and
+    // of the 4 heads' accumulators.  The 32 dot products of a group (4 heads x
+    // 8 positions) are reduced together (warp_reduce_multi): lane l then
+    // holds the score of (head l / 8, position l % 8), and the online softmax
+    // runs per 8-lane group.  With one split the CTA writes ctx of its 4
+    // heads; otherwise each split writes its partial {M, L, 0, 0, acc} and the
+    // last split of the group to finish (ticket attn_cnt[g]) merges them into
+    // ctx.  mx = max |ctx| written by this thread (0 if none).
+    template <int HD>
+    __device__ bool attention_gqa(int layer, unsigned pos, float& mx) {
+        mx = 0.f;
+        if constexpr (HD != 128) {
+            return true;
+        } else {
+            constexpr int QPG = 4, G = 8, W = HD + 2, HALF = HD / 2, PW = HD + 4;
+            const DecodeLayer& L = a.layers[layer];
+            const int S = attn_splits(pos);
+            const int u = blockIdx.x;
+            if (u >= a.KV * S) return true;
+            const int g = u / S, s = u % S;
+            if (!TLD_OK(pos < static_cast<unsigned>(a.max_seq) && a.H == QPG * a.KV, 40, pos, g)) return true;
+            if (!TLD_OK((6 * HD + kConsumerWarps * QPG * W) * 4 <= static_cast<int>(xbuf_bytes(a.D, a.F, a.HD)), 41,
+                        HD, 1))
+                return true;
+            if (!wait_qkv(g, layer)) return false;
+            float* q_s = reinterpret_cast<float*>(sh.xbuf);  // [4][HD]
+            float* k_s = q_s + QPG * HD;
+            float* v_s = k_s + HD;
+            float* wp = v_s + HD;  // [8 warps][4 heads][W]
+            // RoPE (kernels.cpp:78-95) of the group's 4 q heads and its k head; v as is
+            const float* ct = a.cos_tab + static_cast<size_t>(pos) * HALF;
+            const float* st = a.sin_tab + static_cast<size_t>(pos) * HALF;
+            for (int i = t; i < (QPG + 1) * HALF; i += kConsumers) {
+                const int hh = i / HALF, c = i % HALF;
+                const float* src = a.qkv + (hh < QPG ? (g * QPG + hh) * HD : a.H * HD + g * HD);
+                float* dst = hh < QPG ? q_s + hh * HD : k_s;
+                const float cc = __ldg(ct + c), sn = __ldg(st + c);
+                const float x = __ldcg(src + c), y = __ldcg(src + c + HALF);
+                dst[c] = x * cc - y * sn;
+                dst[c + HALF] = x * sn + y * cc;
+            }
+            const float* vn = a.qkv + (a.H + a.KV) * HD + g * HD;
+            for (int i = t; i < HD; i += kConsumers) v_s[i] = __ldcg(vn + i);
+            consumer_sync();
+            float* kc = L.k_cache + static_cast<size_t>(g) * a.max_seq * HD;
+            float* vc = L.v_cache + static_cast<size_t>(g) * a.max_seq * HD;
+            if (s == 0) {  // push_kv (inference_state.h:38-43)
+                for (int i = t; i < HD; i += kConsumers) {
+                    kc[static_cast<size_t>(pos) * HD + i] = k_s[i];
+                    vc[static_cast<size_t>(pos) * HD + i] = v_s[i];
+                }
+            }
+            const int npos = static_cast<int>(pos) + 1;
+            const int chunk = (npos + S - 1) / S;
+            const int p0 = s * chunk, p1 = min(npos, p0 + chunk);
+            float4 q[QPG], acc[QPG];
+            float m[QPG];
+#pragma unroll
+            for (int h = 0; h < QPG; h++) {
+                q[h] = reinterpret_cast<const float4*>(q_s + h * HD)[lane];
+                acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+                m[h] = -INFINITY;
+            }
+            const int my_h = lane >> 3, my_f = lane & 7;
+            float l_lane = 0.f;  // softmax denominator share of (head my_h, position slot my_f)
+            for (int pb = p0 + warp * G; pb < p1; pb += kConsumerWarps * G) {
+                float4 kr[G], vr[G];
+#pragma unroll
+                for (int f = 0; f < G; f++) {
+                    const int p = pb + f;
+                    if (p < p1 && p != static_cast<int>(pos)) {
+                        kr[f] = __ldcg(reinterpret_cast<const float4*>(kc + static_cast<size_t>(p) * HD) + lane);
+                        vr[f] = __ldcg(reinterpret_cast<const float4*>(vc + static_cast<size_t>(p) * HD) + lane);
+                    } else if (p == static_cast<int>(pos)) {  // this step's row: from shared memory
+                        kr[f] = reinterpret_cast<const float4*>(k_s)[lane];
+                        vr[f] = reinterpret_cast<const float4*>(v_s)[lane];
+                    } else {
+                        kr[f] = vr[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                }
+                float v[QPG * G];
+#pragma unroll
+                for (int h = 0; h < QPG; h++)
+#pragma unroll
+                    for (int f = 0; f < G; f++)
+                        v[h * G + f] = q[h].x * kr[f].x + q[h].y * kr[f].y + q[h].z * kr[f].z + q[h].w * kr[f].w;
+                warp_reduce_multi<QPG * G>(v);  // lane l: dot of (head l / 8, position l % 8)
+                const bool valid = pb + my_f < p1;
+                const float sc = valid ? v[0] * a.attn_scale : -INFINITY;
+                float gm = sc;
+                gm = fmaxf(gm, __shfl_xor_sync(FULL, gm, 1));
+                gm = fmaxf(gm, __shfl_xor_sync(FULL, gm, 2));
+                gm = fmaxf(gm, __shfl_xor_sync(FULL, gm, 4));
+                float corr[QPG];
+#pragma unroll
+                for (int h = 0; h < QPG; h++) {
+                    const float mn = fmaxf(m[h], __shfl_sync(FULL, gm, h * G));  // position pb valid: finite
+                    corr[h] = expf(m[h] - mn);  // first group: exp(-inf) = 0
+                    m[h] = mn;
+                    acc[h].x *= corr[h]; acc[h].y *= corr[h]; acc[h].z *= corr[h]; acc[h].w *= corr[h];
+                }
+                // this lane's head: selects, not a dynamically indexed (local-memory) array
+                const float m_my = my_h == 0 ? m[0] : my_h == 1 ? m[1] : my_h == 2 ? m[2] : m[3];
+                const float c_my = my_h == 0 ? corr[0] : my_h == 1 ? corr[1] : my_h == 2 ? corr[2] : corr[3];
+                const float pr = valid ? expf(sc - m_my) : 0.f;
+                l_lane = l_lane * c_my + pr;
+#pragma unroll
+                for (int f = 0; f < G; f++) {
+#pragma unroll
+                    for (int h = 0; h < QPG; h++) {
+                        const float ph = __shfl_sync(FULL, pr, h * G + f);
+                        acc[h].x = fmaf(ph, vr[f].x, acc[h].x);
+                        acc[h].y = fmaf(ph, vr[f].y, acc[h].y);
+                        acc[h].z = fmaf(ph, vr[f].z, acc[h].z);
+                        acc[h].w = fmaf(ph, vr[f].w, acc[h].w);
+                    }
+                }
+            }
+            l_lane += __shfl_xor_sync(FULL, l_lane, 1);
+            l_lane += __shfl_xor_sync(FULL, l_lane, 2);
+            l_lane += __shfl_xor_sync(FULL, l_lane, 4);
+#pragma unroll
+            for (int h = 0; h < QPG; h++) {
+                const float lh = __shfl_sync(FULL, l_lane, h * G);
+                float* mine = wp + (warp * QPG + h) * W;
+                if (lane == 0) {
+                    mine[0] = m[h];
+                    mine[1] = lh;
+                }
+                *reinterpret_cast<float2*>(mine + 2 + 4 * lane) = make_float2(acc[h].x, acc[h].y);
+                *reinterpret_cast<float2*>(mine + 4 + 4 * lane) = make_float2(acc[h].z, acc[h].w);
+            }
+            consumer_sync();
+            // this split over the 8 warps, per head: {M, L, 0, 0, acc}; one split: ctx = acc / L
+            for (int k = t; k < QPG * PW; k += kConsumers) {
+                const int h = k / PW, i = k % PW;
+                float M = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; w++)
+                    if (wp[(w * QPG + h) * W + 1] > 0.f) M = fmaxf(M, wp[(w * QPG + h) * W]);
+                float Ls = 0.f, val = 0.f;
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; w++) {
+                    const float* pw = wp + (w * QPG + h) * W;
+                    if (pw[1] > 0.f) {
+                        const float e = expf(pw[0] - M);
+                        Ls += pw[1] * e;
+                        if (i >= 4) val += pw[2 + (i - 4)] * e;
+                    }
+                }
+                if (S == 1) {
+                    if (i >= 4) {
+                        const float c = val / Ls;
+                        a.ctx[(g * QPG + h) * HD + (i - 4)] = c;
+                        mx = fmaxf(mx, fabsf(c));
+                    }
+                } else {
+                    a.attn_part[static_cast<size_t>((g * QPG + h) * S + s) * PW + i] =
+                        i == 0 ? M : (i == 1 ? Ls : (i >= 4 ? val : 0.f));
+                }
+            }
+            if (S == 1) return true;
+            // the last split of the group to finish merges the S partials
+            consumer_sync();  // every partial store of this CTA precedes thread 0's fence
+            if (t == 0) {
+                __threadfence();
+                const unsigned target = static_cast<unsigned>(layer + 1) * S;
+                sh.flags[2] = (atomicAdd(a.attn_cnt + g, 1u) + 1 == target);
+            }
+            consumer_sync();
+            if (!sh.flags[2]) return true;
+            __threadfence();
+            // warp h (< 4): lane r < S loads split r's {M, L} of head h; all S in one round trip
+            float* wsh = q_s;  // [4][32] merge weights e^(M_r - GM) / GL (q is no longer needed)
+            if (warp < QPG) {
+                const float* ph = a.attn_part + static_cast<size_t>(g * QPG + warp) * S * PW;
+                const float2 ml = lane < S ? __ldcg(reinterpret_cast<const float2*>(ph + lane * PW))
+                                           : make_float2(-INFINITY, 0.f);
+                const bool ok = ml.y > 0.f;
+                const float GM = warp_max(ok ? ml.x : -INFINITY);
+                const float e = ok ? expf(ml.x - GM) : 0.f;
+                const float GL = warp_sum(ml.y * e);
+                wsh[warp * 32 + lane] = e / GL;
+            }
+            consumer_sync();
+            for (int k = t; k < QPG * HALF; k += kConsumers) {  // (head, column pair)
+                const int h = k / HALF, c = 2 * (k % HALF);
+                const float* ph = a.attn_part + static_cast<size_t>(g * QPG + h) * S * PW + 4 + c;
+                float c0 = 0.f, c1 = 0.f;
+#pragma unroll 8
+                for (int r = 0; r < S; r++) {  // every split wrote its row this step (empty: weight 0)
+                    const float2 ac = __ldcg(reinterpret_cast<const float2*>(ph + r * PW));
+                    const float w = wsh[h * 32 + r];
+                    c0 = fmaf(ac.x, w, c0);
+                    c1 = fmaf(ac.y, w, c1);
+                }
+                *reinterpret_cast<float2*>(a.ctx + (g * QPG + h) * HD + c) = make_float2(c0, c1);
+                mx = fmaxf(mx, fmaxf(fabsf(c0), fabsf(c1)));
+            }
+            return true;
+        }
     }
 
     // Attention for (head, split) = divmod(blockIdx.x, S) (modules.cpp:58-88):
@@ -999,26 +1238,7 @@ struct Consumer {
         if (!TLD_OK(pos < static_cast<unsigned>(a.max_seq) && kh < a.KV && h < a.H, 40, pos, kh)) return true;
         if (!TLD_OK((3 * HD + kConsumerWarps * (HD + 2)) * 4 <= static_cast<int>(xbuf_bytes(a.D, a.F, a.HD)), 41, HD, 0))
             return true;
-        // wait until kv group kh's q, k and v rows of this layer are written
-        if (t == 0) {
-            const unsigned target = static_cast<unsigned>(layer + 1) * 6 * HD;
-            const unsigned long long t0 = globaltimer();
-            for (unsigned i = 0;; i++) {
-                if (ld_acquire(a.qkv_cnt + kh) >= target) break;
-                if ((i & 63) == 63) {
-                    if (ld_volatile(a.err)) {
-                        *reinterpret_cast<volatile int*>(&sh.flags[0]) = 1;
-                        break;
-                    }
-                    if (globaltimer() - t0 > kTimeoutNs) {
-                        fail(kErrBarrier);
-                        break;
-                    }
-                }
-            }
-        }
-        consumer_sync();
-        if (aborted()) return false;
+        if (!wait_qkv(kh, layer)) return false;
         float* q_s = reinterpret_cast<float*>(sh.xbuf);
         float* k_s = q_s + HD;
         float* v_s = k_s + HD;
@@ -1302,12 +1522,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         }
         cw.template prefetch_kv<HD>(l, pos);
         if (!cw.template run_i8<0>(NQKV, D, un, nullptr, nullptr)) return;
-        // attention; ctx written by one CTA per head
-        if (!cw.template attention<HD>(l, pos) || cw.aborted()) return;
-        cw.publish(0.f, 0.f);
+        // attention: ctx (GQA), or split partials merged by the o_proj staging
+        const bool gqa = cw.gqa(pos);
+        float ctx_max = 0.f;
+        if (gqa) {
+            if (!cw.template attention_gqa<HD>(l, pos, ctx_max) || cw.aborted()) return;
+        } else {
+            if (!cw.template attention<HD>(l, pos) || cw.aborted()) return;
+        }
+        cw.publish(0.f, ctx_max);
         // h = h + W_o ctx
         if (!cw.wait_all()) return;
-        un = cw.template stage_ctx_digits<HD>(pos);
+        un = gqa ? cw.template stage_digits<false>(a.ctx, a.H * a.HD, nullptr, nullptr)
+                 : cw.template stage_ctx_digits<HD>(pos);
         if (cw.t == 0) prefetch_l2(L.g_post, static_cast<uint32_t>(D) * 4u);  // staged after this phase
         if (!cw.template run_i8<1>(D, a.H * a.HD, un, hin, L.g_post)) return;
         // act = silu(W1 x) * (W3 x), x = rmsnorm(h)
@@ -1456,7 +1683,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         // counters for the next step.
         *a.ticket = 0;
         *a.bar = 0;
-        for (int g = 0; g < a.KV; g++) a.qkv_cnt[g] = 0;
+        for (int g = 0; g < a.KV; g++) {
+            a.qkv_cnt[g] = 0;
+            a.attn_cnt[g] = 0;
+        }
         __threadfence();
     }
 }

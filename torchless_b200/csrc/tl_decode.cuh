@@ -64,8 +64,9 @@ struct DecodeArgs {
     float* h;                   // residual stream [D]
     float* qkv;                 // [(H + 2 KV) hd]
     float* attn_part;           // [H][S][hd + 4] split partials {max, sum, 0, 0, acc}
-    float* ctx;                 // [H hd] (unused: the o_proj staging merges attn_part)
-    unsigned* attn_cnt;         // [H] split tickets per head, zero between launches
+    float* ctx;                 // [H hd] attention output (GQA attention; per-head attention leaves
+                                // the merge of attn_part to the o_proj staging)
+    unsigned* attn_cnt;         // [H] split tickets per kv group, zero between launches
     unsigned* qkv_cnt;          // [KV] q/k/v rows written per kv group, zero between launches
     float* act;                 // [F]
     float* logits;              // [V]
@@ -78,6 +79,12 @@ struct DecodeArgs {
     unsigned* pos;              // in: position; out: position + 1
     uint32_t* history;          // history[pos] = argmax
     int D, F, H, KV, HD, V, max_seq, splits;
+    // GQA attention (hd 128, H = 4 KV): from position gqa_from - 1 on, one CTA
+    // per (kv group, split) serves the group's 4 query heads, at most
+    // gqa_splits splits; gqa_splits 0 = per-head attention only.
+    int gqa_splits, gqa_from;
+    int gqa_rows;               // GQA: cached positions per split (at least)
+    int kv_prefetch_rows;       // K (and V) rows an attention CTA hints into L2 during q/k/v
     int pbuf_floats;            // per-phase partial-sum buffer (decode_kernel_fits)
     float attn_scale;
     // Phase hand-over statistics: [2][kStatsCap] {sum x^2, max |x|} of what

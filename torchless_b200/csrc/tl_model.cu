@@ -50,6 +50,12 @@
 namespace tl {
 namespace {
 
+// Cached positions + 1 from which the persistent decode step runs GQA
+// attention (one CTA per kv group and split) instead of per-head attention.
+constexpr int kGqaFromDefault = 1024;
+constexpr int kGqaRowsDefault = 64;           // GQA attention: cached positions per split (at least)
+constexpr int kKvPrefetchRowsDefault = 256;   // K (and V) rows per attention CTA hinted into L2
+
 struct TensorRec {
     std::string dtype;
     std::vector<int64_t> shape;
@@ -480,6 +486,21 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
                 }
             }
             m->mega_splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(dev_sms / Hl, 256 / Hl)));
+            // GQA attention: one CTA per (kv group, split), up to one split per 64 positions
+            if (HD == 128 && Hl == 4 * KVl) {
+                m->dargs.gqa_splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(32, dev_sms / KVl)));
+                m->dargs.gqa_from = kGqaFromDefault;
+                m->dargs.gqa_rows = kGqaRowsDefault;
+                // Tuning knobs: the position count from which GQA attention replaces per-head
+                // attention, and the positions per split.
+                if (const char* e = std::getenv("TL_DECODE_GQA_FROM")) m->dargs.gqa_from = std::atoi(e);
+                if (const char* e = std::getenv("TL_DECODE_GQA_ROWS"))
+                    m->dargs.gqa_rows = std::max(8, std::min(4096, std::atoi(e)));
+            }
+            m->dargs.kv_prefetch_rows = kKvPrefetchRowsDefault;
+            // Tuning knob: cached K / V rows per attention CTA hinted into L2 ahead of attention.
+            if (const char* e = std::getenv("TL_DECODE_KV_PREFETCH"))
+                m->dargs.kv_prefetch_rows = std::max(0, std::min(1 << 20, std::atoi(e)));
             m->dargs.pbuf_floats = pbuf;
         }
     }
@@ -515,13 +536,16 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     const size_t kv = L * layer_kv_floats(m.get());
     const size_t half = HD / 2;
     const int am_grid = std::max(gemv_f32_grid(V, D, true, true), m->grid);
-    const int part_splits = std::max(m->splits, m->mega_splits);
+    const int part_splits = std::max({m->splits, m->mega_splits, m->dargs.gqa_splits});
     size_t sbytes = 2 * A::pad(kv * 4) + 2 * A::pad(m->max_seq * half * 4) + A::pad(D * 4) + A::pad(NQKVl * 4) +
                     A::pad(Hl * HD * 4) + A::pad(Fl * 4) + A::pad(Vl * 4) + A::pad(Hl * part_splits * (HD + 4) * 4) +
                     A::pad(Hl * 4) * 2 + A::pad(am_grid * 4) * 2 + A::pad(4) * 6 + A::pad(16) + A::pad(m->max_seq * 4) * 2 +
                     A::pad(2 * kStatsCap * sizeof(float2)) + A::pad(D * 4) + A::pad(4);
     TL_TRY(m->state.reserve(sbytes));
     TL_CUDA_TRY(cudaMemsetAsync(m->state.base, 0, sbytes, m->stream));
+    // The stream is non-blocking: the clear must land before the blocking
+    // copies below (RoPE tables, layer table) write into the arena.
+    TL_CUDA_TRY(cudaStreamSynchronize(m->stream));
     m->kc = m->state.take<float>(kv);
     m->vc = m->state.take<float>(kv);
     m->cos_tab = m->state.take<float>(m->max_seq * half);
@@ -1465,10 +1489,10 @@ tl_status tl_batch_read_kv(const tl_batch* b, int seq, int layer, size_t pos, fl
     const size_t hd = m->cfg.head_dim;
     for (size_t kh = 0; kh < static_cast<size_t>(m->lKV); kh++) {
         const size_t off = seq * b->bkv.seq_stride + layer * b->bkv.layer_stride + (kh * b->max_seq + pos) * hd;
-        TL_CUDA_TRY(cudaMemcpy(k + kh * hd, b->bkv.k + off, hd * 4, cudaMemcpyDeviceToHost));
-        TL_CUDA_TRY(cudaMemcpy(v + kh * hd, b->bkv.v + off, hd * 4, cudaMemcpyDeviceToHost));
+        TL_CUDA_TRY(cudaMemcpyAsync(k + kh * hd, b->bkv.k + off, hd * 4, cudaMemcpyDeviceToHost, m->stream));
+        TL_CUDA_TRY(cudaMemcpyAsync(v + kh * hd, b->bkv.v + off, hd * 4, cudaMemcpyDeviceToHost, m->stream));
     }
-    return TL_OK;
+    return sync(const_cast<tl_model*>(m));
 }
 
 tl_status tl_model_launches_per_step(const tl_model* m, int* launches) {
