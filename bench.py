@@ -200,7 +200,8 @@ def run_ours(args, rank, world, local):
     if world > 1:
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600),
                                 device_id=torch.device(f"cuda:{local}"))
-    max_seq = PROMPT_LEN + args.warmup + args.steps + 8
+    ctx = args.context
+    max_seq = (ctx if ctx > 0 else PROMPT_LEN) + args.warmup + args.steps + 8
     if world == 1:
         buf = make_model_bytes(f"cuda:{local}", args.layers)
         m = Model.from_buffer(buf, device=local, max_seq=max_seq)
@@ -218,9 +219,19 @@ def run_ours(args, rank, world, local):
             os.remove(path)
         tp.connect(m)
         buf = None
-    prompt = prompt_ids()
-    for t in prompt[:-1]:
-        m.forward(t, logits=False)
+    if ctx > 0:
+        # long context: a random prompt of ctx ids, ingested untimed (the batched
+        # prompt pass on one GPU; token by token under tensor parallelism)
+        prompt = np.random.default_rng(SEED + 1).integers(0, 32000, ctx).tolist()
+        if world == 1:
+            m.prefill(prompt[:-1], logits=False)
+        else:
+            for t in prompt[:-1]:
+                m.forward(t, logits=False)
+    else:
+        prompt = prompt_ids()
+        for t in prompt[:-1]:
+            m.forward(t, logits=False)
     start_pos = m.pos
     # warm-up greedy steps, then the timed ones continue from the last argmax
     _, warm_ids = m.time_decode(prompt[-1], args.warmup)
@@ -271,15 +282,22 @@ def run_ours(args, rank, world, local):
     achieved = top["bytes_per_launch"] / (avg_ms / 1000.0) / 1e9
     peak, peak_kind = peaks()
     # ncu traffic of the 1-GPU launch; a rank's launch under tensor parallelism is not captured
-    traffic = load_traffic().get(top["name"]) if world == 1 else None
+    traffic = load_traffic().get(top["name"]) if world == 1 and ctx == 0 else None
     total_prof = sum(k["total_ms"] for k in prof)
 
+    # bytes of one token at the mean timed position: weights + the K/V rows read
+    kv_per_pos = 2 * args.layers * 8 * 128 * 4
+    tok_bytes = 7940898816 + kv_per_pos * (start_pos + args.warmup + (args.steps + 1) / 2.0) if ctx > 0 \
+        else 7940898816
+    workload = (f"Mistral-7B int8 bs1 greedy decode ({ctx}-token random prompt, {args.steps} tokens)" if ctx > 0
+                else "Mistral-7B int8 bs1 greedy decode (16-token prompt, 128 tokens)")
     out = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC if ctx == 0 else f"int8 Mistral-7B decode tok/s @bs1, {ctx}-token context",
+        "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": "Mistral-7B int8 bs1 greedy decode (16-token prompt, 128 tokens)"
+        "config": {"workload": workload
                    + ("" if args.layers == 32 else f" [profiling case: {args.layers} of 32 layers]"),
                    "global_batch": 1, "seq_len": max_seq,
                    "parallelism": f"tp{world}" if world > 1 else "single",
@@ -291,13 +309,13 @@ def run_ours(args, rank, world, local):
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "algorithmic_bytes": top["bytes_per_launch"]},
         # N GPUs share the bytes of a token: the roofline is N x peak / bytes
-        "model_roofline": {"bytes_per_token": 7940898816, "tok_s_at_peak": world * peak * 1e9 / 7940898816,
-                           "frac": value / (world * peak * 1e9 / 7940898816)},
+        "model_roofline": {"bytes_per_token": tok_bytes, "tok_s_at_peak": world * peak * 1e9 / tok_bytes,
+                           "frac": value / (world * peak * 1e9 / tok_bytes)},
         "kernel_shares": {k["name"]: round(k["total_ms"] / total_prof, 4) for k in prof},
         "clocks": clocks.summary(),
         "ids_head": ids[:8],
     }
-    if not args.no_cpu_baseline and world == 1:
+    if not args.no_cpu_baseline and world == 1 and ctx == 0:
         try:
             v, secs, cores = cpu_reference_sample(buf, args.cpu_layers)
             out["cpu_baseline"] = {
@@ -525,6 +543,8 @@ def main():
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--gemv-sweep", action="store_true",
                     help="isolated int8 GEMV sweep at Mistral-7B shapes (one JSON line per shape)")
+    ap.add_argument("--context", type=int, default=0,
+                    help="bs1 decode after a random prompt of this many tokens (0: the 16-token prompt)")
     ap.add_argument("--layers", type=int, default=32,
                     help="transformer layers (32 = Mistral-7B; fewer only for small profiling captures)")
     args = ap.parse_args()

@@ -96,15 +96,24 @@ def test_tp2_greedy_matches_reference():
     assert worst < 1e-4
 
 
-def test_tp2_matches_one_gpu_7b_shapes():
+# Attention of the persistent step: per-head CTAs (the default at short
+# context), or GQA CTAs from the first position with 8 positions per split
+# (the long-context path, here with up to 3 splits per kv group).
+ATTN_ENV = {"per_head": {}, "gqa": {"TL_DECODE_GQA_FROM": "0", "TL_DECODE_GQA_ROWS": "8"}}
+
+
+@pytest.mark.parametrize("attn", list(ATTN_ENV))
+def test_tp2_matches_one_gpu_7b_shapes(attn, monkeypatch):
     """Mistral-7B layer shapes (2 layers, N=2 splits of every projection) vs 1 GPU."""
     _need(WORLD)
+    for k, v in ATTN_ENV[attn].items():
+        monkeypatch.setenv(k, v)  # read at load, here and in the spawned ranks
     from torchless_b200 import Model, ops, synthetic as S
     cfg = dict(S.MISTRAL_7B, num_hidden_layers=2)
     buf = S.make_torch_model(cfg, seed=5, norm="random", device="cuda",
                              quantizer=lambda x: ops.quantize_i8(x)).buf
     rng = np.random.default_rng(2)
-    feed = rng.integers(0, 32000, 10).tolist()
+    feed = rng.integers(0, 32000, 10 if attn == "per_head" else 24).tolist()
     one = Model.from_buffer(buf, max_seq=32)
     ref, ref_toks = [], []
     for t in feed:
