@@ -71,6 +71,8 @@ def oracle_lib() -> ctypes.CDLL:
             "tlo_init_freq": (None, [_P, _S, _F]),
             "tlo_rope_cos_sin": (None, [_P, _P, _P, _S, _S, _S]),
             "tlo_argmax": (_U32, [_P, _S]),
+            "tlo_sample_multinomial": (_U32, [_P, _S, _F, _F]),
+            "tlo_sample_uniform": (_F, [ctypes.c_uint64, ctypes.c_uint64]),
             "tlo_quantize": (None, [_P, _P, _P, _S, _S]),
             "tlo_model_new": (_P, [ctypes.POINTER(tlo_config)]),
             "tlo_model_free": (None, [_P]),
@@ -110,6 +112,7 @@ def ref_lib() -> ctypes.CDLL:
             "ref_logits": (ctypes.POINTER(_F), [_P]),
             "ref_hidden": (ctypes.POINTER(_F), [_P]),
             "ref_sample_max": (_U32, [_P]),
+            "ref_sample_logits": (_U32, [_P, _P, _F, _U32, ctypes.POINTER(_F)]),
             "ref_pos": (_S, [_P]),
             "ref_set_pos": (None, [_P, _S]),
             "ref_layer_forward": (_I, [_P, _I, _P]),
@@ -255,13 +258,14 @@ class RefModel:
     def sample_max(self) -> int:
         return ref_lib().ref_sample_max(self._h)
 
-    def write_kv(self, layer: int, pos: int, k: np.ndarray, v: np.ndarray) -> None:
-        """Sets the cache rows at (layer, pos) (test set-up of a pre-filled cache)."""
-        n = int(np.prod(self.kv_shape))
-        kc = np.ctypeslib.as_array(oracle_lib().tlo_model_k_cache(self._h), (n,)).reshape(self.kv_shape)
-        vc = np.ctypeslib.as_array(oracle_lib().tlo_model_v_cache(self._h), (n,)).reshape(self.kv_shape)
-        kc[layer, :, pos] = k
-        vc[layer, :, pos] = v
+    def sample_logits(self, logits: np.ndarray, temp: float, seed: int):
+        """The reference's sample_multinomial (main.cpp:23-43) on `logits` with its
+        generator seeded by `seed`: (index, the uniform draw r it used)."""
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        assert x.size == self.vocab
+        r = _F()
+        idx = ref_lib().ref_sample_logits(self._h, x.ctypes.data, float(temp), int(seed), ctypes.byref(r))
+        return int(idx), float(r.value)
 
     def layer_forward(self, layer: int, h: np.ndarray) -> np.ndarray:
         x = np.array(h, dtype=np.float32, copy=True)
@@ -274,6 +278,17 @@ class RefModel:
         if ref_lib().ref_time_token(self._h, token, first_layer, n_layers, out):
             raise ValueError("reference timing rejected")
         return tuple(out)
+
+
+def sample_multinomial(logits: np.ndarray, temp: float, r: float) -> int:
+    """sample_multinomial (main.cpp:23-43) with the uniform draw r given."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    return int(oracle_lib().tlo_sample_multinomial(x.ctypes.data, x.size, float(temp), float(r)))
+
+
+def sample_uniform(seed: int, pos: int) -> float:
+    """The library's device-side uniform draw for (seed, position)."""
+    return float(oracle_lib().tlo_sample_uniform(int(seed), int(pos)))
 
 
 def greedy(model, prompt, n_new):

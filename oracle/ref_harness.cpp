@@ -17,6 +17,7 @@
 #include <cstdint>
 #include <cstring>
 #include <memory>
+#include <random>
 #include <string>
 #include <vector>
 
@@ -27,6 +28,9 @@
 
 // main.cpp:10-21, linked from the reference's main.cpp (main renamed).
 uint32_t sample_max(InferenceState& infer);
+// main.cpp:23-43 and the generator it draws from (main.cpp:6-8).
+uint32_t sample_multinomial(InferenceState& infer, float temp);
+extern std::mt19937 gen;
 
 namespace {
 
@@ -116,6 +120,20 @@ __attribute__((visibility("default"))) const float* ref_hidden(void* h) {
 }
 __attribute__((visibility("default"))) uint32_t ref_sample_max(void* h) {
     return sample_max(*static_cast<Session*>(h)->infer);
+}
+// sample_multinomial (main.cpp:23-43) on the given logits (vocab_size of
+// them, copied into infer.logits, which the call then divides by temp), with
+// the generator seeded by `seed`; *r_out = the uniform draw the call takes
+// (the same distribution applied to a copy of the seeded generator).
+__attribute__((visibility("default"))) uint32_t ref_sample_logits(void* h, const float* logits, float temp,
+                                                                  uint32_t seed, float* r_out) {
+    auto* s = static_cast<Session*>(h);
+    std::memcpy(s->infer->logits.data, logits, s->infer->logits.numel * sizeof(float));
+    gen.seed(seed);
+    std::mt19937 peek = gen;
+    std::uniform_real_distribution<double> d(0.0, 1.0);
+    *r_out = static_cast<float>(d(peek));
+    return sample_multinomial(*s->infer, temp);
 }
 __attribute__((visibility("default"))) size_t ref_pos(void* h) {
     return static_cast<Session*>(h)->infer->pos;

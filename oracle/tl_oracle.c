@@ -203,6 +203,49 @@ TLO_API uint32_t tlo_argmax(const float* logits, size_t n) {
     return (uint32_t)res;
 }
 
+/* sample_multinomial (main.cpp:23-43) with its uniform draw r supplied by the
+ * caller (the reference draws r = (float)distr(gen), a uniform double in
+ * [0, 1) from a global mt19937).  temp <= 0: sample_max.  temp > 0: every
+ * logit divided by temp (the reference divides infer.logits in place; here a
+ * copy is scaled), softmax (kernels.cpp:55-63), then the first index whose
+ * running fp32 sum of probabilities reaches r; none: the last index. */
+TLO_API uint32_t tlo_sample_multinomial(const float* logits, size_t n, float temp, float r) {
+    if (!(temp > 0)) return tlo_argmax(logits, n);
+    float* x = (float*)malloc(n * sizeof(float));
+    float* p = (float*)malloc(n * sizeof(float));
+    if (!x || !p) {
+        free(x);
+        free(p);
+        return (uint32_t)(n - 1);
+    }
+    for (size_t i = 0; i < n; i++) x[i] = logits[i] / temp;
+    tlo_softmax(p, x, n);
+    float total = 0.0f;
+    uint32_t res = (uint32_t)(n - 1);
+    for (size_t i = 0; i < n; i++) {
+        total += p[i];
+        if (total >= r) {
+            res = (uint32_t)i;
+            break;
+        }
+    }
+    free(x);
+    free(p);
+    return res;
+}
+
+/* The uniform draw of the library's device-side sampling for (seed, pos): the
+ * splitmix64 finaliser of seed + (pos + 1) * 0x9E3779B97F4A7C15, top 24 bits
+ * scaled by 2^-24 (exact in float, in [0, 1)).  Not the reference's draw
+ * (an unseeded mt19937); a fixed function so that runs are reproducible. */
+TLO_API float tlo_sample_uniform(uint64_t seed, uint64_t pos) {
+    uint64_t z = seed + (pos + 1) * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    return (float)(z >> 40) * (1.0f / 16777216.0f);
+}
+
 /* quantize (export_mistral.py:53-68) on fp32 input, torch CPU semantics:
  *   scale = 127 / max|x| over each group; torch evaluates int / tensor as
  *           reciprocal(tensor) * int, i.e. fl(fl(1/max) * 127)

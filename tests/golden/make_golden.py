@@ -18,6 +18,11 @@ Writes:
                            from its own sources) on those models: prompt,
                            greedy ids and per-step logits.
   ref_ops.npz              reference kernels.cpp ops on seeded inputs.
+  ref_sample.npz           the reference's sample_multinomial (main.cpp:23-43)
+                           on TINY-vocabulary logits (the greedy fixture's plus
+                           NaN / inf / tie / flat edge cases) at several
+                           temperatures, its generator seeded: the uniform draw
+                           r of each call and the index it returned.
 
 The tests read only these files; nothing at test time touches the reference
 tree.
@@ -88,11 +93,52 @@ def sha256(b) -> str:
     return hashlib.sha256(bytes(b)).hexdigest()
 
 
+def sample_fixture() -> None:
+    """ref_sample.npz: main.cpp:23-43 through the reference build (oracle/_ref)."""
+    oracle.build(reference=True)
+    cfg, seed = MODELS["tiny"]
+    V = cfg["vocab_size"]
+    rm = oracle.RefModel(S.make_numpy_model(cfg, seed=seed, norm="random").buf, max_seq=16)
+    sets = [l.astype(np.float32) for l in np.load(os.path.join(HERE, "ref_greedy_tiny.npz"))["logits"][:4]]
+    base = sets[0]
+    edge = []
+    x = base.copy(); x[0] = np.nan; edge.append(x)                  # NaN at 0
+    x = base.copy(); x[100] = np.nan; edge.append(x)                # NaN inside
+    x = base.copy(); x[5] = np.inf; edge.append(x)                  # +inf
+    x = np.full(V, -np.inf, np.float32); x[321] = 1.5; edge.append(x)  # one finite
+    edge.append(np.full(V, -np.inf, np.float32))                    # all -inf
+    edge.append((base * 1e30).astype(np.float32))                   # huge
+    x = np.zeros(V, np.float32); x[[7, 8, 700]] = 3.0; edge.append(x)  # ties
+    flat = np.zeros(V, np.float32); edge.append(flat)               # flat: running sum may stop short of r
+    sets += edge
+    temps = [0.0, -1.0, 0.3, 0.8, 1.0, 2.5]
+    rows = []
+    for j, lg in enumerate(sets):
+        for temp in temps:
+            for sd in range(6):
+                idx, r = rm.sample_logits(lg, temp, 1000 * j + sd)
+                rows.append((j, temp, 1000 * j + sd, r, idx))
+    # seeds whose draw is within 1e-4 of 1, on the flat set (the last-index fallback)
+    hi = [sd for sd in range(200000) if rm.sample_logits(flat, 1.0, sd)[1] > 0.9999][:6]
+    for sd in hi:
+        idx, r = rm.sample_logits(flat, 1.0, sd)
+        rows.append((len(sets) - 1, 1.0, sd, r, idx))
+    rm.close()
+    a = np.array(rows, dtype=np.float64)
+    np.savez_compressed(os.path.join(HERE, "ref_sample.npz"), logits=np.stack(sets),
+                        set=a[:, 0].astype(np.int64), temp=a[:, 1].astype(np.float32),
+                        seed=a[:, 2].astype(np.int64), r=a[:, 3].astype(np.float32), idx=a[:, 4].astype(np.int64))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only-sample", action="store_true", help="regenerate ref_sample.npz only")
     args = ap.parse_args()
     ref = args.reference
+    if args.only_sample:
+        sample_fixture()
+        return
 
     exp = read_expected(os.path.join(ref, "test/mistral/expected.txt"))
     with open(os.path.join(HERE, "reference_expected.json"), "w") as f:
@@ -164,6 +210,7 @@ def main() -> None:
     L.ref_silu(y.ctypes.data, x.ctypes.data, 11)
     ops.update(silu_x=x, silu_y=y)
     np.savez_compressed(os.path.join(HERE, "ref_ops.npz"), **ops)
+    sample_fixture()
     print("golden fixtures written to", HERE)
 
 

@@ -159,3 +159,47 @@ def test_oracle_vs_live_reference_random_ops(oracle_lib):
         L.ref_matmul_i8(a.ctypes.data, q.ctypes.data, s.ctypes.data, s.size, x.ctypes.data, n, d)
         oracle_lib.tlo_matmul_i8(b.ctypes.data, q.ctypes.data, s.ctypes.data, s.size, x.ctypes.data, n, d)
         np.testing.assert_array_equal(a, b)
+
+
+def test_sample_multinomial_matches_reference_fixture():
+    """tlo_sample_multinomial (the oracle's main.cpp:23-43) against the
+    reference's own sample_multinomial on the committed fixture: same uniform
+    draw r, same index, bit for bit -- including NaN / inf / all -inf logits,
+    ties, temperature <= 0 (sample_max) and the last-index fallback when the
+    running sum stops short of r."""
+    d = np.load(os.path.join(GOLDEN, "ref_sample.npz"))
+    L = d["logits"]
+    for j, temp, r, idx in zip(d["set"], d["temp"], d["r"], d["idx"]):
+        got = oracle.sample_multinomial(L[j], float(temp), float(r))
+        assert got == idx, (int(j), float(temp), float(r), got, int(idx))
+    assert (d["idx"] == L.shape[1] - 1).sum() >= 6  # the fallback is exercised
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="oracle/_ref not built here")
+def test_sample_multinomial_vs_live_reference():
+    """Fresh logits (a forward of the TINY model, scaled) through both samplers."""
+    from conftest import model_bytes
+    rm = oracle.RefModel(model_bytes("tiny"), max_seq=8)
+    lg = rm.forward(3)
+    rng = np.random.default_rng(17)
+    for k in range(60):
+        x = (lg * rng.uniform(0.2, 5.0) + rng.standard_normal(lg.size) * 0.5).astype(np.float32)
+        temp = float(rng.choice([0.0, 0.5, 1.0, 1.9]))
+        idx, r = rm.sample_logits(x, temp, k)
+        assert oracle.sample_multinomial(x, temp, r) == idx
+    rm.close()
+
+
+def test_sample_uniform_is_the_documented_counter_function():
+    """The device sampling draw: splitmix64 of seed + (pos + 1) * golden ratio, top 24 bits / 2^24."""
+    M = (1 << 64) - 1
+
+    def ref(seed, pos):
+        z = (seed + (pos + 1) * 0x9E3779B97F4A7C15) & M
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+        z ^= z >> 31
+        return (z >> 40) / 16777216.0
+
+    for seed, pos in [(0, 0), (1, 5), (123456789, 1000), (M, 7)]:
+        assert oracle.sample_uniform(seed, pos) == ref(seed, pos)
