@@ -125,6 +125,24 @@ TL_API tl_status tl_argmax(uint32_t* out, const float* logits, size_t n, void* s
  * host threads) race on it and must be serialised by the caller. */
 TL_API tl_status tl_argmax_noalloc(uint32_t* out, const float* logits, size_t n, void* stream);
 
+/* sample_multinomial (main.cpp:23-43) on device logits[n]; *out (device) gets
+ * the index.  temperature <= 0: sample_max (main.cpp:10-21).  temperature > 0:
+ * softmax(logits / temperature) (kernels.cpp:55-63) and the first index whose
+ * running sum of probabilities reaches r; n - 1 if none does, or if a scaled
+ * logit is NaN or +inf, or all are -inf (the reference's NaN then reaches
+ * every probability).  r in [0, 1) replaces the reference's draw from its
+ * global mt19937 (main.cpp:6-8, 35), so a call is reproducible.  The sums
+ * run in parallel (per-thread chunks, then across chunks in order): the index
+ * can differ from the reference's only where r is within rounding of a
+ * running-sum boundary.  One block; no allocation. */
+TL_API tl_status tl_sample_multinomial(uint32_t* out, const float* logits, size_t n, float temperature, float r,
+                                       void* stream);
+
+/* The uniform draw that device-side sampling (tl_model_set_sampling) uses for
+ * the token at position pos: the splitmix64 finaliser of
+ * seed + (pos + 1) * 0x9E3779B97F4A7C15, top 24 bits times 2^-24. */
+TL_API float tl_sample_uniform(uint64_t seed, uint64_t pos);
+
 /* MLP<T>::forward first half (modules.cpp:99-112), fused:
  * out[i] = silu(W1[i,:] @ x) * (W3[i,:] @ x), int8 W1/W3 [n, d] with stored scales. */
 TL_API tl_status tl_mlp_gate_up(float* out, const int8_t* w1, const float* s1, const int8_t* w3,
@@ -215,6 +233,16 @@ TL_API tl_status tl_model_time_prefill(tl_model* m, const uint32_t* tokens, size
  * to out (host).  Only the ids cross the PCIe bus. */
 TL_API tl_status tl_model_generate(tl_model* m, const uint32_t* prompt, size_t n_prompt,
                                    size_t n_new, uint32_t* out);
+
+/* generate() with sample_multinomial(infer, temperature) (main.cpp:23-49) in
+ * place of sample_max: from the next step on, every decode step of the model
+ * (tl_model_forward, tl_model_generate, tl_model_time_decode, the last token
+ * of tl_model_prefill) picks its token as tl_sample_multinomial does, with
+ * r = tl_sample_uniform(seed, p) for the token computed at position p, on
+ * the device (no host round trip).  temperature <= 0 restores sample_max.
+ * The logits returned by the calls stay unscaled.  Not available under tensor
+ * parallelism (TL_ERR_UNSUPPORTED): each rank holds a slice of the vocabulary. */
+TL_API tl_status tl_model_set_sampling(tl_model* m, float temperature, uint64_t seed);
 
 /* InferenceState::pos (inference_state.h:12). */
 TL_API tl_status tl_model_get_pos(const tl_model* m, size_t* pos);

@@ -87,6 +87,9 @@ SIGNATURES = {
     "tl_rotary": [_P, _P, _P, _S, _S, _S, _P],
     "tl_argmax": [_P, _P, _S, _P],
     "tl_argmax_noalloc": [_P, _P, _S, _P],
+    "tl_sample_multinomial": [_P, _P, _S, _F, _F, _P],
+    "tl_sample_uniform": [ctypes.c_uint64, ctypes.c_uint64],  # returns float (set below)
+    "tl_model_set_sampling": [_P, _F, ctypes.c_uint64],
     "tl_mlp_gate_up": [_P, _P, _P, _P, _P, _P, _S, _S, _P],
     "tl_quantize_i8": [_P, _P, _P, _S, _S, _P],
     "tl_gemm_f16": [_P, _P, _P, _S, _S, _S, _S, _I, _P],
@@ -133,6 +136,7 @@ def lib() -> ctypes.CDLL:
             f.restype = ctypes.c_int
         L.tl_last_error.restype = ctypes.c_char_p
         L.tl_last_error.argtypes = []
+        L.tl_sample_uniform.restype = ctypes.c_float
         _lib = L
     return _lib
 

@@ -41,6 +41,7 @@
 
 #include "tl_common.cuh"
 #include "tl_decode.cuh"
+#include "tl_sample.cuh"
 
 namespace tl {
 namespace {
@@ -115,6 +116,9 @@ __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+struct ConsumerSync {
+    __device__ void operator()() const { consumer_sync(); }
+};
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -1675,8 +1679,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         } else if (l0 != l0 || bi == 0xffffffffu) {
             bi = 0;  // sample_max keeps 0 (main.cpp:10-21)
         }
-        *a.token = bi;
-        a.history[pos] = bi;
+        sh.info[3] = bi;
+    }
+    consumer_sync();
+    uint32_t tok = sh.info[3];
+    if (a.temperature > 0.f)  // sample_multinomial (main.cpp:23-43); a whole-vocabulary rank only
+        tok = sample_block<kConsumers>(a.logits, a.V, a.temperature, sample_uniform(a.sample_seed, pos), sh.scratch,
+                                       ConsumerSync{});
+    if (t == 0) {
+        *a.token = tok;
+        a.history[pos] = tok;
         *a.pos = pos + 1;
         *a.epoch = sh.info[2] + 1;
         // Every CTA has passed every barrier and taken its ticket: reset the

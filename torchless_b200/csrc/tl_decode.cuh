@@ -84,6 +84,10 @@ struct DecodeArgs {
     // gqa_splits splits; gqa_splits 0 = per-head attention only.
     int gqa_splits, gqa_from;
     int gqa_rows;               // GQA: cached positions per split (at least)
+    // Sampling (main.cpp:23-43) in place of sample_max when temperature > 0:
+    // the uniform draw of position pos is sample_uniform(sample_seed, pos).
+    float temperature;
+    unsigned long long sample_seed;
     int kv_prefetch_rows;       // K (and V) rows an attention CTA hints into L2 during q/k/v
     int pbuf_floats;            // per-phase partial-sum buffer (decode_kernel_fits)
     float attn_scale;

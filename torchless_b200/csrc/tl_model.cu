@@ -42,6 +42,7 @@
 #include "tl_decode.cuh"
 #include "tl_gemm.cuh"
 #include "tl_prefill.cuh"
+#include "tl_sample.cuh"
 #include "tl_batch.cuh"
 #include "tl_gemv.cuh"
 #include "tl_json.h"
@@ -223,6 +224,8 @@ struct tl_model {
     int splits = 4;
     bool use_graph = true;
     bool pdl = true;
+    float temperature = 0.f;   // > 0: decode steps sample (main.cpp:23-43) instead of sample_max
+    uint64_t sample_seed = 0;  // uniform draw of position p: sample_uniform(sample_seed, p)
     cudaStream_t stream = nullptr;
     DeviceArena weights, state;
     std::vector<LayerW> layers;
@@ -726,6 +729,12 @@ tl_status build_steps(tl_model* m) {
                             a.out_token = m->d_token; a.history = m->d_hist; a.pos = m->d_pos;
                             return launch_gemv_f32(a, true, true, s, pdl);
                         }});
+    if (m->temperature > 0.f)
+        m->steps.push_back({"sample", [=] { return 3.0 * 4 * V; },
+                            [=](cudaStream_t s, bool) {
+                                return sample_step(m->d_token, m->d_hist, m->d_pos, m->logits, V, m->temperature,
+                                                   m->sample_seed, s);
+                            }});
     return TL_OK;
 }
 
@@ -757,6 +766,21 @@ tl_status capture_graph(tl_model* m) {
         return set_error(TL_ERR_CUDA, "graph instantiate failed: %s", cudaGetErrorString(e));
     }
     m->graph = g;
+    return TL_OK;
+}
+
+// Steps and graph again, after a change of what a step's launches capture.
+tl_status rebuild_steps(tl_model* m) {
+    if (m->graph_exec) {
+        cudaGraphExecDestroy(m->graph_exec);
+        m->graph_exec = nullptr;
+    }
+    if (m->graph) {
+        cudaGraphDestroy(m->graph);
+        m->graph = nullptr;
+    }
+    TL_TRY(build_steps(m));
+    if (m->use_graph) TL_TRY(capture_graph(m));
     return TL_OK;
 }
 
@@ -974,17 +998,23 @@ tl_status tl_model_tp_connect(tl_model* m, const void* handles) {
     }
     m->connected = true;
     // the step launch (and its graph) captured the arguments before the peers were known
-    if (m->graph_exec) {
-        cudaGraphExecDestroy(m->graph_exec);
-        m->graph_exec = nullptr;
-    }
-    if (m->graph) {
-        cudaGraphDestroy(m->graph);
-        m->graph = nullptr;
-    }
-    TL_TRY(build_steps(m));
-    if (m->use_graph) TL_TRY(capture_graph(m));
-    return TL_OK;
+    return rebuild_steps(m);
+}
+
+tl_status tl_model_set_sampling(tl_model* m, float temperature, uint64_t seed) {
+    clear_error();
+    TL_REQUIRE(m, "tl_model_set_sampling: null model");
+    TL_REQUIRE(std::isfinite(temperature), "tl_model_set_sampling: temperature must be finite");
+    if (temperature > 0.f && m->tp > 1)
+        return set_error(TL_ERR_UNSUPPORTED, "tl_model_set_sampling: sampling needs the whole vocabulary on one "
+                                             "rank (not available under tensor parallelism)");
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    TL_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    m->temperature = temperature > 0.f ? temperature : 0.f;
+    m->sample_seed = seed;
+    m->dargs.temperature = m->temperature;
+    m->dargs.sample_seed = seed;
+    return rebuild_steps(m);
 }
 
 tl_status tl_model_forward(tl_model* m, uint32_t token, float* logits, uint32_t* next_token) {
@@ -1068,6 +1098,8 @@ tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* log
     a.part_v = m->am_v; a.part_i = m->am_i; a.counter = m->am_cnt;
     a.out_token = m->d_token; a.history = m->d_hist; a.pos = m->d_pos;
     TL_TRY(launch_gemv_f32(a, true, true, s, false));
+    if (m->temperature > 0.f)
+        TL_TRY(sample_step(m->d_token, m->d_hist, m->d_pos, m->logits, V, m->temperature, m->sample_seed, s));
     if (ms_out) TL_CUDA_TRY(cudaEventRecord(e1, s));
     if (logits) TL_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, static_cast<size_t>(V) * 4, cudaMemcpyDeviceToHost, s));
     TL_CUDA_TRY(cudaMemcpyAsync(m->h_pinned + 1, m->d_token, 4, cudaMemcpyDeviceToHost, s));

@@ -100,6 +100,11 @@ class Model:
     def pos(self, value: int) -> None:
         check(lib().tl_model_set_pos(self._h, int(value)))
 
+    def set_sampling(self, temperature: float, seed: int = 0) -> None:
+        """Decode steps sample at `temperature` (main.cpp:23-43) with the draw of
+        position p = ops.sample_uniform(seed, p); temperature <= 0: sample_max."""
+        check(lib().tl_model_set_sampling(self._h, float(temperature), int(seed)))
+
     # ---- Model<T>::forward + sample_max ----
     def forward(self, token: int, logits: bool = True):
         """One token at the current position; returns (logits or None, argmax).

@@ -118,6 +118,21 @@ def argmax(logits):
     return out
 
 
+def sample_multinomial(logits, temperature: float, r: float):
+    """sample_multinomial (main.cpp:23-43) with the uniform draw r given; returns a
+    1-element device tensor (int32) holding the index."""
+    import torch
+    out = torch.empty(1, dtype=torch.int32, device=logits.device)
+    check(lib().tl_sample_multinomial(_ptr(out), _f32(logits), logits.numel(), float(temperature), float(r),
+                                      _stream()))
+    return out
+
+
+def sample_uniform(seed: int, pos: int) -> float:
+    """The uniform draw of device-side sampling for the token at position pos."""
+    return float(lib().tl_sample_uniform(int(seed), int(pos)))
+
+
 def mlp_gate_up(out, w1, s1, w3, s3, x) -> None:
     """silu(w1 @ x) * (w3 @ x) with int8 w1/w3 (modules.cpp:99-112)."""
     n, d = w1.shape
