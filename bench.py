@@ -483,25 +483,61 @@ def run_prefill(args):
 # Batched decode: 64 sequences, each with a 4096-position KV cache of N(0, 1)
 # values (counter-based generator), 64 greedy steps per sequence.
 # ---------------------------------------------------------------------------
-def run_batch(args):
+def run_batch(args, rank=0, world=1, local=0):
     import torch
-    from torchless_b200 import Batch, Model
-    torch.cuda.set_device(0)
+    import torch.distributed as dist
+    from torchless_b200 import Batch, Model, tp
+    torch.cuda.set_device(local)
     B, P, K = args.batch_seqs, args.batch_context, args.steps
-    buf = make_model_bytes("cuda:0", args.layers)
-    m = Model.from_buffer(buf, max_seq=P + args.warmup + K + 8)
-    del buf
+    max_seq = P + args.warmup + K + 8
+    if world == 1:
+        buf = make_model_bytes(f"cuda:{local}", args.layers)
+        m = Model.from_buffer(buf, max_seq=max_seq)
+        del buf
+    else:
+        # N > 1: the same B sequences on every rank, each rank holding its
+        # tensor-parallel slice of the weights and of every sequence's KV heads
+        import tempfile
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600),
+                                device_id=torch.device(f"cuda:{local}"))
+        path = os.path.join(tempfile.gettempdir(), f"tl_bench_model_{os.environ.get('MASTER_PORT', '0')}.bin")
+        if rank == 0:
+            make_model_bytes(f"cuda:{local}", args.layers).tofile(path)
+        dist.barrier()
+        m = Model.load(path, device=local, max_seq=max_seq, tp_size=world, tp_rank=rank)
+        dist.barrier()
+        if rank == 0:
+            os.remove(path)
+        tp.connect(m)
     b = Batch(m, B)
+    if world > 1:
+        tp.connect_batch(b)
     b.fill_kv_random(SEED, P)
     toks = np.random.default_rng(SEED).integers(0, 32000, B).tolist()
     _, ids = b.time_decode(toks, args.warmup)
     first = ids[-1].tolist()
-    with ClockSampler(0) as clocks:
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize()
+
+    with ClockSampler(local) as clocks:
+        barrier()
         ms, ids = b.time_decode(first, K)
-        torch.cuda.synchronize()
+        barrier()
+    if world > 1:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+        dist.barrier()  # no rank unmaps an exchange buffer while a peer kernel runs
     b.close()
     m.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
     L, D, F, H, KV, HD, V = args.layers, 4096, 14336, 32, 8, 128, 32000
     pos_mean = P + args.warmup + (K - 1) / 2.0
     kv_bytes = B * L * 2 * KV * HD * 4 * (pos_mean + 1)  # cache rows read per step (all sequences)
@@ -511,14 +547,17 @@ def run_batch(args):
     peak, peak_kind = peaks()
     algo = kv_bytes + w_int8
     out = {"metric": "int8 Mistral-7B batched decode tok/s (64 seqs x 4096-token KV)", "value": B * K / (ms * 1e-3),
-           "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": args.warmup, "ms_per_step": ms / K,
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": ms / K,
+           "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
            "dtype": "f16 GEMM operands, f32 KV and accumulation", "data": "synthetic",
            "config": {"workload": f"Mistral-7B int8 ({L} layers), {B} sequences, KV pre-filled with {P} positions "
                                   f"of N(0,1) (counter-based generator), {K} greedy steps", "global_batch": B,
-                      "seq_len": P + args.warmup + K},
-           "roofline": {"bound": "hbm", "achieved": algo / step_s / 1e9, "peak": peak, "peak_kind": peak_kind,
-                        "unit": "GB/s", "frac": algo / step_s / 1e9 / peak, "algorithmic_bytes": algo,
+                      "seq_len": P + args.warmup + K,
+                      "parallelism": f"tp{world}" if world > 1 else "single"},
+           # N GPUs share the step's bytes: whole-job bandwidth against N x the per-GPU peak
+           "roofline": {"bound": "hbm", "achieved": algo / step_s / 1e9, "peak": world * peak,
+                        "peak_kind": peak_kind + (f" x {world} GPUs" if world > 1 else ""),
+                        "unit": "GB/s", "frac": algo / step_s / 1e9 / (world * peak), "algorithmic_bytes": algo,
                         "bytes_read_by_this_path": kv_bytes + w_here,
                         "note": "algorithmic = int8 weights + scales + fp32 lm_head + fp32 KV; this path reads "
                                 "fp16 weight copies (2 B per parameter)"},
@@ -558,7 +597,7 @@ def main():
         run_prefill(args)
         return
     if args.batch:
-        run_batch(args)
+        run_batch(args, rank, world, local)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)

@@ -328,6 +328,20 @@ TL_API tl_status tl_batch_time_decode(tl_batch* b, const uint32_t* tokens, size_
 /* K and V rows of sequence `seq` at (layer, pos) into host k, v [n_kv_heads * head_dim]. */
 TL_API tl_status tl_batch_read_kv(const tl_batch* b, int seq, int layer, size_t pos, float* k, float* v);
 
+/* Batched decoding under tensor parallelism (a batch of a model loaded with
+ * tp_size > 1, connected): every rank creates the batch with the same
+ * sequences, then exchanges TL_TP_HANDLE_BYTES handles of its exchange buffer
+ * in rank order (tl_batch_tp_handle, any host transport) and maps the others
+ * (tl_batch_tp_connect) before the first step.  A step's o_proj and down_proj
+ * partial rows are summed across ranks inside the residual + RMSNorm kernel
+ * over NVLink peer memory (modules.cpp:128, 142), and the per-row argmax merges
+ * the ranks' vocabulary slices.  tl_batch_step's logits are this rank's slice
+ * [n_seq][vocab_size / tp]; tl_batch_read_kv returns this rank's kv heads.  A
+ * peer that does not arrive within ~2 s fails the step with TL_ERR_TIMEOUT and
+ * the model must be reloaded on every rank. */
+TL_API tl_status tl_batch_tp_handle(const tl_batch* b, void* handle);
+TL_API tl_status tl_batch_tp_connect(tl_batch* b, const void* handles);
+
 /* Number of kernel launches one decode step issues (all of them this library's). */
 TL_API tl_status tl_model_launches_per_step(const tl_model* m, int* launches);
 

@@ -115,6 +115,8 @@ SIGNATURES = {
     "tl_batch_step": [_P, _P, _P, _P],
     "tl_batch_time_decode": [_P, _P, _S, _P, ctypes.POINTER(_F)],
     "tl_batch_read_kv": [_P, _I, _I, _S, _P, _P],
+    "tl_batch_tp_handle": [_P, _P],
+    "tl_batch_tp_connect": [_P, _P],
     "tl_model_tp_handle": [_P, _P],
     "tl_model_tp_connect": [_P, _P],
 }

@@ -170,6 +170,142 @@ __global__ void k_attention_merge_batch(__half* ctx16, const float* part, int H,
     if (i < HD) ctx16[static_cast<size_t>(bh) * HD + i] = __float2half_rn(acc / GL);
 }
 
+constexpr int kXVec = 4;                         // float4 columns a thread holds (D <= 16384)
+constexpr int kErrXchg = 6;                      // exchange wait gave up
+constexpr unsigned long long kXchgTimeoutNs = 2000000000ull;
+
+// Thread 0: adds this row's arrival to every rank's counter at `cnt_off`, then
+// waits (bounded) for all tp arrivals of exchange `seq`; false on timeout.
+__device__ bool xchg_row_arrive_wait(const BatchXchg& X, size_t cnt_off, unsigned long long seq, int* err) {
+    fence_sys();  // this CTA's stores (ordered before by the caller's barrier) reach the peers first
+    for (int q = 0; q < X.tp; q++) red_add_sys_u64(X.buf[q] + cnt_off, 1ull);
+    const unsigned long long target = (seq + 1) * static_cast<unsigned long long>(X.tp);
+    const unsigned long long t0 = globaltimer();
+    for (unsigned i = 0;; i++) {
+        if (ld_acquire_sys_u64(X.buf[X.rank] + cnt_off) >= target) return true;
+        if ((i & 63) == 63 && globaltimer() - t0 > kXchgTimeoutNs) {
+            atomicCAS(err, 0, kErrXchg);
+            return false;
+        }
+    }
+}
+
+__global__ void k_tp_residual_rmsnorm_rows(__half* x16, float* h, const float* part, int ks, size_t part_stride,
+                                           const float* g, BatchXchg X, unsigned long long xseq, int* err) {
+    __shared__ float red[32];
+    __shared__ int ok;
+    const int b = blockIdx.x, D = X.D, n4 = D / 4, par = static_cast<int>(xseq & 1);
+    const size_t row_off = bx_recv(X.B) + (static_cast<size_t>(par) * X.tp * X.B + b) * D * 4;
+    const size_t sender = static_cast<size_t>(X.B) * D * 4;  // bytes between senders' blocks
+    const float4* pr = reinterpret_cast<const float4*>(part + static_cast<size_t>(b) * D);
+    // this rank's partial row (its split-K partials summed in order) to every rank
+#pragma unroll
+    for (int j = 0; j < kXVec; j++) {
+        const int c = threadIdx.x + j * blockDim.x;
+        if (c >= n4) break;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < ks; r++) {
+            const float4 p = pr[r * (part_stride / 4) + c];
+            a.x += p.x; a.y += p.y; a.z += p.z; a.w += p.w;
+        }
+        for (int q = 0; q < X.tp; q++)
+            reinterpret_cast<float4*>(X.buf[q] + row_off + X.rank * sender)[c] = a;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) ok = xchg_row_arrive_wait(X, 8 * static_cast<size_t>(b), xseq, err);
+    __syncthreads();
+    if (!ok) return;
+    // h += the tp partial rows in rank order, then RMSNorm
+    float4* hr = reinterpret_cast<float4*>(h + static_cast<size_t>(b) * D);
+    const uint8_t* mine = X.buf[X.rank] + row_off;
+    float4 v[kXVec];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kXVec; j++) {
+        const int c = threadIdx.x + j * blockDim.x;
+        if (c >= n4) break;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < X.tp; q++) {
+            const float4 p = __ldcg(reinterpret_cast<const float4*>(mine + q * sender) + c);
+            a.x += p.x; a.y += p.y; a.z += p.z; a.w += p.w;
+        }
+        float4 x = hr[c];
+        x.x += a.x; x.y += a.y; x.z += a.z; x.w += a.w;
+        hr[c] = x;
+        v[j] = x;
+        ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+    }
+    ss = block_sum(ss, red);
+    const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + 1e-5f);
+    uint2* y = reinterpret_cast<uint2*>(x16 + static_cast<size_t>(b) * D);
+#pragma unroll
+    for (int j = 0; j < kXVec; j++) {
+        const int c = threadIdx.x + j * blockDim.x;
+        if (c >= n4) break;
+        const float* gc = g + 4 * c;
+        __half2 o[2] = {__floats2half2_rn((v[j].x * inv) * gc[0], (v[j].y * inv) * gc[1]),
+                        __floats2half2_rn((v[j].z * inv) * gc[2], (v[j].w * inv) * gc[3])};
+        y[c] = *reinterpret_cast<const uint2*>(o);
+    }
+}
+
+__global__ void k_tp_argmax_rows(uint32_t* out, const float* logits, int V, int vocab_off, uint32_t* pos,
+                                 BatchXchg X, unsigned long long aseq, int* err) {
+    __shared__ float sv[32];
+    __shared__ uint32_t si[32];
+    const int b = blockIdx.x;
+    const float* x = logits + static_cast<size_t>(b) * V;
+    float v = -INFINITY;
+    uint32_t idx = 0xffffffffu;
+    for (int i = threadIdx.x; i < V; i += blockDim.x)
+        if (better(x[i], static_cast<uint32_t>(i), v, idx)) {
+            v = x[i];
+            idx = static_cast<uint32_t>(i);
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(FULL, v, o);
+        const uint32_t oi = __shfl_xor_sync(FULL, idx, o);
+        if (better(ov, oi, v, idx)) {
+            v = ov;
+            idx = oi;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        sv[threadIdx.x >> 5] = v;
+        si[threadIdx.x >> 5] = idx;
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); w++)
+        if (better(sv[w], si[w], v, idx)) {
+            v = sv[w];
+            idx = si[w];
+        }
+    uint32_t gi = idx == 0xffffffffu ? 0xffffffffu : idx + static_cast<uint32_t>(vocab_off);
+    if (X.rank == 0 && x[0] != x[0]) gi = 0x80000000u;  // sample_max keeps 0 (main.cpp:10-21)
+    const int par = static_cast<int>(aseq & 1);
+    const unsigned long long slot = (static_cast<unsigned long long>(gi) << 32) | __float_as_uint(v);
+    const size_t off = bx_amslot(X.B) + ((static_cast<size_t>(par) * kBatchMaxTp + X.rank) * X.B + b) * 8;
+    for (int q = 0; q < X.tp; q++) st_relaxed_sys_u64(X.buf[q] + off, slot);
+    if (!xchg_row_arrive_wait(X, 8 * static_cast<size_t>(X.B + b), aseq, err)) return;
+    bool nan0 = false;
+    float bv = -INFINITY;
+    uint32_t bi = 0xffffffffu;
+    for (int q = 0; q < X.tp; q++) {
+        const unsigned long long s = ld_relaxed_sys_u64(
+            X.buf[X.rank] + bx_amslot(X.B) + ((static_cast<size_t>(par) * kBatchMaxTp + q) * X.B + b) * 8);
+        const uint32_t vi = static_cast<uint32_t>(s >> 32);
+        if (vi == 0x80000000u) nan0 = true;
+        else if (better(__uint_as_float(static_cast<uint32_t>(s)), vi, bv, bi)) {
+            bv = __uint_as_float(static_cast<uint32_t>(s));
+            bi = vi;
+        }
+    }
+    out[b] = (nan0 || bi == 0xffffffffu) ? 0u : bi;
+    pos[b]++;
+}
+
 __global__ void k_argmax_rows(uint32_t* out, const float* logits, int V, uint32_t* pos) {
     __shared__ float sv[32];
     __shared__ uint32_t si[32];
@@ -215,7 +351,8 @@ __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
     return x ^ (x >> 31);
 }
 
-__global__ void k_fill_kv_random(BatchKV kv, uint64_t seed, int B, int L, int KV, int HD, int n_pos) {
+__global__ void k_fill_kv_random(BatchKV kv, uint64_t seed, int B, int L, int KV, int HD, int n_pos, int kv_off,
+                                 int KV_total) {
     const size_t total = static_cast<size_t>(B) * L * 2 * KV * n_pos * HD;
     for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
         size_t r = e;
@@ -227,7 +364,7 @@ __global__ void k_fill_kv_random(BatchKV kv, uint64_t seed, int B, int L, int KV
         const int b = static_cast<int>(r / L);
         // key independent of B and n_pos: (sequence, layer, k/v, head, position < 2^20, dim)
         const uint64_t key =
-            ((((static_cast<uint64_t>(b) * L + l) * 2 + which) * KV + kh) * (1ull << 20) + p) * HD + d;
+            ((((static_cast<uint64_t>(b) * L + l) * 2 + which) * KV_total + kh + kv_off) * (1ull << 20) + p) * HD + d;
         const uint64_t rnd = splitmix64(seed ^ splitmix64(key >> 1));
         const float u1 = static_cast<float>((rnd >> 40) + 1) * 5.9604645e-8f;  // (0, 1]
         const float u2 = static_cast<float>((rnd >> 16) & 0xFFFFFF) * 5.9604645e-8f;
@@ -272,14 +409,37 @@ tl_status attention_merge_batch(__half* ctx16, const float* part, int B, int H, 
     return check_launch("attention_merge_batch");
 }
 
+tl_status tp_residual_rmsnorm_rows(__half* x16, float* h, const float* part, int ks, size_t part_stride,
+                                   const float* g, const BatchXchg& X, unsigned long long xseq, int* err,
+                                   cudaStream_t s) {
+    const int D = X.D, n4 = D / 4;
+    const int threads = std::min(1024, (n4 + 31) / 32 * 32);
+    TL_REQUIRE(X.tp >= 2 && X.tp <= kBatchMaxTp && X.rank >= 0 && X.rank < X.tp && ks >= 1,
+               "tp_residual_rmsnorm_rows: tp %d rank %d ks %d", X.tp, X.rank, ks);
+    TL_REQUIRE(D % 4 == 0 && n4 <= kXVec * threads && part_stride % 4 == 0, "tp_residual_rmsnorm_rows: width %d", D);
+    for (int q = 0; q < X.tp; q++) TL_REQUIRE(X.buf[q], "tp_residual_rmsnorm_rows: rank %d buffer not mapped", q);
+    k_tp_residual_rmsnorm_rows<<<X.B, threads, 0, s>>>(x16, h, part, ks, part_stride, g, X, xseq, err);
+    return check_launch("tp_residual_rmsnorm_rows");
+}
+
+tl_status tp_argmax_rows(uint32_t* out, const float* logits, int V, int vocab_off, uint32_t* pos, const BatchXchg& X,
+                         unsigned long long aseq, int* err, cudaStream_t s) {
+    TL_REQUIRE(X.tp >= 2 && X.tp <= kBatchMaxTp && V > 0, "tp_argmax_rows: tp %d V %d", X.tp, V);
+    for (int q = 0; q < X.tp; q++) TL_REQUIRE(X.buf[q], "tp_argmax_rows: rank %d buffer not mapped", q);
+    k_tp_argmax_rows<<<X.B, 1024, 0, s>>>(out, logits, V, vocab_off, pos, X, aseq, err);
+    return check_launch("tp_argmax_rows");
+}
+
 tl_status argmax_rows(uint32_t* out, const float* logits, int B, int V, uint32_t* pos, cudaStream_t s) {
     k_argmax_rows<<<B, 1024, 0, s>>>(out, logits, V, pos);
     return check_launch("argmax_rows");
 }
 
-tl_status fill_kv_random(const BatchKV& kv, uint64_t seed, int B, int L, int KV, int HD, int n_pos, cudaStream_t s) {
+tl_status fill_kv_random(const BatchKV& kv, uint64_t seed, int B, int L, int KV, int HD, int n_pos, int kv_off,
+                         int KV_total, cudaStream_t s) {
+    TL_REQUIRE(kv_off >= 0 && kv_off + KV <= KV_total, "fill_kv_random: heads %d + %d of %d", kv_off, KV, KV_total);
     const size_t total = static_cast<size_t>(B) * L * 2 * KV * n_pos * HD;
-    k_fill_kv_random<<<grid_of(total, 256), 256, 0, s>>>(kv, seed, B, L, KV, HD, n_pos);
+    k_fill_kv_random<<<grid_of(total, 256), 256, 0, s>>>(kv, seed, B, L, KV, HD, n_pos, kv_off, KV_total);
     return check_launch("fill_kv_random");
 }
 

@@ -37,6 +37,45 @@ tl_status rope_cache_batch(float* qf, const float* part, int ks, size_t part_str
 tl_status attention_decode_batch(float* part, const float* qf, const BatchKV& kv, int layer, const uint32_t* pos,
                                  int B, int H, int KV, int HD, int S, float scale, cudaStream_t s);
 
+// ---- tensor parallelism (rank r of tp holds the Megatron-style slice the
+// bs1 path uses: q/kv heads, gate/up rows and down columns of its F slice, o
+// columns of its heads, lm_head rows [vocab_off, vocab_off + V)) ----
+//
+// Each rank's exchange buffer, mapped by its peers (CUDA IPC):
+//   [0, 8 B)          u64 row arrivals of residual exchanges, one per sequence
+//   [8 B, 16 B)       u64 row arrivals of argmax exchanges
+//   bx_amslot         u64 [2][8][B] argmax candidates {value bits | global index << 32}
+//   bx_recv           f32 [2][tp][B][D] o / down partial rows, per sender
+// Counters only grow: exchange x of the batch's life is complete for row b
+// once its counter reaches (x + 1) tp; buffers alternate by the parity of x.
+constexpr int kBatchMaxTp = 8;
+__host__ __device__ inline size_t bx_align(size_t x) { return (x + 255) / 256 * 256; }
+__host__ __device__ inline size_t bx_amslot(int B) { return bx_align(16 * static_cast<size_t>(B)); }
+__host__ __device__ inline size_t bx_recv(int B) { return bx_align(bx_amslot(B) + 2 * kBatchMaxTp * 8 * static_cast<size_t>(B)); }
+__host__ __device__ inline size_t bx_bytes(int tp, int B, int D) { return bx_recv(B) + 2 * static_cast<size_t>(tp) * B * D * 4; }
+
+struct BatchXchg {
+    uint8_t* buf[kBatchMaxTp];  // every rank's buffer, own at [rank]
+    int tp, rank, B, D;
+};
+
+// Residual exchange fused with the next RMSNorm (row b = one CTA): the row's
+// sum of this rank's ks split-K partials goes to every rank's buffer (P2P
+// stores over NVLink), then, once all tp ranks' rows have arrived, h[b] += the
+// tp partial rows summed in rank order (bit-identical on every rank), and
+// x16[b] = rmsnorm(h[b]) * g as residual_rmsnorm_rows.  `xseq` numbers the
+// exchange; a wait that gives up (~2 s) sets *err = 6 and leaves the row.
+tl_status tp_residual_rmsnorm_rows(__half* x16, float* h, const float* part, int ks, size_t part_stride,
+                                   const float* g, const BatchXchg& X, unsigned long long xseq, int* err,
+                                   cudaStream_t s);
+
+// sample_max over the whole vocabulary of each row: every rank sends its
+// slice's best {value, global index} (rank 0 flags a NaN logits[0]) to every
+// rank, which merge them in rank order (= vocabulary order); out[b] = index,
+// pos[b]++.  `aseq` numbers the argmax exchange; timeout as above.
+tl_status tp_argmax_rows(uint32_t* out, const float* logits, int V, int vocab_off, uint32_t* pos, const BatchXchg& X,
+                         unsigned long long aseq, int* err, cudaStream_t s);
+
 // ctx16[b, h hd + i] = merge of the S split partials (fp16, the o_proj input).
 tl_status attention_merge_batch(__half* ctx16, const float* part, int B, int H, int HD, int S, cudaStream_t s);
 
@@ -47,7 +86,11 @@ tl_status argmax_rows(uint32_t* out, const float* logits, int B, int V, uint32_t
 // Every sequence's cache rows [0, n_pos) of every layer = N(0, 1) draws of a
 // counter-based generator keyed by (seed, sequence, layer, k/v, head, position,
 // dim) (splitmix64 + Box-Muller), so any sequence can be regenerated alone.
-tl_status fill_kv_random(const BatchKV& kv, uint64_t seed, int B, int L, int KV, int HD, int n_pos, cudaStream_t s);
+// Under tensor parallelism the local kv heads are global heads kv_off ..
+// kv_off + KV - 1 of KV_total, keyed by their global index: every split of the
+// model sees the same cache contents.
+tl_status fill_kv_random(const BatchKV& kv, uint64_t seed, int B, int L, int KV, int HD, int n_pos, int kv_off,
+                         int KV_total, cudaStream_t s);
 
 // w16 = fp16(w) (fp32 lm_head for the batched logits GEMM).
 tl_status f32_to_f16(__half* w16, const float* w, size_t n, cudaStream_t s);

@@ -1321,6 +1321,12 @@ struct tl_batch {
     uint32_t *tok = nullptr, *pos = nullptr, *next = nullptr;
     float* split = nullptr;  // split-K partials of the small-M GEMMs
     size_t split_floats = 0;
+    // tensor parallelism: this rank's exchange buffer and the peers' (IPC)
+    uint8_t* xbuf = nullptr;
+    uint8_t* xpeer_open[kBatchMaxTp] = {};
+    BatchXchg X = {};
+    unsigned long long xseq = 0, aseq = 0;  // residual / argmax exchanges so far
+    bool connected = false;
     uint32_t* h_pinned = nullptr;       // [B]
     std::vector<size_t> pos_host;
 };
@@ -1353,21 +1359,36 @@ tl_status batch_step(tl_batch* b) {
                                 m->sin_tab, B, H, KV, HD, s));
         TL_TRY(attention_decode_batch(b->part, b->qf, b->bkv, static_cast<int>(l), b->pos, B, H, KV, HD, S, scale, s));
         TL_TRY(attention_merge_batch(b->ctx16, b->part, B, H, HD, S, s));
+        // under tensor parallelism the residual adds sum every rank's partial rows (exchange)
+        auto residual = [&](const float* g) -> tl_status {
+            if (m->tp > 1)
+                return tp_residual_rmsnorm_rows(b->x16, b->hres, b->split, ks, d_stride, g, b->X, b->xseq++, m->err,
+                                                s);
+            return residual_rmsnorm_rows(b->x16, b->hres, b->split, ks, d_stride, g, B, D, s);
+        };
         TL_TRY(gemm_f16_splitk(b->ctx16, B, H * HD, W[1], D, b->split, b->split_floats, &ks, m->err, s));
-        TL_TRY(residual_rmsnorm_rows(b->x16, b->hres, b->split, ks, d_stride, w.g_post, B, D, s));
+        TL_TRY(residual(w.g_post));
         TL_TRY(gemm_f16(kEpiSwiGluF16, b->x16, B, D, W[2], 2 * F, b->act16, F, m->err, s));
         TL_TRY(gemm_f16_splitk(b->act16, B, F, W[3], D, b->split, b->split_floats, &ks, m->err, s));
-        const float* g_next = l + 1 < m->cfg.n_layers ? m->layers[l + 1].g_in : m->norm;
-        TL_TRY(residual_rmsnorm_rows(b->x16, b->hres, b->split, ks, d_stride, g_next, B, D, s));
+        TL_TRY(residual(l + 1 < m->cfg.n_layers ? m->layers[l + 1].g_in : m->norm));
     }
     TL_TRY(gemm_f16(kEpiStoreF32, b->x16, B, D, m->lm16, V, b->logits, V, m->err, s));
-    TL_TRY(argmax_rows(b->next, b->logits, B, V, b->pos, s));
+    if (m->tp > 1)
+        TL_TRY(tp_argmax_rows(b->next, b->logits, V, static_cast<int>(m->rank * m->lV), b->pos, b->X, b->aseq++,
+                              m->err, s));
+    else
+        TL_TRY(argmax_rows(b->next, b->logits, B, V, b->pos, s));
     for (auto& p : b->pos_host) p++;
     return TL_OK;
 }
 
 tl_status batch_ready(const tl_batch* b, size_t steps) {
     TL_REQUIRE(b, "tl_batch: null batch");
+    if (b->m->tp > 1) {
+        if (!b->connected)
+            return set_error(TL_ERR_INVALID_ARGUMENT, "tensor-parallel batch: call tl_batch_tp_connect on every rank");
+        TL_TRY(check_tp_ready(b->m));
+    }
     for (size_t p : b->pos_host)
         if (p + steps > b->max_seq)
             return set_error(TL_ERR_CAPACITY, "tl_batch: position %zu + %zu steps > max_seq %zu", p, steps, b->max_seq);
@@ -1383,7 +1404,10 @@ tl_status tl_batch_create(tl_model* m, int n_seq, size_t max_seq, tl_batch** out
     clear_error();
     TL_REQUIRE(m && out && n_seq > 0 && n_seq <= 4096, "tl_batch_create: bad arguments");
     *out = nullptr;
-    if (m->tp > 1) return set_error(TL_ERR_UNSUPPORTED, "tl_batch_create: not available under tensor parallelism");
+    if (m->tp > 1) {
+        TL_REQUIRE(m->tp <= kBatchMaxTp, "tl_batch_create: tp %d > %d", m->tp, kBatchMaxTp);
+        TL_TRY(check_tp_ready(m));
+    }
     if (max_seq == 0) max_seq = m->max_seq;
     TL_REQUIRE(max_seq <= m->max_seq, "tl_batch_create: max_seq %zu > the model's %zu (RoPE tables)", max_seq,
                m->max_seq);
@@ -1431,6 +1455,16 @@ tl_status tl_batch_create(tl_model* m, int n_seq, size_t max_seq, tl_batch** out
     b->split = b->rows.take<float>(b->split_floats);
     if (!b->split) return set_error(TL_ERR_OUT_OF_MEMORY, "tl_batch rows (internal)");
     TL_CUDA_TRY(cudaMemsetAsync(b->pos, 0, Bn * 4, m->stream));
+    if (m->tp > 1) {  // exchange buffer (mapped by the peers in tl_batch_tp_connect)
+        const size_t xb = bx_bytes(m->tp, n_seq, static_cast<int>(D));
+        TL_CUDA_TRY(cudaMalloc(&b->xbuf, xb));
+        TL_CUDA_TRY(cudaMemsetAsync(b->xbuf, 0, xb, m->stream));
+        b->X.tp = m->tp;
+        b->X.rank = m->rank;
+        b->X.B = n_seq;
+        b->X.D = static_cast<int>(D);
+        b->X.buf[m->rank] = b->xbuf;
+    }
     TL_CUDA_TRY(cudaMallocHost(&b->h_pinned, Bn * 4));
     b->pos_host.assign(Bn, 0);
     TL_CUDA_TRY(cudaStreamSynchronize(m->stream));
@@ -1445,6 +1479,9 @@ tl_status tl_batch_destroy(tl_batch* b) {
     cudaStreamSynchronize(b->m->stream);
     b->kv.release();
     b->rows.release();
+    for (auto* p : b->xpeer_open)
+        if (p) cudaIpcCloseMemHandle(p);
+    if (b->xbuf) cudaFree(b->xbuf);
     if (b->h_pinned) cudaFreeHost(b->h_pinned);
     delete b;
     return TL_OK;
@@ -1456,7 +1493,8 @@ tl_status tl_batch_fill_kv_random(tl_batch* b, uint64_t seed, size_t n_pos) {
     tl_model* m = b->m;
     TL_CUDA_TRY(cudaSetDevice(m->device));
     TL_TRY(fill_kv_random(b->bkv, seed, b->B, static_cast<int>(m->cfg.n_layers), static_cast<int>(m->lKV),
-                          static_cast<int>(m->cfg.head_dim), static_cast<int>(n_pos), m->stream));
+                          static_cast<int>(m->cfg.head_dim), static_cast<int>(n_pos),
+                          static_cast<int>(m->rank * m->lKV), static_cast<int>(m->cfg.n_kv_heads), m->stream));
     for (int i = 0; i < b->B; i++) b->h_pinned[i] = static_cast<uint32_t>(n_pos);
     TL_CUDA_TRY(cudaMemcpyAsync(b->pos, b->h_pinned, b->B * 4, cudaMemcpyHostToDevice, m->stream));
     TL_TRY(sync(m));
@@ -1508,6 +1546,41 @@ tl_status tl_batch_time_decode(tl_batch* b, const uint32_t* tokens, size_t n_ste
     TL_CUDA_TRY(cudaEventElapsedTime(ms, e0, e1));
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
+    return TL_OK;
+}
+
+tl_status tl_batch_tp_handle(const tl_batch* b, void* handle) {
+    clear_error();
+    TL_REQUIRE(b && handle, "tl_batch_tp_handle: null argument");
+    if (b->m->tp < 2) return set_error(TL_ERR_INVALID_ARGUMENT, "tl_batch_tp_handle: model is not tensor-parallel");
+    TL_CUDA_TRY(cudaSetDevice(b->m->device));
+    cudaIpcMemHandle_t h;
+    TL_CUDA_TRY(cudaIpcGetMemHandle(&h, b->xbuf));
+    std::memcpy(handle, &h, sizeof(h));
+    return TL_OK;
+}
+
+tl_status tl_batch_tp_connect(tl_batch* b, const void* handles) {
+    clear_error();
+    TL_REQUIRE(b && handles, "tl_batch_tp_connect: null argument");
+    tl_model* m = b->m;
+    if (m->tp < 2) return set_error(TL_ERR_INVALID_ARGUMENT, "tl_batch_tp_connect: model is not tensor-parallel");
+    if (b->connected) return set_error(TL_ERR_INVALID_ARGUMENT, "tl_batch_tp_connect: already connected");
+    TL_CUDA_TRY(cudaSetDevice(m->device));
+    TL_CUDA_TRY(cudaStreamSynchronize(m->stream));  // the buffer's clear has landed
+    for (int q = 0; q < m->tp; q++) {
+        if (q == m->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t*>(handles) + static_cast<size_t>(q) * TL_TP_HANDLE_BYTES, sizeof(h));
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            return set_error(TL_ERR_CUDA, "tl_batch_tp_connect: opening rank %d's exchange buffer failed: %s", q,
+                             cudaGetErrorString(e));
+        b->xpeer_open[q] = static_cast<uint8_t*>(p);
+        b->X.buf[q] = static_cast<uint8_t*>(p);
+    }
+    b->connected = true;
     return TL_OK;
 }
 

@@ -214,7 +214,8 @@ class Batch:
     def step(self, tokens: Sequence[int], logits: bool = True):
         """One token per sequence; returns (logits [B, V] or None, next tokens [B])."""
         t = np.ascontiguousarray(tokens, dtype=np.uint32)
-        out = np.empty((self.n_seq, self.model.config["vocab_size"]), dtype=np.float32) if logits else None
+        v = self.model.config["vocab_size"] // self.model.tp_size  # this rank's vocabulary slice
+        out = np.empty((self.n_seq, v), dtype=np.float32) if logits else None
         nxt = np.empty(self.n_seq, dtype=np.uint32)
         check(lib().tl_batch_step(self._h, t.ctypes.data, out.ctypes.data if logits else None, nxt.ctypes.data))
         return out, nxt
@@ -228,8 +229,24 @@ class Batch:
         return ms.value, out
 
     def read_kv(self, seq: int, layer: int, pos: int):
+        """K and V rows of one sequence at `pos` (this rank's kv heads under tensor parallelism)."""
         c = self.model.config
-        k = np.empty(c["n_kv_heads"] * c["head_dim"], dtype=np.float32)
+        kv = c["n_kv_heads"] // self.model.tp_size
+        k = np.empty(kv * c["head_dim"], dtype=np.float32)
         v = np.empty_like(k)
         check(lib().tl_batch_read_kv(self._h, seq, layer, pos, k.ctypes.data, v.ctypes.data))
-        return k.reshape(c["n_kv_heads"], c["head_dim"]), v.reshape(c["n_kv_heads"], c["head_dim"])
+        return k.reshape(kv, c["head_dim"]), v.reshape(kv, c["head_dim"])
+
+    def tp_handle(self) -> bytes:
+        """This rank's exchange-buffer handle (tensor parallelism)."""
+        from . import TP_HANDLE_BYTES
+        buf = ctypes.create_string_buffer(TP_HANDLE_BYTES)
+        check(lib().tl_batch_tp_handle(self._h, buf))
+        return buf.raw
+
+    def tp_connect(self, handles: Sequence[bytes]) -> None:
+        """Maps every other rank's exchange buffer (handles in rank order)."""
+        from . import TP_HANDLE_BYTES
+        blob = b"".join(handles)
+        assert len(blob) == TP_HANDLE_BYTES * len(handles)
+        check(lib().tl_batch_tp_connect(self._h, blob))

@@ -26,3 +26,11 @@ def connect(model, group=None) -> None:
     import torch.distributed as dist
     model.tp_connect(gather_handles(model.tp_handle(), group))
     dist.barrier(group)
+
+
+def connect_batch(batch, group=None) -> None:
+    """Same for a tensor-parallel Batch (tl_batch_*): its own exchange buffers
+    carry the residual and argmax exchanges of batched decoding."""
+    import torch.distributed as dist
+    batch.tp_connect(gather_handles(batch.tp_handle(), group))
+    dist.barrier(group)
