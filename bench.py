@@ -62,13 +62,16 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+LM_HEAD_INT8 = False  # --lm-head-int8: the int8 lm_head format extension
+
+
 def make_model_bytes(device: str, layers: int = 32):
     """Seeded Mistral-7B int8 binary, drawn and quantised on `device`."""
     from torchless_b200 import ops, synthetic as S
     t0 = time.time()
     quant = (lambda x: ops.quantize_i8(x)) if device.startswith("cuda") else None
     cfg = dict(S.MISTRAL_7B, num_hidden_layers=layers)
-    w = S.make_torch_model(cfg, seed=SEED, device=device, quantizer=quant)
+    w = S.make_torch_model(cfg, seed=SEED, device=device, quantizer=quant, quant_lm_head=LM_HEAD_INT8)
     log(f"generated {w.size / 1e9:.2f} GB model on {device} in {time.time() - t0:.1f}s")
     return w.buf
 
@@ -282,15 +285,18 @@ def run_ours(args, rank, world, local):
     achieved = top["bytes_per_launch"] / (avg_ms / 1000.0) / 1e9
     peak, peak_kind = peaks()
     # ncu traffic of the 1-GPU launch; a rank's launch under tensor parallelism is not captured
-    traffic = load_traffic().get(top["name"]) if world == 1 and ctx == 0 else None
+    traffic = load_traffic().get(top["name"]) if world == 1 and ctx == 0 and not LM_HEAD_INT8 else None
     total_prof = sum(k["total_ms"] for k in prof)
 
     # bytes of one token at the mean timed position: weights + the K/V rows read
+    w_bytes = 7940898816 - (32000 * 4096 * 4 - 32000 * 4096 * (1 + 4 / 64) if LM_HEAD_INT8 else 0)
     kv_per_pos = 2 * args.layers * 8 * 128 * 4
-    tok_bytes = 7940898816 + kv_per_pos * (start_pos + args.warmup + (args.steps + 1) / 2.0) if ctx > 0 \
-        else 7940898816
+    tok_bytes = w_bytes + kv_per_pos * (start_pos + args.warmup + (args.steps + 1) / 2.0) if ctx > 0 \
+        else w_bytes
     workload = (f"Mistral-7B int8 bs1 greedy decode ({ctx}-token random prompt, {args.steps} tokens)" if ctx > 0
                 else "Mistral-7B int8 bs1 greedy decode (16-token prompt, 128 tokens)")
+    if LM_HEAD_INT8:
+        workload += " [format extension: int8 lm_head]"
     out = {
         "metric": METRIC if ctx == 0 else f"int8 Mistral-7B decode tok/s @bs1, {ctx}-token context",
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -302,7 +308,7 @@ def run_ours(args, rank, world, local):
                    "global_batch": 1, "seq_len": max_seq,
                    "parallelism": f"tp{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (7.94 GB of weights per step)",
-                   "weights_bytes_per_token": 7940898816},
+                   "weights_bytes_per_token": int(w_bytes)},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
         "gpu_launches": launches * args.steps,
         "roofline": {"bound": "hbm", "kernel": top["name"], "achieved": achieved, "peak": peak,
@@ -315,7 +321,7 @@ def run_ours(args, rank, world, local):
         "clocks": clocks.summary(),
         "ids_head": ids[:8],
     }
-    if not args.no_cpu_baseline and world == 1 and ctx == 0:
+    if not args.no_cpu_baseline and world == 1 and ctx == 0 and not LM_HEAD_INT8:
         try:
             v, secs, cores = cpu_reference_sample(buf, args.cpu_layers)
             out["cpu_baseline"] = {
@@ -582,6 +588,8 @@ def main():
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--gemv-sweep", action="store_true",
                     help="isolated int8 GEMV sweep at Mistral-7B shapes (one JSON line per shape)")
+    ap.add_argument("--lm-head-int8", action="store_true",
+                    help="bs1 decode of the same model with its lm_head stored int8 (format extension)")
     ap.add_argument("--context", type=int, default=0,
                     help="bs1 decode after a random prompt of this many tokens (0: the 16-token prompt)")
     ap.add_argument("--layers", type=int, default=32,
@@ -589,6 +597,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    global LM_HEAD_INT8
+    LM_HEAD_INT8 = args.lm_head_int8
     rank, world, local = dist_env()
     if args.gemv_sweep:
         run_gemv_sweep(args)

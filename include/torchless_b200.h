@@ -203,6 +203,8 @@ TL_API tl_status tl_model_load(const char* path, const tl_model_options* opts, t
 TL_API tl_status tl_model_load_buffer(const void* data, size_t size, const tl_model_options* opts,
                                       tl_model** out);
 
+/* Frees the model.  Its batches (tl_batch_create) must be destroyed first:
+ * while any exists this returns TL_ERR_INVALID_ARGUMENT and frees nothing. */
 TL_API tl_status tl_model_destroy(tl_model* m);
 TL_API tl_status tl_model_config(const tl_model* m, tl_config* out);
 

@@ -124,3 +124,25 @@ def test_loader_rejects_unsupported_models(tmp_path):
     w.save(str(p))
     st, msg = _load_status(str(p))
     assert st == 2 and "h/4" in msg
+
+
+def test_int8_lm_head_layout():
+    """quant_lm_head stores lm_head.weight like a _proj tensor: int8, then its
+    per-64-group fp32 scales, each block 64-byte aligned; everything else as
+    the reference exporter writes it."""
+    from torchless_b200 import synthetic as S
+    from torchless_b200.binfmt import ModelFile, quantize_i8
+    plain = ModelFile(S.make_numpy_model(S.TINY, seed=7, norm="random").buf)
+    i8 = ModelFile(S.make_numpy_model(S.TINY, seed=7, norm="random", quant_lm_head=True).buf)
+    t = i8.tensors["lm_head.weight"]
+    assert t.dtype == "int8" and t.offset % 64 == 0 and t.scale_offset % 64 == 0
+    assert plain.tensors["lm_head.weight"].dtype == "f32"
+    w, _ = plain.tensor("lm_head.weight")
+    q, s = i8.tensor("lm_head.weight")
+    q2, s2 = quantize_i8(np.asarray(w))
+    np.testing.assert_array_equal(q, q2)
+    np.testing.assert_array_equal(s, s2)
+    for name in plain.tensors:
+        if name != "lm_head.weight":
+            a, b = plain.tensor(name), i8.tensor(name)
+            np.testing.assert_array_equal(a[0], b[0])

@@ -164,18 +164,25 @@ class ModelFile:
         return self.tensor(f"model.layers.{layer}.{name}")
 
 
+LM_HEAD = "lm_head.weight"
+
+
 def build_header(metadata: dict, tensors: Iterable[Tuple[str, Tuple[int, ...]]], quant: str,
-                 tokenizer: dict) -> Tuple[dict, int]:
+                 tokenizer: dict, quant_lm_head: bool = False) -> Tuple[dict, int]:
     """The header dict and payload size for tensors in the given order.
 
     Offsets follow load_tensor_map (export_mistral.py:107-135): int8 only for
     names containing "_proj" when quant != "f32", each block padded to 64.
+    quant_lm_head (a format extension; the reference exporter keeps the
+    lm_head fp32, export_mistral.py:119) also stores ``lm_head.weight`` as
+    int8 + per-64-group scales, the layout of the ``_proj`` tensors: its dtype
+    entry in the header is what tells a loader.
     """
     header = {"metadata": dict(metadata), "tensors": {}}
     start = 0
     for name, shape in tensors:
         numel = int(np.prod(shape))
-        if "_proj" in name and quant != "f32":
+        if quant != "f32" and ("_proj" in name or (quant_lm_head and name == LM_HEAD)):
             entry = {"dtype": quant, "shape": list(shape)[:4], "offset": start}
             start += numel
             start += pad_to_64(start)
@@ -221,8 +228,8 @@ class BinWriter:
     """
 
     def __init__(self, metadata: dict, tensors: List[Tuple[str, Tuple[int, ...]]], quant: str,
-                 tokenizer: dict, buffer: Optional[np.ndarray] = None):
-        self.header, payload = build_header(metadata, tensors, quant, tokenizer)
+                 tokenizer: dict, buffer: Optional[np.ndarray] = None, quant_lm_head: bool = False):
+        self.header, payload = build_header(metadata, tensors, quant, tokenizer, quant_lm_head)
         hb = json.dumps(self.header).encode("utf-8")
         pad = pad_to_64(8 + len(hb))
         self.header_size = len(hb) + pad

@@ -439,6 +439,7 @@ tl_status fill_kv_random(const BatchKV& kv, uint64_t seed, int B, int L, int KV,
                          int KV_total, cudaStream_t s) {
     TL_REQUIRE(kv_off >= 0 && kv_off + KV <= KV_total, "fill_kv_random: heads %d + %d of %d", kv_off, KV, KV_total);
     const size_t total = static_cast<size_t>(B) * L * 2 * KV * n_pos * HD;
+    if (total == 0) return TL_OK;  // no cached positions to fill
     k_fill_kv_random<<<grid_of(total, 256), 256, 0, s>>>(kv, seed, B, L, KV, HD, n_pos, kv_off, KV_total);
     return check_launch("fill_kv_random");
 }

@@ -233,10 +233,11 @@ __device__ Seg seg_info(const DecodeArgs& a, int s) {
     const int ksD = tile_slices(a.D);
     Seg g;
     if (s >= 4 * a.n_layers) {
+        const int rows = a.lm_i8 ? kTileRowsI8 : kTileRowsF32;
         g.src = a.lm_head;
-        g.n_rb = (a.V + kTileRowsF32 - 1) / kTileRowsF32;
+        g.n_rb = (a.V + rows - 1) / rows;
         g.ksn = ksD;
-        g.tb = kTileBytesF32;
+        g.tb = a.lm_i8 ? kTileBytesI8 : kTileBytesF32;
     } else {
         const DecodeLayer& L = a.layers[s >> 2];
         g.tb = kTileBytesI8;
@@ -1534,26 +1535,34 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         if (cw.t == 0) prefetch_l2(g_next, static_cast<uint32_t>(D) * 4u);  // staged after this phase
         if (!cw.template run_i8<3>(D, F, un, a.h, g_next)) return;
     }
-    // logits = lm_head rmsnorm(h); token = argmax (main.cpp:10-21)
+    // logits = lm_head rmsnorm(h); token = argmax (main.cpp:10-21).  An int8
+    // lm_head runs like a projection: RMSNorm fused into the digit staging,
+    // integer tiles of 16 rows.
+    const bool lm8 = a.lm_i8 != 0;
+    float lm_un = 1.0f;
     if (tp) {
         if (!cw.xchg_wait()) return;
-        cw.template stage_xchg<true>(a.h, a.h2, a.g_final);
+        if (lm8) lm_un = cw.template stage_xchg<false>(a.h, a.h2, a.g_final);
+        else cw.template stage_xchg<true>(a.h, a.h2, a.g_final);
     } else {
         if (!cw.wait_all()) return;
-        cw.stage_f32(a.h, D, a.g_final);
+        if (lm8) lm_un = cw.template stage_digits<true>(a.h, D, a.g_final, nullptr);
+        else cw.stage_f32(a.h, D, a.g_final);
     }
     const int ksD = tile_slices(D);
-    const int n_rb = (a.V + kTileRowsF32 - 1) / kTileRowsF32;
+    const int lm_rows = lm8 ? kTileRowsI8 : kTileRowsF32;
+    const int n_rb = (a.V + lm_rows - 1) / lm_rows;
     int nrl = 0;
-    const int rb0 = cw.template run_tiles<true>(n_rb, ksD, nrl);
+    const int rb0 = lm8 ? cw.template run_tiles<false>(n_rb, ksD, nrl) : cw.template run_tiles<true>(n_rb, ksD, nrl);
     if (rb0 < 0) return;
     float best_v = -INFINITY;
     uint32_t best_i = 0xffffffffu;
     const int t = threadIdx.x, lane = t & 31;
-    for (int j = t; j < nrl * 4; j += kConsumers) {
-        const int row = rb0 * 4 + j;
+    for (int j = t; j < nrl * lm_rows; j += kConsumers) {
+        const int row = rb0 * lm_rows + j;
         if (row < a.V) {
-            const float val = cw.row_sum(j / 4, j % 4, ksD, 4);
+            const float val = lm8 ? cw.row_sum(j / kTileRowsI8, j % kTileRowsI8, ksD, kTileRowsI8) * lm_un
+                                  : cw.row_sum(j / kTileRowsF32, j % kTileRowsF32, ksD, kTileRowsF32);
             a.logits[row] = val;
             if (better(val, row, best_v, best_i)) {
                 best_v = val;
@@ -1774,6 +1783,7 @@ bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers
     pb = std::max(pb, need(2 * F, kTileRowsI8, D));
     pb = std::max(pb, need(D, kTileRowsI8, F));
     pb = std::max(pb, need(V, kTileRowsF32, D));
+    pb = std::max(pb, need(V, kTileRowsI8, D));  // int8 lm_head
     const size_t fixed = fixed_bytes(D, F, HD, pb);
     if (static_cast<size_t>(max_smem) <= fixed) return false;
     int st = static_cast<int>((static_cast<size_t>(max_smem) - fixed) / (kStageBytes + 16));

@@ -58,7 +58,8 @@ struct DecodeArgs {
     int n_layers;
     const float* embed;         // [V, D]
     const float* g_final;       // [D]
-    const uint8_t* lm_head;     // fp32 tiles
+    const uint8_t* lm_head;     // fp32 tiles, or int8 tiles when lm_i8
+    int lm_i8;                  // lm_head stored int8 + group scales (format extension)
     const float* cos_tab;       // [max_seq][hd/2]
     const float* sin_tab;
     float* h;                   // residual stream [D]

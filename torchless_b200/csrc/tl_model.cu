@@ -230,6 +230,11 @@ struct tl_model {
     DeviceArena weights, state;
     std::vector<LayerW> layers;
     float *embed = nullptr, *norm = nullptr, *lm_head = nullptr;
+    // lm_head stored int8 + group scales (format extension): lm_q / lm_s (1 / s) instead of lm_head
+    int n_batches = 0;  // live tl_batch objects on this model
+    bool lm_i8 = false;
+    int8_t* lm_q = nullptr;
+    float* lm_s = nullptr;
     float *kc = nullptr, *vc = nullptr, *cos_tab = nullptr, *sin_tab = nullptr;
     float *h = nullptr, *qkv = nullptr, *ctx = nullptr, *act = nullptr, *logits = nullptr;
     float *attn_part = nullptr, *am_v = nullptr;
@@ -355,7 +360,13 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     const TensorRec *emb, *nrm, *lmh;
     TL_TRY(find(h, "model.embed_tokens.weight", "f32", {V, D}, emb));
     TL_TRY(find(h, "model.norm.weight", "f32", {D}, nrm));
-    TL_TRY(find(h, "lm_head.weight", "f32", {V, D}, lmh));
+    // lm_head: fp32 as export_mistral.py writes it (:119), or int8 + per-64-group
+    // scales like the _proj tensors (format extension; the header's dtype says which)
+    const auto lm_it = h.tensors.find("lm_head.weight");
+    const bool lm8 = lm_it != h.tensors.end() && lm_it->second.dtype == "int8";
+    TL_TRY(find(h, "lm_head.weight", lm8 ? "int8" : "f32", {V, D}, lmh));
+    if (lm8 && (!lmh->has_scales || D % 64))
+        return set_error(TL_ERR_FORMAT, "int8 lm_head needs per-64-group scales");
     for (int64_t l = 0; l < L; l++) {
         const std::string p = "model.layers." + std::to_string(l) + ".";
         LayerRecs& r = recs[l];
@@ -408,17 +419,32 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
 
     // ---- weights arena (this rank's slices) ----
     using A = DeviceArena;
-    size_t wbytes = A::pad(V * D * 4) + A::pad(Vl * D * 4) + A::pad(D * 4);
+    size_t wbytes = A::pad(V * D * 4) + (lm8 ? A::pad(Vl * D) + A::pad(Vl * D / 64 * 4) : A::pad(Vl * D * 4)) +
+                    A::pad(D * 4);
     const size_t per_layer = A::pad(NQKVl * D) + A::pad(D * Hl * HD) + 2 * A::pad(Fl * D) + A::pad(D * Fl) +
                              A::pad(NQKVl * D / 64 * 4) + A::pad(D * Hl * HD / 64 * 4) + 2 * A::pad(Fl * D / 64 * 4) +
                              A::pad(D * Fl / 64 * 4) + 2 * A::pad(D * 4);
     wbytes += per_layer * L;
     TL_TRY(m->weights.reserve(wbytes));
     m->embed = m->weights.take<float>(V * D);
-    m->lm_head = m->weights.take<float>(Vl * D);
+    m->lm_i8 = lm8;
+    if (lm8) {
+        m->lm_q = m->weights.take<int8_t>(Vl * D);
+        m->lm_s = m->weights.take<float>(Vl * D / 64);
+    } else {
+        m->lm_head = m->weights.take<float>(Vl * D);
+    }
     m->norm = m->weights.take<float>(D);
     TL_TRY(upload(m->embed, h, emb->offset, V * D * 4));
-    TL_TRY(upload(m->lm_head, h, lmh->offset + static_cast<uint64_t>(rank) * Vl * D * 4, Vl * D * 4));
+    if (lm8) {  // this rank's vocabulary rows and their scales; stored s = 127/absmax becomes 1/s
+        TL_TRY(upload(m->lm_q, h, lmh->offset + static_cast<uint64_t>(rank) * Vl * D, Vl * D));
+        TL_TRY(upload(m->lm_s, h, lmh->scale_offset + static_cast<uint64_t>(rank) * Vl * (D / 64) * 4,
+                      Vl * (D / 64) * 4));
+        k_invert<<<256, 256, 0, m->stream>>>(m->lm_s, static_cast<size_t>(Vl * D / 64));
+        TL_TRY(check_launch("invert lm_head scales"));
+    } else {
+        TL_TRY(upload(m->lm_head, h, lmh->offset + static_cast<uint64_t>(rank) * Vl * D * 4, Vl * D * 4));
+    }
     TL_TRY(upload(m->norm, h, nrm->offset, D * 4));
     m->layers.resize(L);
     const int64_t G = D / 64;  // scale groups per row of a [*, D] tensor
@@ -512,7 +538,8 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     if (m->persistent) {
         const size_t per = tiles_i8_bytes(NQKVl, D) + tiles_i8_bytes(D, Hl * HD) + tiles_i8_bytes(2 * Fl, D) +
                            tiles_i8_bytes(D, Fl);
-        TL_TRY(m->tiles.reserve(per * L + tiles_f32_bytes(Vl, D) + 256 * (4 * L + 1)));
+        const size_t lm_tiles = lm8 ? tiles_i8_bytes(Vl, D) : tiles_f32_bytes(Vl, D);
+        TL_TRY(m->tiles.reserve(per * L + lm_tiles + 256 * (4 * L + 1)));
         std::vector<DecodeLayer> dl(L);
         for (int64_t l = 0; l < L; l++) {
             const LayerW& w = m->layers[l];
@@ -526,9 +553,11 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
             TL_TRY(repack_i8(t2, w.w2, w.s2, D, Fl, m->stream));
             dl[l] = DecodeLayer{tq, to, t13, t2, w.g_in, w.g_post, nullptr, nullptr};
         }
-        uint8_t* tl = m->tiles.take<uint8_t>(tiles_f32_bytes(Vl, D));
-        TL_TRY(repack_f32(tl, m->lm_head, Vl, D, m->stream));
+        uint8_t* tl = m->tiles.take<uint8_t>(lm_tiles);
+        if (lm8) TL_TRY(repack_i8(tl, m->lm_q, m->lm_s, Vl, D, m->stream));
+        else TL_TRY(repack_f32(tl, m->lm_head, Vl, D, m->stream));
         m->dargs.lm_head = tl;
+        m->dargs.lm_i8 = lm8 ? 1 : 0;
         TL_CUDA_TRY(cudaMalloc(&m->d_layers, sizeof(DecodeLayer) * L));
         // KV pointers are filled once the state arena exists (below).
         m->dargs.layers = m->d_layers;
@@ -707,7 +736,7 @@ tl_status build_steps(tl_model* m) {
         const double Vr = double(m->lV);
         // int8 weights + fp32 scales of every projection, fp32 lm_head, norms, one embedding row
         const double per_layer = (NQKV * D + D * H * HD + 3.0 * F * D) * (1 + 4.0 / 64) + 8.0 * D;
-        const double fixed = per_layer * L + Vr * D * 4 + 8.0 * D;
+        const double fixed = per_layer * L + Vr * D * (m->lm_i8 ? 1 + 4.0 / 64 : 4.0) + 8.0 * D;
         m->steps.push_back({"decode_step",
                             [=] { return fixed + 2.0 * L * KV * (double(m->pos) + 1) * HD * 4; },
                             [=](cudaStream_t s, bool) {
@@ -720,6 +749,19 @@ tl_status build_steps(tl_model* m) {
                             return launch_embed(m->h, m->embed, m->d_token, D, s, pdl);
                         }});
     for (int l = 0; l < static_cast<int>(c.n_layers); l++) add_layer_steps(m, l, m->steps);
+    if (m->lm_i8) {  // int8 lm_head: the projection GEMV with the final norm fused, then the argmax
+        m->steps.push_back({"gemv_lm_head_i8", [=] { return double(V) * D * (1 + 4.0 / 64) + 8.0 * D + 4.0 * V; },
+                            [=](cudaStream_t s, bool pdl) {
+                                GemvI8Args a = {};
+                                a.w = m->lm_q; a.s = m->lm_s; a.x = m->h; a.g = m->norm; a.eps = 1e-5f;
+                                a.y = m->logits; a.n = V; a.d = D;
+                                return launch_gemv_i8(a, I8Mode::Store, true, true, s, pdl);
+                            }});
+        m->steps.push_back({"argmax", [=] { return 4.0 * V; },
+                            [=](cudaStream_t s, bool) {
+                                return argmax_step(m->d_token, m->d_hist, m->d_pos, m->logits, V, s);
+                            }});
+    } else
     m->steps.push_back({"gemv_lm_head_argmax", [=] { return double(V) * D * 4 + 8.0 * D + 4.0 * V; },
                         [=](cudaStream_t s, bool pdl) {
                             GemvF32Args a = {};
@@ -939,6 +981,9 @@ tl_status tl_model_load(const char* path, const tl_model_options* opts, tl_model
 tl_status tl_model_destroy(tl_model* m) {
     clear_error();
     if (!m) return TL_OK;
+    if (m->n_batches > 0)  // each holds the model; destroying it first would leave them dangling
+        return set_error(TL_ERR_INVALID_ARGUMENT, "tl_model_destroy: %d batch(es) of this model still exist; "
+                                                  "tl_batch_destroy them first", m->n_batches);
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
@@ -1092,12 +1137,20 @@ tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* log
     TL_CUDA_TRY(cudaMemcpyAsync(m->h, m->p_h + static_cast<size_t>(M - 1) * D, D * 4, cudaMemcpyDeviceToDevice, s));
     m->h_pinned[2] = static_cast<uint32_t>(p0 + M - 1);
     TL_CUDA_TRY(cudaMemcpyAsync(m->d_pos, m->h_pinned + 2, 4, cudaMemcpyHostToDevice, s));
-    GemvF32Args a = {};
-    a.w = m->lm_head; a.x = m->h; a.g = m->norm; a.eps = 1e-5f; a.y = m->logits;
-    a.n = V; a.d = D;
-    a.part_v = m->am_v; a.part_i = m->am_i; a.counter = m->am_cnt;
-    a.out_token = m->d_token; a.history = m->d_hist; a.pos = m->d_pos;
-    TL_TRY(launch_gemv_f32(a, true, true, s, false));
+    if (m->lm_i8) {
+        GemvI8Args a = {};
+        a.w = m->lm_q; a.s = m->lm_s; a.x = m->h; a.g = m->norm; a.eps = 1e-5f; a.y = m->logits;
+        a.n = V; a.d = D;
+        TL_TRY(launch_gemv_i8(a, I8Mode::Store, true, true, s, false));
+        TL_TRY(argmax_step(m->d_token, m->d_hist, m->d_pos, m->logits, V, s));
+    } else {
+        GemvF32Args a = {};
+        a.w = m->lm_head; a.x = m->h; a.g = m->norm; a.eps = 1e-5f; a.y = m->logits;
+        a.n = V; a.d = D;
+        a.part_v = m->am_v; a.part_i = m->am_i; a.counter = m->am_cnt;
+        a.out_token = m->d_token; a.history = m->d_hist; a.pos = m->d_pos;
+        TL_TRY(launch_gemv_f32(a, true, true, s, false));
+    }
     if (m->temperature > 0.f)
         TL_TRY(sample_step(m->d_token, m->d_hist, m->d_pos, m->logits, V, m->temperature, m->sample_seed, s));
     if (ms_out) TL_CUDA_TRY(cudaEventRecord(e1, s));
@@ -1419,7 +1472,8 @@ tl_status tl_batch_create(tl_model* m, int n_seq, size_t max_seq, tl_batch** out
     if (!m->lm16) {
         TL_TRY(m->lm16_arena.reserve(DeviceArena::pad(V * D * 2)));
         m->lm16 = m->lm16_arena.take<__half>(V * D);
-        TL_TRY(f32_to_f16(m->lm16, m->lm_head, static_cast<size_t>(V) * D, m->stream));
+        if (m->lm_i8) TL_TRY(dequant_f16(m->lm16, m->lm_q, m->lm_s, nullptr, nullptr, V, D, false, m->stream));
+        else TL_TRY(f32_to_f16(m->lm16, m->lm_head, static_cast<size_t>(V) * D, m->stream));
     }
     std::unique_ptr<tl_batch> b(new tl_batch());
     b->m = m;
@@ -1468,6 +1522,7 @@ tl_status tl_batch_create(tl_model* m, int n_seq, size_t max_seq, tl_batch** out
     TL_CUDA_TRY(cudaMallocHost(&b->h_pinned, Bn * 4));
     b->pos_host.assign(Bn, 0);
     TL_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    m->n_batches++;
     *out = b.release();
     return TL_OK;
 }
@@ -1483,6 +1538,7 @@ tl_status tl_batch_destroy(tl_batch* b) {
         if (p) cudaIpcCloseMemHandle(p);
     if (b->xbuf) cudaFree(b->xbuf);
     if (b->h_pinned) cudaFreeHost(b->h_pinned);
+    b->m->n_batches--;
     delete b;
     return TL_OK;
 }

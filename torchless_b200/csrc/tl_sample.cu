@@ -73,7 +73,26 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample_step(uint32_t* token,
     }
 }
 
+__global__ void __launch_bounds__(kSampleThreads) k_argmax_step(uint32_t* token, uint32_t* history, unsigned* pos,
+                                                                 const float* logits, int n) {
+    __shared__ float sv[kSampleThreads / 32];
+    __shared__ uint32_t si[kSampleThreads / 32];
+    const uint32_t v = argmax_block(logits, n, sv, si);
+    if (threadIdx.x == 0) {
+        const unsigned p = *pos;
+        *token = v;
+        history[p] = v;
+        *pos = p + 1;
+    }
+}
+
 }  // namespace
+
+tl_status argmax_step(uint32_t* token, uint32_t* history, unsigned* pos, const float* logits, int V, cudaStream_t s) {
+    TL_REQUIRE(V > 0, "argmax_step: V %d", V);
+    k_argmax_step<<<1, kSampleThreads, 0, s>>>(token, history, pos, logits, V);
+    return check_launch("argmax_step");
+}
 
 tl_status sample_step(uint32_t* token, uint32_t* history, const unsigned* pos, const float* logits, int V, float temp,
                       uint64_t seed, cudaStream_t s) {

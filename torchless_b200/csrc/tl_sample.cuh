@@ -119,6 +119,10 @@ __device__ uint32_t sample_block(const float* logits, int n, float temp, float r
     return res == 0xffffffffu ? static_cast<uint32_t>(n - 1) : res;
 }
 
+// sample_max (main.cpp:10-21) of logits[0, V) as one step's token: *token,
+// history[*pos] = the index, then (*pos)++ (one CTA).
+tl_status argmax_step(uint32_t* token, uint32_t* history, unsigned* pos, const float* logits, int V, cudaStream_t s);
+
 // After a greedy lm_head step that wrote token / history[pos - 1] and
 // advanced *pos: replaces the token with the sample at temperature temp of
 // logits[0, V) using sample_uniform(seed, *pos - 1) (one CTA).

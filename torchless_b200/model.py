@@ -7,6 +7,7 @@ library here are host numpy arrays.
 from __future__ import annotations
 
 import ctypes
+import weakref
 from typing import Dict, List, Optional, Sequence
 
 import numpy as np
@@ -24,6 +25,7 @@ class Model:
 
     def __init__(self, handle: ctypes.c_void_p, tp_size: int = 1, tp_rank: int = 0):
         self._h = handle
+        self._batches = weakref.WeakSet()  # live Batch objects, closed before the model
         self.tp_size, self.tp_rank = max(1, tp_size), tp_rank
         cfg = tl_config()
         check(lib().tl_model_config(self._h, ctypes.byref(cfg)))
@@ -74,6 +76,8 @@ class Model:
 
     def close(self) -> None:
         if self._h:
+            for b in list(self._batches):  # a model outlives its batches
+                b.close()
             check(lib().tl_model_destroy(self._h))
             self._h = None
 
@@ -196,6 +200,7 @@ class Batch:
         h = ctypes.c_void_p()
         check(lib().tl_batch_create(model._h, n_seq, max_seq, ctypes.byref(h)))
         self._h = h
+        model._batches.add(self)
 
     def close(self) -> None:
         if self._h:

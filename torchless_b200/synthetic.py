@@ -90,9 +90,11 @@ def numpy_tensors(cfg: dict, seed: int, std: float = 0.02,
 
 
 def make_numpy_model(cfg: dict, seed: int, quant: str = "int8", std: float = 0.02,
-                     norm: str = "ones") -> BinWriter:
-    """A complete model binary built on the CPU (small configs)."""
-    w = BinWriter(metadata_from_hf(cfg, quant), tensor_list(cfg), quant, PLACEHOLDER_TOKENIZER)
+                     norm: str = "ones", quant_lm_head: bool = False) -> BinWriter:
+    """A complete model binary built on the CPU (small configs).  quant_lm_head:
+    the lm_head stored int8 too (format extension, see binfmt.build_header)."""
+    w = BinWriter(metadata_from_hf(cfg, quant), tensor_list(cfg), quant, PLACEHOLDER_TOKENIZER,
+                  quant_lm_head=quant_lm_head)
     for name, x in numpy_tensors(cfg, seed, std, norm):
         w.put_fp32(name, x)
     return w
@@ -100,7 +102,7 @@ def make_numpy_model(cfg: dict, seed: int, quant: str = "int8", std: float = 0.0
 
 def make_torch_model(cfg: dict, seed: int, quant: str = "int8", std: float = 0.02,
                      norm: str = "ones", device: str = "cuda", quantizer=None,
-                     buffer: Optional[np.ndarray] = None) -> BinWriter:
+                     buffer: Optional[np.ndarray] = None, quant_lm_head: bool = False) -> BinWriter:
     """A complete model binary whose random draws happen on ``device``.
 
     ``quantizer(x_device) -> (q_device, scales_device)`` quantises on the
@@ -110,7 +112,7 @@ def make_torch_model(cfg: dict, seed: int, quant: str = "int8", std: float = 0.0
     import torch
 
     w = BinWriter(metadata_from_hf(cfg, quant), tensor_list(cfg), quant, PLACEHOLDER_TOKENIZER,
-                  buffer=buffer)
+                  buffer=buffer, quant_lm_head=quant_lm_head)
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     for name, shape in tensor_list(cfg):
