@@ -186,6 +186,13 @@ typedef struct tl_model_options {
                      /*    fits (default), else per-op kernels; 1: per-op kernels */
     int tp_size;     /* tensor-parallel ranks (0 or 1: none; 2, 4, 8)              */
     int tp_rank;     /* this process's rank in [0, tp_size)                        */
+    int sliding_window; /* 0: attend to every cached position, as the reference     */
+                        /*    (modules.cpp:75-83) does (default); > 0: only the     */
+                        /*    last W positions (HF Mistral's sliding window);       */
+                        /*    < 0: W = the binary's sliding_window (its config      */
+                        /*    field, parameters.cpp:41, unused by the reference).   */
+                        /*    Opt-in: results then differ from the reference's past */
+                        /*    W positions.                                          */
 } tl_model_options;
 
 /* Bytes of one rank's exchange-buffer handle (tl_model_tp_handle). */

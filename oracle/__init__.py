@@ -40,7 +40,7 @@ def _f(a: np.ndarray):
 
 class tlo_config(ctypes.Structure):
     _fields_ = [(n, _S) for n in ("hidden", "inter", "n_layers", "n_heads", "n_kv_heads", "vocab",
-                                  "head_dim", "max_seq")] + [("rope_theta", _F)]
+                                  "head_dim", "max_seq")] + [("rope_theta", _F), ("window", _S)]
 
 
 _oracle: Optional[ctypes.CDLL] = None
@@ -150,11 +150,13 @@ _GLOBAL = {"model.embed_tokens.weight": 0, "model.norm.weight": 1, "lm_head.weig
 class OracleModel:
     """Model<T>::forward restated in C, over a binfmt.ModelFile."""
 
-    def __init__(self, mf, max_seq: int = 1024):
+    def __init__(self, mf, max_seq: int = 1024, window: int = 0):
+        """window > 0: sliding-window attention over the last `window` positions
+        (an opt-in departure from the reference, which attends to all)."""
         self.mf = mf  # keeps the buffer alive
         c = mf.config
         cfg = tlo_config(c.hidden_size, c.intermediate_size, c.n_layers, c.n_heads, c.n_kv_heads,
-                         c.vocab_size, c.head_dim, max_seq, c.rope_theta)
+                         c.vocab_size, c.head_dim, max_seq, c.rope_theta, window)
         L = oracle_lib()
         self._h = L.tlo_model_new(ctypes.byref(cfg))
         if not self._h:

@@ -275,6 +275,10 @@ TLO_API void tlo_quantize(int8_t* q, float* scales, const float* x,
 typedef struct {
     size_t hidden, inter, n_layers, n_heads, n_kv_heads, vocab, head_dim, max_seq;
     float rope_theta;
+    /* 0: every cached position (the reference).  W > 0: sliding-window
+     * attention over the last W positions (HF Mistral's sliding_window; the
+     * reference parses it, parameters.cpp:41, and never uses it). */
+    size_t window;
 } tlo_config;
 
 /* Tensor kinds, mirroring the names the reference looks up with
@@ -403,15 +407,17 @@ static void tlo_attention(tlo_model* m, size_t l) {
     /* 1/sqrt(head_dim) is evaluated in double and passed as a float. */
     const float scale = (float)(1.0 / sqrt((double)hd));
     const size_t npos = m->pos + 1;
+    const size_t lo = (c->window > 0 && npos > c->window) ? npos - c->window : 0;
+    const size_t span = npos - lo; /* positions lo .. pos */
     for (size_t h = 0; h < c->n_heads; h++) {
         const size_t kh = h / 4; /* hard-coded GQA ratio, modules.cpp:70-71 */
-        const float* kcache = m->kc + (l * c->n_kv_heads + kh) * c->max_seq * hd;
-        const float* vcache = m->vc + (l * c->n_kv_heads + kh) * c->max_seq * hd;
+        const float* kcache = m->kc + ((l * c->n_kv_heads + kh) * c->max_seq + lo) * hd;
+        const float* vcache = m->vc + ((l * c->n_kv_heads + kh) * c->max_seq + lo) * hd;
         float* sc = m->scores + h * c->max_seq;
-        tlo_matmul_f32(sc, kcache, m->q + h * hd, npos, hd);
-        tlo_mul_scalar(sc, sc, scale, npos);
-        tlo_softmax(sc, sc, npos);
-        tlo_row_matmul(m->ctx + h * hd, sc, vcache, npos, hd);
+        tlo_matmul_f32(sc, kcache, m->q + h * hd, span, hd);
+        tlo_mul_scalar(sc, sc, scale, span);
+        tlo_softmax(sc, sc, span);
+        tlo_row_matmul(m->ctx + h * hd, sc, vcache, span, hd);
     }
     tlo_linear(m->h, &W[TLO_WO], m->ctx);
 }

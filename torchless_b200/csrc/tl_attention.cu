@@ -78,8 +78,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnArgs a
     }
 
     const int npos = static_cast<int>(pos) + 1;
-    const int chunk = (npos + S - 1) / S;
-    const int p0 = s * chunk;
+    const int lo = a.window > 0 ? max(0, npos - a.window) : 0;  // attended positions [lo, pos]
+    const int chunk = (npos - lo + S - 1) / S;
+    const int p0 = lo + s * chunk;
     const int p1 = min(npos, p0 + chunk);
 
     float q[VPL];

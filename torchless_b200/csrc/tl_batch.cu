@@ -47,15 +47,16 @@ constexpr int kBW = 8;  // warps per attention CTA
 template <int HD>
 __global__ void __launch_bounds__(kBW * 32) k_attention_decode_batch(float* part, const float* qf, BatchKV kv,
                                                                      int layer, const uint32_t* pos, int H, int S,
-                                                                     float scale) {
+                                                                     float scale, int window) {
     static_assert(HD == 128, "lane owns 4 of 128 dims");
     constexpr int QPG = 4, W = HD + 2, G = 8;  // heads per kv head, partial row, positions per group
     __shared__ float wp[kBW * QPG * W];
     const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int npos = static_cast<int>(pos[b]) + 1;
-    const int chunk = (npos + S - 1) / S;
-    const int p0 = s * chunk, p1 = min(npos, p0 + chunk);
+    const int lo = window > 0 ? max(0, npos - window) : 0;  // attended positions [lo, pos]
+    const int chunk = (npos - lo + S - 1) / S;
+    const int p0 = lo + s * chunk, p1 = min(npos, p0 + chunk);
     const float* kc = kv.k + b * kv.seq_stride + layer * kv.layer_stride + static_cast<size_t>(g) * kv.max_seq * HD;
     const float* vc = kv.v + b * kv.seq_stride + layer * kv.layer_stride + static_cast<size_t>(g) * kv.max_seq * HD;
     float4 q[QPG], acc[QPG];
@@ -396,11 +397,11 @@ tl_status rope_cache_batch(float* qf, const float* part, int ks, size_t part_str
 }
 
 tl_status attention_decode_batch(float* part, const float* qf, const BatchKV& kv, int layer, const uint32_t* pos,
-                                 int B, int H, int KV, int HD, int S, float scale, cudaStream_t s) {
+                                 int B, int H, int KV, int HD, int S, float scale, int window, cudaStream_t s) {
     TL_REQUIRE(H == 4 * KV && S >= 1, "attention_decode_batch: H == 4 KV, S >= 1");
     const dim3 grid(S, KV, B);
     if (HD != 128) return set_error(TL_ERR_UNSUPPORTED, "attention_decode_batch: head_dim %d (128 built)", HD);
-    k_attention_decode_batch<128><<<grid, kBW * 32, 0, s>>>(part, qf, kv, layer, pos, H, S, scale);
+    k_attention_decode_batch<128><<<grid, kBW * 32, 0, s>>>(part, qf, kv, layer, pos, H, S, scale, window);
     return check_launch("attention_decode_batch");
 }
 

@@ -31,11 +31,11 @@ tl_status rope_cache_batch(float* qf, const float* part, int ks, size_t part_str
                            int HD, cudaStream_t s);
 
 // Attention (modules.cpp:58-88) of each sequence's new query over its cache
-// positions [0, pos[b]] in S splits; CTA (b, kv head g, split) serves the 4 q
+// positions [0, pos[b]] (window > 0: the last `window` of them) in S splits; CTA (b, kv head g, split) serves the 4 q
 // heads g * 4 .. g * 4 + 3 (kv head h / 4, modules.cpp:70), so every K / V row
 // is read once.  part[(b H + h) S + split] = {max, sum, 0, 0, acc[hd]}.
 tl_status attention_decode_batch(float* part, const float* qf, const BatchKV& kv, int layer, const uint32_t* pos,
-                                 int B, int H, int KV, int HD, int S, float scale, cudaStream_t s);
+                                 int B, int H, int KV, int HD, int S, float scale, int window, cudaStream_t s);
 
 // ---- tensor parallelism (rank r of tp holds the Megatron-style slice the
 // bs1 path uses: q/kv heads, gate/up rows and down columns of its F slice, o

@@ -941,15 +941,22 @@ struct Consumer {
         return F32 ? 1.0f : ldexpf(1.0f, -k);
     }
 
+    // The query at `pos` attends to positions [attn_lo(pos), pos]: all of them
+    // (modules.cpp:75-83), or the last a.window with a sliding window.
+    __device__ int attn_lo(unsigned pos) const {
+        return a.window > 0 ? ::max(0, static_cast<int>(pos) + 1 - a.window) : 0;
+    }
+    __device__ int attn_span(unsigned pos) const { return static_cast<int>(pos) + 1 - attn_lo(pos); }
     // GQA attention (attention_gqa) at this position?
     __device__ bool gqa(unsigned pos) const {
-        return a.HD == 128 && a.gqa_splits > 0 && static_cast<int>(pos) + 1 >= a.gqa_from;
+        return a.HD == 128 && a.gqa_splits > 0 && attn_span(pos) >= a.gqa_from;
     }
-    // Splits over cached positions for attention at `pos`: one per a.gqa_rows
-    // (GQA, at most a.gqa_splits) or per 64 (per head, at most a.splits).
+    // Splits over the attended positions: one per a.gqa_rows (GQA, at most
+    // a.gqa_splits) or per 64 (per head, at most a.splits).
     __device__ int attn_splits(unsigned pos) const {
-        if (gqa(pos)) return ::min(a.gqa_splits, (static_cast<int>(pos) + a.gqa_rows) / a.gqa_rows);
-        return ::min(a.splits, (static_cast<int>(pos) + 64) / 64);
+        const int span = attn_span(pos);
+        if (gqa(pos)) return ::min(a.gqa_splits, (span + a.gqa_rows - 1) / a.gqa_rows);
+        return ::min(a.splits, (span + 63) / 64);
     }
 
     // Thread 0 polls until kv group g's q, k and v rows of this layer are
@@ -986,9 +993,9 @@ struct Consumer {
         const int units = gqa(pos) ? a.KV * S : a.H * S;
         if (t != 0 || u >= units || pos == 0) return;
         const int s = u % S, kh = gqa(pos) ? u / S : (u / S) / 4;
-        const int npos = static_cast<int>(pos);  // rows 0 .. pos - 1 are cached
-        const int chunk = (npos + 1 + S - 1) / S;
-        const int p0 = s * chunk, p1 = min(npos, p0 + chunk);
+        const int npos = static_cast<int>(pos);  // rows .. pos - 1 are cached
+        const int chunk = (attn_span(pos) + S - 1) / S;
+        const int p0 = attn_lo(pos) + s * chunk, p1 = min(npos, p0 + chunk);
         if (p1 <= p0) return;
         const DecodeLayer& L = a.layers[layer];
         const size_t off = (static_cast<size_t>(kh) * a.max_seq + p0) * HD;
@@ -1053,8 +1060,8 @@ struct Consumer {
                 }
             }
             const int npos = static_cast<int>(pos) + 1;
-            const int chunk = (npos + S - 1) / S;
-            const int p0 = s * chunk, p1 = min(npos, p0 + chunk);
+            const int chunk = (attn_span(pos) + S - 1) / S;
+            const int p0 = attn_lo(pos) + s * chunk, p1 = min(npos, p0 + chunk);
             float4 q[QPG], acc[QPG];
             float m[QPG];
 #pragma unroll
@@ -1251,8 +1258,8 @@ struct Consumer {
             }
         }
         const int npos = static_cast<int>(pos) + 1;
-        const int chunk = (npos + S - 1) / S;
-        const int p0 = s * chunk, p1 = min(npos, p0 + chunk);
+        const int chunk = (attn_span(pos) + S - 1) / S;
+        const int p0 = attn_lo(pos) + s * chunk, p1 = min(npos, p0 + chunk);
         float q[VPL], acc[VPL];
 #pragma unroll
         for (int j = 0; j < VPL; j++) {

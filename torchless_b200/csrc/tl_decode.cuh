@@ -85,6 +85,7 @@ struct DecodeArgs {
     // gqa_splits splits; gqa_splits 0 = per-head attention only.
     int gqa_splits, gqa_from;
     int gqa_rows;               // GQA: cached positions per split (at least)
+    int window;                 // > 0: attention over the last `window` positions (sliding window)
     // Sampling (main.cpp:23-43) in place of sample_max when temperature > 0:
     // the uniform draw of position pos is sample_uniform(sample_seed, pos).
     float temperature;

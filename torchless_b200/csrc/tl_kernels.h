@@ -41,6 +41,7 @@ struct AttnArgs {
     unsigned* counters;    // scratch: [H], zero between launches
     int n_heads, n_kv_heads, head_dim, max_seq, splits;
     float scale;           // (float)(1/sqrt(head_dim))
+    int window;            // > 0: attend to the last `window` positions only (sliding window)
 };
 tl_status launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 

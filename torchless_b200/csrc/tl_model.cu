@@ -232,6 +232,7 @@ struct tl_model {
     float *embed = nullptr, *norm = nullptr, *lm_head = nullptr;
     // lm_head stored int8 + group scales (format extension): lm_q / lm_s (1 / s) instead of lm_head
     int n_batches = 0;  // live tl_batch objects on this model
+    int window = 0;     // > 0: sliding-window attention over the last `window` positions (opt-in)
     bool lm_i8 = false;
     int8_t* lm_q = nullptr;
     float* lm_s = nullptr;
@@ -385,6 +386,15 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     m->cfg = c;
     m->device = opts ? opts->device : 0;
     m->max_seq = (opts && opts->max_seq) ? opts->max_seq : 1024;
+    // sliding window (opt-in; the reference attends to every position): 0 off,
+    // < 0 the binary's sliding_window (parameters.cpp:41), > 0 that many positions
+    if (opts && opts->sliding_window != 0) {
+        const long long w = opts->sliding_window < 0 ? static_cast<long long>(c.sliding_window)
+                                                     : static_cast<long long>(opts->sliding_window);
+        TL_REQUIRE(w > 0 && w < (1ll << 30), "sliding_window: %lld positions (the binary says %zu)", w,
+                   c.sliding_window);
+        m->window = static_cast<int>(w);
+    }
     m->use_graph = opts ? opts->use_graph != 0 : true;
     // Tensor parallelism (Megatron split of modules.cpp's layers): this rank
     // keeps q heads / kv heads / F rows / vocab rows [rank n / tp, (rank + 1) n / tp).
@@ -635,7 +645,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
             TL_CUDA_TRY(cudaMemset(m->xbuf, 0, xb));
             d.xpeer[rank] = m->xbuf;
         }
-        d.max_seq = static_cast<int>(m->max_seq); d.splits = m->mega_splits;
+        d.max_seq = static_cast<int>(m->max_seq); d.splits = m->mega_splits; d.window = m->window;
         d.attn_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
     }
 
@@ -697,6 +707,7 @@ void add_layer_steps(tl_model* m, int l, std::vector<Step>& steps) {
                          a.n_heads = H; a.n_kv_heads = KV; a.head_dim = HD;
                          a.max_seq = static_cast<int>(m->max_seq); a.splits = m->splits;
                          a.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
+                         a.window = m->window;
                          return launch_attention(a, s, pdl);
                      }});
     steps.push_back({"gemv_o_residual",
@@ -1127,7 +1138,8 @@ tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* log
         TL_TRY(rmsnorm_rows_f16(m->p_x16, m->p_h, w.g_in, M, D, s));
         TL_TRY(gemm_f16(kEpiStoreF32, m->p_x16, M, D, W[0], NQKV, m->p_qkv, NQKV, m->err, s));
         TL_TRY(rope_cache_rows(m->p_q16, m->p_qkv, kc, vc, m->cos_tab, m->sin_tab, M, p0, H, KV, HD, ms, s));
-        TL_TRY(attention_prefill(m->p_ctx16, m->p_q16, m->p_k16, m->p_v16, kc, vc, M, p0, H, KV, HD, ms, scale, s));
+        TL_TRY(attention_prefill(m->p_ctx16, m->p_q16, m->p_k16, m->p_v16, kc, vc, M, p0, H, KV, HD, ms, scale,
+                                 m->window, s));
         TL_TRY(gemm_f16(kEpiAddF32, m->p_ctx16, M, H * HD, W[1], D, m->p_h, D, m->err, s));
         TL_TRY(rmsnorm_rows_f16(m->p_x16, m->p_h, w.g_post, M, D, s));
         TL_TRY(gemm_f16(kEpiSwiGluF16, m->p_x16, M, D, W[2], 2 * F, m->p_act16, F, m->err, s));
@@ -1410,7 +1422,8 @@ tl_status batch_step(tl_batch* b) {
         TL_TRY(gemm_f16_splitk(b->x16, B, D, W[0], NQKV, b->split, b->split_floats, &ks, m->err, s));
         TL_TRY(rope_cache_batch(b->qf, b->split, ks, qkv_stride, b->bkv, static_cast<int>(l), b->pos, m->cos_tab,
                                 m->sin_tab, B, H, KV, HD, s));
-        TL_TRY(attention_decode_batch(b->part, b->qf, b->bkv, static_cast<int>(l), b->pos, B, H, KV, HD, S, scale, s));
+        TL_TRY(attention_decode_batch(b->part, b->qf, b->bkv, static_cast<int>(l), b->pos, B, H, KV, HD, S, scale,
+                                      m->window, s));
         TL_TRY(attention_merge_batch(b->ctx16, b->part, B, H, HD, S, s));
         // under tensor parallelism the residual adds sum every rank's partial rows (exchange)
         auto residual = [&](const float* g) -> tl_status {

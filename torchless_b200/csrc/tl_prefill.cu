@@ -174,7 +174,7 @@ constexpr int kAQ = 64, kAK = 64;
 template <int HD>
 __global__ void __launch_bounds__(128) k_attention_prefill(__half* ctx16, const __half* q16, const __half* k16,
                                                            const __half* v16, int M, int p0, int H, int T,
-                                                           float scale) {
+                                                           float scale, int window) {
     constexpr int KP = HD + 8;  // padded row (halves): 16-byte aligned, conflict-free ldmatrix
     extern __shared__ __align__(16) __half smem_h[];
     __half* Ks = smem_h;                 // [2][kAK][KP]
@@ -208,6 +208,9 @@ __global__ void __launch_bounds__(128) k_attention_prefill(__half* ctx16, const 
     const bool row_a = (r0 + g) < M, row_b = (r0 + g + 8) < M;
     const int kmax = p0 + qend;  // keys [0, kmax) exist for this CTA
     const int nkb = (kmax + kAK - 1) / kAK;
+    // sliding window: query at position p sees keys (p - window, p]; the CTA's
+    // first query bounds the first key block any of its queries needs
+    const int kb0 = window > 0 ? max(0, p0 + q0 - window + 1) / kAK : 0;
 
     auto stage = [&](int kb, int buf) {  // keys >= kmax are zero rows
         const int k0 = kb * kAK;
@@ -225,10 +228,10 @@ __global__ void __launch_bounds__(128) k_attention_prefill(__half* ctx16, const 
         }
         cp_async_commit();
     };
-    stage(0, 0);
+    stage(kb0, 0);
     const int mi = lane >> 3, mr = lane & 7;  // ldmatrix: matrix index, row within it
-    for (int kb = 0; kb < nkb; kb++) {
-        const int buf = kb & 1, k0 = kb * kAK;
+    for (int kb = kb0; kb < nkb; kb++) {
+        const int buf = (kb - kb0) & 1, k0 = kb * kAK;
         if (kb + 1 < nkb) {
             stage(kb + 1, buf ^ 1);
             cp_async_wait<1>();
@@ -259,8 +262,10 @@ __global__ void __launch_bounds__(128) k_attention_prefill(__half* ctx16, const 
 #pragma unroll
             for (int e = 0; e < 2; e++) {
                 const int key = k0 + j * 8 + 2 * t + e;
-                s[j][e] = (row_a && key <= pos_a) ? s[j][e] * scale : -INFINITY;
-                s[j][2 + e] = (row_b && key <= pos_b) ? s[j][2 + e] * scale : -INFINITY;
+                const bool in_a = row_a && key <= pos_a && (window <= 0 || key > pos_a - window);
+                const bool in_b = row_b && key <= pos_b && (window <= 0 || key > pos_b - window);
+                s[j][e] = in_a ? s[j][e] * scale : -INFINITY;
+                s[j][2 + e] = in_b ? s[j][2 + e] * scale : -INFINITY;
                 mx_a = fmaxf(mx_a, s[j][e]);
                 mx_b = fmaxf(mx_b, s[j][2 + e]);
             }
@@ -367,7 +372,7 @@ tl_status rope_cache_rows(__half* q16, const float* qkv, float* k_cache, float* 
 
 tl_status attention_prefill(__half* ctx16, const __half* q16, __half* k16, __half* v16, const float* k_cache,
                             const float* v_cache, int M, int p0, int H, int KV, int HD, int max_seq, float scale,
-                            cudaStream_t s) {
+                            int window, cudaStream_t s) {
     TL_REQUIRE(H == 4 * KV, "attention_prefill: kv head h / 4 needs H == 4 KV");
     const int T = p0 + M;  // cached positions the queries can see
     const size_t n4 = static_cast<size_t>(KV) * T * HD / 4;
@@ -377,7 +382,7 @@ tl_status attention_prefill(__half* ctx16, const __half* q16, __half* k16, __hal
     switch (HD) {
         case 64: {
             const size_t smem = 4 * kAK * (64 + 8) * 2;
-            k_attention_prefill<64><<<grid, 128, smem, s>>>(ctx16, q16, k16, v16, M, p0, H, T, scale);
+            k_attention_prefill<64><<<grid, 128, smem, s>>>(ctx16, q16, k16, v16, M, p0, H, T, scale, window);
             break;
         }
         case 128: {
@@ -388,7 +393,7 @@ tl_status attention_prefill(__half* ctx16, const __half* q16, __half* k16, __hal
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
                 attr = true;
             }
-            k_attention_prefill<128><<<grid, 128, smem, s>>>(ctx16, q16, k16, v16, M, p0, H, T, scale);
+            k_attention_prefill<128><<<grid, 128, smem, s>>>(ctx16, q16, k16, v16, M, p0, H, T, scale, window);
             break;
         }
         default: return set_error(TL_ERR_UNSUPPORTED, "attention_prefill: head_dim %d", HD);

@@ -41,11 +41,12 @@ tl_status rope_cache_rows(__half* q16, const float* qkv, float* k_cache, float* 
                           const float* sin_tab, int M, int p0, int H, int KV, int HD, int max_seq, cudaStream_t s);
 
 // Causal GQA attention (modules.cpp:58-88) of the M new queries over cache
-// positions [0, p0 + i] (kv head h / 4); ctx16 [M, H hd] fp16.  Cache rows
+// positions [0, p0 + i] (window > 0: only the last `window` of them; kv head
+// h / 4); ctx16 [M, H hd] fp16.  Cache rows
 // [0, p0 + M) are first converted to fp16 scratch k16 / v16 [KV][p0 + M][hd];
 // tensor cores (mma m16n8k16, fp16 inputs, fp32 accumulation and softmax).
 tl_status attention_prefill(__half* ctx16, const __half* q16, __half* k16, __half* v16, const float* k_cache,
                             const float* v_cache, int M, int p0, int H, int KV, int HD, int max_seq, float scale,
-                            cudaStream_t s);
+                            int window, cudaStream_t s);
 
 }  // namespace tl
