@@ -354,6 +354,32 @@ TL_API tl_status tl_batch_tp_connect(tl_batch* b, const void* handles);
 /* Number of kernel launches one decode step issues (all of them this library's). */
 TL_API tl_status tl_model_launches_per_step(const tl_model* m, int* launches);
 
+/* ---- Tokenizer (host; tokenizer.cpp:1-209) ----
+ * The Mistral BPE tokenizer stored in the model binary's header ("tokenizer":
+ * {vocab, merges}): Metaspace pre-tokenisation, UTF-8 pieces with <0xXX> byte
+ * fallback, repeated merges of the lowest-ranked adjacent pair, BOS (<s>)
+ * prepended; decode concatenates the pieces with "\u2581" -> " " (byte
+ * pieces stay as written, as in the reference).  Where the reference is
+ * undefined (a byte piece or <s> missing, an id outside the vocabulary) these
+ * return TL_ERR_FORMAT / TL_ERR_INVALID_ARGUMENT. */
+typedef struct tl_tokenizer tl_tokenizer;
+
+/* From a model binary on disk (reads its header only) or in memory. */
+TL_API tl_status tl_tokenizer_load(const char* path, tl_tokenizer** out);
+TL_API tl_status tl_tokenizer_load_buffer(const void* data, size_t size, tl_tokenizer** out);
+/* From the tokenizer object's JSON text ({"vocab": {...}, "merges": [...]}). */
+TL_API tl_status tl_tokenizer_load_json(const char* json, size_t len, tl_tokenizer** out);
+TL_API tl_status tl_tokenizer_destroy(tl_tokenizer* t);
+TL_API tl_status tl_tokenizer_vocab_size(const tl_tokenizer* t, size_t* n);
+/* Tokenizer::encode (tokenizer.cpp:121-177) of text[len] into ids[cap];
+ * *n_out = the id count (also when cap is too small: TL_ERR_CAPACITY). */
+TL_API tl_status tl_tokenizer_encode(const tl_tokenizer* t, const char* text, size_t len, uint32_t* ids,
+                                     size_t cap, size_t* n_out);
+/* Tokenizer::decode (tokenizer.cpp:203-209) of ids[n] into out[cap] (NUL
+ * appended); *len_out = the byte count (also on TL_ERR_CAPACITY). */
+TL_API tl_status tl_tokenizer_decode(const tl_tokenizer* t, const uint32_t* ids, size_t n, char* out, size_t cap,
+                                     size_t* len_out);
+
 #ifdef __cplusplus
 }
 #endif

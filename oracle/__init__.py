@@ -113,6 +113,10 @@ def ref_lib() -> ctypes.CDLL:
             "ref_hidden": (ctypes.POINTER(_F), [_P]),
             "ref_sample_max": (_U32, [_P]),
             "ref_sample_logits": (_U32, [_P, _P, _F, _U32, ctypes.POINTER(_F)]),
+            "ref_tokenizer_new": (_P, [ctypes.c_char_p, _S]),
+            "ref_tokenizer_free": (None, [_P]),
+            "ref_tokenizer_encode": (_S, [_P, ctypes.c_char_p, _S, _P, _S]),
+            "ref_tokenizer_decode": (_S, [_P, _P, _S, _P, _S]),
             "ref_pos": (_S, [_P]),
             "ref_set_pos": (None, [_P, _S]),
             "ref_layer_forward": (_I, [_P, _I, _P]),
@@ -280,6 +284,41 @@ class RefModel:
         if ref_lib().ref_time_token(self._h, token, first_layer, n_layers, out):
             raise ValueError("reference timing rejected")
         return tuple(out)
+
+
+class RefTokenizer:
+    """The reference's own Tokenizer (tokenizer.cpp, built into oracle/_ref)."""
+
+    def __init__(self, tok):
+        import json
+        text = (tok if isinstance(tok, str) else json.dumps(tok)).encode("utf-8")
+        self._h = ref_lib().ref_tokenizer_new(text, len(text))
+        if not self._h:
+            raise ValueError("reference tokenizer rejected the JSON")
+
+    def close(self):
+        if self._h:
+            ref_lib().ref_tokenizer_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def encode(self, text) -> list:
+        b = text.encode("utf-8") if isinstance(text, str) else bytes(text)
+        cap = 2 * len(b) + 8
+        ids = np.empty(cap, dtype=np.uint32)
+        n = ref_lib().ref_tokenizer_encode(self._h, b, len(b), ids.ctypes.data, cap)
+        assert n <= cap
+        return ids[:n].tolist()
+
+    def decode_bytes(self, ids) -> bytes:
+        a = np.ascontiguousarray(ids, dtype=np.uint32)
+        cap = 64 + 64 * len(a)
+        out = ctypes.create_string_buffer(cap)
+        n = ref_lib().ref_tokenizer_decode(self._h, a.ctypes.data, a.size, out, cap)
+        assert n <= cap
+        return out.raw[:n]
 
 
 def sample_multinomial(logits: np.ndarray, temp: float, r: float) -> int:

@@ -13,6 +13,7 @@
 // RotaryEmbedding::init_freq (main.cpp never does, test_modules.cpp:169 does),
 // and guard the KV cache bound (the reference overruns it silently under
 // NDEBUG, inference_state.h:38-43).
+#include <algorithm>
 #include <chrono>
 #include <cstdint>
 #include <cstring>
@@ -25,6 +26,7 @@
 #include "src/loader/parameters.h"
 #include "src/model/mistral/inference_state.h"
 #include "src/model/mistral/modules.h"
+#include "src/tokenizer/tokenizer.h"
 
 // main.cpp:10-21, linked from the reference's main.cpp (main renamed).
 uint32_t sample_max(InferenceState& infer);
@@ -134,6 +136,32 @@ __attribute__((visibility("default"))) uint32_t ref_sample_logits(void* h, const
     std::uniform_real_distribution<double> d(0.0, 1.0);
     *r_out = static_cast<float>(d(peek));
     return sample_multinomial(*s->infer, temp);
+}
+// Tokenizer::load (tokenizer.cpp:37-68) on a tokenizer object's JSON text;
+// null if the JSON does not parse.
+__attribute__((visibility("default"))) void* ref_tokenizer_new(const char* json, size_t len) {
+    try {
+        auto* t = new Tokenizer();
+        t->load(nlohmann::json::parse(std::string(json, len)));
+        return t;
+    } catch (...) {
+        return nullptr;
+    }
+}
+__attribute__((visibility("default"))) void ref_tokenizer_free(void* t) { delete static_cast<Tokenizer*>(t); }
+// Tokenizer::encode (tokenizer.cpp:121-177): the id count; the first `cap` ids to `ids`.
+__attribute__((visibility("default"))) size_t ref_tokenizer_encode(void* t, const char* text, size_t len,
+                                                                    uint32_t* ids, size_t cap) {
+    const std::vector<uint32_t> v = static_cast<Tokenizer*>(t)->encode(std::string(text, len));
+    std::memcpy(ids, v.data(), std::min(cap, v.size()) * sizeof(uint32_t));
+    return v.size();
+}
+// Tokenizer::decode (tokenizer.cpp:203-209): the byte count; the first `cap` bytes to `out`.
+__attribute__((visibility("default"))) size_t ref_tokenizer_decode(void* t, const uint32_t* ids, size_t n, char* out,
+                                                                    size_t cap) {
+    const std::string s = static_cast<Tokenizer*>(t)->decode(std::vector<uint32_t>(ids, ids + n));
+    std::memcpy(out, s.data(), std::min(cap, s.size()));
+    return s.size();
 }
 __attribute__((visibility("default"))) size_t ref_pos(void* h) {
     return static_cast<Session*>(h)->infer->pos;

@@ -18,6 +18,12 @@ Writes:
                            from its own sources) on those models: prompt,
                            greedy ids and per-step logits.
   ref_ops.npz              reference kernels.cpp ops on seeded inputs.
+  ref_tokenizer.json       the reference's Tokenizer (tokenizer.cpp) with the
+                           synthetic BPE tokenizer of torchless_b200.synthetic:
+                           the tokenizer object, then for fixed and seeded random
+                           byte strings (words, multi-byte UTF-8, invalid bytes,
+                           spaces) the ids encode() returns and the bytes decode()
+                           returns for them.
   ref_sample.npz           the reference's sample_multinomial (main.cpp:23-43)
                            on TINY-vocabulary logits (the greedy fixture's plus
                            NaN / inf / tie / flat edge cases) at several
@@ -130,14 +136,55 @@ def sample_fixture() -> None:
                         seed=a[:, 2].astype(np.int64), r=a[:, 3].astype(np.float32), idx=a[:, 4].astype(np.int64))
 
 
+def tokenizer_texts(seed: int = 21, n: int = 60):
+    """Fixed strings, then seeded random byte strings."""
+    fixed = ["the model reads its weights once", "", " ", "  two  spaces ", "caf\u00e9 \u4e2d\u6587 \U0001F600",
+             "Unknown Words Here", "tokenizer tokens token", "a", "the", "e "]
+    out = [t.encode("utf-8") for t in fixed] + [b"\xff\xfe\x80 raw", b"\xe4\xb8", b"abc\xf0"]
+    rng = np.random.default_rng(seed)
+    words = S.TOKENIZER_CORPUS.split()
+    extra = ["\u00e9", "\u00df", "\u4e2d", "\u6587", "\U0001F600", "\u2581", "Z", "Q", "\t", "7"]
+    for _ in range(n):
+        parts = []
+        for _ in range(int(rng.integers(1, 12))):
+            r = rng.random()
+            if r < 0.6:
+                parts.append(words[int(rng.integers(len(words)))].encode("utf-8"))
+            elif r < 0.9:
+                parts.append(extra[int(rng.integers(len(extra)))].encode("utf-8"))
+            else:
+                parts.append(bytes([int(rng.integers(128, 256))]))
+            parts.append(b" " * int(rng.integers(0, 3)))
+        out.append(b"".join(parts))
+    return out
+
+
+def tokenizer_fixture() -> None:
+    """ref_tokenizer.json: tokenizer.cpp through the reference build (oracle/_ref)."""
+    oracle.build(reference=True)
+    tok = S.make_bpe_tokenizer()
+    rt = oracle.RefTokenizer(tok)
+    cases = []
+    for t in tokenizer_texts():
+        ids = rt.encode(t)
+        cases.append({"text": t.hex(), "ids": ids, "decoded": rt.decode_bytes(ids).hex()})
+    rt.close()
+    with open(os.path.join(HERE, "ref_tokenizer.json"), "w") as f:
+        json.dump({"tokenizer": tok, "cases": cases}, f)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
     ap.add_argument("--only-sample", action="store_true", help="regenerate ref_sample.npz only")
+    ap.add_argument("--only-tokenizer", action="store_true", help="regenerate ref_tokenizer.json only")
     args = ap.parse_args()
     ref = args.reference
     if args.only_sample:
         sample_fixture()
+        return
+    if args.only_tokenizer:
+        tokenizer_fixture()
         return
 
     exp = read_expected(os.path.join(ref, "test/mistral/expected.txt"))
@@ -211,6 +258,7 @@ def main() -> None:
     ops.update(silu_x=x, silu_y=y)
     np.savez_compressed(os.path.join(HERE, "ref_ops.npz"), **ops)
     sample_fixture()
+    tokenizer_fixture()
     print("golden fixtures written to", HERE)
 
 

@@ -118,6 +118,13 @@ SIGNATURES = {
     "tl_batch_read_kv": [_P, _I, _I, _S, _P, _P],
     "tl_batch_tp_handle": [_P, _P],
     "tl_batch_tp_connect": [_P, _P],
+    "tl_tokenizer_load": [ctypes.c_char_p, ctypes.POINTER(_P)],
+    "tl_tokenizer_load_buffer": [_P, _S, ctypes.POINTER(_P)],
+    "tl_tokenizer_load_json": [ctypes.c_char_p, _S, ctypes.POINTER(_P)],
+    "tl_tokenizer_destroy": [_P],
+    "tl_tokenizer_vocab_size": [_P, ctypes.POINTER(_S)],
+    "tl_tokenizer_encode": [_P, ctypes.c_char_p, _S, _P, _S, ctypes.POINTER(_S)],
+    "tl_tokenizer_decode": [_P, _P, _S, _P, _S, ctypes.POINTER(_S)],
     "tl_model_tp_handle": [_P, _P],
     "tl_model_tp_connect": [_P, _P],
 }
@@ -151,5 +158,6 @@ def check(status: int) -> None:
 
 from . import ops  # noqa: E402  (needs lib/check)
 from .model import Batch, Model  # noqa: E402
+from .tokenizer import Tokenizer  # noqa: E402
 
-__all__ = ["lib", "check", "TLError", "ops", "Model", "Batch", "LIB_PATH", "SIGNATURES"]
+__all__ = ["lib", "check", "TLError", "ops", "Model", "Batch", "Tokenizer", "LIB_PATH", "SIGNATURES"]

@@ -89,11 +89,68 @@ def numpy_tensors(cfg: dict, seed: int, std: float = 0.02,
         yield name, x
 
 
+META = "\u2581"  # the Metaspace marker of Mistral's pre-tokeniser
+
+# A short text for training the synthetic BPE tokenizer (plain prose written
+# for this purpose, with a few accented, CJK and emoji characters so that the
+# UTF-8 and byte-fallback paths are exercised).
+TOKENIZER_CORPUS = (
+    "the model reads its weights once from the binary file and keeps them resident in memory. "
+    "every decode step reads the weights again, so the speed of a step is set by memory bandwidth. "
+    "a prompt is split into pieces by the tokenizer, and each piece becomes one id in the vocabulary. "
+    "the pieces are merged pair by pair, the lowest ranked pair first, until no pair can be merged. "
+    "caf\u00e9 na\u00efve r\u00e9sum\u00e9 \u4e2d\u6587 \u6587\u5b57 \U0001F600 tokens and the tokenizer again. "
+)
+
+
+def make_bpe_tokenizer(corpus: str = TOKENIZER_CORPUS, n_merges: int = 200) -> dict:
+    """A small Mistral-style BPE tokenizer object {vocab, merges}: <unk>, <s>,
+    </s>, the 256 byte pieces <0xXX>, the corpus's characters after Metaspace
+    pre-tokenisation, then `n_merges` merges of the most frequent adjacent
+    pair (ties: the pair seen first), trained over the whole text the way
+    tokenizer.cpp applies them."""
+    vocab = {"<unk>": 0, "<s>": 1, "</s>": 2}
+    for b in range(256):
+        vocab[f"<0x{b:02X}>"] = len(vocab)
+    text = META + corpus.replace(" ", META)
+    seq = list(text)
+    for ch in seq:
+        if ch not in vocab:
+            vocab[ch] = len(vocab)
+    merges = []
+    for _ in range(n_merges):
+        counts, first = {}, {}
+        for i in range(len(seq) - 1):
+            p = (seq[i], seq[i + 1])
+            counts[p] = counts.get(p, 0) + 1
+            first.setdefault(p, i)
+        if not counts:
+            break
+        best = max(counts, key=lambda p: (counts[p], -first[p]))
+        if counts[best] < 2:
+            break
+        a, b = best
+        merges.append(f"{a} {b}")
+        if a + b not in vocab:
+            vocab[a + b] = len(vocab)
+        out, i = [], 0
+        while i < len(seq):
+            if i + 1 < len(seq) and seq[i] == a and seq[i + 1] == b:
+                out.append(a + b)
+                i += 2
+            else:
+                out.append(seq[i])
+                i += 1
+        seq = out
+    return {"vocab": vocab, "merges": merges}
+
+
 def make_numpy_model(cfg: dict, seed: int, quant: str = "int8", std: float = 0.02,
-                     norm: str = "ones", quant_lm_head: bool = False) -> BinWriter:
+                     norm: str = "ones", quant_lm_head: bool = False, tokenizer: Optional[dict] = None) -> BinWriter:
     """A complete model binary built on the CPU (small configs).  quant_lm_head:
-    the lm_head stored int8 too (format extension, see binfmt.build_header)."""
-    w = BinWriter(metadata_from_hf(cfg, quant), tensor_list(cfg), quant, PLACEHOLDER_TOKENIZER,
+    the lm_head stored int8 too (format extension, see binfmt.build_header);
+    tokenizer: the header's tokenizer object (default: a 3-piece placeholder)."""
+    w = BinWriter(metadata_from_hf(cfg, quant), tensor_list(cfg), quant, tokenizer or PLACEHOLDER_TOKENIZER,
                   quant_lm_head=quant_lm_head)
     for name, x in numpy_tensors(cfg, seed, std, norm):
         w.put_fp32(name, x)
