@@ -92,16 +92,15 @@ __global__ void k_residual_rmsnorm_rows(__half* x16, float* h, const float* part
     }
 }
 
+// Block (row i, head slot hh), thread c < hd / 2: the rotated pair (c, c + hd / 2)
+// of q / k head hh, or the two v values of kv head hh - H - KV.
 __global__ void k_rope_cache_rows(__half* q16, const float* qkv, float* kc, float* vc, const float* cos_tab,
                                   const float* sin_tab, int p0, int H, int KV, int HD, int max_seq) {
-    const int i = blockIdx.x, pos = p0 + i, half = HD / 2;
-    const float* row = qkv + static_cast<size_t>(i) * (H + 2 * KV) * HD;
-    const float* ct = cos_tab + static_cast<size_t>(pos) * half;
-    const float* st = sin_tab + static_cast<size_t>(pos) * half;
-    for (int k = threadIdx.x; k < (H + KV) * half; k += blockDim.x) {
-        const int hh = k / half, c = k % half;
-        const float x = row[hh * HD + c], y = row[hh * HD + c + half];
-        const float cc = ct[c], sn = st[c];
+    const int i = blockIdx.x, hh = blockIdx.y, c = threadIdx.x, pos = p0 + i, half = HD / 2;
+    const float* row = qkv + static_cast<size_t>(i) * (H + 2 * KV) * HD + hh * HD;
+    const float x = row[c], y = row[c + half];
+    if (hh < H + KV) {
+        const float cc = cos_tab[static_cast<size_t>(pos) * half + c], sn = sin_tab[static_cast<size_t>(pos) * half + c];
         const float xr = x * cc - y * sn, yr = x * sn + y * cc;
         if (hh < H) {
             __half* q = q16 + static_cast<size_t>(i) * H * HD + hh * HD;
@@ -112,10 +111,10 @@ __global__ void k_rope_cache_rows(__half* q16, const float* qkv, float* kc, floa
             k[c] = xr;
             k[c + half] = yr;
         }
-    }
-    for (int k = threadIdx.x; k < KV * HD; k += blockDim.x) {
-        const int kh = k / HD, c = k % HD;
-        vc[(static_cast<size_t>(kh) * max_seq + pos) * HD + c] = row[(H + KV) * HD + k];
+    } else {
+        float* v = vc + (static_cast<size_t>(hh - H - KV) * max_seq + pos) * HD;
+        v[c] = x;
+        v[c + half] = y;
     }
 }
 
@@ -354,7 +353,9 @@ tl_status rmsnorm_rows_f16(__half* x16, const float* h, const float* g, int M, i
 tl_status residual_rmsnorm_rows(__half* x16, float* h, const float* part, int ks, size_t part_stride, const float* g,
                                 int M, int D, cudaStream_t s) {
     const int n4 = D / 4;
-    const int threads = std::min(1024, (n4 + 31) / 32 * 32);
+    // each thread holds up to kNormVec float4 columns: few threads per row keep
+    // many rows resident per SM (the kernel is latency-bound, one row per CTA)
+    const int threads = std::min(1024, std::max(32, ((n4 + kNormVec - 1) / kNormVec + 31) / 32 * 32));
     TL_REQUIRE(D % 4 == 0 && n4 <= kNormVec * threads, "rmsnorm rows: width %d (multiple of 4, at most %d)", D,
                kNormVec * 4 * 1024);
     TL_REQUIRE(((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(part)) & 15) == 0 &&
@@ -366,7 +367,9 @@ tl_status residual_rmsnorm_rows(__half* x16, float* h, const float* part, int ks
 
 tl_status rope_cache_rows(__half* q16, const float* qkv, float* k_cache, float* v_cache, const float* cos_tab,
                           const float* sin_tab, int M, int p0, int H, int KV, int HD, int max_seq, cudaStream_t s) {
-    k_rope_cache_rows<<<M, 128, 0, s>>>(q16, qkv, k_cache, v_cache, cos_tab, sin_tab, p0, H, KV, HD, max_seq);
+    TL_REQUIRE(HD % 2 == 0 && HD <= 2048, "rope_cache_rows: head_dim %d", HD);
+    k_rope_cache_rows<<<dim3(M, H + 2 * KV), HD / 2, 0, s>>>(q16, qkv, k_cache, v_cache, cos_tab, sin_tab, p0, H, KV,
+                                                              HD, max_seq);
     return check_launch("rope_cache_rows");
 }
 
