@@ -25,13 +25,14 @@
 
 #include "tl_common.cuh"
 #include "tl_gemm.cuh"
+#include "tl_tc.cuh"
 
 namespace tl {
 namespace {
 
+using namespace tc;
 constexpr int kBM = 128, kBK = 64;
 constexpr int kGemmThreads = 192;
-constexpr unsigned long long kGemmTimeoutNs = 2000000000ull;
 
 template <int BN>
 struct GemmCfg {
@@ -51,100 +52,6 @@ struct GemmArgs {
     int* err;
     int ksplit;  // K-block ranges per output tile (1: none); split s stores into C + s * M * ldc
 };
-
-__device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-__device__ __forceinline__ unsigned long long gtime() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
-}
-__device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool bar_test(uint64_t* b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(su32(b)), "r"(parity), "r"(10000u)
-        : "memory");
-    return ok != 0;
-}
-// false after ~2 s
-__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity) {
-    if (bar_test(b, parity)) return true;
-    const unsigned long long t0 = gtime();
-    for (unsigned i = 1;; i++) {
-        if (bar_test(b, parity)) return true;
-        if ((i & 63) == 0 && gtime() - t0 > kGemmTimeoutNs) return false;
-    }
-}
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            su32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(su32(bar))
-        : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major operand, SWIZZLE_128B (rows of 64
-// fp16 = 128 bytes, 8-row atoms 1024 bytes apart), descriptor version 1.
-__device__ __forceinline__ uint64_t sdesc_k128(uint32_t addr) {
-    uint64_t d = 0;
-    d |= static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
-    d |= static_cast<uint64_t>(16 >> 4) << 16;    // leading byte offset (unused for this layout)
-    d |= static_cast<uint64_t>(1024 >> 4) << 32;  // stride byte offset: next 8-row atom
-    d |= static_cast<uint64_t>(1) << 46;          // version
-    d |= static_cast<uint64_t>(2) << 61;          // SWIZZLE_128B
-    return d;
-}
-// Instruction descriptor, kind::f16: D fp32, A/B fp16, both K-major, M 128, N.
-template <int BN>
-__host__ __device__ constexpr uint32_t idesc_f16() {
-    return (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
-}
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 32 consecutive fp32 columns of this thread's tensor-memory lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
-}
-
-// Waits like bar_wait but also gives up as soon as the CTA has aborted.
-__device__ __forceinline__ bool bar_wait_ab(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
-    if (bar_test(b, parity)) return true;
-    const unsigned long long t0 = gtime();
-    for (unsigned i = 1;; i++) {
-        if (bar_test(b, parity)) return true;
-        if ((i & 15) == 0 && (*abort_flag || gtime() - t0 > kGemmTimeoutNs)) return false;
-    }
-}
 
 // The epilogue of one 128 x BN accumulator (tensor-memory columns tcol ..)
 // for tile rows m0 .., columns n0 ..; called by the 4 epilogue warps.
@@ -342,35 +249,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
     }
-}
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point.
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
-// [rows, K] fp16 row-major, box {64, box_rows}, SWIZZLE_128B, zero fill outside.
-tl_status encode_kmajor(CUtensorMap* map, const __half* ptr, int rows, int K, int box_rows) {
-    auto fn = encode_fn();
-    if (!fn) return set_error(TL_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
-    const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(ptr), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(TL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
-    return TL_OK;
 }
 
 template <int BN, int EPI>

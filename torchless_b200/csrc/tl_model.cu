@@ -900,7 +900,8 @@ tl_status ensure_prefill(tl_model* m, size_t n) {
         m->rows = DeviceArena();
         const size_t cap = std::max<size_t>(n, 64);
         using A = DeviceArena;
-        const size_t kvh = static_cast<size_t>(KV) * m->max_seq * HD;
+        // fp16 K and (transposed, rows padded to 64 keys) V of one layer's cache
+        const size_t kvh = static_cast<size_t>(KV) * ((m->max_seq + 63) / 64 * 64) * HD;
         TL_TRY(m->rows.reserve(A::pad(cap * D * 4) + A::pad(cap * NQKV * 4) + A::pad(cap * D * 2) +
                                2 * A::pad(cap * H * HD * 2) + A::pad(cap * F * 2) + A::pad(cap * 4) +
                                2 * A::pad(kvh * 2)));
@@ -920,13 +921,13 @@ tl_status ensure_prefill(tl_model* m, size_t n) {
 }
 
 tl_status sync(tl_model* m) {
-    if (m->persistent) {
+    {  // the device error flag (bounded waits of the persistent step and the tensor-core kernels)
         cudaError_t e = cudaMemcpyAsync(m->h_pinned + 3, m->err, 4, cudaMemcpyDeviceToHost, m->stream);
         if (e != cudaSuccess) return set_error(TL_ERR_CUDA, "error-flag read: %s", cudaGetErrorString(e));
     }
     cudaError_t e = cudaStreamSynchronize(m->stream);
     if (e != cudaSuccess) return set_error(TL_ERR_CUDA, "decode step failed: %s", cudaGetErrorString(e));
-    if (m->persistent && m->h_pinned[3] != 0) {
+    if (m->h_pinned[3] != 0) {
         const unsigned code = m->h_pinned[3];
         if (code >= 1000) {
             int dbg[4] = {0, 0, 0, 0};
@@ -1138,8 +1139,12 @@ tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* log
         TL_TRY(rmsnorm_rows_f16(m->p_x16, m->p_h, w.g_in, M, D, s));
         TL_TRY(gemm_f16(kEpiStoreF32, m->p_x16, M, D, W[0], NQKV, m->p_qkv, NQKV, m->err, s));
         TL_TRY(rope_cache_rows(m->p_q16, m->p_qkv, kc, vc, m->cos_tab, m->sin_tab, M, p0, H, KV, HD, ms, s));
-        TL_TRY(attention_prefill(m->p_ctx16, m->p_q16, m->p_k16, m->p_v16, kc, vc, M, p0, H, KV, HD, ms, scale,
-                                 m->window, s));
+        if (HD == 128 && H == 4 * KV)  // tensor-core attention (tcgen05, tensor memory)
+            TL_TRY(attention_prefill_tc(m->p_ctx16, m->p_q16, m->p_k16, m->p_v16, kc, vc, M, p0, H, KV, HD, ms,
+                                        scale, m->window, m->err, s));
+        else
+            TL_TRY(attention_prefill(m->p_ctx16, m->p_q16, m->p_k16, m->p_v16, kc, vc, M, p0, H, KV, HD, ms, scale,
+                                     m->window, s));
         TL_TRY(gemm_f16(kEpiAddF32, m->p_ctx16, M, H * HD, W[1], D, m->p_h, D, m->err, s));
         TL_TRY(rmsnorm_rows_f16(m->p_x16, m->p_h, w.g_post, M, D, s));
         TL_TRY(gemm_f16(kEpiSwiGluF16, m->p_x16, M, D, W[2], 2 * F, m->p_act16, F, m->err, s));

@@ -92,29 +92,36 @@ __global__ void k_residual_rmsnorm_rows(__half* x16, float* h, const float* part
     }
 }
 
-// Block (row i, head slot hh), thread c < hd / 2: the rotated pair (c, c + hd / 2)
-// of q / k head hh, or the two v values of kv head hh - H - KV.
+// Block = row i (position p0 + i); its threads walk the (head slot, pair)
+// items: rotated pair (c, c + hd / 2) of q / k head hh, or two v values of
+// kv head hh - H - KV.
 __global__ void k_rope_cache_rows(__half* q16, const float* qkv, float* kc, float* vc, const float* cos_tab,
                                   const float* sin_tab, int p0, int H, int KV, int HD, int max_seq) {
-    const int i = blockIdx.x, hh = blockIdx.y, c = threadIdx.x, pos = p0 + i, half = HD / 2;
-    const float* row = qkv + static_cast<size_t>(i) * (H + 2 * KV) * HD + hh * HD;
-    const float x = row[c], y = row[c + half];
-    if (hh < H + KV) {
-        const float cc = cos_tab[static_cast<size_t>(pos) * half + c], sn = sin_tab[static_cast<size_t>(pos) * half + c];
-        const float xr = x * cc - y * sn, yr = x * sn + y * cc;
-        if (hh < H) {
-            __half* q = q16 + static_cast<size_t>(i) * H * HD + hh * HD;
-            q[c] = __float2half_rn(xr);
-            q[c + half] = __float2half_rn(yr);
+    const int i = blockIdx.x, pos = p0 + i, half = HD / 2;
+    const float* ct = cos_tab + static_cast<size_t>(pos) * half;
+    const float* st = sin_tab + static_cast<size_t>(pos) * half;
+    const float* base = qkv + static_cast<size_t>(i) * (H + 2 * KV) * HD;
+    for (int k = threadIdx.x; k < (H + 2 * KV) * half; k += blockDim.x) {
+        const int hh = k / half, c = k % half;
+        const float* row = base + hh * HD;
+        const float x = row[c], y = row[c + half];
+        if (hh < H + KV) {
+            const float cc = ct[c], sn = st[c];
+            const float xr = x * cc - y * sn, yr = x * sn + y * cc;
+            if (hh < H) {
+                __half* q = q16 + static_cast<size_t>(i) * H * HD + hh * HD;
+                q[c] = __float2half_rn(xr);
+                q[c + half] = __float2half_rn(yr);
+            } else {
+                float* kr = kc + (static_cast<size_t>(hh - H) * max_seq + pos) * HD;
+                kr[c] = xr;
+                kr[c + half] = yr;
+            }
         } else {
-            float* k = kc + (static_cast<size_t>(hh - H) * max_seq + pos) * HD;
-            k[c] = xr;
-            k[c + half] = yr;
+            float* vr = vc + (static_cast<size_t>(hh - H - KV) * max_seq + pos) * HD;
+            vr[c] = x;
+            vr[c + half] = y;
         }
-    } else {
-        float* v = vc + (static_cast<size_t>(hh - H - KV) * max_seq + pos) * HD;
-        v[c] = x;
-        v[c + half] = y;
     }
 }
 
@@ -367,9 +374,8 @@ tl_status residual_rmsnorm_rows(__half* x16, float* h, const float* part, int ks
 
 tl_status rope_cache_rows(__half* q16, const float* qkv, float* k_cache, float* v_cache, const float* cos_tab,
                           const float* sin_tab, int M, int p0, int H, int KV, int HD, int max_seq, cudaStream_t s) {
-    TL_REQUIRE(HD % 2 == 0 && HD <= 2048, "rope_cache_rows: head_dim %d", HD);
-    k_rope_cache_rows<<<dim3(M, H + 2 * KV), HD / 2, 0, s>>>(q16, qkv, k_cache, v_cache, cos_tab, sin_tab, p0, H, KV,
-                                                              HD, max_seq);
+    TL_REQUIRE(HD % 2 == 0, "rope_cache_rows: head_dim %d", HD);
+    k_rope_cache_rows<<<M, 256, 0, s>>>(q16, qkv, k_cache, v_cache, cos_tab, sin_tab, p0, H, KV, HD, max_seq);
     return check_launch("rope_cache_rows");
 }
 

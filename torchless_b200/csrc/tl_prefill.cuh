@@ -49,4 +49,13 @@ tl_status attention_prefill(__half* ctx16, const __half* q16, __half* k16, __hal
                             const float* v_cache, int M, int p0, int H, int KV, int HD, int max_seq, float scale,
                             int window, cudaStream_t s);
 
+// The same attention on the 5th-generation tensor cores (tl_attn_tc.cu;
+// head_dim 128, H = 4 KV): cache rows [0, p0 + M) become fp16 K [KV][T][hd]
+// (k16) and V transposed [KV][hd][Tp] (vt16, Tp = T rounded up to 64, zero
+// padded; room for Tp <= max_seq rounded up to 64), then one CTA per 32
+// queries x kv group.  `err` receives a nonzero code if a bounded wait gave up.
+tl_status attention_prefill_tc(__half* ctx16, const __half* q16, __half* k16, __half* vt16, const float* k_cache,
+                               const float* v_cache, int M, int p0, int H, int KV, int HD, int max_seq, float scale,
+                               int window, int* err, cudaStream_t s);
+
 }  // namespace tl
