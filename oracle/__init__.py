@@ -77,6 +77,9 @@ def oracle_lib() -> ctypes.CDLL:
             "tlo_model_new": (_P, [ctypes.POINTER(tlo_config)]),
             "tlo_model_free": (None, [_P]),
             "tlo_model_set_tensor": (_I, [_P, _I, _I, _P, _P, _S, _S, _S]),
+            "tlo_model_set_tensor_fp8": (_I, [_P, _I, _I, _P, _S, _S]),
+            "tlo_fp8_to_f32": (_F, [ctypes.c_uint8]),
+            "tlo_matmul_f8": (None, [_P, _P, _P, _S, _S]),
             "tlo_model_pos": (_S, [_P]),
             "tlo_model_set_pos": (None, [_P, _S]),
             "tlo_model_logits": (ctypes.POINTER(_F), [_P]),
@@ -175,11 +178,15 @@ class OracleModel:
             sp = scales.ctypes.data if scales is not None else None
             ns = scales.size if scales is not None else 0
             if name in _GLOBAL:
-                rc = L.tlo_model_set_tensor(self._h, -1, _GLOBAL[name], data.ctypes.data, sp, ns, rows, cols)
+                layer, kind = -1, _GLOBAL[name]
             else:
                 rest = name[len("model.layers."):]
-                layer, key = rest.split(".", 1)
-                rc = L.tlo_model_set_tensor(self._h, int(layer), _KINDS[key], data.ctypes.data, sp, ns, rows, cols)
+                lstr, key = rest.split(".", 1)
+                layer, kind = int(lstr), _KINDS[key]
+            if info.dtype == "fp8":
+                rc = L.tlo_model_set_tensor_fp8(self._h, layer, kind, data.ctypes.data, rows, cols)
+            else:
+                rc = L.tlo_model_set_tensor(self._h, layer, kind, data.ctypes.data, sp, ns, rows, cols)
             if rc:
                 raise ValueError(f"oracle rejected tensor {name}")
 
@@ -189,7 +196,10 @@ class OracleModel:
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:  # interpreter teardown: the module's globals may be gone
+            pass
 
     @property
     def pos(self) -> int:
@@ -246,7 +256,10 @@ class RefModel:
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:  # interpreter teardown: the module's globals may be gone
+            pass
 
     @property
     def pos(self) -> int:
@@ -302,7 +315,10 @@ class RefTokenizer:
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:  # interpreter teardown: the module's globals may be gone
+            pass
 
     def encode(self, text) -> list:
         b = text.encode("utf-8") if isinstance(text, str) else bytes(text)

@@ -66,6 +66,32 @@ TLO_API void tlo_matmul_i8(float* xout, const int8_t* w, const float* scales,
     }
 }
 
+/* fp8 export (format extension after the roadmap item README.md:160, "a cast
+ * tensor.to(torch.float8_e5m2) during model export"): an e5m2 byte is sign,
+ * 5 exponent bits (bias 15) and 2 mantissa bits; exponent 0 is subnormal
+ * (m * 2^-16), exponent 31 is infinity (m = 0) or NaN.  Exact in fp32. */
+TLO_API float tlo_fp8_to_f32(uint8_t b) {
+    const int sign = b >> 7, e = (b >> 2) & 31, m = b & 3;
+    float v;
+    if (e == 31) v = m ? NAN : INFINITY;
+    else if (e == 0) v = ldexpf((float)m, -16);
+    else v = ldexpf((float)(4 + m), e - 17);
+    return sign ? -v : v;
+}
+
+/* kernels.cpp:21-33 with the weight's get(i) = the e5m2 value of byte i:
+ * converted to fp32, multiplied by x[j], added to the running fp32 sum. */
+TLO_API void tlo_matmul_f8(float* xout, const uint8_t* w, const float* x, size_t n, size_t d) {
+    long long nn = (long long)n;
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < nn; i++) {
+        const uint8_t* row = w + (size_t)i * d;
+        float acc = 0.0f;
+        for (size_t j = 0; j < d; j++) acc += tlo_fp8_to_f32(row[j]) * x[j];
+        xout[i] = acc;
+    }
+}
+
 /* kernels.cpp:37-49  x (n,) @ W (n,d) -> xout (d,), sequential j. */
 TLO_API void tlo_row_matmul(float* xout, const float* x, const float* w,
                             size_t n, size_t d) {
@@ -300,10 +326,11 @@ enum {
 };
 
 typedef struct {
-    const void* data;      /* int8 when scales != NULL, else fp32 */
+    const void* data;      /* int8 when scales != NULL, e5m2 bytes when fp8, else fp32 */
     const float* scales;
     size_t n_scales;
     size_t rows, cols;
+    int fp8;
 } tlo_weight;
 
 typedef struct {
@@ -361,7 +388,7 @@ TLO_API void tlo_model_free(tlo_model* m) {
 TLO_API int tlo_model_set_tensor(tlo_model* m, int layer, int kind, const void* data,
                                  const float* scales, size_t n_scales, size_t rows,
                                  size_t cols) {
-    tlo_weight w = {data, scales, n_scales, rows, cols};
+    tlo_weight w = {data, scales, n_scales, rows, cols, 0};
     if (layer < 0) {
         if (kind < 0 || kind > TLO_LM_HEAD) return 1;
         m->global[kind] = w;
@@ -369,6 +396,17 @@ TLO_API int tlo_model_set_tensor(tlo_model* m, int layer, int kind, const void* 
     }
     if ((size_t)layer >= m->c.n_layers || kind < TLO_IN_NORM || kind >= TLO_N_KINDS) return 1;
     m->layer[(size_t)layer * TLO_N_KINDS + kind] = w;
+    return 0;
+}
+
+/* An fp8 (e5m2) projection or lm_head: no scales. */
+TLO_API int tlo_model_set_tensor_fp8(tlo_model* m, int layer, int kind, const uint8_t* data, size_t rows,
+                                     size_t cols) {
+    if (layer < 0 ? kind != TLO_LM_HEAD : kind < TLO_WQ) return 1;
+    const int rc = tlo_model_set_tensor(m, layer, kind, data, NULL, 0, rows, cols);
+    if (rc) return rc;
+    if (layer < 0) m->global[kind].fp8 = 1;
+    else m->layer[(size_t)layer * TLO_N_KINDS + kind].fp8 = 1;
     return 0;
 }
 
@@ -381,7 +419,9 @@ TLO_API float* tlo_model_v_cache(tlo_model* m) { return m->vc; }
 
 /* Dispatch on the stored dtype like matmul(Tensor<T>...) overloads. */
 static void tlo_linear(float* y, const tlo_weight* w, const float* x) {
-    if (w->scales)
+    if (w->fp8)
+        tlo_matmul_f8(y, (const uint8_t*)w->data, x, w->rows, w->cols);
+    else if (w->scales)
         tlo_matmul_i8(y, (const int8_t*)w->data, w->scales, w->n_scales, x, w->rows, w->cols);
     else
         tlo_matmul_f32(y, (const float*)w->data, x, w->rows, w->cols);

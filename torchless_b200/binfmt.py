@@ -22,6 +22,13 @@ engine dequantises with ``q / scale`` (src/common/tensor.cpp:101-104).
 This module writes byte-identical files to the reference exporter for the
 same fp32 inputs and tensor order (checked by tests/golden/make_golden.py
 against export_mistral.py itself).
+
+fp8 (format extension; the reference's roadmap item "Support fp8 with a cast
+``tensor.to(torch.float8_e5m2)`` during model export", README.md:160): with
+``quant = "fp8"`` every ``*_proj`` tensor is that cast, one byte per element
+(the e5m2 bit pattern: sign, 5 exponent bits with bias 15, 2 mantissa bits),
+dtype ``"fp8"`` in the header, no scales, each block padded to 64.  The
+engine's weight is the e5m2 value itself.
 """
 from __future__ import annotations
 
@@ -33,6 +40,7 @@ from typing import Dict, Iterable, List, Optional, Tuple
 import numpy as np
 
 GROUP_SIZE = 64  # export_mistral.py:194
+QUANTS = ("f32", "int8", "fp8")  # export_mistral.py:187 accepts f32 and int8; fp8 is the extension
 
 
 def pad_to_64(offset: int) -> int:
@@ -61,10 +69,26 @@ def quantize_i8(x: np.ndarray, group: int = GROUP_SIZE) -> Tuple[np.ndarray, np.
     return q.reshape(x.shape), scales
 
 
+def quantize_fp8(x: np.ndarray) -> np.ndarray:
+    """The fp8 export: ``x.to(torch.float8_e5m2)`` (round to nearest even; values
+    beyond the e5m2 range become infinities), returned as the uint8 bit
+    patterns, shaped like ``x``."""
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32))
+    return t.to(torch.float8_e5m2).view(torch.uint8).numpy().copy()
+
+
+def fp8_to_f32(b: np.ndarray) -> np.ndarray:
+    """e5m2 bit patterns to fp32, exactly: an e5m2 byte is the high byte of the
+    IEEE half with the same value (same sign, exponent width and bias)."""
+    return (np.asarray(b, dtype=np.uint8).astype(np.uint16) << 8).view(np.float16).astype(np.float32)
+
+
 @dataclass
 class TensorInfo:
     name: str
-    dtype: str            # "f32" or "int8"
+    dtype: str            # "f32", "int8" or "fp8"
     shape: List[int]
     offset: int
     scale_offset: Optional[int] = None
@@ -150,7 +174,9 @@ class ModelFile:
         return self.buf[start:start + nbytes]
 
     def tensor(self, name: str):
-        """(data, scales-or-None) as numpy views; data shaped like the tensor."""
+        """(data, scales-or-None) as numpy views; data shaped like the tensor:
+        float32 (f32), int8 with fp32 scales (int8), or uint8 e5m2 bit
+        patterns without scales (fp8)."""
         t = self.tensors[name]
         if t.dtype == "f32":
             return self._slice(t.offset, 4 * t.numel).view(np.float32).reshape(t.shape), None
@@ -158,6 +184,8 @@ class ModelFile:
             q = self._slice(t.offset, t.numel).view(np.int8).reshape(t.shape)
             s = self._slice(t.scale_offset, 4 * t.scale_size).view(np.float32)
             return q, s
+        if t.dtype == "fp8":
+            return self._slice(t.offset, t.numel).reshape(t.shape), None
         raise ValueError(f"unknown dtype {t.dtype!r} for {name}")
 
     def layer_tensor(self, layer: int, name: str):
@@ -174,10 +202,13 @@ def build_header(metadata: dict, tensors: Iterable[Tuple[str, Tuple[int, ...]]],
     Offsets follow load_tensor_map (export_mistral.py:107-135): int8 only for
     names containing "_proj" when quant != "f32", each block padded to 64.
     quant_lm_head (a format extension; the reference exporter keeps the
-    lm_head fp32, export_mistral.py:119) also stores ``lm_head.weight`` as
-    int8 + per-64-group scales, the layout of the ``_proj`` tensors: its dtype
-    entry in the header is what tells a loader.
+    lm_head fp32, export_mistral.py:119) also stores ``lm_head.weight`` in the
+    ``_proj`` tensors' format (int8 + per-64-group scales, or fp8): its dtype
+    entry in the header is what tells a loader.  quant "fp8" stores one e5m2
+    byte per element and no scales.
     """
+    if quant not in QUANTS:
+        raise ValueError(f"quant {quant!r} not in {QUANTS}")
     header = {"metadata": dict(metadata), "tensors": {}}
     start = 0
     for name, shape in tensors:
@@ -186,10 +217,11 @@ def build_header(metadata: dict, tensors: Iterable[Tuple[str, Tuple[int, ...]]],
             entry = {"dtype": quant, "shape": list(shape)[:4], "offset": start}
             start += numel
             start += pad_to_64(start)
-            entry["scale_offset"] = start
-            entry["scale_size"] = numel // GROUP_SIZE
-            start += numel // GROUP_SIZE * 4
-            start += pad_to_64(start)
+            if quant == "int8":
+                entry["scale_offset"] = start
+                entry["scale_size"] = numel // GROUP_SIZE
+                start += numel // GROUP_SIZE * 4
+                start += pad_to_64(start)
         else:
             entry = {"dtype": "f32", "shape": list(shape)[:4], "offset": start}
             start += numel * 4
@@ -245,21 +277,27 @@ class BinWriter:
         self.buf[8 + len(hb):self.payload_offset] = 0
 
     def view(self, name: str):
-        """Writable numpy views (data, scales-or-None) for tensor ``name``."""
+        """Writable numpy views (data, scales-or-None) for tensor ``name``, typed
+        as ModelFile.tensor returns them."""
         e = self.header["tensors"][name]
         numel = int(np.prod(e["shape"]))
         o = self.payload_offset + e["offset"]
         if e["dtype"] == "f32":
             return self.buf[o:o + 4 * numel].view(np.float32).reshape(e["shape"]), None
+        if e["dtype"] == "fp8":
+            return self.buf[o:o + numel].reshape(e["shape"]), None
         q = self.buf[o:o + numel].view(np.int8).reshape(e["shape"])
         so = self.payload_offset + e["scale_offset"]
         s = self.buf[so:so + 4 * e["scale_size"]].view(np.float32)
         return q, s
 
     def put_fp32(self, name: str, x: np.ndarray) -> None:
-        """Store an fp32 source tensor, quantising it when the header says int8."""
+        """Store an fp32 source tensor, quantising it when the header says int8
+        or casting it when it says fp8."""
         d, s = self.view(name)
-        if s is None:
+        if d.dtype == np.uint8:
+            d[...] = quantize_fp8(np.asarray(x, dtype=np.float32).reshape(d.shape))
+        elif s is None:
             d[...] = np.asarray(x, dtype=np.float32).reshape(d.shape)
         else:
             q, sc = quantize_i8(np.asarray(x, dtype=np.float32).reshape(d.shape))

@@ -147,8 +147,9 @@ def make_bpe_tokenizer(corpus: str = TOKENIZER_CORPUS, n_merges: int = 200) -> d
 
 def make_numpy_model(cfg: dict, seed: int, quant: str = "int8", std: float = 0.02,
                      norm: str = "ones", quant_lm_head: bool = False, tokenizer: Optional[dict] = None) -> BinWriter:
-    """A complete model binary built on the CPU (small configs).  quant_lm_head:
-    the lm_head stored int8 too (format extension, see binfmt.build_header);
+    """A complete model binary built on the CPU (small configs).  quant: "int8",
+    "fp8" (the e5m2 cast) or "f32"; quant_lm_head: the lm_head stored in the
+    projections' format too (format extension, see binfmt.build_header);
     tokenizer: the header's tokenizer object (default: a 3-piece placeholder)."""
     w = BinWriter(metadata_from_hf(cfg, quant), tensor_list(cfg), quant, tokenizer or PLACEHOLDER_TOKENIZER,
                   quant_lm_head=quant_lm_head)
@@ -181,7 +182,9 @@ def make_torch_model(cfg: dict, seed: int, quant: str = "int8", std: float = 0.0
         else:
             x = torch.randn(shape, generator=g, dtype=torch.float32, device=device) * std
         d, s = w.view(name)
-        if s is None:
+        if d.dtype == np.uint8:  # fp8 export: the e5m2 cast, on the device
+            d[...] = x.to(torch.float8_e5m2).view(torch.uint8).cpu().numpy()
+        elif s is None:
             d[...] = x.cpu().numpy()
         elif quantizer is not None:
             q, sc = quantizer(x)
