@@ -63,15 +63,26 @@ def peaks():
 
 
 LM_HEAD_INT8 = False  # --lm-head-int8: the int8 lm_head format extension
+WEIGHTS = "int8"      # --fp8: projection weights as the fp8 (e5m2) cast, a format extension
+
+
+def weight_bytes_per_token(lm_8bit: bool) -> float:
+    """Weight bytes one Mistral-7B decode token reads: the projections (int8 +
+    fp32 scale per 64, or fp8 bytes), the lm_head (fp32, or the projections'
+    format), the final and per-layer norms, one embedding row."""
+    proj, lm = 6979321856, 32000 * 4096
+    qb = 1.0 if WEIGHTS == "fp8" else 1 + 4 / 64
+    return proj * qb + lm * (qb if lm_8bit else 4.0) + 1064960 + 16384
 
 
 def make_model_bytes(device: str, layers: int = 32):
-    """Seeded Mistral-7B int8 binary, drawn and quantised on `device`."""
+    """Seeded Mistral-7B int8 (or, with --fp8, e5m2) binary, drawn and quantised on `device`."""
     from torchless_b200 import ops, synthetic as S
     t0 = time.time()
-    quant = (lambda x: ops.quantize_i8(x)) if device.startswith("cuda") else None
+    quant = (lambda x: ops.quantize_i8(x)) if device.startswith("cuda") and WEIGHTS == "int8" else None
     cfg = dict(S.MISTRAL_7B, num_hidden_layers=layers)
-    w = S.make_torch_model(cfg, seed=SEED, device=device, quantizer=quant, quant_lm_head=LM_HEAD_INT8)
+    w = S.make_torch_model(cfg, seed=SEED, device=device, quant=WEIGHTS, quantizer=quant,
+                           quant_lm_head=LM_HEAD_INT8)
     log(f"generated {w.size / 1e9:.2f} GB model on {device} in {time.time() - t0:.1f}s")
     return w.buf
 
@@ -285,20 +296,24 @@ def run_ours(args, rank, world, local):
     achieved = top["bytes_per_launch"] / (avg_ms / 1000.0) / 1e9
     peak, peak_kind = peaks()
     # ncu traffic of the 1-GPU launch; a rank's launch under tensor parallelism is not captured
-    traffic = load_traffic().get(top["name"]) if world == 1 and ctx == 0 and not LM_HEAD_INT8 else None
+    ext = LM_HEAD_INT8 or WEIGHTS != "int8"  # a format-extension run
+    traffic = load_traffic().get(top["name"]) if world == 1 and ctx == 0 and not ext else None
     total_prof = sum(k["total_ms"] for k in prof)
 
     # bytes of one token at the mean timed position: weights + the K/V rows read
-    w_bytes = 7940898816 - (32000 * 4096 * 4 - 32000 * 4096 * (1 + 4 / 64) if LM_HEAD_INT8 else 0)
+    w_bytes = weight_bytes_per_token(LM_HEAD_INT8)
     kv_per_pos = 2 * args.layers * 8 * 128 * 4
     tok_bytes = w_bytes + kv_per_pos * (start_pos + args.warmup + (args.steps + 1) / 2.0) if ctx > 0 \
         else w_bytes
     workload = (f"Mistral-7B int8 bs1 greedy decode ({ctx}-token random prompt, {args.steps} tokens)" if ctx > 0
                 else "Mistral-7B int8 bs1 greedy decode (16-token prompt, 128 tokens)")
     if LM_HEAD_INT8:
-        workload += " [format extension: int8 lm_head]"
+        workload += f" [format extension: {WEIGHTS} lm_head]"
+    if WEIGHTS == "fp8":
+        workload = workload.replace("int8 bs1", "fp8 (e5m2) bs1") + " [format extension: fp8 weights, no scales]"
     out = {
-        "metric": METRIC if ctx == 0 else f"int8 Mistral-7B decode tok/s @bs1, {ctx}-token context",
+        "metric": (METRIC if ctx == 0 else f"int8 Mistral-7B decode tok/s @bs1, {ctx}-token context")
+        if WEIGHTS == "int8" else f"fp8 Mistral-7B decode tok/s @bs1{f', {ctx}-token context' if ctx else ''}",
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
@@ -321,7 +336,7 @@ def run_ours(args, rank, world, local):
         "clocks": clocks.summary(),
         "ids_head": ids[:8],
     }
-    if not args.no_cpu_baseline and world == 1 and ctx == 0 and not LM_HEAD_INT8:
+    if not args.no_cpu_baseline and world == 1 and ctx == 0 and not ext:
         try:
             v, secs, cores = cpu_reference_sample(buf, args.cpu_layers)
             out["cpu_baseline"] = {
@@ -470,7 +485,7 @@ def run_prefill(args):
     tflops = flops / (ms_prefill * 1e-3) / 1e12
     pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peak = json.load(open(pk))["bf16_tflops"] if os.path.exists(pk) else 1590.0
-    out = {"metric": "int8 Mistral-7B prefill tok/s (2048-token prompt)", "value": T / (ms_prefill * 1e-3),
+    out = {"metric": f"{WEIGHTS} Mistral-7B prefill tok/s (2048-token prompt)", "value": T / (ms_prefill * 1e-3),
            "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_prefill,
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 operands, f32 accumulate",
            "data": "synthetic",
@@ -552,7 +567,7 @@ def run_batch(args, rank=0, world=1, local=0):
     step_s = ms * 1e-3 / K
     peak, peak_kind = peaks()
     algo = kv_bytes + w_int8
-    out = {"metric": "int8 Mistral-7B batched decode tok/s (64 seqs x 4096-token KV)", "value": B * K / (ms * 1e-3),
+    out = {"metric": f"{WEIGHTS} Mistral-7B batched decode tok/s (64 seqs x 4096-token KV)", "value": B * K / (ms * 1e-3),
            "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": ms / K,
            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
            "dtype": "f16 GEMM operands, f32 KV and accumulation", "data": "synthetic",
@@ -590,6 +605,8 @@ def main():
                     help="isolated int8 GEMV sweep at Mistral-7B shapes (one JSON line per shape)")
     ap.add_argument("--lm-head-int8", action="store_true",
                     help="bs1 decode of the same model with its lm_head stored int8 (format extension)")
+    ap.add_argument("--fp8", action="store_true",
+                    help="the same workloads on the fp8 (e5m2) export of the model (format extension)")
     ap.add_argument("--context", type=int, default=0,
                     help="bs1 decode after a random prompt of this many tokens (0: the 16-token prompt)")
     ap.add_argument("--layers", type=int, default=32,
@@ -597,8 +614,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    global LM_HEAD_INT8
+    global LM_HEAD_INT8, WEIGHTS
     LM_HEAD_INT8 = args.lm_head_int8
+    WEIGHTS = "fp8" if args.fp8 else "int8"
     rank, world, local = dist_env()
     if args.gemv_sweep:
         run_gemv_sweep(args)

@@ -60,6 +60,12 @@ TL_API tl_status tl_matmul_f32(float* xout, const float* w, const float* x, size
 TL_API tl_status tl_matmul_i8(float* xout, const int8_t* w, const float* scales, size_t n_scales,
                               const float* x, size_t n, size_t d, void* stream);
 
+/* matmul(xout, W, x) with fp8 weights (format extension after the roadmap
+ * item README.md:160, "fp8 with a cast tensor.to(torch.float8_e5m2)"): W is
+ * [n, d] e5m2 bytes, each weight the e5m2 value itself (no scales);
+ * xout[n] = W @ x[d] with fp32 sums (kernels.cpp:21-33 with that get()). */
+TL_API tl_status tl_matmul_f8(float* xout, const uint8_t* w, const float* x, size_t n, size_t d, void* stream);
+
 /* kernels.h:13  row_matmul(xout, x, w): xout[d] = x[n] @ W[n,d] (kernels.cpp:37-49). */
 TL_API tl_status tl_row_matmul(float* xout, const float* x, const float* w, size_t n, size_t d,
                                void* stream);

@@ -73,6 +73,7 @@ _U32 = ctypes.c_uint32
 SIGNATURES = {
     "tl_matmul_f32": [_P, _P, _P, _S, _S, _P],
     "tl_matmul_i8": [_P, _P, _P, _S, _P, _S, _S, _P],
+    "tl_matmul_f8": [_P, _P, _P, _S, _S, _P],
     "tl_row_matmul": [_P, _P, _P, _S, _S, _P],
     "tl_softmax": [_P, _P, _S, _P],
     "tl_rope": [_P, _P, _P, _P, _S, _S, _P],

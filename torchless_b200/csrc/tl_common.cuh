@@ -1,6 +1,7 @@
 // tl_common.cuh -- shared host/device helpers for the sm_100a kernels.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -149,6 +150,24 @@ __device__ __forceinline__ float dot16_i8(uint4 w, const float2 (&xp)[8]) {
         i8x4_biased(words[j], lo, hi);
         lo = fadd2(lo, nb);
         hi = fadd2(hi, nb);
+        acc0 = ffma2(lo, xp[2 * j], acc0);
+        acc1 = ffma2(hi, xp[2 * j + 1], acc1);
+    }
+    const float2 s = fadd2(acc0, acc1);
+    return s.x + s.y;
+}
+
+// Sum over the 16 fp8 (e5m2) weights in w (byte j = column j) of weight * x:
+// each byte is the high byte of the fp16 with the same value, so two byte
+// permutes give the exact fp16 pairs of a word.
+__device__ __forceinline__ float dot16_f8(uint4 w, const float2 (&xp)[8]) {
+    float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint32_t p01 = __byte_perm(words[j], 0u, 0x1404), p23 = __byte_perm(words[j], 0u, 0x3424);
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&p01));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&p23));
         acc0 = ffma2(lo, xp[2 * j], acc0);
         acc1 = ffma2(hi, xp[2 * j + 1], acc1);
     }

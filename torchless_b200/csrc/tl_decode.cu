@@ -18,7 +18,10 @@
 // mma.m16n8k32 (s8 x s8 -> s32) with the raw int8 weights as A and the three
 // digit vectors as B columns: each 64-column group's three dot products are
 // exact integers, combined in fp32 and scaled by the group's 1/s
-// (tensor.cpp:101-104 dequantisation applied once per group).  Tile row sums
+// (tensor.cpp:101-104 dequantisation applied once per group).  fp8 (e5m2)
+// weights instead (a separate instantiation): x 2^k staged as two fp16 planes
+// (hi + lo, 22 significant bits), the weight bytes widened to fp16 by byte
+// permutes, and fp16 mma.m16n8k16 with fp32 accumulation (exact products).  Tile row sums
 // go to a shared buffer and, after the phase, each row is summed over its
 // tiles in a fixed order and the fused epilogue runs:
 //   q/k/v                       -> qkv buffer         (modules.cpp:53-55)
@@ -57,6 +60,8 @@ constexpr int kThreads = kConsumers + 32;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 // Staged digits of one 64-column group: d0 (x 2^16), d1 (x 2^8), d2 rows of 64 bytes.
 constexpr int kGroupDigitBytes = 192;
+// Staged fp16 planes of one 64-column group (fp8 weights): hi, lo rows of 64 halves.
+constexpr int kGroupHalfBytes = 256;
 
 enum ErrCode : int { kErrBarrier = 1, kErrFull = 2, kErrEmpty = 3, kErrInput = 5 };
 
@@ -133,6 +138,16 @@ __device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1,
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// D = A(16x16 f16, row) * B(16x8 f16, col) + D (f32).
+__device__ __forceinline__ void hmma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // Low bytes of four ints, packed little-endian.
 __device__ __forceinline__ uint32_t pack_lo_bytes(int x0, int x1, int x2, int x3) {
     const uint32_t lo = __byte_perm(static_cast<uint32_t>(x0), static_cast<uint32_t>(x1), 0x0040);
@@ -171,11 +186,11 @@ struct Shared {
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-// Digits of the longest staged vector (3 bytes per column), the fp32 lm_head
-// input, or the attention scratch.
-__host__ __device__ inline size_t xbuf_bytes(int D, int F, int HD) {
+// Digits of the longest staged vector (3 bytes per column; fp16 planes for
+// fp8 weights: 4), the fp32 lm_head input, or the attention scratch.
+__host__ __device__ inline size_t xbuf_bytes(int D, int F, int HD, bool f8) {
     const int Dp = tile_slices(D) * kTileCols, Fp = tile_slices(F) * kTileCols;
-    size_t x = 3 * static_cast<size_t>(Dp > Fp ? Dp : Fp);
+    size_t x = (f8 ? 4 : 3) * static_cast<size_t>(Dp > Fp ? Dp : Fp);
     if (4 * static_cast<size_t>(D) > x) x = 4 * static_cast<size_t>(D);
     const size_t attn = (3 * HD + kConsumerWarps * (HD + 2)) * 4;  // q, k, v + warp partials
     if (attn > x) x = attn;
@@ -184,8 +199,8 @@ __host__ __device__ inline size_t xbuf_bytes(int D, int F, int HD) {
     return align_up(x, 128);
 }
 
-__host__ __device__ inline size_t fixed_bytes(int D, int F, int HD, int pbuf_floats) {
-    return xbuf_bytes(D, F, HD) + align_up(static_cast<size_t>(pbuf_floats) * 4, 128) + 64 * 4 + 64;
+__host__ __device__ inline size_t fixed_bytes(int D, int F, int HD, bool f8, int pbuf_floats) {
+    return xbuf_bytes(D, F, HD, f8) + align_up(static_cast<size_t>(pbuf_floats) * 4, 128) + 64 * 4 + 64;
 }
 
 __device__ Shared carve(uint8_t* base, int stages, const DecodeArgs& a) {
@@ -194,7 +209,7 @@ __device__ Shared carve(uint8_t* base, int stages, const DecodeArgs& a) {
     s.ring = base;
     off += static_cast<size_t>(stages) * kStageBytes;
     s.xbuf = base + off;
-    off += xbuf_bytes(a.D, a.F, a.HD);
+    off += xbuf_bytes(a.D, a.F, a.HD, a.w_f8 != 0);
     s.pbuf = reinterpret_cast<float*>(base + off);
     off += align_up(static_cast<size_t>(a.pbuf_floats) * 4, 128);
     s.scratch = reinterpret_cast<float*>(base + off);
@@ -232,15 +247,16 @@ __device__ Seg seg_info(const DecodeArgs& a, int s) {
     const int NQKV = (a.H + 2 * a.KV) * a.HD;
     const int ksD = tile_slices(a.D);
     Seg g;
+    const uint32_t tbq = a.w_f8 ? kTileBytesF8 : kTileBytesI8;  // 8-bit tile bytes
     if (s >= 4 * a.n_layers) {
-        const int rows = a.lm_i8 ? kTileRowsI8 : kTileRowsF32;
+        const int rows = a.lm_8bit ? kTileRowsI8 : kTileRowsF32;
         g.src = a.lm_head;
         g.n_rb = (a.V + rows - 1) / rows;
         g.ksn = ksD;
-        g.tb = a.lm_i8 ? kTileBytesI8 : kTileBytesF32;
+        g.tb = a.lm_8bit ? tbq : kTileBytesF32;
     } else {
         const DecodeLayer& L = a.layers[s >> 2];
-        g.tb = kTileBytesI8;
+        g.tb = tbq;
         switch (s & 3) {
             case 0: g.src = L.qkv; g.n_rb = (NQKV + 15) / 16; g.ksn = ksD; break;
             case 1: g.src = L.o; g.n_rb = (a.D + 15) / 16; g.ksn = tile_slices(a.H * a.HD); break;
@@ -353,7 +369,10 @@ struct Producer {
 // the rows are reduced over their tiles in a fixed order, so results do not
 // depend on timing.
 // ---------------------------------------------------------------------------
-template <bool TP>  // TP: tensor-parallel exchange paths compiled in
+// TP: tensor-parallel exchange paths compiled in; F8: fp8 (e5m2) weight
+// tiles and fp16-plane staging instead of int8 tiles and digits (a separate
+// instantiation, so neither format's kernel carries the other's code).
+template <bool TP, bool F8>
 struct Consumer {
     const DecodeArgs& a;
     const Shared& sh;
@@ -511,6 +530,62 @@ struct Consumer {
         *reinterpret_cast<uint4*>(dst + 128) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
     }
 
+    // fp8 weights: 16 staged columns (block b) as two fp16 planes of
+    // X = x sc: hi = fp16(X), lo = fp16(X - hi).  Column 64 j + i of plane n
+    // lands at byte 256 j + 128 n + 2 i, the B-operand rows of tile_f8.
+    __device__ __forceinline__ void put_halves(int b, const float (&v)[16], float sc) {
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            const float x0 = v[2 * q] * sc, x1 = v[2 * q + 1] * sc;
+            const __half2 h = __floats2half2_rn(x0, x1);
+            const float2 hf = __half22float2(h);
+            const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+            hi[q] = *reinterpret_cast<const uint32_t*>(&h);
+            lo[q] = *reinterpret_cast<const uint32_t*>(&l);
+        }
+        uint8_t* dst = sh.xbuf + (b >> 2) * kGroupHalfBytes + (b & 3) * 32;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(dst + 16) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+        *reinterpret_cast<uint4*>(dst + 128) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(dst + 144) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+    }
+
+    // Stages 16 columns (block b) for the weights' tile kind.
+    __device__ __forceinline__ void put_x(int b, const float (&v)[16], float sc) {
+        if constexpr (F8) put_halves(b, v, sc);
+        else put_digits(b, v, sc);
+    }
+
+    // Zero staged columns of block b (padding columns: their weights are zero).
+    __device__ __forceinline__ void zero_x(int b) {
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        if constexpr (F8) {
+            uint8_t* dst = sh.xbuf + (b >> 2) * kGroupHalfBytes + (b & 3) * 32;
+            *reinterpret_cast<uint4*>(dst) = z;
+            *reinterpret_cast<uint4*>(dst + 16) = z;
+            *reinterpret_cast<uint4*>(dst + 128) = z;
+            *reinterpret_cast<uint4*>(dst + 144) = z;
+        } else {
+            uint8_t* dst = sh.xbuf + (b >> 2) * kGroupDigitBytes + (b & 3) * 16;
+            *reinterpret_cast<uint4*>(dst) = z;
+            *reinterpret_cast<uint4*>(dst + 64) = z;
+            *reinterpret_cast<uint4*>(dst + 128) = z;
+        }
+    }
+
+    // Staging exponent k for a vector with max |x| <= amax: int8 digits hold
+    // |x 2^k| <= 2^22; fp16 planes keep |x 2^k| < 2^14 (finite planes, and
+    // products with e5m2 weights far inside fp32).
+    __device__ __forceinline__ int stage_exp(float amax) const {
+        int e = 0;
+        if (amax > 0.f) frexpf(amax, &e);  // amax < 2^e
+        return ::min(::max((F8 ? 14 : 22) - e, -120), 120);
+    }
+
+    // Staged bytes per column.
+    static constexpr int x_bytes() { return F8 ? 4 : 3; }
+
     // Stages the phase input x into xbuf as int8 digits of X = rint(x 2^k):
     //   X = 2^16 d0 + 2^8 d1 + d2, |X| <= 2^22, so |d0| <= 64 and d1, d2 are
     //   the balanced base-256 digits in [-128, 127].
@@ -525,15 +600,12 @@ struct Consumer {
     __device__ float stage_digits(const float* vec, int d, const float* g, const float2* local) {
         constexpr int NB = NORM ? 2 : 4;
         const int dp = tile_slices(d) * kTileCols;  // padded to whole tiles
-        if (!TLD_OK(3 * static_cast<size_t>(dp) <= xbuf_bytes(a.D, a.F, a.HD) && d % 64 == 0, 30, d, dp)) return 1.0f;
+        if (!TLD_OK(x_bytes() * static_cast<size_t>(dp) <= xbuf_bytes(a.D, a.F, a.HD, F8) && d % 64 == 0, 30, d,
+                    dp))
+            return 1.0f;
         const int nb = d / 16;
-        // digits of the padding columns (zero weights) must be finite: zero them
-        for (int b = nb + t; b < dp / 16; b += kConsumers) {
-            uint8_t* dst = sh.xbuf + (b >> 2) * kGroupDigitBytes + (b & 3) * 16;
-            *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-            *reinterpret_cast<uint4*>(dst + 64) = make_uint4(0, 0, 0, 0);
-            *reinterpret_cast<uint4*>(dst + 128) = make_uint4(0, 0, 0, 0);
-        }
+        // staged padding columns (zero weights) must be finite: zero them
+        for (int b = nb + t; b < dp / 16; b += kConsumers) zero_x(b);
         const float4* v4 = reinterpret_cast<const float4*>(vec);
         const float4* g4 = reinterpret_cast<const float4*>(g);
         float4 vb[NB][4], gb[NB][4];
@@ -549,9 +621,7 @@ struct Consumer {
         const float2 st = local ? *local : read_stats();
         const float inv = NORM ? 1.0f / sqrtf(st.x / static_cast<float>(d) + 1e-5f) : 1.0f;
         const float amax = NORM ? st.y * inv * 1.0001f : st.y;  // bound on max|x|
-        int e = 0;
-        if (amax > 0.f) frexpf(amax, &e);  // amax < 2^e
-        const int k = ::min(::max(22 - e, -120), 120);
+        const int k = stage_exp(amax);
         const float sc = ldexpf(1.0f, k);
         for (int base = 0;; base += NB * kConsumers) {
 #pragma unroll
@@ -569,7 +639,7 @@ struct Consumer {
                         }
                         v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
                     }
-                    put_digits(b, v, sc);
+                    put_x(b, v, sc);
                 }
             }
             if (base + NB * kConsumers >= nb) break;
@@ -591,7 +661,7 @@ struct Consumer {
 
     // Stages RMSNorm(vec) (modules.cpp:31-46) as fp32 for the fp32 lm_head tiles.
     __device__ void stage_f32(const float* vec, int d, const float* g) {
-        if (!TLD_OK(4 * static_cast<size_t>(d) <= xbuf_bytes(a.D, a.F, a.HD) && d % 4 == 0, 31, d, 0)) return;
+        if (!TLD_OK(4 * static_cast<size_t>(d) <= xbuf_bytes(a.D, a.F, a.HD, F8) && d % 4 == 0, 31, d, 0)) return;
         const float2 st = read_stats();
         const float inv = 1.0f / sqrtf(st.x / static_cast<float>(d) + 1e-5f);
         float4* xs = reinterpret_cast<float4*>(sh.xbuf);
@@ -645,6 +715,48 @@ struct Consumer {
         }
     }
 
+    // One fp8 tile (16 rows x 512 columns of e5m2 bytes in tile_i8's byte
+    // layout, no scales) into pbuf[tile][0..15].  Lane (r, c) holds columns
+    // [16 c, 16 c + 16) of rows r and r + 8 of each 64-column group.  Word m
+    // of those 16 bytes (columns 16 c + 4 m ..) becomes two fp16 pairs by
+    // byte permutes (an e5m2 byte is the high byte of the same value's fp16):
+    // the A registers of m16n8k16 MMA m, whose k = {2c, 2c+1} / {2c+8, 2c+9}
+    // stand for columns 16 c + 4 m + {0, 1} / {2, 3}.  B column 0 is the hi
+    // plane of x, 1 the lo plane (lanes with r = 0 / 1 load the same columns
+    // of them), 2..7 zero.  fp16 products are exact and accumulate in fp32;
+    // lane c = 0 holds row r (d0 + d1) and row r + 8 (d2 + d3).  Each group
+    // starts two fresh accumulators (even / odd m), so no MMA waits on more
+    // than one other and the groups' chains overlap.
+    __device__ __forceinline__ void tile_f8(const uint8_t* st, int ks, float* out) {
+        const int r = lane >> 2, c = lane & 3;
+        const uint8_t* xh = sh.xbuf + ks * (8 * kGroupHalfBytes) + (r < 2 ? r : 0) * 128 + c * 32;
+        float yr = 0.f, yr8 = 0.f;
+#pragma unroll
+        for (int g = 0; g < 8; g++) {
+            const uint4 ar = lds128(st + g * 1024 + lane * 16);
+            const uint4 ar8 = lds128(st + g * 1024 + 512 + lane * 16);
+            uint4 b0 = make_uint4(0, 0, 0, 0), b1 = make_uint4(0, 0, 0, 0);
+            if (r < 2) {
+                b0 = lds128(xh + g * kGroupHalfBytes);
+                b1 = lds128(xh + g * kGroupHalfBytes + 16);
+            }
+            const uint32_t wa[4] = {ar.x, ar.y, ar.z, ar.w};
+            const uint32_t wb[4] = {ar8.x, ar8.y, ar8.z, ar8.w};
+            const uint32_t bx[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+            float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int m = 0; m < 4; m++)
+                hmma16816(d[m & 1], __byte_perm(wa[m], 0u, 0x1404), __byte_perm(wb[m], 0u, 0x1404),
+                          __byte_perm(wa[m], 0u, 0x3424), __byte_perm(wb[m], 0u, 0x3424), bx[2 * m], bx[2 * m + 1]);
+            yr += (d[0][0] + d[0][1]) + (d[1][0] + d[1][1]);
+            yr8 += (d[0][2] + d[0][3]) + (d[1][2] + d[1][3]);
+        }
+        if (c == 0) {
+            out[r] = yr;
+            out[r + 8] = yr8;
+        }
+    }
+
     // One fp32 lm_head tile (4 rows x 512 columns) into pbuf[tile][0..3].
     __device__ __forceinline__ void tile_f32(const uint8_t* st, int ks, float* out) {
         const float* xf = reinterpret_cast<const float*>(sh.xbuf) + ks * kTileCols + 2 * lane;
@@ -678,7 +790,7 @@ struct Consumer {
         const int n_tiles = n_rb_local * ksn;
         const int n_slots = (n_tiles + kTilesPerStage - 1) / kTilesPerStage;
         constexpr int ROWS = F32 ? kTileRowsF32 : kTileRowsI8;
-        constexpr int TB = F32 ? kTileBytesF32 : kTileBytesI8;
+        constexpr int TB = F32 ? kTileBytesF32 : (F8 ? kTileBytesF8 : kTileBytesI8);
         int my_i = warp;         // next tile of this warp
         int my_ks = warp % ksn;  // its k-slice, kept incrementally
         for (int j = 0; j < n_slots; j++) {
@@ -696,7 +808,8 @@ struct Consumer {
                 if (TLD_OK((my_i + 1) * ROWS <= a.pbuf_floats, 12, my_i, a.pbuf_floats)) {
                     const uint8_t* st = sh.ring + static_cast<size_t>(s) * kStageBytes + (my_i % kTilesPerStage) * TB;
                     float* out = sh.pbuf + static_cast<size_t>(my_i) * ROWS;
-                    if (F32) tile_f32(st, my_ks, out);
+                    if constexpr (F32) tile_f32(st, my_ks, out);
+                    else if constexpr (F8) tile_f8(st, my_ks, out);
                     else tile_i8(st, my_ks, out);
                 }
                 my_i += kConsumerWarps;
@@ -861,7 +974,7 @@ struct Consumer {
     template <bool F32>
     __device__ float stage_xchg(const float* hprev, float* hout, const float* g) {
         const int D = a.D, nb = D / 16;
-        if (!TLD_OK(nb <= 2 * kConsumers && (F32 ? 4 : 3) * static_cast<size_t>(D) <= xbuf_bytes(a.D, a.F, a.HD),
+        if (!TLD_OK(nb <= 2 * kConsumers && (F32 ? 4 : x_bytes()) * static_cast<size_t>(D) <= xbuf_bytes(a.D, a.F, a.HD, F8),
                     33, D, 0))
             return 1.0f;
         const float* recv = reinterpret_cast<const float*>(a.xpeer[a.tp_rank] + kXchgRecv) +
@@ -908,10 +1021,7 @@ struct Consumer {
         float sc = 1.0f;
         int k = 0;
         if (!F32) {
-            const float amax = st.y * inv * 1.0001f;
-            int e = 0;
-            if (amax > 0.f) frexpf(amax, &e);
-            k = ::min(::max(22 - e, -120), 120);
+            k = stage_exp(st.y * inv * 1.0001f);
             sc = ldexpf(1.0f, k);
         }
 #pragma unroll
@@ -933,7 +1043,7 @@ struct Consumer {
                     reinterpret_cast<float4*>(sh.xbuf)[4 * b + qd] =
                         make_float4(x[4 * qd], x[4 * qd + 1], x[4 * qd + 2], x[4 * qd + 3]);
             } else {
-                put_digits(b, x, sc);
+                put_x(b, x, sc);
             }
         }
         consumer_sync();
@@ -1028,7 +1138,7 @@ struct Consumer {
             if (u >= a.KV * S) return true;
             const int g = u / S, s = u % S;
             if (!TLD_OK(pos < static_cast<unsigned>(a.max_seq) && a.H == QPG * a.KV, 40, pos, g)) return true;
-            if (!TLD_OK((6 * HD + kConsumerWarps * QPG * W) * 4 <= static_cast<int>(xbuf_bytes(a.D, a.F, a.HD)), 41,
+            if (!TLD_OK((6 * HD + kConsumerWarps * QPG * W) * 4 <= static_cast<int>(xbuf_bytes(a.D, a.F, a.HD, F8)), 41,
                         HD, 1))
                 return true;
             if (!wait_qkv(g, layer)) return false;
@@ -1225,7 +1335,7 @@ struct Consumer {
         if (u >= a.H * S) return true;
         const int h = u / S, s = u % S, kh = h / 4;  // kv head h/4 (modules.cpp:70)
         if (!TLD_OK(pos < static_cast<unsigned>(a.max_seq) && kh < a.KV && h < a.H, 40, pos, kh)) return true;
-        if (!TLD_OK((3 * HD + kConsumerWarps * (HD + 2)) * 4 <= static_cast<int>(xbuf_bytes(a.D, a.F, a.HD)), 41, HD, 0))
+        if (!TLD_OK((3 * HD + kConsumerWarps * (HD + 2)) * 4 <= static_cast<int>(xbuf_bytes(a.D, a.F, a.HD, F8)), 41, HD, 0))
             return true;
         if (!wait_qkv(kh, layer)) return false;
         float* q_s = reinterpret_cast<float*>(sh.xbuf);
@@ -1347,7 +1457,7 @@ struct Consumer {
         return true;
     }
 
-    // Stages ctx = attention output as int8 digits for o_proj: merges, for
+    // Stages ctx = attention output (int8 digits or fp16 planes) for o_proj: merges, for
     // each head, the S split partials {M, L, acc} written by attention
     // (softmax over all positions = sum_s acc_s e^(M_s - M) / sum_s L_s e^(M_s - M),
     // M = max_s M_s), takes the CTA-wide max |ctx| for the digit scale and
@@ -1357,7 +1467,12 @@ struct Consumer {
         const int S = attn_splits(pos);
         const int d = a.H * HD;
         const int nb = d / 16;
-        if (!TLD_OK(3 * static_cast<size_t>(d) <= xbuf_bytes(a.D, a.F, a.HD), 32, d, 0)) return 1.0f;
+        const int dp = tile_slices(d) * kTileCols;  // padded to whole tiles
+        if (!TLD_OK(x_bytes() * static_cast<size_t>(dp) <= xbuf_bytes(a.D, a.F, a.HD, F8), 32, d, dp)) return 1.0f;
+        // fp16 planes of padding columns (zero weights) must be finite: zero them
+        // (stale int8 digits are finite integers, 0 x anything = 0)
+        if constexpr (F8)
+            for (int b = nb + t; b < dp / 16; b += kConsumers) zero_x(b);
         // first block of 16 columns per thread (the only one when H hd <= 4096)
         float v[16];
         float mx = 0.f;
@@ -1377,15 +1492,13 @@ struct Consumer {
             for (int j = 0; j < 16; j++) mx = fmaxf(mx, fabsf(w[j]));
         }
         const float amax = sum_max(0.f, mx).y;
-        int e = 0;
-        if (amax > 0.f) frexpf(amax, &e);
-        const int k = ::min(::max(22 - e, -120), 120);
+        const int k = stage_exp(amax);
         const float sc = ldexpf(1.0f, k);
-        if (b0 < nb) put_digits(b0, v, sc);
+        if (b0 < nb) put_x(b0, v, sc);
         for (int b = b0 + kConsumers; b < nb; b += kConsumers) {
             float w[16];
             merge_ctx_block<HD>(b, S, w);
-            put_digits(b, w, sc);
+            put_x(b, w, sc);
         }
         consumer_sync();
         stamp(2);
@@ -1442,7 +1555,7 @@ struct Consumer {
     }
 };
 
-template <int HD, bool TP>
+template <int HD, bool TP, bool F8>
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, int stages) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Shared sh = carve(smem_raw, stages, a);
@@ -1487,7 +1600,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
     }
 
     // ---------------- consumer warps ----------------
-    Consumer<TP> cw(a, sh, stages);
+    Consumer<TP, F8> cw(a, sh, stages);
     cw.stamp(0);
     const unsigned pos = sh.info[0];
     const uint32_t token = sh.info[1];
@@ -1542,10 +1655,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         if (cw.t == 0) prefetch_l2(g_next, static_cast<uint32_t>(D) * 4u);  // staged after this phase
         if (!cw.template run_i8<3>(D, F, un, a.h, g_next)) return;
     }
-    // logits = lm_head rmsnorm(h); token = argmax (main.cpp:10-21).  An int8
-    // lm_head runs like a projection: RMSNorm fused into the digit staging,
-    // integer tiles of 16 rows.
-    const bool lm8 = a.lm_i8 != 0;
+    // logits = lm_head rmsnorm(h); token = argmax (main.cpp:10-21).  An 8-bit
+    // lm_head runs like a projection: RMSNorm fused into the staging, the
+    // projections' tiles of 16 rows.
+    const bool lm8 = a.lm_8bit != 0;
     float lm_un = 1.0f;
     if (tp) {
         if (!cw.xchg_wait()) return;
@@ -1699,8 +1812,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
 // ---------------------------------------------------------------------------
 // Repacking kernels
 // ---------------------------------------------------------------------------
+// Tiles of kTileBytesI8 (int8 + scales) or, with null scales, kTileBytesF8
+// (the e5m2 bytes in the same layout).
 __global__ void k_repack_i8(uint8_t* dst, const int8_t* w1, const float* s1, const int8_t* w3, const float* s3,
                             int n, int d, int swiglu) {
+    const size_t tb = s1 ? kTileBytesI8 : kTileBytesF8;
     const int ksn = tile_slices(d), dp = ksn * kTileCols;  // columns >= d: zero padding
     const int n_rb = swiglu ? (2 * n + 15) / 16 : (n + 15) / 16;
     const size_t chunks = static_cast<size_t>(n_rb) * 16 * (dp / 16);
@@ -1720,12 +1836,13 @@ __global__ void k_repack_i8(uint8_t* dst, const int8_t* w1, const float* s1, con
         const int col = ch * 16, ks = col / kTileCols, cc = col % kTileCols;
         const int w = cc / 64, c = (cc % 64) / 16, r = rr & 7, half = rr >> 3;
         const int lane = 4 * r + c;
-        uint8_t* out = dst + (static_cast<size_t>(rb) * ksn + ks) * kTileBytesI8 + w * 1024 + half * 512 + lane * 16;
+        uint8_t* out = dst + (static_cast<size_t>(rb) * ksn + ks) * tb + w * 1024 + half * 512 + lane * 16;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (row < n && col < d) v = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(row) * d + col);
         *reinterpret_cast<uint4*>(out) = v;
     }
     // scales (already 1/s): one per (logical row, group); padding groups 0
+    if (!s1) return;
     const int gpr = d / 64, gprp = dp / 64;
     const size_t groups = static_cast<size_t>(n_rb) * 16 * gprp;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < groups; idx += (size_t)gridDim.x * blockDim.x) {
@@ -1770,8 +1887,8 @@ __global__ void k_repack_f32(uint8_t* dst, const float* w, int n, int d) {
 
 }  // namespace
 
-bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers, int grid, int max_smem,
-                        int* stages, size_t* smem_bytes, int* pbuf_floats) {
+bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers, bool w_f8, int grid,
+                        int max_smem, int* stages, size_t* smem_bytes, int* pbuf_floats) {
     if (D % kTileCols || F % 64 || (H * HD) % 64) return false;
     // H: this rank's q heads (H hd == D on one GPU, D / tp under tensor parallelism)
     if (!(HD == 64 || HD == 128 || HD == 256) || H * HD > D || grid < 1) return false;
@@ -1790,8 +1907,8 @@ bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers
     pb = std::max(pb, need(2 * F, kTileRowsI8, D));
     pb = std::max(pb, need(D, kTileRowsI8, F));
     pb = std::max(pb, need(V, kTileRowsF32, D));
-    pb = std::max(pb, need(V, kTileRowsI8, D));  // int8 lm_head
-    const size_t fixed = fixed_bytes(D, F, HD, pb);
+    pb = std::max(pb, need(V, kTileRowsI8, D));  // 8-bit lm_head
+    const size_t fixed = fixed_bytes(D, F, HD, w_f8, pb);
     if (static_cast<size_t>(max_smem) <= fixed) return false;
     int st = static_cast<int>((static_cast<size_t>(max_smem) - fixed) / (kStageBytes + 16));
     st = st > 24 ? 24 : st;
@@ -1806,14 +1923,19 @@ tl_status launch_decode_step(const DecodeArgs& a, int grid, int stages, size_t s
     DecodeArgs copy = a;
     void* args[] = {&copy, &stages};
     const void* fn = nullptr;
-    const bool tp = a.tp_size > 1;
+    const int v = (a.tp_size > 1 ? 1 : 0) + (a.w_f8 ? 2 : 0);  // (TP, F8) instantiation
+    auto pick = [&](auto k00, auto k10, auto k01, auto k11) {
+        const void* ks[4] = {reinterpret_cast<const void*>(k00), reinterpret_cast<const void*>(k10),
+                             reinterpret_cast<const void*>(k01), reinterpret_cast<const void*>(k11)};
+        return ks[v];
+    };
     switch (a.HD) {
-        case 64: fn = tp ? reinterpret_cast<const void*>(decode_step_kernel<64, true>)
-                         : reinterpret_cast<const void*>(decode_step_kernel<64, false>); break;
-        case 128: fn = tp ? reinterpret_cast<const void*>(decode_step_kernel<128, true>)
-                          : reinterpret_cast<const void*>(decode_step_kernel<128, false>); break;
-        case 256: fn = tp ? reinterpret_cast<const void*>(decode_step_kernel<256, true>)
-                          : reinterpret_cast<const void*>(decode_step_kernel<256, false>); break;
+        case 64: fn = pick(decode_step_kernel<64, false, false>, decode_step_kernel<64, true, false>,
+                           decode_step_kernel<64, false, true>, decode_step_kernel<64, true, true>); break;
+        case 128: fn = pick(decode_step_kernel<128, false, false>, decode_step_kernel<128, true, false>,
+                            decode_step_kernel<128, false, true>, decode_step_kernel<128, true, true>); break;
+        case 256: fn = pick(decode_step_kernel<256, false, false>, decode_step_kernel<256, true, false>,
+                            decode_step_kernel<256, false, true>, decode_step_kernel<256, true, true>); break;
         default: return set_error(TL_ERR_UNSUPPORTED, "persistent decode: head_dim %d", a.HD);
     }
     int have = 0;

@@ -22,6 +22,8 @@ namespace tl {
 //                                                 group 8 ks + w.
 // gate/up are interleaved: tile row rr < 8 is gate row 8 rb + rr, rr >= 8 is
 // up row 8 rb + rr - 8, so one tile yields 8 SwiGLU outputs.
+// fp8 matrices (e5m2 bytes, no scales) use the same 16 x 512 tiles and byte
+// layout without the scale block: 8192 bytes per tile.
 // The persistent kernel gives each tile to one consumer warp.
 // fp32 lm_head tiles are 4 rows x 512 columns (8192 bytes):
 //   float w*256 + (rr/2)*128 + lane*4 + (rr%2)*2 + e  holds
@@ -29,6 +31,7 @@ namespace tl {
 constexpr int kTileCols = 512;
 constexpr int kTileRowsI8 = 16;
 constexpr int kTileBytesI8 = 8192 + 512;
+constexpr int kTileBytesF8 = 8192;
 constexpr int kTileRowsF32 = 4;
 constexpr int kTileBytesF32 = 8192;
 constexpr int kStatsCap = 1024;  // most CTAs / heads publishing statistics
@@ -58,8 +61,9 @@ struct DecodeArgs {
     int n_layers;
     const float* embed;         // [V, D]
     const float* g_final;       // [D]
-    const uint8_t* lm_head;     // fp32 tiles, or int8 tiles when lm_i8
-    int lm_i8;                  // lm_head stored int8 + group scales (format extension)
+    const uint8_t* lm_head;     // fp32 tiles, or 8-bit tiles like the projections' when lm_8bit
+    int lm_8bit;                // lm_head stored in the projections' format (format extension)
+    int w_f8;                   // projection tiles hold fp8 (e5m2) weights, not int8 + scales
     const float* cos_tab;       // [max_seq][hd/2]
     const float* sin_tab;
     float* h;                   // residual stream [D]
@@ -122,13 +126,14 @@ constexpr int kTraceEvents = 8;
 
 // Shared-memory bytes, pipeline depth and partial-buffer size for a model
 // shape on `grid` CTAs; false when the shape cannot run in the persistent kernel.
-bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers, int grid, int max_smem,
-                        int* stages, size_t* smem_bytes, int* pbuf_floats);
+bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers, bool w_f8, int grid,
+                        int max_smem, int* stages, size_t* smem_bytes, int* pbuf_floats);
 
 // Launch one decode step (cooperative: every CTA resident on its own SM).
 tl_status launch_decode_step(const DecodeArgs& a, int grid, int stages, size_t smem, cudaStream_t s);
 
-// Weight repacking into the tiled layout (run once at model load).
+// Weight repacking into the tiled layout (run once at model load).  Null
+// scales: the bytes are fp8 (e5m2) weights and the tiles kTileBytesF8 long.
 tl_status repack_i8(uint8_t* dst, const int8_t* w, const float* s, int n, int d, cudaStream_t st);
 tl_status repack_i8_swiglu(uint8_t* dst, const int8_t* w1, const float* s1, const int8_t* w3,
                            const float* s3, int n, int d, cudaStream_t st);
@@ -136,8 +141,9 @@ tl_status repack_f32(uint8_t* dst, const float* w, int n, int d, cudaStream_t st
 
 // Tiles per row block: columns rounded up to whole tiles (padding is zero).
 __host__ __device__ inline int tile_slices(int d) { return (d + kTileCols - 1) / kTileCols; }
-inline size_t tiles_i8_bytes(int n_rows, int d) {
-    return static_cast<size_t>((n_rows + kTileRowsI8 - 1) / kTileRowsI8) * tile_slices(d) * kTileBytesI8;
+inline size_t tiles_q_bytes(int n_rows, int d, bool f8) {
+    return static_cast<size_t>((n_rows + kTileRowsI8 - 1) / kTileRowsI8) * tile_slices(d) *
+           (f8 ? kTileBytesF8 : kTileBytesI8);
 }
 inline size_t tiles_f32_bytes(int n_rows, int d) {
     return static_cast<size_t>((n_rows + kTileRowsF32 - 1) / kTileRowsF32) * tile_slices(d) * kTileBytesF32;

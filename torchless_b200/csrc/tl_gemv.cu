@@ -44,9 +44,9 @@ int wave_grid(K kernel, int block, size_t smem, int units) {
     return std::max(1, std::min(units, per_sm * sm_count()));
 }
 
-template <int C, int MAXT, bool INV, bool NORM, int EPI>
+template <int C, int MAXT, bool INV, bool NORM, int EPI, bool F8>
 tl_status run_i8(GemvI8Args a, cudaStream_t s, bool pdl) {
-    auto k = gemv_i8_kernel<kRowsI8, C, MAXT, INV, NORM, EPI>;
+    auto k = gemv_i8_kernel<kRowsI8, C, MAXT, INV, NORM, EPI, F8>;
     const int T = a.d / (16 * C);
     const int out_rows = (EPI == kSwiGLU) ? kRowsI8 / 2 : kRowsI8;
     const int units = (a.n + out_rows - 1) / out_rows;
@@ -55,16 +55,16 @@ tl_status run_i8(GemvI8Args a, cudaStream_t s, bool pdl) {
     return launch(k, grid, T, smem, s, pdl, "gemv_i8", &a);
 }
 
-template <bool INV, bool NORM, int EPI>
+template <bool INV, bool NORM, int EPI, bool F8 = false>
 tl_status dispatch_i8(const GemvI8Args& a, cudaStream_t s, bool pdl) {
     const int C = chunks_for(a.d);
     const int T = a.d / (16 * C);
     if (C == 1) {
-        if (T <= 128) return run_i8<1, 128, INV, NORM, EPI>(a, s, pdl);
-        if (T <= 256) return run_i8<1, 256, INV, NORM, EPI>(a, s, pdl);
-        return run_i8<1, 512, INV, NORM, EPI>(a, s, pdl);
+        if (T <= 128) return run_i8<1, 128, INV, NORM, EPI, F8>(a, s, pdl);
+        if (T <= 256) return run_i8<1, 256, INV, NORM, EPI, F8>(a, s, pdl);
+        return run_i8<1, 512, INV, NORM, EPI, F8>(a, s, pdl);
     }
-    return run_i8<2, 512, INV, NORM, EPI>(a, s, pdl);
+    return run_i8<2, 512, INV, NORM, EPI, F8>(a, s, pdl);
 }
 
 template <int MAXT, bool NORM, bool ARGMAX>
@@ -122,6 +122,16 @@ bool gemv_f32_fast_ok(size_t n, size_t d, const void* w, const void* x) {
 
 tl_status launch_gemv_i8(const GemvI8Args& a, I8Mode mode, bool inv, bool norm, cudaStream_t s,
                          bool pdl) {
+    if (a.f8) {  // fp8 weights (model paths: the fused modes of the decode step)
+        switch (mode) {
+            case I8Mode::Store:
+                return norm ? dispatch_i8<true, true, kStore, true>(a, s, pdl)
+                            : dispatch_i8<true, false, kStore, true>(a, s, pdl);
+            case I8Mode::AddResidual: return dispatch_i8<true, false, kAddResidual, true>(a, s, pdl);
+            case I8Mode::SwiGLU: return dispatch_i8<true, true, kSwiGLU, true>(a, s, pdl);
+        }
+        return set_error(TL_ERR_INVALID_ARGUMENT, "unknown GEMV mode");
+    }
     switch (mode) {
         case I8Mode::Store:
             if (inv) return norm ? dispatch_i8<true, true, kStore>(a, s, pdl)

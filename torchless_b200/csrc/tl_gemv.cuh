@@ -34,8 +34,8 @@ namespace tl {
 enum GemvEpi : int { kStore = 0, kAddResidual = 1, kSwiGLU = 2 };
 
 struct GemvI8Args {
-    const int8_t* w;   // [n, d] row-major (gate_proj in SwiGLU mode)
-    const float* s;    // [n * d / 64] group scales (inverted when INV)
+    const int8_t* w;   // [n, d] row-major (gate_proj in SwiGLU mode); e5m2 bytes when f8
+    const float* s;    // [n * d / 64] group scales (inverted when INV); unused when f8
     const int8_t* w2;  // up_proj in SwiGLU mode
     const float* s2;
     const float* x;    // activation [d]; with NORM the un-normalised hidden state
@@ -44,6 +44,7 @@ struct GemvI8Args {
     float* y;          // output [n]
     const float* res;  // residual [n] (kAddResidual); may alias y
     int n, d;
+    int f8;            // the weights are fp8 (e5m2) without scales (format extension)
 };
 
 // Loads 16 fp32 activations for chunk `ch` as 8 packed pairs.
@@ -85,8 +86,8 @@ __device__ __forceinline__ void rmsnorm_slice(float2 (&xp)[C][8], const float* g
 
 // R rows per iteration, C chunks per thread.  Block size T = d / (16 C),
 // a multiple of 32 and <= MAXT.  Dynamic shared memory: 32 + 2 * (T/32) * R
-// floats.
-template <int R, int C, int MAXT, bool INV, bool NORM, int EPI>
+// floats.  F8: the weight bytes are e5m2 values, used as they are (no scale).
+template <int R, int C, int MAXT, bool INV, bool NORM, int EPI, bool F8>
 __global__ void __launch_bounds__(MAXT) gemv_i8_kernel(GemvI8Args a) {
     extern __shared__ float smem[];
     const int T = blockDim.x;
@@ -128,7 +129,7 @@ __global__ void __launch_bounds__(MAXT) gemv_i8_kernel(GemvI8Args a) {
                 const int ch = t + c * T;
                 if (ok) {
                     wv[r][c] = ld_stream(wp + static_cast<size_t>(row) * a.d + 16 * ch);
-                    sc[r][c] = __ldg(sp + static_cast<size_t>(row) * gpr + (ch >> 2));
+                    sc[r][c] = F8 ? 1.f : __ldg(sp + static_cast<size_t>(row) * gpr + (ch >> 2));
                 } else {
                     wv[r][c] = make_uint4(0, 0, 0, 0);
                     sc[r][c] = 1.f;
@@ -156,8 +157,12 @@ __global__ void __launch_bounds__(MAXT) gemv_i8_kernel(GemvI8Args a) {
             float acc = 0.f;
 #pragma unroll
             for (int c = 0; c < C; c++) {
-                const float d16 = dot16_i8(wv[r][c], xp[c]);
-                acc += INV ? d16 * sc[r][c] : d16 / sc[r][c];
+                if (F8) {
+                    acc += dot16_f8(wv[r][c], xp[c]);
+                } else {
+                    const float d16 = dot16_i8(wv[r][c], xp[c]);
+                    acc += INV ? d16 * sc[r][c] : d16 / sc[r][c];
+                }
             }
             p[r] = acc;
         }

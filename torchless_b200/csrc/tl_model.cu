@@ -156,7 +156,7 @@ tl_status parse_header(const uint8_t* data, size_t size, Header& h) {
             r.scale_offset = static_cast<uint64_t>(so->i);
             r.scale_size = static_cast<uint64_t>(ss->i);
             r.has_scales = true;
-        } else if (r.dtype != "f32") {
+        } else if (r.dtype != "f32" && r.dtype != "fp8") {
             return set_error(TL_ERR_FORMAT, "tensor %s: unknown dtype %s", kv.first.c_str(), r.dtype.c_str());
         }
         h.tensors[kv.first] = r;
@@ -201,9 +201,9 @@ __global__ void k_invert(float* s, size_t n) {
 }
 
 struct LayerW {
-    int8_t *wqkv, *wo, *w1, *w3, *w2;
-    float *sqkv, *so, *s1, *s3, *s2;
-    float *g_in, *g_post;
+    int8_t *wqkv = nullptr, *wo = nullptr, *w1 = nullptr, *w3 = nullptr, *w2 = nullptr;  // int8 or e5m2 bytes
+    float *sqkv = nullptr, *so = nullptr, *s1 = nullptr, *s3 = nullptr, *s2 = nullptr;  // 1 / s (int8 only)
+    float *g_in = nullptr, *g_post = nullptr;
 };
 
 struct Step {
@@ -230,10 +230,12 @@ struct tl_model {
     DeviceArena weights, state;
     std::vector<LayerW> layers;
     float *embed = nullptr, *norm = nullptr, *lm_head = nullptr;
-    // lm_head stored int8 + group scales (format extension): lm_q / lm_s (1 / s) instead of lm_head
     int n_batches = 0;  // live tl_batch objects on this model
     int window = 0;     // > 0: sliding-window attention over the last `window` positions (opt-in)
-    bool lm_i8 = false;
+    bool w_f8 = false;  // projection weights are fp8 (e5m2) bytes without scales, not int8 + scales
+    // lm_head stored in the projections' 8-bit format (format extension): lm_q
+    // (int8 or e5m2 bytes) and, for int8, lm_s (1 / s) instead of lm_head
+    bool lm_8bit = false;
     int8_t* lm_q = nullptr;
     float* lm_s = nullptr;
     float *kc = nullptr, *vc = nullptr, *cos_tab = nullptr, *sin_tab = nullptr;
@@ -289,8 +291,10 @@ size_t layer_kv_floats(const tl_model* m) { return m->lKV * m->max_seq * m->cfg.
 
 tl_status check_shapes(const Header& h) {
     const tl_config& c = h.cfg;
-    if (std::string(c.quant) != "int8")
-        return set_error(TL_ERR_UNSUPPORTED, "quant \"%s\": only int8 models (export_mistral.py --quant int8) are built",
+    if (std::string(c.quant) != "int8" && std::string(c.quant) != "fp8")
+        return set_error(TL_ERR_UNSUPPORTED,
+                         "quant \"%s\": only int8 models (export_mistral.py --quant int8) and fp8 (e5m2) models "
+                         "are built",
                          c.quant);
     if (c.n_heads != 4 * c.n_kv_heads)
         return set_error(TL_ERR_UNSUPPORTED,
@@ -316,7 +320,7 @@ tl_status find(const Header& h, const std::string& name, const char* dtype, std:
     if (r.dtype != dtype)
         return set_error(TL_ERR_FORMAT, "tensor %s has dtype %s, expected %s", name.c_str(), r.dtype.c_str(), dtype);
     if (r.shape != shape) return set_error(TL_ERR_FORMAT, "tensor %s has an unexpected shape", name.c_str());
-    const uint64_t bytes = r.numel() * (r.dtype == "int8" ? 1 : 4);
+    const uint64_t bytes = r.numel() * (r.dtype == "f32" ? 4 : 1);
     if (r.offset > h.payload_size || bytes > h.payload_size - r.offset)
         return set_error(TL_ERR_FORMAT, "tensor %s extends past the end of the file", name.c_str());
     if (r.has_scales) {
@@ -361,23 +365,27 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     const TensorRec *emb, *nrm, *lmh;
     TL_TRY(find(h, "model.embed_tokens.weight", "f32", {V, D}, emb));
     TL_TRY(find(h, "model.norm.weight", "f32", {D}, nrm));
-    // lm_head: fp32 as export_mistral.py writes it (:119), or int8 + per-64-group
-    // scales like the _proj tensors (format extension; the header's dtype says which)
+    // Projection weights: int8 + per-64-group scales (export_mistral.py --quant
+    // int8), or fp8 e5m2 bytes without scales (the format extension "fp8").
+    const char* wdt = c.quant;
+    const bool f8 = std::string(wdt) == "fp8";
+    // lm_head: fp32 as export_mistral.py writes it (:119), or in the _proj
+    // tensors' format (format extension; the header's dtype says which)
     const auto lm_it = h.tensors.find("lm_head.weight");
-    const bool lm8 = lm_it != h.tensors.end() && lm_it->second.dtype == "int8";
-    TL_TRY(find(h, "lm_head.weight", lm8 ? "int8" : "f32", {V, D}, lmh));
-    if (lm8 && (!lmh->has_scales || D % 64))
+    const bool lm8 = lm_it != h.tensors.end() && lm_it->second.dtype == wdt;
+    TL_TRY(find(h, "lm_head.weight", lm8 ? wdt : "f32", {V, D}, lmh));
+    if (lm8 && !f8 && (!lmh->has_scales || D % 64))
         return set_error(TL_ERR_FORMAT, "int8 lm_head needs per-64-group scales");
     for (int64_t l = 0; l < L; l++) {
         const std::string p = "model.layers." + std::to_string(l) + ".";
         LayerRecs& r = recs[l];
-        TL_TRY(find(h, p + "self_attn.q_proj.weight", "int8", {H * HD, D}, r.q));
-        TL_TRY(find(h, p + "self_attn.k_proj.weight", "int8", {KV * HD, D}, r.k));
-        TL_TRY(find(h, p + "self_attn.v_proj.weight", "int8", {KV * HD, D}, r.v));
-        TL_TRY(find(h, p + "self_attn.o_proj.weight", "int8", {D, H * HD}, r.o));
-        TL_TRY(find(h, p + "mlp.gate_proj.weight", "int8", {F, D}, r.g));
-        TL_TRY(find(h, p + "mlp.up_proj.weight", "int8", {F, D}, r.u));
-        TL_TRY(find(h, p + "mlp.down_proj.weight", "int8", {D, F}, r.d));
+        TL_TRY(find(h, p + "self_attn.q_proj.weight", wdt, {H * HD, D}, r.q));
+        TL_TRY(find(h, p + "self_attn.k_proj.weight", wdt, {KV * HD, D}, r.k));
+        TL_TRY(find(h, p + "self_attn.v_proj.weight", wdt, {KV * HD, D}, r.v));
+        TL_TRY(find(h, p + "self_attn.o_proj.weight", wdt, {D, H * HD}, r.o));
+        TL_TRY(find(h, p + "mlp.gate_proj.weight", wdt, {F, D}, r.g));
+        TL_TRY(find(h, p + "mlp.up_proj.weight", wdt, {F, D}, r.u));
+        TL_TRY(find(h, p + "mlp.down_proj.weight", wdt, {D, F}, r.d));
         TL_TRY(find(h, p + "input_layernorm.weight", "f32", {D}, r.ni));
         TL_TRY(find(h, p + "post_attention_layernorm.weight", "f32", {D}, r.np));
     }
@@ -429,29 +437,34 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
 
     // ---- weights arena (this rank's slices) ----
     using A = DeviceArena;
-    size_t wbytes = A::pad(V * D * 4) + (lm8 ? A::pad(Vl * D) + A::pad(Vl * D / 64 * 4) : A::pad(Vl * D * 4)) +
+    // fp32 scales (int8 only): one per 64 weights
+    auto sc_bytes = [&](int64_t numel) { return f8 ? size_t(0) : A::pad(numel / 64 * 4); };
+    size_t wbytes = A::pad(V * D * 4) + (lm8 ? A::pad(Vl * D) + sc_bytes(Vl * D) : A::pad(Vl * D * 4)) +
                     A::pad(D * 4);
     const size_t per_layer = A::pad(NQKVl * D) + A::pad(D * Hl * HD) + 2 * A::pad(Fl * D) + A::pad(D * Fl) +
-                             A::pad(NQKVl * D / 64 * 4) + A::pad(D * Hl * HD / 64 * 4) + 2 * A::pad(Fl * D / 64 * 4) +
-                             A::pad(D * Fl / 64 * 4) + 2 * A::pad(D * 4);
+                             sc_bytes(NQKVl * D) + sc_bytes(D * Hl * HD) + 2 * sc_bytes(Fl * D) + sc_bytes(D * Fl) +
+                             2 * A::pad(D * 4);
     wbytes += per_layer * L;
     TL_TRY(m->weights.reserve(wbytes));
     m->embed = m->weights.take<float>(V * D);
-    m->lm_i8 = lm8;
+    m->w_f8 = f8;
+    m->lm_8bit = lm8;
     if (lm8) {
         m->lm_q = m->weights.take<int8_t>(Vl * D);
-        m->lm_s = m->weights.take<float>(Vl * D / 64);
+        if (!f8) m->lm_s = m->weights.take<float>(Vl * D / 64);
     } else {
         m->lm_head = m->weights.take<float>(Vl * D);
     }
     m->norm = m->weights.take<float>(D);
     TL_TRY(upload(m->embed, h, emb->offset, V * D * 4));
-    if (lm8) {  // this rank's vocabulary rows and their scales; stored s = 127/absmax becomes 1/s
+    if (lm8) {  // this rank's vocabulary rows and (int8) their scales; stored s = 127/absmax becomes 1/s
         TL_TRY(upload(m->lm_q, h, lmh->offset + static_cast<uint64_t>(rank) * Vl * D, Vl * D));
-        TL_TRY(upload(m->lm_s, h, lmh->scale_offset + static_cast<uint64_t>(rank) * Vl * (D / 64) * 4,
-                      Vl * (D / 64) * 4));
-        k_invert<<<256, 256, 0, m->stream>>>(m->lm_s, static_cast<size_t>(Vl * D / 64));
-        TL_TRY(check_launch("invert lm_head scales"));
+        if (!f8) {
+            TL_TRY(upload(m->lm_s, h, lmh->scale_offset + static_cast<uint64_t>(rank) * Vl * (D / 64) * 4,
+                          Vl * (D / 64) * 4));
+            k_invert<<<256, 256, 0, m->stream>>>(m->lm_s, static_cast<size_t>(Vl * D / 64));
+            TL_TRY(check_launch("invert lm_head scales"));
+        }
     } else {
         TL_TRY(upload(m->lm_head, h, lmh->offset + static_cast<uint64_t>(rank) * Vl * D * 4, Vl * D * 4));
     }
@@ -466,11 +479,13 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         w.w1 = m->weights.take<int8_t>(Fl * D);
         w.w3 = m->weights.take<int8_t>(Fl * D);
         w.w2 = m->weights.take<int8_t>(D * Fl);
-        w.sqkv = m->weights.take<float>(NQKVl * D / 64);
-        w.so = m->weights.take<float>(D * Hl * HD / 64);
-        w.s1 = m->weights.take<float>(Fl * D / 64);
-        w.s3 = m->weights.take<float>(Fl * D / 64);
-        w.s2 = m->weights.take<float>(D * Fl / 64);
+        if (!f8) {  // fp8 weights have no scales (the pointers stay null)
+            w.sqkv = m->weights.take<float>(NQKVl * D / 64);
+            w.so = m->weights.take<float>(D * Hl * HD / 64);
+            w.s1 = m->weights.take<float>(Fl * D / 64);
+            w.s3 = m->weights.take<float>(Fl * D / 64);
+            w.s2 = m->weights.take<float>(D * Fl / 64);
+        }
         w.g_in = m->weights.take<float>(D);
         w.g_post = m->weights.take<float>(D);
         if (!w.g_post) return set_error(TL_ERR_OUT_OF_MEMORY, "weights arena too small (internal)");
@@ -479,28 +494,30 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         TL_TRY(upload(w.wqkv, h, r.q->offset + q0 * D, Hl * HD * D));
         TL_TRY(upload(w.wqkv + Hl * HD * D, h, r.k->offset + k0 * D, KVl * HD * D));
         TL_TRY(upload(w.wqkv + (Hl + KVl) * HD * D, h, r.v->offset + k0 * D, KVl * HD * D));
-        TL_TRY(upload(w.sqkv, h, r.q->scale_offset + q0 * G * 4, Hl * HD * G * 4));
-        TL_TRY(upload(w.sqkv + Hl * HD * G, h, r.k->scale_offset + k0 * G * 4, KVl * HD * G * 4));
-        TL_TRY(upload(w.sqkv + (Hl + KVl) * HD * G, h, r.v->scale_offset + k0 * G * 4, KVl * HD * G * 4));
         // o_proj: this rank's head columns of [D, H hd] (row-parallel)
         TL_TRY(upload_cols(w.wo, h, r.o->offset, D, H * HD, q0, Hl * HD));
-        TL_TRY(upload_cols(w.so, h, r.o->scale_offset, D, H * HD / 64 * 4, q0 / 64 * 4, Hl * HD / 64 * 4));
         // gate/up: this rank's F rows; down_proj: its F columns (row-parallel)
         TL_TRY(upload(w.w1, h, r.g->offset + rank * Fl * D, Fl * D));
-        TL_TRY(upload(w.s1, h, r.g->scale_offset + rank * Fl * G * 4, Fl * G * 4));
         TL_TRY(upload(w.w3, h, r.u->offset + rank * Fl * D, Fl * D));
-        TL_TRY(upload(w.s3, h, r.u->scale_offset + rank * Fl * G * 4, Fl * G * 4));
         TL_TRY(upload_cols(w.w2, h, r.d->offset, D, F, rank * Fl, Fl));
-        TL_TRY(upload_cols(w.s2, h, r.d->scale_offset, D, F / 64 * 4, rank * Fl / 64 * 4, Fl / 64 * 4));
         TL_TRY(upload(w.g_in, h, r.ni->offset, D * 4));
         TL_TRY(upload(w.g_post, h, r.np->offset, D * 4));
-        // Stored scales s = 127/absmax become 1/s: the GEMV multiplies.
-        const size_t ns[5] = {static_cast<size_t>(NQKVl * D / 64), static_cast<size_t>(D * Hl * HD / 64),
-                              static_cast<size_t>(Fl * D / 64), static_cast<size_t>(Fl * D / 64),
-                              static_cast<size_t>(D * Fl / 64)};
-        float* sp[5] = {w.sqkv, w.so, w.s1, w.s3, w.s2};
-        for (int k = 0; k < 5; k++) k_invert<<<256, 256, 0, m->stream>>>(sp[k], ns[k]);
-        TL_TRY(check_launch("invert scales"));
+        if (!f8) {  // the int8 tensors' scales, sliced like their weights
+            TL_TRY(upload(w.sqkv, h, r.q->scale_offset + q0 * G * 4, Hl * HD * G * 4));
+            TL_TRY(upload(w.sqkv + Hl * HD * G, h, r.k->scale_offset + k0 * G * 4, KVl * HD * G * 4));
+            TL_TRY(upload(w.sqkv + (Hl + KVl) * HD * G, h, r.v->scale_offset + k0 * G * 4, KVl * HD * G * 4));
+            TL_TRY(upload_cols(w.so, h, r.o->scale_offset, D, H * HD / 64 * 4, q0 / 64 * 4, Hl * HD / 64 * 4));
+            TL_TRY(upload(w.s1, h, r.g->scale_offset + rank * Fl * G * 4, Fl * G * 4));
+            TL_TRY(upload(w.s3, h, r.u->scale_offset + rank * Fl * G * 4, Fl * G * 4));
+            TL_TRY(upload_cols(w.s2, h, r.d->scale_offset, D, F / 64 * 4, rank * Fl / 64 * 4, Fl / 64 * 4));
+            // Stored scales s = 127/absmax become 1/s: the GEMV multiplies.
+            const size_t ns[5] = {static_cast<size_t>(NQKVl * D / 64), static_cast<size_t>(D * Hl * HD / 64),
+                                  static_cast<size_t>(Fl * D / 64), static_cast<size_t>(Fl * D / 64),
+                                  static_cast<size_t>(D * Fl / 64)};
+            float* sp[5] = {w.sqkv, w.so, w.s1, w.s3, w.s2};
+            for (int k = 0; k < 5; k++) k_invert<<<256, 256, 0, m->stream>>>(sp[k], ns[k]);
+            TL_TRY(check_launch("invert scales"));
+        }
     }
 
     // ---- persistent decode kernel: tiled weight copies ----
@@ -513,7 +530,8 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         int pbuf = 0;
         if (coop && decode_kernel_fits(static_cast<int>(D), static_cast<int>(Fl), static_cast<int>(Hl),
                                        static_cast<int>(KVl), static_cast<int>(HD), static_cast<int>(Vl),
-                                       static_cast<int>(L), dev_sms, max_smem, &m->stages, &m->mega_smem, &pbuf)) {
+                                       static_cast<int>(L), f8, dev_sms, max_smem, &m->stages, &m->mega_smem,
+                                       &pbuf)) {
             m->persistent = true;
             m->grid = dev_sms;
             // Tuning knob: a shallower weight ring (fewer bytes in flight per SM).
@@ -546,17 +564,17 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     if (tp > 1 && !m->persistent)
         return set_error(TL_ERR_UNSUPPORTED, "tensor parallelism needs the persistent decode kernel (shape or device)");
     if (m->persistent) {
-        const size_t per = tiles_i8_bytes(NQKVl, D) + tiles_i8_bytes(D, Hl * HD) + tiles_i8_bytes(2 * Fl, D) +
-                           tiles_i8_bytes(D, Fl);
-        const size_t lm_tiles = lm8 ? tiles_i8_bytes(Vl, D) : tiles_f32_bytes(Vl, D);
+        const size_t per = tiles_q_bytes(NQKVl, D, f8) + tiles_q_bytes(D, Hl * HD, f8) +
+                           tiles_q_bytes(2 * Fl, D, f8) + tiles_q_bytes(D, Fl, f8);
+        const size_t lm_tiles = lm8 ? tiles_q_bytes(Vl, D, f8) : tiles_f32_bytes(Vl, D);
         TL_TRY(m->tiles.reserve(per * L + lm_tiles + 256 * (4 * L + 1)));
         std::vector<DecodeLayer> dl(L);
         for (int64_t l = 0; l < L; l++) {
             const LayerW& w = m->layers[l];
-            uint8_t* tq = m->tiles.take<uint8_t>(tiles_i8_bytes(NQKVl, D));
-            uint8_t* to = m->tiles.take<uint8_t>(tiles_i8_bytes(D, Hl * HD));
-            uint8_t* t13 = m->tiles.take<uint8_t>(tiles_i8_bytes(2 * Fl, D));
-            uint8_t* t2 = m->tiles.take<uint8_t>(tiles_i8_bytes(D, Fl));
+            uint8_t* tq = m->tiles.take<uint8_t>(tiles_q_bytes(NQKVl, D, f8));
+            uint8_t* to = m->tiles.take<uint8_t>(tiles_q_bytes(D, Hl * HD, f8));
+            uint8_t* t13 = m->tiles.take<uint8_t>(tiles_q_bytes(2 * Fl, D, f8));
+            uint8_t* t2 = m->tiles.take<uint8_t>(tiles_q_bytes(D, Fl, f8));
             TL_TRY(repack_i8(tq, w.wqkv, w.sqkv, NQKVl, D, m->stream));
             TL_TRY(repack_i8(to, w.wo, w.so, D, Hl * HD, m->stream));
             TL_TRY(repack_i8_swiglu(t13, w.w1, w.s1, w.w3, w.s3, Fl, D, m->stream));
@@ -567,7 +585,8 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         if (lm8) TL_TRY(repack_i8(tl, m->lm_q, m->lm_s, Vl, D, m->stream));
         else TL_TRY(repack_f32(tl, m->lm_head, Vl, D, m->stream));
         m->dargs.lm_head = tl;
-        m->dargs.lm_i8 = lm8 ? 1 : 0;
+        m->dargs.lm_8bit = lm8 ? 1 : 0;
+        m->dargs.w_f8 = f8 ? 1 : 0;
         TL_CUDA_TRY(cudaMalloc(&m->d_layers, sizeof(DecodeLayer) * L));
         // KV pointers are filled once the state arena exists (below).
         m->dargs.layers = m->d_layers;
@@ -683,12 +702,14 @@ void add_layer_steps(tl_model* m, int l, std::vector<Step>& steps) {
     const int NQKV = (H + 2 * KV) * HD;
     const LayerW* w = &m->layers[l];
     const float eps = 1e-5f;  // RMSNorm::e, hard-coded in modules.h:24
+    const double qb = m->w_f8 ? 1.0 : 1 + 4.0 / 64;  // bytes per weight, scales included
+    const int f8 = m->w_f8 ? 1 : 0;
 
     steps.push_back({"gemv_qkv_rmsnorm",
-                     [=] { return double(NQKV) * D * (1 + 4.0 / 64) + 8.0 * D + 4.0 * NQKV; },
+                     [=] { return double(NQKV) * D * qb + 8.0 * D + 4.0 * NQKV; },
                      [=](cudaStream_t s, bool pdl) {
                          GemvI8Args a = {};
-                         a.w = w->wqkv; a.s = w->sqkv; a.x = m->h; a.g = w->g_in; a.eps = eps;
+                         a.w = w->wqkv; a.s = w->sqkv; a.f8 = f8; a.x = m->h; a.g = w->g_in; a.eps = eps;
                          a.y = m->qkv; a.n = NQKV; a.d = D;
                          return launch_gemv_i8(a, I8Mode::Store, true, true, s, pdl);
                      }});
@@ -711,26 +732,27 @@ void add_layer_steps(tl_model* m, int l, std::vector<Step>& steps) {
                          return launch_attention(a, s, pdl);
                      }});
     steps.push_back({"gemv_o_residual",
-                     [=] { return double(D) * H * HD * (1 + 4.0 / 64) + 4.0 * H * HD + 8.0 * D; },
+                     [=] { return double(D) * H * HD * qb + 4.0 * H * HD + 8.0 * D; },
                      [=](cudaStream_t s, bool pdl) {
                          GemvI8Args a = {};
-                         a.w = w->wo; a.s = w->so; a.x = m->ctx; a.y = m->h; a.res = m->h;
+                         a.w = w->wo; a.s = w->so; a.f8 = f8; a.x = m->ctx; a.y = m->h; a.res = m->h;
                          a.n = D; a.d = H * HD;
                          return launch_gemv_i8(a, I8Mode::AddResidual, true, false, s, pdl);
                      }});
     steps.push_back({"gemv_gate_up_silu",
-                     [=] { return 2.0 * F * D * (1 + 4.0 / 64) + 8.0 * D + 4.0 * F; },
+                     [=] { return 2.0 * F * D * qb + 8.0 * D + 4.0 * F; },
                      [=](cudaStream_t s, bool pdl) {
                          GemvI8Args a = {};
-                         a.w = w->w1; a.s = w->s1; a.w2 = w->w3; a.s2 = w->s3; a.x = m->h; a.g = w->g_post;
+                         a.w = w->w1; a.s = w->s1; a.w2 = w->w3; a.s2 = w->s3; a.f8 = f8; a.x = m->h;
+                         a.g = w->g_post;
                          a.eps = eps; a.y = m->act; a.n = F; a.d = D;
                          return launch_gemv_i8(a, I8Mode::SwiGLU, true, true, s, pdl);
                      }});
     steps.push_back({"gemv_down_residual",
-                     [=] { return double(D) * F * (1 + 4.0 / 64) + 4.0 * F + 8.0 * D; },
+                     [=] { return double(D) * F * qb + 4.0 * F + 8.0 * D; },
                      [=](cudaStream_t s, bool pdl) {
                          GemvI8Args a = {};
-                         a.w = w->w2; a.s = w->s2; a.x = m->act; a.y = m->h; a.res = m->h;
+                         a.w = w->w2; a.s = w->s2; a.f8 = f8; a.x = m->act; a.y = m->h; a.res = m->h;
                          a.n = D; a.d = F;
                          return launch_gemv_i8(a, I8Mode::AddResidual, true, false, s, pdl);
                      }});
@@ -745,9 +767,11 @@ tl_status build_steps(tl_model* m) {
         const double F = m->lF, H = m->lH, KV = m->lKV, HD = c.head_dim, L = c.n_layers;
         const double NQKV = (H + 2 * KV) * HD;
         const double Vr = double(m->lV);
-        // int8 weights + fp32 scales of every projection, fp32 lm_head, norms, one embedding row
-        const double per_layer = (NQKV * D + D * H * HD + 3.0 * F * D) * (1 + 4.0 / 64) + 8.0 * D;
-        const double fixed = per_layer * L + Vr * D * (m->lm_i8 ? 1 + 4.0 / 64 : 4.0) + 8.0 * D;
+        // 8-bit weights (+ fp32 scales for int8) of every projection, the lm_head, norms,
+        // one embedding row
+        const double qb = m->w_f8 ? 1.0 : 1 + 4.0 / 64;
+        const double per_layer = (NQKV * D + D * H * HD + 3.0 * F * D) * qb + 8.0 * D;
+        const double fixed = per_layer * L + Vr * D * (m->lm_8bit ? qb : 4.0) + 8.0 * D;
         m->steps.push_back({"decode_step",
                             [=] { return fixed + 2.0 * L * KV * (double(m->pos) + 1) * HD * 4; },
                             [=](cudaStream_t s, bool) {
@@ -760,11 +784,13 @@ tl_status build_steps(tl_model* m) {
                             return launch_embed(m->h, m->embed, m->d_token, D, s, pdl);
                         }});
     for (int l = 0; l < static_cast<int>(c.n_layers); l++) add_layer_steps(m, l, m->steps);
-    if (m->lm_i8) {  // int8 lm_head: the projection GEMV with the final norm fused, then the argmax
-        m->steps.push_back({"gemv_lm_head_i8", [=] { return double(V) * D * (1 + 4.0 / 64) + 8.0 * D + 4.0 * V; },
+    if (m->lm_8bit) {  // 8-bit lm_head: the projection GEMV with the final norm fused, then the argmax
+        const double qb = m->w_f8 ? 1.0 : 1 + 4.0 / 64;
+        m->steps.push_back({"gemv_lm_head_i8", [=] { return double(V) * D * qb + 8.0 * D + 4.0 * V; },
                             [=](cudaStream_t s, bool pdl) {
                                 GemvI8Args a = {};
-                                a.w = m->lm_q; a.s = m->lm_s; a.x = m->h; a.g = m->norm; a.eps = 1e-5f;
+                                a.w = m->lm_q; a.s = m->lm_s; a.f8 = m->w_f8 ? 1 : 0; a.x = m->h; a.g = m->norm;
+                                a.eps = 1e-5f;
                                 a.y = m->logits; a.n = V; a.d = D;
                                 return launch_gemv_i8(a, I8Mode::Store, true, true, s, pdl);
                             }});
@@ -888,7 +914,7 @@ tl_status ensure_prefill(tl_model* m, size_t n) {
             W[1] = m->w16.take<__half>(D * H * HD);
             W[2] = m->w16.take<__half>(2 * F * D);
             W[3] = m->w16.take<__half>(D * F);
-            // the arena's scales are already 1/s
+            // the arena's scales are already 1/s; fp8 weights (null scales) convert exactly
             TL_TRY(dequant_f16(W[0], w.wqkv, w.sqkv, nullptr, nullptr, NQKV, D, false, m->stream));
             TL_TRY(dequant_f16(W[1], w.wo, w.so, nullptr, nullptr, D, H * HD, false, m->stream));
             TL_TRY(dequant_f16(W[2], w.w1, w.s1, w.w3, w.s3, F, D, true, m->stream));
@@ -1154,10 +1180,10 @@ tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* log
     TL_CUDA_TRY(cudaMemcpyAsync(m->h, m->p_h + static_cast<size_t>(M - 1) * D, D * 4, cudaMemcpyDeviceToDevice, s));
     m->h_pinned[2] = static_cast<uint32_t>(p0 + M - 1);
     TL_CUDA_TRY(cudaMemcpyAsync(m->d_pos, m->h_pinned + 2, 4, cudaMemcpyHostToDevice, s));
-    if (m->lm_i8) {
+    if (m->lm_8bit) {
         GemvI8Args a = {};
-        a.w = m->lm_q; a.s = m->lm_s; a.x = m->h; a.g = m->norm; a.eps = 1e-5f; a.y = m->logits;
-        a.n = V; a.d = D;
+        a.w = m->lm_q; a.s = m->lm_s; a.f8 = m->w_f8 ? 1 : 0; a.x = m->h; a.g = m->norm; a.eps = 1e-5f;
+        a.y = m->logits; a.n = V; a.d = D;
         TL_TRY(launch_gemv_i8(a, I8Mode::Store, true, true, s, false));
         TL_TRY(argmax_step(m->d_token, m->d_hist, m->d_pos, m->logits, V, s));
     } else {
@@ -1490,7 +1516,7 @@ tl_status tl_batch_create(tl_model* m, int n_seq, size_t max_seq, tl_batch** out
     if (!m->lm16) {
         TL_TRY(m->lm16_arena.reserve(DeviceArena::pad(V * D * 2)));
         m->lm16 = m->lm16_arena.take<__half>(V * D);
-        if (m->lm_i8) TL_TRY(dequant_f16(m->lm16, m->lm_q, m->lm_s, nullptr, nullptr, V, D, false, m->stream));
+        if (m->lm_8bit) TL_TRY(dequant_f16(m->lm16, m->lm_q, m->lm_s, nullptr, nullptr, V, D, false, m->stream));
         else TL_TRY(f32_to_f16(m->lm16, m->lm_head, static_cast<size_t>(V) * D, m->stream));
     }
     std::unique_ptr<tl_batch> b(new tl_batch());

@@ -157,6 +157,21 @@ __global__ void k_matmul_i8_rows(float* y, const int8_t* w, const float* scales,
     if (lane == 0) y[row] = acc;
 }
 
+// fp8 (e5m2) weights: get(i) is the e5m2 value (the high byte of its fp16).
+__global__ void k_matmul_f8_rows(float* y, const uint8_t* w, const float* x, size_t n, size_t d) {
+    const size_t row = blockIdx.x * (size_t)(blockDim.x / 32) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    const uint8_t* wr = w + row * d;
+    float acc = 0.f;
+    for (size_t j = lane; j < d; j += 32) {
+        const unsigned short bits = static_cast<unsigned short>(wr[j]) << 8;
+        acc += __half2float(__ushort_as_half(bits)) * x[j];
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) y[row] = acc;
+}
+
 // row_matmul (kernels.cpp:37-49): one thread per output column, loop over rows.
 __global__ void k_row_matmul(float* y, const float* x, const float* w, size_t n, size_t d) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < d; i += (size_t)gridDim.x * blockDim.x) {
@@ -291,6 +306,21 @@ tl_status tl_matmul_i8(float* xout, const int8_t* w, const float* scales, size_t
     const size_t blocks = (n + 7) / 8;
     k_matmul_i8_rows<<<static_cast<unsigned>(blocks), 256, 0, s>>>(xout, w, scales, n_scales, x, n, d);
     return launched("matmul_i8");
+}
+
+tl_status tl_matmul_f8(float* xout, const uint8_t* w, const float* x, size_t n, size_t d, void* stream) {
+    clear_error();
+    TL_REQUIRE(xout && w && x, "tl_matmul_f8: null pointer");
+    TL_REQUIRE(n > 0 && d > 0, "tl_matmul_f8: empty shape");
+    cudaStream_t s = as_stream(stream);
+    if (d % 64 == 0 && gemv_i8_fast_ok(n, d, n * d / 64, w, x)) {
+        GemvI8Args a = {};
+        a.w = reinterpret_cast<const int8_t*>(w); a.f8 = 1; a.x = x; a.y = xout;
+        a.n = static_cast<int>(n); a.d = static_cast<int>(d);
+        return launch_gemv_i8(a, I8Mode::Store, true, false, s, false);
+    }
+    k_matmul_f8_rows<<<static_cast<unsigned>((n + 7) / 8), 256, 0, s>>>(xout, w, x, n, d);
+    return launched("matmul_f8");
 }
 
 tl_status tl_row_matmul(float* xout, const float* x, const float* w, size_t n, size_t d, void* stream) {

@@ -31,6 +31,13 @@ __global__ void k_dequant_f16(__half* w16, const int8_t* q1, const float* inv1, 
             }
         }
         const int2 raw = *reinterpret_cast<const int2*>(q + r * d + c);
+        if (!inv) {  // e5m2 bytes: each is the high byte of the same value's fp16 (exact)
+            const uint32_t x = static_cast<uint32_t>(raw.x), y = static_cast<uint32_t>(raw.y);
+            *reinterpret_cast<uint4*>(w16 + R * d + c) =
+                make_uint4(__byte_perm(x, 0u, 0x1404), __byte_perm(x, 0u, 0x3424), __byte_perm(y, 0u, 0x1404),
+                           __byte_perm(y, 0u, 0x3424));
+            continue;
+        }
         const float s = inv[(r * d + c) / 64];
         const int8_t* b8 = reinterpret_cast<const int8_t*>(&raw);
         __half2 out[4];

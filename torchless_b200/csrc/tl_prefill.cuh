@@ -17,7 +17,8 @@ namespace tl {
 
 // w16[r, c] = fp16(q[r, c] * inv_s[r, c / 64]); rows re-ordered when `swiglu`:
 // output block b of 256 rows = gate rows [128 b, 128 b + 128) then up rows of
-// the same range (q1/inv1 gate, q3/inv3 up).
+// the same range (q1/inv1 gate, q3/inv3 up).  Null scales: the bytes are fp8
+// e5m2 weights, converted exactly (w16 = the e5m2 value).
 tl_status dequant_f16(__half* w16, const int8_t* q1, const float* inv1, const int8_t* q3, const float* inv3, int n,
                       int d, bool swiglu, cudaStream_t s);
 

@@ -34,12 +34,18 @@ def _f32(t):
 
 
 def matmul(xout, w, x, scales=None) -> None:
-    """kernels.h:11-12: xout[n] = w[n, d] @ x[d]; int8 ``w`` needs its stored ``scales``."""
+    """kernels.h:11-12: xout[n] = w[n, d] @ x[d]; int8 ``w`` needs its stored
+    ``scales``; fp8 ``w`` (torch.float8_e5m2, or uint8 holding e5m2 bit
+    patterns: the fp8 export) has none."""
     import torch
     n, d = w.shape
     if x.numel() != d or xout.numel() < n:
         raise ValueError("matmul shape mismatch")  # kernels.cpp:10, 25
-    if w.dtype == torch.int8:
+    if w.dtype in (torch.float8_e5m2, torch.uint8):
+        if scales is not None:
+            raise ValueError("fp8 weights have no scales")
+        check(lib().tl_matmul_f8(_f32(xout), _ptr(w), _f32(x), n, d, _stream()))
+    elif w.dtype == torch.int8:
         if scales is None:
             raise ValueError("int8 matmul needs scales")
         check(lib().tl_matmul_i8(_f32(xout), _ptr(w), _f32(scales), scales.numel(), _f32(x), n, d, _stream()))
