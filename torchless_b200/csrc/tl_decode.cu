@@ -55,6 +55,9 @@ constexpr int kConsumerWarps = 8;
 // single 8.7 KB tiles top out near 6.
 constexpr int kTilesPerStage = 2;
 constexpr int kStageBytes = kTilesPerStage * kTileBytesI8;
+// Ring slot bytes for the weights' format (fp8 tiles carry no scale block;
+// fp32 lm_head tiles, 8192 bytes, fit either).
+__host__ __device__ constexpr int stage_bytes(bool f8) { return kTilesPerStage * (f8 ? kTileBytesF8 : kTileBytesI8); }
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
@@ -174,7 +177,7 @@ __device__ __noinline__ void tld_report(int* dbg, int* err, int site, long long 
 // Shared memory map
 // ---------------------------------------------------------------------------
 struct Shared {
-    uint8_t* ring;     // stages * kStageBytes
+    uint8_t* ring;     // stages * stage_bytes(w_f8)
     uint8_t* xbuf;     // staged activation (int8 digits, fp32 for lm_head) or attention scratch
     float* pbuf;       // per-tile row partial sums of the current phase
     float* scratch;    // 64 floats for block reductions
@@ -207,7 +210,7 @@ __device__ Shared carve(uint8_t* base, int stages, const DecodeArgs& a) {
     Shared s;
     size_t off = 0;
     s.ring = base;
-    off += static_cast<size_t>(stages) * kStageBytes;
+    off += static_cast<size_t>(stages) * stage_bytes(a.w_f8 != 0);
     s.xbuf = base + off;
     off += xbuf_bytes(a.D, a.F, a.HD, a.w_f8 != 0);
     s.pbuf = reinterpret_cast<float*>(base + off);
@@ -312,6 +315,7 @@ struct Producer {
     }
 
     __device__ void run() {
+        const int sb = stage_bytes(a.w_f8 != 0);  // ring slot bytes
         if (a.prefetch > 0) {
             pg = seg_info(a, 0);
             for (int j = 0; j < a.prefetch; j++) prefetch_next();
@@ -335,7 +339,7 @@ struct Producer {
                 }
                 const uint32_t bytes = static_cast<uint32_t>(min(kTilesPerStage, g.n - i)) * g.tb;
                 const uint8_t* gsrc = g.src + static_cast<size_t>(i) * g.tb;
-                if (!TLD_OK(bytes > 0 && bytes <= kStageBytes && (bytes & 15) == 0, 3, bytes, i) ||
+                if (!TLD_OK(bytes > 0 && bytes <= static_cast<uint32_t>(sb) && (bytes & 15) == 0, 3, bytes, i) ||
                     !TLD_OK(static_cast<size_t>(g.b0 * g.ksn + i) * g.tb + bytes <=
                                 static_cast<size_t>(g.n_rb) * g.ksn * g.tb, 4, g.b0 * g.ksn + i, g.n_rb * g.ksn) ||
                     !TLD_OK((reinterpret_cast<uintptr_t>(gsrc) & 15) == 0, 5, reinterpret_cast<uintptr_t>(gsrc) & 15,
@@ -344,7 +348,7 @@ struct Producer {
                     break;
                 }
                 mbar_expect_tx(&sh.full[s], bytes);
-                bulk_load(sh.ring + static_cast<size_t>(s) * kStageBytes, gsrc, bytes, &sh.full[s]);
+                bulk_load(sh.ring + static_cast<size_t>(s) * sb, gsrc, bytes, &sh.full[s]);
                 if (a.prefetch > 0) prefetch_next();
             }
             stamp(sg);
@@ -806,7 +810,8 @@ struct Consumer {
             }
             if (my_i < n_tiles && my_i / kTilesPerStage == j) {
                 if (TLD_OK((my_i + 1) * ROWS <= a.pbuf_floats, 12, my_i, a.pbuf_floats)) {
-                    const uint8_t* st = sh.ring + static_cast<size_t>(s) * kStageBytes + (my_i % kTilesPerStage) * TB;
+                    const uint8_t* st =
+                        sh.ring + static_cast<size_t>(s) * stage_bytes(F8) + (my_i % kTilesPerStage) * TB;
                     float* out = sh.pbuf + static_cast<size_t>(my_i) * ROWS;
                     if constexpr (F32) tile_f32(st, my_ks, out);
                     else if constexpr (F8) tile_f8(st, my_ks, out);
@@ -1910,12 +1915,12 @@ bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers
     pb = std::max(pb, need(V, kTileRowsI8, D));  // 8-bit lm_head
     const size_t fixed = fixed_bytes(D, F, HD, w_f8, pb);
     if (static_cast<size_t>(max_smem) <= fixed) return false;
-    int st = static_cast<int>((static_cast<size_t>(max_smem) - fixed) / (kStageBytes + 16));
+    int st = static_cast<int>((static_cast<size_t>(max_smem) - fixed) / (stage_bytes(w_f8) + 16));
     st = st > 24 ? 24 : st;
     if (st < 4) return false;
     *stages = st;
     *pbuf_floats = pb;
-    *smem_bytes = static_cast<size_t>(st) * kStageBytes + fixed + static_cast<size_t>(st) * 16;
+    *smem_bytes = static_cast<size_t>(st) * stage_bytes(w_f8) + fixed + static_cast<size_t>(st) * 16;
     return true;
 }
 

@@ -538,7 +538,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
             if (const char* e = std::getenv("TL_DECODE_STAGES")) {
                 const int want = std::atoi(e);
                 if (want >= 4 && want < m->stages) {
-                    m->mega_smem -= static_cast<size_t>(m->stages - want) * (2 * kTileBytesI8 + 16);
+                    m->mega_smem -= static_cast<size_t>(m->stages - want) * (2 * (f8 ? kTileBytesF8 : kTileBytesI8) + 16);
                     m->stages = want;
                 }
             }
