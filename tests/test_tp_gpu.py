@@ -102,10 +102,12 @@ def test_tp2_greedy_matches_reference():
 ATTN_ENV = {"per_head": {}, "gqa": {"TL_DECODE_GQA_FROM": "0", "TL_DECODE_GQA_ROWS": "8"}}
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("attn", list(ATTN_ENV))
-def test_tp2_matches_one_gpu_7b_shapes(attn, monkeypatch):
-    """Mistral-7B layer shapes (2 layers, N=2 splits of every projection) vs 1 GPU."""
-    _need(WORLD)
+def test_tp_matches_one_gpu_7b_shapes(attn, world, monkeypatch):
+    """Mistral-7B layer shapes (2 layers, N = 2, 4, 8 splits of every
+    projection; at N = 8 one kv head per rank) vs 1 GPU."""
+    _need(world)
     for k, v in ATTN_ENV[attn].items():
         monkeypatch.setenv(k, v)  # read at load, here and in the spawned ranks
     from torchless_b200 import Model, ops, synthetic as S
@@ -125,8 +127,8 @@ def test_tp2_matches_one_gpu_7b_shapes(attn, monkeypatch):
         path = os.path.join(d, "m7b2.bin")
         buf.tofile(path)
         del buf
-        logits, toks = run_tp(path, feed, max_seq=32)
-    assert toks[0] == toks[1]
+        logits, toks = run_tp(path, feed, max_seq=32, world=world)
+    assert all(t == toks[0] for t in toks), "ranks disagree on the token"
     for step in range(len(feed)):
         e = rel_err(logits[step], ref[step])
         assert e < 1e-4, (step, e)
@@ -187,13 +189,13 @@ def _one_gpu_batch(buf, n_seq, n_pos, steps):
     return np.stack(logits), np.stack(ids)
 
 
-@pytest.mark.parametrize("which", ["small", "7b_shapes"])
-def test_tp2_batch_matches_one_gpu(which):
-    """Batched decode, 2 ranks (o / down rows summed across ranks inside the
-    residual + RMSNorm kernel, argmax merged over the vocabulary slices) vs
+@pytest.mark.parametrize("which,world", [("small", 2), ("7b_shapes", 2), ("7b_shapes", 4), ("7b_shapes", 8)])
+def test_tp_batch_matches_one_gpu(which, world):
+    """Batched decode on `world` ranks (o / down rows summed across ranks inside
+    the residual + RMSNorm kernel, argmax merged over the vocabulary slices) vs
     the same batch on 1 GPU: every step's logits of every sequence and the
     tokens."""
-    _need(WORLD)
+    _need(world)
     import torch.multiprocessing as mp
     if which == "small":
         buf, n_seq, n_pos, steps = model_bytes("small"), 3, 40, 5
@@ -208,11 +210,11 @@ def test_tp2_batch_matches_one_gpu(which):
         path = os.path.join(d, "m.bin")
         buf.tofile(path)
         init_file = os.path.join(d, "init")
-        mp.start_processes(_rank_batch_main, args=(WORLD, init_file, path, n_seq, n_pos, steps, d), nprocs=WORLD,
+        mp.start_processes(_rank_batch_main, args=(world, init_file, path, n_seq, n_pos, steps, d), nprocs=world,
                            join=True, start_method="spawn")
-        res = [np.load(os.path.join(d, f"batch{r}.npz")) for r in range(WORLD)]
+        res = [np.load(os.path.join(d, f"batch{r}.npz")) for r in range(world)]
     logits = np.concatenate([r["logits"] for r in res], axis=2)  # vocabulary slices in rank order
-    assert np.array_equal(res[0]["ids"], res[1]["ids"]), "ranks disagree on the tokens"
+    assert all(np.array_equal(res[0]["ids"], r["ids"]) for r in res), "ranks disagree on the tokens"
     # The batched path feeds its GEMMs fp16 activations: a last-bit change of the
     # fp32 residual (another summation order: split-K ranges and ranks) can flip
     # an fp16 rounding, so the two runs agree to the batched path's own
@@ -225,4 +227,4 @@ def test_tp2_batch_matches_one_gpu(which):
             assert e < 3e-3, (s, q, e)
             if res[0]["ids"][s, q] != ref_ids[s, q]:
                 assert margin(ref[s, q]) < TIE, (s, q)
-    print(f"tp{WORLD} batch {which}: worst logits rel err {worst:.2e}")
+    print(f"tp{world} batch {which}: worst logits rel err {worst:.2e}")
