@@ -228,3 +228,72 @@ def test_tp_batch_matches_one_gpu(which, world):
             if res[0]["ids"][s, q] != ref_ids[s, q]:
                 assert margin(ref[s, q]) < TIE, (s, q)
     print(f"tp{world} batch {which}: worst logits rel err {worst:.2e}")
+
+
+def _rank_depth_main(rank, world, init_file, model_path, prompt, n_new, out_dir):
+    """Child process: prompt token by token, then n_new greedy steps through the
+    timed loop (tl_model_time_decode) and again through forward() with logits."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from torchless_b200 import Model, tp
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=300))
+    m = Model.load(model_path, device=rank, max_seq=64, tp_size=world, tp_rank=rank)
+    tp.connect(m)
+    for t in prompt[:-1]:
+        m.forward(int(t), logits=False)
+    p0 = m.pos
+    _, ids = m.time_decode(int(prompt[-1]), n_new)
+    m.pos = p0
+    logits, t = [], int(prompt[-1])
+    for _ in range(n_new):
+        lg, t = m.forward(t)
+        logits.append(lg)
+    dist.barrier()
+    m.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    np.savez(os.path.join(out_dir, f"depth{rank}.npz"), ids=np.array(ids), logits=np.stack(logits))
+
+
+def test_tp2_full_depth_7b():
+    """All 32 Mistral-7B layers at N = 2 vs 1 GPU: tokens of the timed loop and
+    of forward(), and logits.  Loading a full-size slice exercises the upload
+    ordering (pageable copies against kernels on the model's stream)."""
+    _need(2)
+    import torch.multiprocessing as mp
+    from torchless_b200 import Model, ops, synthetic as S
+    buf = S.make_torch_model(dict(S.MISTRAL_7B), seed=21, device="cuda", quantizer=lambda x: ops.quantize_i8(x)).buf
+    prompt = np.random.default_rng(21).integers(0, 32000, 8).tolist()
+    n_new = 6
+    one = Model.from_buffer(buf, max_seq=64)
+    for t in prompt[:-1]:
+        one.forward(t, logits=False)
+    p0 = one.pos
+    _, ref_ids = one.time_decode(prompt[-1], n_new)
+    one.pos = p0
+    ref, t = [], prompt[-1]
+    for _ in range(n_new):
+        lg, t = one.forward(t)
+        ref.append(lg)
+    one.close()
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "m7b.bin")
+        buf.tofile(path)
+        del buf
+        mp.start_processes(_rank_depth_main, args=(2, os.path.join(d, "init"), path, prompt, n_new, d), nprocs=2,
+                           join=True, start_method="spawn")
+        res = [np.load(os.path.join(d, f"depth{r}.npz")) for r in range(2)]
+    logits = np.concatenate([r["logits"] for r in res], axis=1)
+    assert np.all(np.isfinite(logits))
+    assert res[0]["ids"].tolist() == res[1]["ids"].tolist()
+    for step in range(n_new):
+        e = rel_err(logits[step], ref[step])
+        assert e < 1e-4, (step, e)
+        if res[0]["ids"][step] != ref_ids[step]:
+            assert margin(ref[step]) < TIE, step

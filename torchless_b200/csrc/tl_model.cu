@@ -340,6 +340,14 @@ tl_status upload(void* dst, const Header& h, uint64_t offset, size_t bytes) {
     return TL_OK;
 }
 
+// A cudaMemcpy from pageable host memory may return before its DMA has
+// landed, and the model's kernels run on a non-blocking stream that is not
+// ordered after it: wait for every upload before a kernel reads uploaded bytes.
+tl_status uploads_landed() {
+    TL_CUDA_TRY(cudaDeviceSynchronize());
+    return TL_OK;
+}
+
 // Columns [col0, col0 + width) (in bytes) of every row of a row-major tensor.
 tl_status upload_cols(void* dst, const Header& h, uint64_t offset, size_t rows, size_t row_bytes, size_t col0,
                       size_t width) {
@@ -462,6 +470,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         if (!f8) {
             TL_TRY(upload(m->lm_s, h, lmh->scale_offset + static_cast<uint64_t>(rank) * Vl * (D / 64) * 4,
                           Vl * (D / 64) * 4));
+            TL_TRY(uploads_landed());
             k_invert<<<256, 256, 0, m->stream>>>(m->lm_s, static_cast<size_t>(Vl * D / 64));
             TL_TRY(check_launch("invert lm_head scales"));
         }
@@ -515,10 +524,13 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
                                   static_cast<size_t>(Fl * D / 64), static_cast<size_t>(Fl * D / 64),
                                   static_cast<size_t>(D * Fl / 64)};
             float* sp[5] = {w.sqkv, w.so, w.s1, w.s3, w.s2};
+            TL_TRY(uploads_landed());
             for (int k = 0; k < 5; k++) k_invert<<<256, 256, 0, m->stream>>>(sp[k], ns[k]);
             TL_TRY(check_launch("invert scales"));
         }
     }
+
+    TL_TRY(uploads_landed());  // the repack and dequant kernels read the uploaded weights
 
     // ---- persistent decode kernel: tiled weight copies ----
     const int kmode = opts ? opts->kernel_mode : 0;
@@ -685,6 +697,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     }
     TL_CUDA_TRY(cudaMallocHost(&m->h_pinned, 4 * sizeof(uint32_t)));
     TL_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    TL_TRY(uploads_landed());  // the layer table and RoPE tables, before any step reads them
 
     TL_TRY(build_steps(m.get()));
     if (m->use_graph) TL_TRY(capture_graph(m.get()));
