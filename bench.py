@@ -4,11 +4,14 @@
 
 Workload (one "step" = one decode token, forward + argmax): the Mistral-7B
 architecture with seeded random-init weights N(0, 0.02), quantised to int8
-per 64-group in the export_mistral.py layout; a 16-token uniform-random
-prompt is forwarded first (15 forwards, untimed, as main.cpp:69-71), then W
-warm-up and K timed greedy steps, each feeding its argmax to the next.  The
-7.9 GB of weights read per step are far larger than the 126 MB L2, so no L2
-flush is needed between steps.
+per 64-group in the export_mistral.py layout (synthetic.make_seeded_model:
+the same bytes on every host, so both arms and the full-depth parity fixture
+decode the identical binary); a 16-token uniform-random prompt is forwarded
+first (15 forwards, untimed, as main.cpp:69-71), then W warm-up and K timed
+greedy steps, each feeding its argmax to the next.  The 7.9 GB of weights
+read per step are far larger than the 126 MB L2, so no L2 flush is needed
+between steps.  The W + K greedy ids are checked against the oracle's ids in
+tests/golden/greedy_7b.npz (the "parity" key).
 
 Prints one JSON line (rank 0).  `value` is device time (CUDA events around
 K back-to-back CUDA-graph replays); `e2e` is the same K steps through the
@@ -20,9 +23,10 @@ kernel over NVLink): strong scaling, the timed region is bracketed by
 barriers and the slowest rank's time counts.
 
 --impl reference times the reference's own CPU code (oracle/_ref, built from
-the reference sources) on this host: each step is one decode token at
-Mistral-7B shape, measured as embedding + ONE transformer layer (rotating
-through the 32) + final norm + lm_head, with the layer time multiplied by 32.
+the reference sources) on this host, on the same binary: W untimed and K
+timed whole decode tokens (Model<int8_t>::forward over all 32 layers +
+sample_max, main.cpp:69-77), starting from position 0.  Its int8 matmul is
+single-threaded, so a token takes ~20 s; the run takes (W + K) x that.
 """
 from __future__ import annotations
 
@@ -75,16 +79,49 @@ def weight_bytes_per_token(lm_8bit: bool) -> float:
     return proj * qb + lm * (qb if lm_8bit else 4.0) + 1064960 + 16384
 
 
-def make_model_bytes(device: str, layers: int = 32):
-    """Seeded Mistral-7B int8 (or, with --fp8, e5m2) binary, drawn and quantised on `device`."""
-    from torchless_b200 import ops, synthetic as S
+def make_model_bytes(layers: int = 32):
+    """The seeded Mistral-7B binary (int8, or with --fp8 the e5m2 cast), built
+    on the host CPU by synthetic.make_seeded_model: identical bytes on every
+    host and for both arms."""
+    from torchless_b200 import synthetic as S
     t0 = time.time()
-    quant = (lambda x: ops.quantize_i8(x)) if device.startswith("cuda") and WEIGHTS == "int8" else None
     cfg = dict(S.MISTRAL_7B, num_hidden_layers=layers)
-    w = S.make_torch_model(cfg, seed=SEED, device=device, quant=WEIGHTS, quantizer=quant,
-                           quant_lm_head=LM_HEAD_INT8)
-    log(f"generated {w.size / 1e9:.2f} GB model on {device} in {time.time() - t0:.1f}s")
+    w = S.make_seeded_model(cfg, seed=SEED, quant=WEIGHTS, quant_lm_head=LM_HEAD_INT8)
+    log(f"generated {w.size / 1e9:.2f} GB model on {os.cpu_count()} host threads in {time.time() - t0:.1f}s")
     return w.buf
+
+
+def decode_config(args, max_seq: int) -> dict:
+    """The bs1 decode workload, as both arms name it."""
+    return {"workload": f"Mistral-7B int8 bs1 greedy decode (seeded N(0,0.02) weights, 16-token random prompt, "
+                        f"{args.warmup} warm-up + {args.steps} timed tokens)",
+            "global_batch": 1, "seq_len": max_seq,
+            "l2": "inputs larger than L2 (7.94 GB of weights per step)",
+            "weights_bytes_per_token": int(weight_bytes_per_token(LM_HEAD_INT8))}
+
+
+def fixture_ids():
+    """The oracle's greedy ids of the bs1 workload (tests/golden/greedy_7b.npz), or None."""
+    p = os.path.join(ROOT, "tests", "golden", "greedy_7b.npz")
+    if not os.path.exists(p):
+        return None
+    d = np.load(p)
+    return d["ids"].tolist(), d["margin"], d["maxabs"]
+
+
+def ids_parity(ids) -> dict:
+    """Greedy ids produced after the prompt against the oracle fixture's."""
+    fx = fixture_ids()
+    if fx is None:
+        return {"checked": 0, "note": "fixture missing"}
+    want, margin, maxabs = fx
+    n = min(len(ids), len(want))
+    bad = next((i for i in range(n) if ids[i] != want[i]), None)
+    out = {"checked": n, "identical": bad is None, "against": "oracle greedy ids (tests/golden/greedy_7b.npz)"}
+    if bad is not None:
+        out["first_mismatch"] = bad
+        out["near_tie_there"] = bool(margin[bad] < 1e-3 * maxabs[bad])
+    return out
 
 
 def prompt_ids():
@@ -161,40 +198,51 @@ def cpu_reference_sample(buf, n_layers: int):
 
 
 def run_reference(args, rank, world):
+    """The reference's own CPU decode (oracle/_ref) on the same binary, whole tokens."""
     if rank != 0:
         return
     import oracle
     if not oracle.ref_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built (needs the reference tree at build time)"}))
         return
-    import torch
-    dev = "cuda" if torch.cuda.is_available() else "cpu"
-    buf = make_model_bytes(dev)
-    rm = oracle.RefModel(buf, max_seq=64)
+    buf = make_model_bytes(args.layers)
+    n = args.warmup + args.steps
+    max_seq = max(PROMPT_LEN, n) + 8
+    rm = oracle.RefModel(buf, max_seq=max_seq)
     toks = prompt_ids()
-    per = []
-    for i in range(args.warmup + args.steps):
-        e, l1, h = rm.time_token(toks[i % len(toks)], i % 32, 1)
+    tok, ids, times = toks[0], [], []
+    for i in range(n):  # main.cpp:69-77 from position 0: prompt tokens, then greedy
+        t0 = time.perf_counter()
+        rm.forward(tok)
+        nxt = rm.sample_max()
+        t1 = time.perf_counter()
         if i >= args.warmup:
-            per.append(e + 32.0 * l1 + h)
+            times.append(t1 - t0)
+        if i + 1 < len(toks):
+            tok = toks[i + 1]
+        else:
+            ids.append(nxt)
+            tok = nxt
+        log(f"reference token {i}: {t1 - t0:.2f} s")
     rm.close()
-    total = sum(per)
+    total = sum(times)
     value = args.steps / total
     cores = os.cpu_count()
-    sample = ("each step: one Mistral-7B int8 decode token through the reference's own "
-              "Embedding/Layer<int8_t>/RMSNorm/LMHead/sample_max; one layer run per step "
-              "(rotating 0..31) and its time x32")
-    print(json.dumps({
+    sample = (f"the reference's own Model<int8_t>::forward (all 32 layers) + sample_max on the same binary, "
+              f"{args.warmup} untimed + {args.steps} timed whole tokens at positions 0..{n - 1} "
+              f"(prompt forwards, then greedy); int8 matmul single-threaded, fp32 lm_head on OpenMP")
+    out = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic",
-        "config": {"workload": "Mistral-7B int8 bs1 greedy decode (16-token prompt, 128 tokens)",
-                   "global_batch": 1, "parallelism": "cpu (reference int8 matmul is single-threaded)"},
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "reference",
-                         "sample": sample},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "parallelism": "cpu", "config": decode_config(args, PROMPT_LEN + n + 8),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "reference", "sample": sample},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }))
+        "ids_head": ids[:8],
+    }
+    if args.layers == 32 and WEIGHTS == "int8" and not LM_HEAD_INT8:
+        out["parity"] = ids_parity(ids)
+    print(json.dumps(out))
 
 
 def load_traffic():
@@ -217,7 +265,7 @@ def run_ours(args, rank, world, local):
     ctx = args.context
     max_seq = (ctx if ctx > 0 else PROMPT_LEN) + args.warmup + args.steps + 8
     if world == 1:
-        buf = make_model_bytes(f"cuda:{local}", args.layers)
+        buf = make_model_bytes(args.layers)
         m = Model.from_buffer(buf, device=local, max_seq=max_seq)
     else:
         # N > 1: one sequence, tensor-parallel over the N GPUs.  Rank 0 writes
@@ -225,7 +273,7 @@ def run_ours(args, rank, world, local):
         import tempfile
         path = os.path.join(tempfile.gettempdir(), f"tl_bench_model_{os.environ.get('MASTER_PORT', '0')}.bin")
         if rank == 0:
-            make_model_bytes(f"cuda:{local}", args.layers).tofile(path)
+            make_model_bytes(args.layers).tofile(path)
         dist.barrier()
         m = Model.load(path, device=local, max_seq=max_seq, tp_size=world, tp_rank=rank)
         dist.barrier()
@@ -292,7 +340,9 @@ def run_ours(args, rank, world, local):
         return
 
     top = max(prof, key=lambda k: k["total_ms"])  # the dominant kernel
-    avg_ms = top["total_ms"] / top["launches"]
+    # one launch per step (the persistent kernel): its average duration is the
+    # timed region's; otherwise the per-launch event pairs of the profile pass
+    avg_ms = ms / args.steps if launches == 1 else top["total_ms"] / top["launches"]
     achieved = top["bytes_per_launch"] / (avg_ms / 1000.0) / 1e9
     peak, peak_kind = peaks()
     # ncu traffic of the 1-GPU launch; a rank's launch under tensor parallelism is not captured
@@ -305,25 +355,27 @@ def run_ours(args, rank, world, local):
     kv_per_pos = 2 * args.layers * 8 * 128 * 4
     tok_bytes = w_bytes + kv_per_pos * (start_pos + args.warmup + (args.steps + 1) / 2.0) if ctx > 0 \
         else w_bytes
-    workload = (f"Mistral-7B int8 bs1 greedy decode ({ctx}-token random prompt, {args.steps} tokens)" if ctx > 0
-                else "Mistral-7B int8 bs1 greedy decode (16-token prompt, 128 tokens)")
+    cfg = decode_config(args, max_seq)
+    if ctx > 0:
+        cfg["workload"] = (f"Mistral-7B int8 bs1 greedy decode ({ctx}-token random prompt, "
+                           f"{args.warmup} warm-up + {args.steps} timed tokens)")
     if LM_HEAD_INT8:
-        workload += f" [format extension: {WEIGHTS} lm_head]"
+        cfg["workload"] += f" [format extension: {WEIGHTS} lm_head]"
     if WEIGHTS == "fp8":
-        workload = workload.replace("int8 bs1", "fp8 (e5m2) bs1") + " [format extension: fp8 weights, no scales]"
+        cfg["workload"] = cfg["workload"].replace("int8 bs1", "fp8 (e5m2) bs1") + " [format extension: fp8 weights, no scales]"
+    if args.layers != 32:
+        cfg["workload"] += f" [profiling case: {args.layers} of 32 layers]"
+    dtype = ("f16 x f16 -> f32 (e5m2 weights widened exactly, x as two fp16 planes)" if WEIGHTS == "fp8" else
+             "s8 x s8 -> s32 (int8 weights x 22-bit fixed-point activation digits), f32 group combine")
     out = {
         "metric": (METRIC if ctx == 0 else f"int8 Mistral-7B decode tok/s @bs1, {ctx}-token context")
         if WEIGHTS == "int8" else f"fp8 Mistral-7B decode tok/s @bs1{f', {ctx}-token context' if ctx else ''}",
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic",
-        "config": {"workload": workload
-                   + ("" if args.layers == 32 else f" [profiling case: {args.layers} of 32 layers]"),
-                   "global_batch": 1, "seq_len": max_seq,
-                   "parallelism": f"tp{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2 (7.94 GB of weights per step)",
-                   "weights_bytes_per_token": int(w_bytes)},
+        # one sequence: the total work is fixed however many GPUs share it
+        "scaling": "strong", "vs_baseline": None, "dtype": dtype,
+        "data": "synthetic", "parallelism": f"tp{world}" if world > 1 else "single",
+        "config": cfg,
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
         "gpu_launches": launches * args.steps,
         "roofline": {"bound": "hbm", "kernel": top["name"], "achieved": achieved, "peak": peak,
@@ -336,6 +388,8 @@ def run_ours(args, rank, world, local):
         "clocks": clocks.summary(),
         "ids_head": ids[:8],
     }
+    if ctx == 0 and args.layers == 32 and not ext:
+        out["parity"] = ids_parity(warm_ids + ids)
     if not args.no_cpu_baseline and world == 1 and ctx == 0 and not ext:
         try:
             v, secs, cores = cpu_reference_sample(buf, args.cpu_layers)
@@ -462,7 +516,7 @@ def run_prefill(args):
     from torchless_b200 import Model
     torch.cuda.set_device(0)
     T, N_DEC = args.prefill_tokens, 32
-    buf = make_model_bytes("cuda:0", args.layers)
+    buf = make_model_bytes(args.layers)
     m = Model.from_buffer(buf, max_seq=T + N_DEC + 8)
     rng = np.random.default_rng(SEED)
     prompt = rng.integers(0, 32000, T).tolist()
@@ -512,7 +566,7 @@ def run_batch(args, rank=0, world=1, local=0):
     B, P, K = args.batch_seqs, args.batch_context, args.steps
     max_seq = P + args.warmup + K + 8
     if world == 1:
-        buf = make_model_bytes(f"cuda:{local}", args.layers)
+        buf = make_model_bytes(args.layers)
         m = Model.from_buffer(buf, max_seq=max_seq)
         del buf
     else:
@@ -523,7 +577,7 @@ def run_batch(args, rank=0, world=1, local=0):
                                 device_id=torch.device(f"cuda:{local}"))
         path = os.path.join(tempfile.gettempdir(), f"tl_bench_model_{os.environ.get('MASTER_PORT', '0')}.bin")
         if rank == 0:
-            make_model_bytes(f"cuda:{local}", args.layers).tofile(path)
+            make_model_bytes(args.layers).tofile(path)
         dist.barrier()
         m = Model.load(path, device=local, max_seq=max_seq, tp_size=world, tp_rank=rank)
         dist.barrier()

@@ -126,9 +126,12 @@ TL_API tl_status tl_argmax(uint32_t* out, const float* logits, size_t n, void* s
  * partials of 1024 logits), so n must be <= 524288; larger n returns
  * TL_ERR_CAPACITY.  The first call on a device looks up that array's address
  * (cudaGetSymbolAddress, with that device current) and caches it; make that
- * first call before any stream capture begins.  The array is shared by all
- * calls on a device: calls whose kernels overlap in time (other streams or
- * host threads) race on it and must be serialised by the caller. */
+ * first call before any stream capture begins.  The cached address belongs
+ * to the device's primary context and is never looked up again: a process
+ * that destroys that context (cudaDeviceReset) must not call this entry point
+ * on that device afterwards.  The array is shared by all calls on a device:
+ * calls whose kernels overlap in time (other streams or host threads) race on
+ * it and must be serialised by the caller. */
 TL_API tl_status tl_argmax_noalloc(uint32_t* out, const float* logits, size_t n, void* stream);
 
 /* sample_multinomial (main.cpp:23-43) on device logits[n]; *out (device) gets

@@ -22,16 +22,20 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libtorchless_ref.so")
-REFERENCE_TREE = "/root/reference"
+# The reference source tree, for building _ref: given by the caller or the
+# TORCHLESS_REFERENCE environment variable (no default; absent -> _ref is not built).
+REFERENCE_ENV = "TORCHLESS_REFERENCE"
 
 _P, _S, _F, _I, _U32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_float, ctypes.c_int, ctypes.c_uint32
 
 
-def build(reference: bool = True) -> None:
-    """make liboracle.so, and _ref when the reference tree is present."""
+def build(reference: bool = True, tree: Optional[str] = None) -> None:
+    """make liboracle.so, and _ref when a reference tree (`tree`, else
+    $TORCHLESS_REFERENCE) is given and present."""
     subprocess.run(["make", "-s", "-C", HERE, "liboracle.so"], check=True)
-    if reference and os.path.isdir(os.path.join(REFERENCE_TREE, "src")):
-        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={REFERENCE_TREE}"], check=True)
+    tree = tree or os.environ.get(REFERENCE_ENV)
+    if reference and tree and os.path.isdir(os.path.join(tree, "src")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={tree}"], check=True)
 
 
 def _f(a: np.ndarray):

@@ -1,8 +1,9 @@
 """Regenerates the golden fixtures in tests/golden/ from the reference itself.
 
-Run in a container that has the reference tree (default /root/reference):
+Run in a container that has the reference tree, given by --reference or the
+TORCHLESS_REFERENCE environment variable:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference tree>
 
 Writes:
   reference_expected.json  weight-independent vectors of the reference's own
@@ -59,6 +60,7 @@ WEIGHT_INDEPENDENT = ["inv_freq", "cos0", "sin0", "cos3", "sin3", "rope0", "rope
 # Seeds and sizes of the checked models (shared with tests/conftest.py).
 MODELS = {"tiny": (S.TINY, 7), "small": (S.SMALL, 3)}
 PROMPT_LEN, N_NEW = 16, 24
+REF_TREE = None  # set from --reference / $TORCHLESS_REFERENCE in main()
 
 
 def read_expected(path: str) -> dict:
@@ -101,7 +103,7 @@ def sha256(b) -> str:
 
 def sample_fixture() -> None:
     """ref_sample.npz: main.cpp:23-43 through the reference build (oracle/_ref)."""
-    oracle.build(reference=True)
+    oracle.build(reference=True, tree=REF_TREE)
     cfg, seed = MODELS["tiny"]
     V = cfg["vocab_size"]
     rm = oracle.RefModel(S.make_numpy_model(cfg, seed=seed, norm="random").buf, max_seq=16)
@@ -161,7 +163,7 @@ def tokenizer_texts(seed: int = 21, n: int = 60):
 
 def tokenizer_fixture() -> None:
     """ref_tokenizer.json: tokenizer.cpp through the reference build (oracle/_ref)."""
-    oracle.build(reference=True)
+    oracle.build(reference=True, tree=REF_TREE)
     tok = S.make_bpe_tokenizer()
     rt = oracle.RefTokenizer(tok)
     cases = []
@@ -175,11 +177,15 @@ def tokenizer_fixture() -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("TORCHLESS_REFERENCE"),
+                    help="the reference source tree (default: $TORCHLESS_REFERENCE)")
     ap.add_argument("--only-sample", action="store_true", help="regenerate ref_sample.npz only")
     ap.add_argument("--only-tokenizer", action="store_true", help="regenerate ref_tokenizer.json only")
     args = ap.parse_args()
-    ref = args.reference
+    global REF_TREE
+    if not args.reference:
+        ap.error("the reference tree is needed: --reference <tree> or TORCHLESS_REFERENCE")
+    ref = REF_TREE = args.reference
     if args.only_sample:
         sample_fixture()
         return
@@ -193,7 +199,7 @@ def main() -> None:
                    "vectors": {k: exp[k] for k in WEIGHT_INDEPENDENT},
                    "kats": kats()}, f)
 
-    oracle.build(reference=True)
+    oracle.build(reference=True, tree=REF_TREE)
     hashes = {}
     for name, (cfg, seed) in MODELS.items():
         tmp = tempfile.mkdtemp()

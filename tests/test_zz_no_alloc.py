@@ -84,19 +84,39 @@ def test_noalloc_matches_tl_argmax_on_consecutive_calls():
 
 @pytest.mark.gpu
 def test_noalloc_takes_no_device_memory():
-    """After the first call, repeated calls leave the device's free memory unchanged."""
+    """The call allocates nothing stream-ordered: the high watermark of the
+    device's default memory pool (the pool tl_argmax's cudaMallocAsync draws
+    from) stays at zero over repeated calls, while one tl_argmax call raises
+    it, which shows that the probe sees such allocations.  The watermark is
+    per pool, so other processes on the GPU do not move it."""
     torch = pytest.importorskip("torch")
+    rt = pytest.importorskip("cuda.bindings.runtime")
     torch.cuda.set_device(0)
     L = lib()
     stream = torch.cuda.current_stream().cuda_stream
     x = torch.randn(100_000, device="cuda")
     o = torch.empty(1, dtype=torch.int32, device="cuda")
-    assert L.tl_argmax_noalloc(o.data_ptr(), x.data_ptr(), x.numel(), stream) == TL_OK
-    torch.cuda.synchronize()
-    free0, _ = torch.cuda.mem_get_info()
+    err, pool = rt.cudaDeviceGetDefaultMemPool(0)
+    assert err == rt.cudaError_t.cudaSuccess
+    high = rt.cudaMemPoolAttr.cudaMemPoolAttrUsedMemHigh
+
+    def reset_high():
+        torch.cuda.synchronize()
+        (e,) = rt.cudaMemPoolSetAttribute(pool, high, rt.cuuint64_t(0))
+        assert e == rt.cudaError_t.cudaSuccess
+
+    def used_high():
+        torch.cuda.synchronize()
+        e, v = rt.cudaMemPoolGetAttribute(pool, high)
+        assert e == rt.cudaError_t.cudaSuccess
+        return int(v)
+
+    assert L.tl_argmax_noalloc(o.data_ptr(), x.data_ptr(), x.numel(), stream) == TL_OK  # set-up call
+    reset_high()
+    assert L.tl_argmax(o.data_ptr(), x.data_ptr(), x.numel(), stream) == TL_OK
+    assert used_high() > 0, "the allocating tl_argmax should show in the pool's watermark"
+    reset_high()
     for _ in range(50):
         assert L.tl_argmax_noalloc(o.data_ptr(), x.data_ptr(), x.numel(), stream) == TL_OK
-    torch.cuda.synchronize()
-    free1, _ = torch.cuda.mem_get_info()
-    assert free1 == free0
+    assert used_high() == 0
     assert int(o.item()) == int(torch.argmax(x).item())

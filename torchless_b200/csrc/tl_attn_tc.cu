@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 if (j < nb) ok = load_k(j);
                 if (ok && j >= 1) ok = load_v(j - 1);
             }
-            if (!ok) fail(11);
+            if (!ok) fail(kDevErrAttnLoad);
             // every copy issued lands before the CTA exits
             for (int k = max(0, nk - kNst); k < nk; k++) bar_wait(&k_full[k % kNst], (k / kNst) & 1);
             for (int k = max(0, nv - kNst); k < nv; k++) bar_wait(&v_full[k % kNst], (k / kNst) & 1);
@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 ok = issue_pv(j);
                 if (ok && j + 2 < nb) ok = issue_s(j + 2);
             }
-            if (!ok) fail(12);
+            if (!ok) fail(kDevErrAttnMma);
             umma_commit(mma_done);  // completes once every MMA issued above has
             bar_wait(mma_done, 0);
         }
@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             pair_sync();
             tc_fence_after();
             if (!good) {
-                if (ok) fail(13);
+                if (ok) fail(kDevErrAttnS);
                 ok = false;
                 continue;
             }
@@ -291,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
             if (__any_sync(FULL, move && f != 1.f)) {  // this half's 64 O columns, warp-wide
                 if (!__all_sync(FULL, wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1))) {
-                    fail(14);
+                    fail(kDevErrAttnPv);
                     ok = false;
                     continue;
                 }
@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 }
             }
         } else if (ok) {
-            fail(16);
+            fail(kDevErrAttnEpi);
         }
     }
     tc_fence_before();

@@ -172,21 +172,27 @@ __global__ void k_attention_merge_batch(__half* ctx16, const float* part, int H,
 }
 
 constexpr int kXVec = 4;                         // float4 columns a thread holds (D <= 16384)
-constexpr int kErrXchg = 6;                      // exchange wait gave up
 constexpr unsigned long long kXchgTimeoutNs = 2000000000ull;
 
 // Thread 0: adds this row's arrival to every rank's counter at `cnt_off`, then
-// waits (bounded) for all tp arrivals of exchange `seq`; false on timeout.
+// waits (bounded) for all tp arrivals of exchange `seq`; false on timeout or
+// when an earlier wait of the step already failed (*err set): the kernels
+// queued after a failed exchange then return at once instead of each
+// spinning to its own timeout.
 __device__ bool xchg_row_arrive_wait(const BatchXchg& X, size_t cnt_off, unsigned long long seq, int* err) {
+    if (*reinterpret_cast<volatile int*>(err)) return false;
     fence_sys();  // this CTA's stores (ordered before by the caller's barrier) reach the peers first
     for (int q = 0; q < X.tp; q++) red_add_sys_u64(X.buf[q] + cnt_off, 1ull);
     const unsigned long long target = (seq + 1) * static_cast<unsigned long long>(X.tp);
     const unsigned long long t0 = globaltimer();
     for (unsigned i = 0;; i++) {
         if (ld_acquire_sys_u64(X.buf[X.rank] + cnt_off) >= target) return true;
-        if ((i & 63) == 63 && globaltimer() - t0 > kXchgTimeoutNs) {
-            atomicCAS(err, 0, kErrXchg);
-            return false;
+        if ((i & 63) == 63) {
+            if (*reinterpret_cast<volatile int*>(err)) return false;
+            if (globaltimer() - t0 > kXchgTimeoutNs) {
+                atomicCAS(err, 0, kDevErrBatchXchg);
+                return false;
+            }
         }
     }
 }

@@ -9,6 +9,27 @@
 
 namespace tl {
 
+// Codes a kernel writes into the model's device error word when a bounded
+// wait gives up (or an input is out of range); the host reads the word after
+// each step.  1-5: persistent decode step, 6: batched tensor-parallel
+// exchange, 11-16: tensor-core prefill attention, 21-24: tcgen05 GEMM.
+enum DeviceErr : int {
+    kDevErrBarrier = 1,      // decode: grid barrier, readiness counter or TP exchange
+    kDevErrRingFull = 2,     // decode: a weight tile did not arrive
+    kDevErrRingEmpty = 3,    // decode: a ring slot was not released
+    kDevErrInput = 5,        // decode: token or position out of range
+    kDevErrBatchXchg = 6,    // batched TP: a peer's row did not arrive
+    kDevErrAttnLoad = 11,    // prefill attention: K / V load slot
+    kDevErrAttnMma = 12,     // prefill attention: MMA issue waits
+    kDevErrAttnS = 13,       // prefill attention: scores not ready
+    kDevErrAttnPv = 14,      // prefill attention: P V not done
+    kDevErrAttnEpi = 16,     // prefill attention: epilogue
+    kGemmErrSlot = 21,       // GEMM: stage slot not freed
+    kGemmErrStage = 22,      // GEMM: stage data did not arrive
+    kGemmErrAccReady = 23,   // GEMM: accumulator not ready
+    kGemmErrAccFree = 24,    // GEMM: accumulator not drained
+};
+
 // Records a formatted message for tl_last_error() and returns `s`.
 tl_status set_error(tl_status s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 void clear_error();

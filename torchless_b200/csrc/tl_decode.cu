@@ -66,7 +66,8 @@ constexpr int kGroupDigitBytes = 192;
 // Staged fp16 planes of one 64-column group (fp8 weights): hi, lo rows of 64 halves.
 constexpr int kGroupHalfBytes = 256;
 
-enum ErrCode : int { kErrBarrier = 1, kErrFull = 2, kErrEmpty = 3, kErrInput = 5 };
+constexpr int kErrBarrier = kDevErrBarrier, kErrFull = kDevErrRingFull, kErrEmpty = kDevErrRingEmpty,
+              kErrInput = kDevErrInput;
 
 // ---------------------------------------------------------------------------
 // PTX helpers

@@ -122,7 +122,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* empty = full + S;
     uint64_t* tfull = empty + S;   // [2] accumulator ready
     uint64_t* tempty = tfull + 2;  // [2] accumulator drained by the epilogue
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* mma_done = tempty + 2;  // every MMA this CTA issued has completed (before dealloc)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -146,6 +147,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             bar_init(&tfull[b], 1);
             bar_init(&tempty[b], 4);  // one arrival per epilogue warp
         }
+        bar_init(mma_done, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -173,7 +175,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 for (int kb = kb0; kb < kb0 + nk; kb++, it++) {
                     const int s = it % S;
                     if (it >= S && !bar_wait_ab(&empty[s], ((it / S) - 1) & 1, abort_flag)) {
-                        fail(1);
+                        fail(kGemmErrSlot);
                         break;
                     }
                     uint8_t* sa = base + s * Cfg::kStageBytes;
@@ -194,7 +196,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x, i++) {
                 const int buf = i & 1;
                 if (i >= 2 && !bar_wait_ab(&tempty[buf], ((i / 2) - 1) & 1, abort_flag)) {
-                    fail(4);
+                    fail(kGemmErrAccFree);
                     break;
                 }
                 tc_fence_after();
@@ -205,7 +207,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 for (int kb = 0; kb < nk; kb++, it++) {
                     const int s = it % S;
                     if (!bar_wait_ab(&full[s], (it / S) & 1, abort_flag)) {
-                        fail(2);
+                        fail(kGemmErrStage);
                         ok = false;
                         break;
                     }
@@ -220,6 +222,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 umma_commit(&tfull[buf]);  // accumulator ready (also on abort: frees the epilogue)
                 if (!ok) break;
             }
+            // also on abort: tensor memory is freed only after every issued MMA has written it
+            umma_commit(mma_done);
+            bar_wait(mma_done, 0);
         }
     } else {
         const int sub = warp & 3;  // tensor-memory lanes 32 sub .. (tcgen05.ld lane quarter of this warp)
@@ -227,7 +232,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, i++) {
             const int buf = i & 1;
             if (!bar_wait_ab(&tfull[buf], (i / 2) & 1, abort_flag)) {
-                fail(3);
+                fail(kGemmErrAccReady);
                 break;
             }
             tc_fence_after();

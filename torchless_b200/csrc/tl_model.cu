@@ -167,6 +167,47 @@ tl_status parse_header(const uint8_t* data, size_t size, Header& h) {
 }
 
 // Bump allocator over one cudaMalloc, 256-byte aligned pieces.
+// What a device error code (DeviceErr) means, for the host's message.
+const char* device_err_text(unsigned code) {
+    switch (code) {
+        case kDevErrBarrier: return "decode grid barrier, readiness counter or tensor-parallel exchange";
+        case kDevErrRingFull: return "decode weight tile arrival";
+        case kDevErrRingEmpty: return "decode ring slot release";
+        case kDevErrBatchXchg: return "batched tensor-parallel exchange (a peer's row did not arrive)";
+        case kDevErrAttnLoad: return "prefill attention K/V load";
+        case kDevErrAttnMma: return "prefill attention MMA issue";
+        case kDevErrAttnS: return "prefill attention scores";
+        case kDevErrAttnPv: return "prefill attention P V";
+        case kDevErrAttnEpi: return "prefill attention epilogue";
+        case kGemmErrSlot: return "GEMM stage slot release";
+        case kGemmErrStage: return "GEMM stage data arrival";
+        case kGemmErrAccReady: return "GEMM accumulator ready";
+        case kGemmErrAccFree: return "GEMM accumulator drained";
+        default: return "unknown wait";
+    }
+}
+
+// CUDA events for device timing, destroyed on every return path.
+struct Events {
+    std::vector<cudaEvent_t> ev;
+    tl_status create(size_t n) {
+        ev.assign(n, nullptr);
+        for (auto& e : ev) {
+            const cudaError_t r = cudaEventCreate(&e);
+            if (r != cudaSuccess) {
+                e = nullptr;
+                return set_error(TL_ERR_CUDA, "cudaEventCreate: %s", cudaGetErrorString(r));
+            }
+        }
+        return TL_OK;
+    }
+    cudaEvent_t operator[](size_t i) const { return ev[i]; }
+    ~Events() {
+        for (auto e : ev)
+            if (e) cudaEventDestroy(e);
+    }
+};
+
 struct DeviceArena {
     char* base = nullptr;
     size_t cap = 0, used = 0;
@@ -987,11 +1028,9 @@ tl_status sync(tl_model* m) {
         cudaMemsetAsync(m->err, 0, 4, m->stream);
         cudaStreamSynchronize(m->stream);
         m->h_pinned[3] = 0;
-        if (code == 5) return set_error(TL_ERR_INVALID_ARGUMENT, "decode kernel: token or position out of range");
+        if (code == kDevErrInput) return set_error(TL_ERR_INVALID_ARGUMENT, "decode kernel: token or position out of range");
         if (m->tp > 1) m->broken = true;
-        return set_error(TL_ERR_TIMEOUT,
-                         "decode kernel wait timed out (code %u: 1 grid barrier, 2 tile arrival, 3 ring slot)",
-                         code);
+        return set_error(TL_ERR_TIMEOUT, "device wait timed out (code %u: %s)", code, device_err_text(code));
     }
     return TL_OK;
 }
@@ -1163,11 +1202,10 @@ tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* log
     const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));  // modules.cpp:79-80
     cudaStream_t s = m->stream;
     TL_CUDA_TRY(cudaMemcpyAsync(m->p_tok, tokens, n * 4, cudaMemcpyHostToDevice, s));
-    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    Events ev;
     if (ms_out) {  // device time of the whole pass, token ids resident
-        TL_CUDA_TRY(cudaEventCreate(&e0));
-        TL_CUDA_TRY(cudaEventCreate(&e1));
-        TL_CUDA_TRY(cudaEventRecord(e0, s));
+        TL_TRY(ev.create(2));
+        TL_CUDA_TRY(cudaEventRecord(ev[0], s));
     }
     TL_TRY(embed_rows(m->p_h, m->embed, m->p_tok, M, D, s));
     for (size_t l = 0; l < m->cfg.n_layers; l++) {
@@ -1209,15 +1247,11 @@ tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* log
     }
     if (m->temperature > 0.f)
         TL_TRY(sample_step(m->d_token, m->d_hist, m->d_pos, m->logits, V, m->temperature, m->sample_seed, s));
-    if (ms_out) TL_CUDA_TRY(cudaEventRecord(e1, s));
+    if (ms_out) TL_CUDA_TRY(cudaEventRecord(ev[1], s));
     if (logits) TL_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, static_cast<size_t>(V) * 4, cudaMemcpyDeviceToHost, s));
     TL_CUDA_TRY(cudaMemcpyAsync(m->h_pinned + 1, m->d_token, 4, cudaMemcpyDeviceToHost, s));
     TL_TRY(sync(m));
-    if (ms_out) {
-        TL_CUDA_TRY(cudaEventElapsedTime(ms_out, e0, e1));
-        cudaEventDestroy(e0);
-        cudaEventDestroy(e1);
-    }
+    if (ms_out) TL_CUDA_TRY(cudaEventElapsedTime(ms_out, ev[0], ev[1]));
     m->pos = p0 + n;
     if (next_token) *next_token = m->h_pinned[1];
     return TL_OK;
@@ -1305,24 +1339,21 @@ tl_status tl_model_time_decode(tl_model* m, uint32_t token, size_t n, uint32_t* 
     TL_CUDA_TRY(cudaSetDevice(m->device));
     TL_TRY(check_capacity(m, n));
     TL_TRY(set_token(m, token));
-    cudaEvent_t e0, e1;
-    TL_CUDA_TRY(cudaEventCreate(&e0));
-    TL_CUDA_TRY(cudaEventCreate(&e1));
+    Events ev;
+    TL_TRY(ev.create(2));
     const size_t first = m->pos;
     tl_status st = TL_OK;
-    cudaEventRecord(e0, m->stream);
+    cudaEventRecord(ev[0], m->stream);
     for (size_t i = 0; i < n && st == TL_OK; i++) st = run_step(m);
-    cudaEventRecord(e1, m->stream);
+    cudaEventRecord(ev[1], m->stream);
     if (st == TL_OK) st = sync(m);
     if (st == TL_OK) {
-        cudaEventElapsedTime(ms, e0, e1);
+        cudaEventElapsedTime(ms, ev[0], ev[1]);
         m->pos += n;
         if (out) {
             cudaMemcpy(out, m->d_hist + first, n * 4, cudaMemcpyDeviceToHost);
         }
     }
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
     return st;
 }
 
@@ -1335,8 +1366,8 @@ tl_status tl_model_profile(tl_model* m, uint32_t token, size_t n, tl_kernel_time
     TL_TRY(check_capacity(m, n));
     TL_TRY(set_token(m, token));
     const size_t S = m->steps.size();
-    std::vector<cudaEvent_t> ev(S + 1);
-    for (auto& e : ev) TL_CUDA_TRY(cudaEventCreate(&e));
+    Events ev;
+    TL_TRY(ev.create(S + 1));
     std::vector<std::string> names;
     std::vector<double> total_ms, bytes;
     std::vector<int> launches;
@@ -1368,7 +1399,6 @@ tl_status tl_model_profile(tl_model* m, uint32_t token, size_t n, tl_kernel_time
             launches[k] += 1;
         }
     }
-    for (auto& e : ev) cudaEventDestroy(e);
     if (st != TL_OK) return st;
     *n_kinds = static_cast<int>(std::min<size_t>(names.size(), max_kinds));
     for (int k = 0; k < *n_kinds; k++) {
@@ -1643,10 +1673,9 @@ tl_status tl_batch_time_decode(tl_batch* b, const uint32_t* tokens, size_t n_ste
     TL_CUDA_TRY(cudaSetDevice(m->device));
     std::memcpy(b->h_pinned, tokens, b->B * 4);
     TL_CUDA_TRY(cudaMemcpyAsync(b->tok, b->h_pinned, b->B * 4, cudaMemcpyHostToDevice, m->stream));
-    cudaEvent_t e0, e1;
-    TL_CUDA_TRY(cudaEventCreate(&e0));
-    TL_CUDA_TRY(cudaEventCreate(&e1));
-    TL_CUDA_TRY(cudaEventRecord(e0, m->stream));
+    Events ev;
+    TL_TRY(ev.create(2));
+    TL_CUDA_TRY(cudaEventRecord(ev[0], m->stream));
     for (size_t i = 0; i < n_steps; i++) {
         TL_TRY(batch_step(b));
         // the argmax of this step is the next step's token (main.cpp:72-77 per sequence)
@@ -1654,11 +1683,9 @@ tl_status tl_batch_time_decode(tl_batch* b, const uint32_t* tokens, size_t n_ste
         if (out)
             TL_CUDA_TRY(cudaMemcpyAsync(out + i * b->B, b->next, b->B * 4, cudaMemcpyDeviceToHost, m->stream));
     }
-    TL_CUDA_TRY(cudaEventRecord(e1, m->stream));
+    TL_CUDA_TRY(cudaEventRecord(ev[1], m->stream));
     TL_TRY(sync(m));
-    TL_CUDA_TRY(cudaEventElapsedTime(ms, e0, e1));
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
+    TL_CUDA_TRY(cudaEventElapsedTime(ms, ev[0], ev[1]));
     return TL_OK;
 }
 

@@ -7,9 +7,12 @@ N(0, std) (std 0.02 by default) with a fixed seed; norm weights are 1.0
 tests so the norm gain is exercised).  Tensor names and shapes follow the HF
 Mistral checkpoint that the reference loads (src/model/mistral/modules.h:77-116).
 
-Two generators produce the same layout:
-  * ``numpy`` (PCG64): small models, and the HF directory that
+Three generators produce the same layout:
+  * ``numpy`` (one PCG64 stream): small models, and the HF directory that
     tests/golden/make_golden.py feeds to the reference's own exporter;
+  * ``seeded`` (PCG64 streams per row block, host threads): the Mistral-7B
+    workload model of the benchmarks and of the full-depth parity fixture,
+    identical bytes on every host (about 20 s on 8 cores);
   * ``torch`` on a device (CUDA when present): Mistral-7B sized models in a few
     seconds, quantised on the device by the library's own quantiser.
 """
@@ -21,7 +24,7 @@ from typing import Dict, Iterator, List, Optional, Tuple
 
 import numpy as np
 
-from .binfmt import BinWriter, metadata_from_hf, quantize_i8
+from .binfmt import BinWriter, metadata_from_hf, quantize_fp8, quantize_i8
 
 # Mistral-7B-v0.1 architecture (the reference's target model).
 MISTRAL_7B = dict(
@@ -156,6 +159,85 @@ def make_numpy_model(cfg: dict, seed: int, quant: str = "int8", std: float = 0.0
     for name, x in numpy_tensors(cfg, seed, std, norm):
         w.put_fp32(name, x)
     return w
+
+
+# Seeded chunks: the unit of the parallel generator below.  Tensor t of
+# ``tensor_list`` is cut into blocks of whole rows of about CHUNK_ELEMS
+# elements; block c of tensor t draws from its own PCG64 stream keyed by
+# SeedSequence([seed, t, c]).  The blocks are fixed by the shapes alone, so
+# the bytes do not depend on the thread count or the machine (numpy's PCG64
+# and ziggurat normal sampler are platform-independent).  Quantisation
+# groups (64 along a row) never straddle a block.
+CHUNK_ELEMS = 1 << 22
+
+
+def _chunks(cfg: dict):
+    for t, (name, shape) in enumerate(tensor_list(cfg)):
+        if _is_norm(name):
+            yield t, 0, name, shape, 0, shape[0]
+            continue
+        rows, cols = shape
+        per = max(1, CHUNK_ELEMS // cols)
+        for c, r0 in enumerate(range(0, rows, per)):
+            yield t, c, name, shape, r0, min(rows, r0 + per)
+
+
+def make_seeded_model(cfg: dict, seed: int, quant: str = "int8", std: float = 0.02,
+                      quant_lm_head: bool = False, threads: Optional[int] = None,
+                      buffer: Optional[np.ndarray] = None) -> BinWriter:
+    """A complete model binary built on the host CPU, in parallel, from seeded
+    row blocks (CHUNK_ELEMS above): every ``*_proj`` matrix, the embedding and
+    the lm_head ~ N(0, std), norm weights 1.0; quantised by ``quantize_i8``
+    (the export_mistral.py arithmetic) or cast to e5m2 for quant "fp8".
+
+    This is the workload model of the Mistral-7B benchmarks and of the
+    full-depth parity fixture: the same seed gives the same bytes on any
+    host, so the CPU checkers and the GPU load the identical binary."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    w = BinWriter(metadata_from_hf(cfg, quant), tensor_list(cfg), quant, PLACEHOLDER_TOKENIZER,
+                  buffer=buffer, quant_lm_head=quant_lm_head)
+
+    def job(item):
+        t, c, name, shape, r0, r1 = item
+        d, s = w.view(name)
+        if _is_norm(name):
+            d[...] = 1.0
+            return
+        rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([seed, t, c])))
+        x = rng.standard_normal((r1 - r0, shape[1]), dtype=np.float32)
+        x *= np.float32(std)
+        if d.dtype == np.uint8:
+            d[r0:r1] = quantize_fp8(x)
+        elif s is None:
+            d[r0:r1] = x
+        else:
+            q, sc = quantize_i8(x)
+            d[r0:r1] = q
+            g = shape[1] // 64
+            s[r0 * g:r1 * g] = sc
+
+    with ThreadPoolExecutor(threads or os.cpu_count() or 1) as ex:
+        for _ in ex.map(job, list(_chunks(cfg))):
+            pass
+    return w
+
+
+def model_digest(buf: np.ndarray, stride: int = 1 << 20, block: int = 4096) -> str:
+    """sha256 of the header and of one `block`-byte window every `stride` bytes
+    of a model binary: a quick fingerprint that tells two multi-GB binaries
+    apart without hashing all of them."""
+    import hashlib
+    import struct
+
+    b = np.ascontiguousarray(buf).view(np.uint8)
+    h = hashlib.sha256()
+    (hsize,) = struct.unpack("<Q", b[:8].tobytes())
+    h.update(b[:8 + hsize].tobytes())
+    h.update(str(b.size).encode())
+    for o in range(8 + hsize, b.size, stride):
+        h.update(b[o:o + block].tobytes())
+    return h.hexdigest()
 
 
 def make_torch_model(cfg: dict, seed: int, quant: str = "int8", std: float = 0.02,
