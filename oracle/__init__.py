@@ -22,6 +22,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libtorchless_ref.so")
+# the same harness and reference sources with the CUDA backend for kernels.h
+REF_CUDA_SO = os.path.join(HERE, "_ref", "libtorchless_ref_cuda.so")
 # The reference source tree, for building _ref: given by the caller or the
 # TORCHLESS_REFERENCE environment variable (no default; absent -> _ref is not built).
 REFERENCE_ENV = "TORCHLESS_REFERENCE"
@@ -36,6 +38,9 @@ def build(reference: bool = True, tree: Optional[str] = None) -> None:
     tree = tree or os.environ.get(REFERENCE_ENV)
     if reference and tree and os.path.isdir(os.path.join(tree, "src")):
         subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={tree}"], check=True)
+        # the reference's model loop over the CUDA backend, once the CUDA library exists
+        if os.path.exists(os.path.join(os.path.dirname(HERE), "torchless_b200", "libtorchless_b200.so")):
+            subprocess.run(["make", "-s", "-C", HERE, "ref-cuda", f"REF={tree}"], check=True)
 
 
 def _f(a: np.ndarray):
@@ -106,43 +111,64 @@ def ref_available() -> bool:
 
 
 def ref_lib() -> ctypes.CDLL:
+    """The reference's own code (oracle/_ref/libtorchless_ref.so)."""
     global _ref
     if _ref is None:
-        if not os.path.exists(REF_SO):
-            raise RuntimeError(f"{REF_SO} not built (make -C oracle ref needs the reference tree)")
-        L = ctypes.CDLL(REF_SO)
-        sig = {
-            "ref_load_file": (_P, [ctypes.c_char_p, _S]),
-            "ref_load_buffer": (_P, [_P, _S, _S]),
-            "ref_free": (None, [_P]),
-            "ref_forward": (_I, [_P, _U32]),
-            "ref_logits": (ctypes.POINTER(_F), [_P]),
-            "ref_hidden": (ctypes.POINTER(_F), [_P]),
-            "ref_sample_max": (_U32, [_P]),
-            "ref_sample_logits": (_U32, [_P, _P, _F, _U32, ctypes.POINTER(_F)]),
-            "ref_tokenizer_new": (_P, [ctypes.c_char_p, _S]),
-            "ref_tokenizer_free": (None, [_P]),
-            "ref_tokenizer_encode": (_S, [_P, ctypes.c_char_p, _S, _P, _S]),
-            "ref_tokenizer_decode": (_S, [_P, _P, _S, _P, _S]),
-            "ref_pos": (_S, [_P]),
-            "ref_set_pos": (None, [_P, _S]),
-            "ref_layer_forward": (_I, [_P, _I, _P]),
-            "ref_time_token": (_I, [_P, _U32, _I, _I, ctypes.POINTER(ctypes.c_double)]),
-            "ref_matmul_i8": (None, [_P, _P, _P, _S, _P, _S, _S]),
-            "ref_matmul_f32": (None, [_P, _P, _P, _S, _S]),
-            "ref_row_matmul": (None, [_P, _P, _P, _S, _S]),
-            "ref_softmax": (None, [_P, _P, _S]),
-            "ref_rope": (None, [_P, _P, _P, _P, _S, _S]),
-            "ref_silu": (None, [_P, _P, _S]),
-            "ref_rmsnorm": (None, [_P, _P, _P]),
-            "ref_rotary": (None, [_P, _S, _P, _P, _P]),
-        }
-        for name, (res, args) in sig.items():
-            fn = getattr(L, name)
-            fn.restype = res
-            fn.argtypes = args
-        _ref = L
+        _ref = _load_ref(REF_SO)
     return _ref
+
+
+_ref_cuda: Optional[ctypes.CDLL] = None
+
+
+def ref_cuda_available() -> bool:
+    return os.path.exists(REF_CUDA_SO)
+
+
+def ref_cuda_lib() -> ctypes.CDLL:
+    """The reference's model loop over the CUDA backend of its op API
+    (oracle/_ref/libtorchless_ref_cuda.so; same entry points as ref_lib())."""
+    global _ref_cuda
+    if _ref_cuda is None:
+        _ref_cuda = _load_ref(REF_CUDA_SO)
+    return _ref_cuda
+
+
+def _load_ref(path: str) -> ctypes.CDLL:
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} not built (make -C oracle ref / ref-cuda needs the reference tree)")
+    L = ctypes.CDLL(path)
+    sig = {
+        "ref_load_file": (_P, [ctypes.c_char_p, _S]),
+        "ref_load_buffer": (_P, [_P, _S, _S]),
+        "ref_free": (None, [_P]),
+        "ref_forward": (_I, [_P, _U32]),
+        "ref_logits": (ctypes.POINTER(_F), [_P]),
+        "ref_hidden": (ctypes.POINTER(_F), [_P]),
+        "ref_sample_max": (_U32, [_P]),
+        "ref_sample_logits": (_U32, [_P, _P, _F, _U32, ctypes.POINTER(_F)]),
+        "ref_tokenizer_new": (_P, [ctypes.c_char_p, _S]),
+        "ref_tokenizer_free": (None, [_P]),
+        "ref_tokenizer_encode": (_S, [_P, ctypes.c_char_p, _S, _P, _S]),
+        "ref_tokenizer_decode": (_S, [_P, _P, _S, _P, _S]),
+        "ref_pos": (_S, [_P]),
+        "ref_set_pos": (None, [_P, _S]),
+        "ref_layer_forward": (_I, [_P, _I, _P]),
+        "ref_time_token": (_I, [_P, _U32, _I, _I, ctypes.POINTER(ctypes.c_double)]),
+        "ref_matmul_i8": (None, [_P, _P, _P, _S, _P, _S, _S]),
+        "ref_matmul_f32": (None, [_P, _P, _P, _S, _S]),
+        "ref_row_matmul": (None, [_P, _P, _P, _S, _S]),
+        "ref_softmax": (None, [_P, _P, _S]),
+        "ref_rope": (None, [_P, _P, _P, _P, _S, _S]),
+        "ref_silu": (None, [_P, _P, _S]),
+        "ref_rmsnorm": (None, [_P, _P, _P]),
+        "ref_rotary": (None, [_P, _S, _P, _P, _P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    return L
 
 
 # ---------------------------------------------------------------------------
@@ -242,21 +268,30 @@ class OracleModel:
 
 
 class RefModel:
-    """The reference's own Model<T> (oracle/_ref) over an in-memory binary."""
+    """The reference's own Model<T> (oracle/_ref) over an in-memory binary, or
+    over a file (path=...), which the reference's loader maps read-only
+    (Parameters::load_parameters, parameters.cpp:95-129).  lib: ref_lib()
+    (default) or ref_cuda_lib()."""
 
-    def __init__(self, buf: np.ndarray, max_seq: int = 500):
-        self.buf = np.ascontiguousarray(buf)
-        L = ref_lib()
-        self._h = L.ref_load_buffer(self.buf.ctypes.data, self.buf.nbytes, max_seq)
+    def __init__(self, buf: Optional[np.ndarray] = None, max_seq: int = 500, path: Optional[str] = None,
+                 lib: Optional[ctypes.CDLL] = None):
+        self._lib = L = lib or ref_lib()
+        from torchless_b200.binfmt import ModelFile
+        if path is not None:
+            self.buf = None
+            self._h = L.ref_load_file(path.encode(), max_seq)
+            c = ModelFile.open(path).config
+        else:
+            self.buf = np.ascontiguousarray(buf)
+            self._h = L.ref_load_buffer(self.buf.ctypes.data, self.buf.nbytes, max_seq)
+            c = ModelFile(self.buf).config
         if not self._h:
             raise ValueError("reference rejected the model binary")
-        from torchless_b200.binfmt import ModelFile
-        c = ModelFile(self.buf).config
         self.vocab, self.hidden = c.vocab_size, c.hidden_size
 
     def close(self):
         if self._h:
-            ref_lib().ref_free(self._h)
+            self._lib.ref_free(self._h)
             self._h = None
 
     def __del__(self):
@@ -267,19 +302,19 @@ class RefModel:
 
     @property
     def pos(self) -> int:
-        return ref_lib().ref_pos(self._h)
+        return self._lib.ref_pos(self._h)
 
     @pos.setter
     def pos(self, p: int):
-        ref_lib().ref_set_pos(self._h, p)
+        self._lib.ref_set_pos(self._h, p)
 
     def forward(self, token: int) -> np.ndarray:
-        if ref_lib().ref_forward(self._h, token):
+        if self._lib.ref_forward(self._h, token):
             raise ValueError("reference forward rejected")
-        return np.ctypeslib.as_array(ref_lib().ref_logits(self._h), (self.vocab,)).copy()
+        return np.ctypeslib.as_array(self._lib.ref_logits(self._h), (self.vocab,)).copy()
 
     def sample_max(self) -> int:
-        return ref_lib().ref_sample_max(self._h)
+        return self._lib.ref_sample_max(self._h)
 
     def sample_logits(self, logits: np.ndarray, temp: float, seed: int):
         """The reference's sample_multinomial (main.cpp:23-43) on `logits` with its
@@ -287,18 +322,18 @@ class RefModel:
         x = np.ascontiguousarray(logits, dtype=np.float32)
         assert x.size == self.vocab
         r = _F()
-        idx = ref_lib().ref_sample_logits(self._h, x.ctypes.data, float(temp), int(seed), ctypes.byref(r))
+        idx = self._lib.ref_sample_logits(self._h, x.ctypes.data, float(temp), int(seed), ctypes.byref(r))
         return int(idx), float(r.value)
 
     def layer_forward(self, layer: int, h: np.ndarray) -> np.ndarray:
         x = np.array(h, dtype=np.float32, copy=True)
-        if ref_lib().ref_layer_forward(self._h, layer, x.ctypes.data):
+        if self._lib.ref_layer_forward(self._h, layer, x.ctypes.data):
             raise ValueError("reference layer forward rejected")
         return x
 
     def time_token(self, token: int, first_layer: int, n_layers: int):
         out = (ctypes.c_double * 3)()
-        if ref_lib().ref_time_token(self._h, token, first_layer, n_layers, out):
+        if self._lib.ref_time_token(self._h, token, first_layer, n_layers, out):
             raise ValueError("reference timing rejected")
         return tuple(out)
 

@@ -91,6 +91,7 @@ def test_noalloc_takes_no_device_memory():
     per pool, so other processes on the GPU do not move it."""
     torch = pytest.importorskip("torch")
     rt = pytest.importorskip("cuda.bindings.runtime")
+    drv = pytest.importorskip("cuda.bindings.driver")
     torch.cuda.set_device(0)
     L = lib()
     stream = torch.cuda.current_stream().cuda_stream
@@ -102,7 +103,7 @@ def test_noalloc_takes_no_device_memory():
 
     def reset_high():
         torch.cuda.synchronize()
-        (e,) = rt.cudaMemPoolSetAttribute(pool, high, rt.cuuint64_t(0))
+        (e,) = rt.cudaMemPoolSetAttribute(pool, high, drv.cuuint64_t(0))
         assert e == rt.cudaError_t.cudaSuccess
 
     def used_high():
