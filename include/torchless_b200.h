@@ -295,9 +295,9 @@ TL_API tl_status tl_model_profile(tl_model* m, uint32_t token, size_t n, tl_kern
 /* Phase trace of one persistent-kernel decode step (tracing aid; the step is a
  * normal forward of `token` at the current position, launched without the
  * graph).  out[0] = CTAs, out[1] = phases (5 per layer + lm_head), then
- * %globaltimer ns stamps [cta][phase][8] = {phase begin, activation loads
- * landed, activation staged, tiles done, epilogue done, grid barrier passed,
- * producer's last issue, unused};
+ * %globaltimer ns stamps [cta][phase][8] = {phase begin, grid barrier passed,
+ * activation staged, tiles done, epilogue done, staging loads landed,
+ * producer's last issue, first tile of warp 0 done};
  * stamps a CTA does not reach stay 0.  cap is the capacity of out in
  * elements; *n_written receives the element count.  TL_ERR_UNSUPPORTED when
  * the model runs per-op kernels. */

@@ -59,6 +59,10 @@ constexpr int kStageBytes = kTilesPerStage * kTileBytesI8;
 // fp32 lm_head tiles, 8192 bytes, fit either).
 __host__ __device__ constexpr int stage_bytes(bool f8) { return kTilesPerStage * (f8 ? kTileBytesF8 : kTileBytesI8); }
 constexpr int kConsumers = kConsumerWarps * 32;
+// Warps that own each ring slot (its tile positions); the ring has a multiple
+// of kConsumerWarps / kWarpsPerSlot slots so that a slot keeps its owners.
+constexpr int kWarpsPerSlot = kTilesPerStage;
+constexpr int kSlotsPerOwnerCycle = kConsumerWarps / kWarpsPerSlot;
 constexpr int kThreads = kConsumers + 32;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 // Staged digits of one 64-column group: d0 (x 2^16), d1 (x 2^8), d2 rows of 64 bytes.
@@ -383,8 +387,7 @@ struct Consumer {
     const Shared& sh;
     int stages;
     int t, lane, warp;
-    int slot = 0;            // ring slot of the next tile pair
-    uint32_t phase_bit = 0;  // parity of its current round
+    uint32_t ring_it = 0;    // ring slots consumed so far by the CTA (same in every warp)
     int phase = 0;           // current phase: 5 per layer (qkv, attention, o, gate/up, down), then lm_head
     int arrivals = 0;        // grid barriers this CTA has arrived at (4 per layer)
     int* a_dbg;
@@ -402,6 +405,17 @@ struct Consumer {
     }
 
     __device__ bool aborted() const { return *reinterpret_cast<volatile int*>(&sh.flags[0]) != 0; }
+
+    // mbar_wait that also gives up once the CTA has aborted (a warp whose
+    // slot will never be filled does not sit out the whole timeout).
+    __device__ bool mbar_wait_ab(uint64_t* b, uint32_t parity) const {
+        if (mbar_test(b, parity)) return true;
+        const unsigned long long t0 = globaltimer();
+        for (unsigned i = 1;; i++) {
+            if (mbar_test(b, parity)) return true;
+            if ((i & 255) == 0 && (aborted() || globaltimer() - t0 > kTimeoutNs)) return false;
+        }
+    }
 
     __device__ void fail(int code) {
         atomicCAS(a.err, 0, code);
@@ -624,6 +638,7 @@ struct Consumer {
             }
         }
         const float2 st = local ? *local : read_stats();
+        stamp(5);  // the statistics (loaded with the vector's first blocks) have landed
         const float inv = NORM ? 1.0f / sqrtf(st.x / static_cast<float>(d) + 1e-5f) : 1.0f;
         const float amax = NORM ? st.y * inv * 1.0001f : st.y;  // bound on max|x|
         const int k = stage_exp(amax);
@@ -780,12 +795,17 @@ struct Consumer {
         if ((lane & 7) == 0) out[lane >> 3] = acc[0];
     }
 
-    // All tiles of one phase: warp w computes the CTA's tiles w, w + 8, ...,
-    // but every warp waits on and releases EVERY ring slot in order (the
-    // empty barriers expect one arrival per consumer warp).  A warp therefore
-    // never waits on a slot more than one round ahead of what it has seen
-    // complete, which keeps the parity waits unambiguous even though bulk
-    // copies may land out of order.
+    // All tiles of one phase.  Ring slots are owned by warps: slot counter j
+    // (counted over the whole step, like the producer's) holds tile positions
+    // 2 j and 2 j + 1, and position q belongs to warp q % 8, so warp w takes
+    // position w & 1 of every slot j with j % 4 == w / 2.  The ring has a
+    // multiple of 4 slots, so a slot is always used by the same two warps:
+    // only they wait on its full barrier and release it (the empty barrier
+    // expects two arrivals), and a warp waits on a slot only after releasing
+    // that slot's previous round itself, which keeps the parity waits
+    // unambiguous.  Tile i of the phase sits at position 2 j0 + i, j0 the
+    // phase's first slot (a phase with an odd tile count leaves the second
+    // position of its last slot empty).
     // Returns the CTA's first row block, or -1 on error (uniform over warps).
     template <bool F32>
     __device__ int run_tiles(int n_rb, int ksn, int& n_rb_local) {
@@ -793,38 +813,33 @@ struct Consumer {
         split(n_rb, rb0, rb1);
         n_rb_local = rb1 - rb0;
         const int n_tiles = n_rb_local * ksn;
-        const int n_slots = (n_tiles + kTilesPerStage - 1) / kTilesPerStage;
+        const uint32_t n_slots = static_cast<uint32_t>((n_tiles + kTilesPerStage - 1) / kTilesPerStage);
         constexpr int ROWS = F32 ? kTileRowsF32 : kTileRowsI8;
         constexpr int TB = F32 ? kTileBytesF32 : (F8 ? kTileBytesF8 : kTileBytesI8);
-        int my_i = warp;         // next tile of this warp
-        int my_ks = warp % ksn;  // its k-slice, kept incrementally
-        for (int j = 0; j < n_slots; j++) {
-            const int s = slot;
-            const uint32_t par = phase_bit;
-            if (++slot == stages) {
-                slot = 0;
-                phase_bit ^= 1u;
-            }
-            if (!mbar_wait(&sh.full[s], par)) {
+        const uint32_t first = ring_it, end = ring_it + n_slots;
+        const int pos_k = warp & 1;  // this warp's position in its slots
+        static_assert(kWarpsPerSlot == 2 && kSlotsPerOwnerCycle == 4, "slot ownership below assumes 8 warps, 2 tiles");
+        for (uint32_t j = first + ((static_cast<uint32_t>(warp >> 1) - first) & 3u); j < end; j += 4) {
+            const int s = static_cast<int>(j % static_cast<uint32_t>(stages));
+            const uint32_t par = (j / static_cast<uint32_t>(stages)) & 1u;
+            if (!mbar_wait_ab(&sh.full[s], par)) {
                 fail(kErrFull);
                 break;
             }
-            if (my_i < n_tiles && my_i / kTilesPerStage == j) {
-                if (TLD_OK((my_i + 1) * ROWS <= a.pbuf_floats, 12, my_i, a.pbuf_floats)) {
-                    const uint8_t* st =
-                        sh.ring + static_cast<size_t>(s) * stage_bytes(F8) + (my_i % kTilesPerStage) * TB;
-                    float* out = sh.pbuf + static_cast<size_t>(my_i) * ROWS;
-                    if constexpr (F32) tile_f32(st, my_ks, out);
-                    else if constexpr (F8) tile_f8(st, my_ks, out);
-                    else tile_i8(st, my_ks, out);
-                }
-                my_i += kConsumerWarps;
-                my_ks += kConsumerWarps;
-                while (my_ks >= ksn) my_ks -= ksn;
+            const int ti = 2 * static_cast<int>(j - first) + pos_k;
+            if (ti < n_tiles && TLD_OK((ti + 1) * ROWS <= a.pbuf_floats, 12, ti, a.pbuf_floats)) {
+                const uint8_t* st = sh.ring + static_cast<size_t>(s) * stage_bytes(F8) + pos_k * TB;
+                float* out = sh.pbuf + static_cast<size_t>(ti) * ROWS;
+                const int ks = ti % ksn;
+                if constexpr (F32) tile_f32(st, ks, out);
+                else if constexpr (F8) tile_f8(st, ks, out);
+                else tile_i8(st, ks, out);
+                if (j < first + 4) stamp(7);  // warp 0's first tile of the phase is done
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh.empty[s]);
         }
+        ring_it = end;
         consumer_sync();
         stamp(3);
         return aborted() ? -1 : rb0;
@@ -1068,11 +1083,11 @@ struct Consumer {
         return a.HD == 128 && a.gqa_splits > 0 && attn_span(pos) >= a.gqa_from;
     }
     // Splits over the attended positions: one per a.gqa_rows (GQA, at most
-    // a.gqa_splits) or per 64 (per head, at most a.splits).
+    // a.gqa_splits) or per a.split_rows (per head, at most a.splits).
     __device__ int attn_splits(unsigned pos) const {
         const int span = attn_span(pos);
         if (gqa(pos)) return ::min(a.gqa_splits, (span + a.gqa_rows - 1) / a.gqa_rows);
-        return ::min(a.splits, (span + 63) / 64);
+        return ::min(a.splits, (span + a.split_rows - 1) / a.split_rows);
     }
 
     // Thread 0 polls until kv group g's q, k and v rows of this layer are
@@ -1578,7 +1593,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; s++) {
             mbar_init(&sh.full[s], 1);
-            mbar_init(&sh.empty[s], kConsumerWarps);
+            mbar_init(&sh.empty[s], kWarpsPerSlot);
         }
         sh.flags[0] = 0;
         sh.flags[1] = 0;
@@ -1918,7 +1933,8 @@ bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers
     if (static_cast<size_t>(max_smem) <= fixed) return false;
     int st = static_cast<int>((static_cast<size_t>(max_smem) - fixed) / (stage_bytes(w_f8) + 16));
     st = st > 24 ? 24 : st;
-    if (st < 4) return false;
+    st -= st % kSlotsPerOwnerCycle;  // slots keep their owner warps
+    if (st < kSlotsPerOwnerCycle) return false;
     *stages = st;
     *pbuf_floats = pb;
     *smem_bytes = static_cast<size_t>(st) * stage_bytes(w_f8) + fixed + static_cast<size_t>(st) * 16;

@@ -84,6 +84,7 @@ struct DecodeArgs {
     unsigned* pos;              // in: position; out: position + 1
     uint32_t* history;          // history[pos] = argmax
     int D, F, H, KV, HD, V, max_seq, splits;
+    int split_rows;             // per-head attention: cached positions per split (at least)
     // GQA attention (hd 128, H = 4 KV): from position gqa_from - 1 on, one CTA
     // per (kv group, split) serves the group's 4 query heads, at most
     // gqa_splits splits; gqa_splits 0 = per-head attention only.
@@ -119,9 +120,9 @@ struct DecodeArgs {
     int* dbg;
 };
 
-// Trace events per phase: 0 begin, 1 activation loads landed, 2 activation
-// staged, 3 tiles done, 4 epilogue done, 5 barrier passed, 6 producer's last
-// issue of the phase, 7 unused.
+// Trace events per phase: 0 begin, 1 grid barrier (or exchange) passed,
+// 2 activation staged, 3 tiles done, 4 epilogue done, 5 staging loads
+// landed, 6 producer's last issue of the phase, 7 warp 0's first tile done.
 constexpr int kTraceEvents = 8;
 
 // Shared-memory bytes, pipeline depth and partial-buffer size for a model

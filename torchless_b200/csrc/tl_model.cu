@@ -55,6 +55,7 @@ namespace {
 // attention (one CTA per kv group and split) instead of per-head attention.
 constexpr int kGqaFromDefault = 1024;
 constexpr int kGqaRowsDefault = 64;           // GQA attention: cached positions per split (at least)
+constexpr int kSplitRowsDefault = 64;         // per-head attention: cached positions per split (at least)
 constexpr int kKvPrefetchRowsDefault = 256;   // K (and V) rows per attention CTA hinted into L2
 
 struct TensorRec {
@@ -590,7 +591,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
             // Tuning knob: a shallower weight ring (fewer bytes in flight per SM).
             if (const char* e = std::getenv("TL_DECODE_STAGES")) {
                 const int want = std::atoi(e);
-                if (want >= 4 && want < m->stages) {
+                if (want >= 4 && want % 4 == 0 && want < m->stages) {  // slots keep their owner warps (x4)
                     m->mega_smem -= static_cast<size_t>(m->stages - want) * (2 * (f8 ? kTileBytesF8 : kTileBytesI8) + 16);
                     m->stages = want;
                 }
@@ -718,6 +719,9 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
             d.xpeer[rank] = m->xbuf;
         }
         d.max_seq = static_cast<int>(m->max_seq); d.splits = m->mega_splits; d.window = m->window;
+        // Tuning knob: positions per per-head attention split (more splits = more CTAs at short context).
+        d.split_rows = kSplitRowsDefault;
+        if (const char* e = std::getenv("TL_DECODE_SPLIT_ROWS")) d.split_rows = std::max(8, std::min(4096, std::atoi(e)));
         d.attn_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
     }
 
