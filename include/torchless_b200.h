@@ -170,6 +170,21 @@ TL_API tl_status tl_mlp_gate_up(float* out, const int8_t* w1, const float* s1, c
 TL_API tl_status tl_gemm_f16(void* c, const void* a, const void* b, size_t m, size_t n, size_t k, size_t ldc,
                              int epilogue, void* stream);
 
+/* tl_gemm_f16 with 8-bit weights, dequantised inside the GEMM (the batched
+ * paths' form; no counterpart in the reference, see tl_gemm_f16): b is int8
+ * [n, k] (row-major, k contiguous) with inv_scales_t = 1 / s of each 64-column
+ * group transposed to [k / 64][n] fp32, and each weight enters the tensor
+ * cores as fp16(q) * fp16(1 / s) rounded to fp16 (tensor.cpp:101-104's
+ * dequantisation in fp16 arithmetic); with inv_scales_t NULL, b
+ * holds e5m2 bytes, widened exactly.  epilogue 0 / 1 as tl_gemm_f16; 2
+ * (SwiGLU): b / inv_scales_t are the gate rows [n / 2, k] and b2 /
+ * inv_scales_t2 the up rows, c is fp16 [m, ldc] with column 128 block + j =
+ * silu(gate_j) * up_j over blocks of 128 rows.  k % 64 == 0, n % 4 == 0
+ * (SwiGLU: n % 256 == 0); device pointers 16-byte aligned. */
+TL_API tl_status tl_gemm_q8(void* c, const void* a, const void* b, const float* inv_scales_t, const void* b2,
+                            const float* inv_scales_t2, size_t m, size_t n, size_t k, size_t ldc, int epilogue,
+                            void* stream);
+
 /* quantize (export_mistral.py:53-68): per group of `group` elements
  * scales[g] = fl(fl(1/max|x|) * 127), q = round_half_even(x * scales[g]). */
 TL_API tl_status tl_quantize_i8(int8_t* q, float* scales, const float* x, size_t numel,

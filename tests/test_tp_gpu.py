@@ -297,3 +297,66 @@ def test_tp2_full_depth_7b():
         assert e < 1e-4, (step, e)
         if res[0]["ids"][step] != ref_ids[step]:
             assert margin(ref[step]) < TIE, step
+
+
+def _rank_timeout_main(rank, world, init_file, model_path, feed, out_dir):
+    """Child: step 0 on both ranks; at step 1 rank 1 stays away (no kernel of its
+    own in flight), so rank 0's exchange wait runs out; then both reload."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ["TL_WAIT_TIMEOUT_MS"] = "200"  # read at load: a short bound for the test
+    from torchless_b200 import Model, TLError, tp
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    m = Model.load(model_path, device=rank, max_seq=32, tp_size=world, tp_rank=rank)
+    tp.connect(m)
+    _, first = m.forward(int(feed[0]))
+    statuses = []
+    if rank == 0:
+        for _ in range(2):  # the run-out wait, then the model refuses further steps
+            try:
+                m.forward(int(feed[1]))
+                statuses.append(0)
+            except TLError as e:
+                statuses.append(e.status)
+    dist.barrier()  # rank 0's failed step has ended before anyone unmaps its buffers
+    m.close()
+    dist.barrier()
+    # recovery: reload on every rank and run the steps again
+    m = Model.load(model_path, device=rank, max_seq=32, tp_size=world, tp_rank=rank)
+    tp.connect(m)
+    toks = [m.forward(int(t))[1] for t in feed]
+    dist.barrier()
+    m.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), first=first, statuses=np.array(statuses, np.int64),
+             toks=np.array(toks))
+
+
+def test_tp2_peer_absent_times_out_and_reload_recovers(small_bin):
+    """A rank that does not join a step: the other rank's bounded exchange wait
+    ends the step with TL_ERR_TIMEOUT (no GPU fault, no hang), the model then
+    refuses further steps, and a reload on both ranks decodes as before."""
+    _need(2)
+    import torch.multiprocessing as mp
+    from torchless_b200 import STATUS
+    prompt, ids, _ = golden_greedy("small")
+    feed = [prompt[0], prompt[1], prompt[2]]
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "m.bin")
+        np.asarray(small_bin).tofile(path)
+        init_file = os.path.join(d, "init")
+        mp.start_processes(_rank_timeout_main, args=(2, init_file, path, feed, d), nprocs=2, join=True,
+                           start_method="spawn")
+        r0, r1 = (np.load(os.path.join(d, f"rank{r}.npz")) for r in range(2))
+    timeout = [k for k, v in STATUS.items() if v == "TL_ERR_TIMEOUT"][0]
+    assert r0["statuses"].tolist() == [timeout, timeout]
+    assert int(r0["first"]) == int(r1["first"])
+    assert r0["toks"].tolist() == r1["toks"].tolist()
+    assert int(r0["toks"][0]) == int(r0["first"])  # the reloaded model repeats the clean step 0

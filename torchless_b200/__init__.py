@@ -95,6 +95,7 @@ SIGNATURES = {
     "tl_mlp_gate_up": [_P, _P, _P, _P, _P, _P, _S, _S, _P],
     "tl_quantize_i8": [_P, _P, _P, _S, _S, _P],
     "tl_gemm_f16": [_P, _P, _P, _S, _S, _S, _S, _I, _P],
+    "tl_gemm_q8": [_P, _P, _P, _P, _P, _P, _S, _S, _S, _S, _I, _P],
     "tl_model_load": [ctypes.c_char_p, ctypes.POINTER(tl_model_options), ctypes.POINTER(_P)],
     "tl_model_load_buffer": [_P, _S, ctypes.POINTER(tl_model_options), ctypes.POINTER(_P)],
     "tl_model_destroy": [_P],

@@ -24,7 +24,7 @@ BUILD = os.path.join(HERE, "_build")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(HERE, "libtorchless_b200.so")
 
-SOURCES = ["tl_errors.cpp", "tl_ops.cu", "tl_gemv.cu", "tl_attention.cu", "tl_decode.cu", "tl_gemm.cu", "tl_prefill.cu", "tl_attn_tc.cu", "tl_batch.cu", "tl_sample.cu", "tl_tokenizer.cu", "tl_model.cu"]
+SOURCES = ["tl_errors.cpp", "tl_ops.cu", "tl_gemv.cu", "tl_attention.cu", "tl_decode.cu", "tl_gemm.cu", "tl_gemm_q8.cu", "tl_prefill.cu", "tl_attn_tc.cu", "tl_batch.cu", "tl_sample.cu", "tl_tokenizer.cu", "tl_model.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -64,6 +64,8 @@ constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kWarpsPerSlot = kTilesPerStage;
 constexpr int kSlotsPerOwnerCycle = kConsumerWarps / kWarpsPerSlot;
 constexpr int kThreads = kConsumers + 32;
+// Bound of the waits on this CTA's own weight copies; waits on other CTAs or
+// ranks use DecodeArgs::timeout_ns.
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 // Staged digits of one 64-column group: d0 (x 2^16), d1 (x 2^8), d2 rows of 64 bytes.
 constexpr int kGroupDigitBytes = 192;
@@ -492,7 +494,7 @@ struct Consumer {
                         *reinterpret_cast<volatile int*>(&sh.flags[0]) = 1;
                         break;
                     }
-                    if (globaltimer() - t0 > kTimeoutNs) {
+                    if (globaltimer() - t0 > a.timeout_ns) {
                         fail(kErrBarrier);
                         break;
                     }
@@ -865,7 +867,7 @@ struct Consumer {
         // the first epilogue row's residual and next-norm gain, loaded before
         // the tiles so the epilogue does not wait on them
         float res0 = 0.f, g0 = 0.f;
-        if ((KIND == 1 || KIND == 3) && !xchg) {
+        if (KIND == 1 || KIND == 3) {
             int b0, b1;
             split(n_rb, b0, b1);
             const int row = b0 * 16 + t;
@@ -890,6 +892,27 @@ struct Consumer {
                     mx = fmaxf(mx, fabsf(v));
                 }
             }
+        } else if (xchg) {
+            // tensor parallel: this rank's partial rows to every rank, then
+            // the CTA's rows summed over the ranks (every rank's CTA owns the
+            // same rows, so each rank ends with the same h)
+            const unsigned tag = xchg_tag();
+            for (int j = t; j < nrl * 16; j += kConsumers) {
+                const int row = (rb0 + j / 16) * 16 + j % 16;
+                if (row < n_rows) xchg_send(row, row_sum(j / 16, j % 16, ksn, 16) * unscale, tag);
+            }
+            for (int j = t; j < nrl * 16; j += kConsumers) {
+                const int row = (rb0 + j / 16) * 16 + j % 16;
+                if (row < n_rows) {
+                    const bool first = (j == t);
+                    float hv = first ? res0 : __ldcg(res + row);
+                    if (!xchg_gather(row, tag, hv)) break;
+                    a.h[row] = hv;
+                    ss += hv * hv;
+                    mx = fmaxf(mx, fabsf(hv * (first ? g0 : __ldg(g_next + row))));
+                }
+            }
+            xk++;
         } else {
             for (int j = t; j < nrl * 16; j += kConsumers) {
                 const int rbl = j / 16, rr = j % 16;
@@ -902,11 +925,6 @@ struct Consumer {
                         const int hh = row / a.HD;
                         const int grp = hh < a.H ? hh / 4 : (hh < a.H + a.KV ? hh - a.H : hh - a.H - a.KV);
                         atomicAdd(reinterpret_cast<unsigned*>(sh.scratch) + 32 + grp, 1u);
-                    } else if (xchg) {
-                        // row of this rank's partial to every rank's receive buffer
-                        const size_t off = kXchgRecv + ((static_cast<size_t>(xk & 1) * a.tp_size + a.tp_rank) *
-                                                            a.D + row) * 4;
-                        for (int q = 0; q < a.tp_size; q++) *reinterpret_cast<float*>(a.xpeer[q] + off) = v;
                     } else {
                         const bool first = (j == t);
                         const float hv = v + (first ? res0 : __ldcg(res + row));
@@ -931,145 +949,61 @@ struct Consumer {
             stamp(4);
             phase++;
             stamp(0);
-        } else if (xchg) {
-            xchg_arrive();
         } else {
             publish(ss, mx);
         }
-        return true;
-    }
-
-    // ---- tensor-parallel exchange (o_proj and down_proj partials) ----------
-    // Exchange xk of a step: every CTA of every rank stores its partial rows
-    // into buffer xk % 2 of every rank, then (one thread, after a CTA-wide
-    // bar.sync and a system-scope fence) adds 1 to every rank's arrival
-    // counter.  The counters are 64-bit and never reset, so exchange xk of
-    // step e is complete on a rank when its counter reaches
-    // (e * 2 L + xk + 1) * tp * G.  Every rank then sums the tp partials in
-    // rank order: the ranks hold bit-identical residuals.
-    int xk = 0;          // exchanges this CTA has arrived at in this step
-    unsigned epoch = 0;  // steps run before this one
-
-    __device__ void xchg_arrive() {
-        consumer_sync();
-        if (t == 0) {
-            fence_sys();
-            for (int q = 0; q < a.tp_size; q++) red_add_sys_u64(a.xpeer[q] + kXchgCnt, 1ull);
-        }
-        xk++;
-        stamp(4);
-        phase++;
-        stamp(0);
-    }
-
-    __device__ bool xchg_wait() {
-        if (t == 0) {
-            const unsigned long long target =
-                (static_cast<unsigned long long>(epoch) * 2 * a.n_layers + xk) * a.tp_size * gridDim.x;
-            const void* cnt = a.xpeer[a.tp_rank] + kXchgCnt;
-            const unsigned long long t0 = globaltimer();
-            for (unsigned i = 0;; i++) {
-                if (ld_acquire_sys_u64(cnt) >= target) break;
-                if ((i & 63) == 63) {
-                    if (ld_volatile(a.err)) {
-                        *reinterpret_cast<volatile int*>(&sh.flags[0]) = 1;
-                        break;
-                    }
-                    if (globaltimer() - t0 > kTimeoutNs) {
-                        fail(kErrBarrier);
-                        break;
-                    }
-                }
-            }
-        }
-        consumer_sync();
-        stamp(1);
         return !aborted();
     }
 
-    // After exchange xk - 1: h = hprev + sum over ranks (rank order) of the
-    // received partials; this CTA stores its share of h into hout; then
-    // RMSNorm(h) with gain g (modules.cpp:31-46) is staged as int8 digits
-    // (F32 false, returns 2^-k) or as fp32 (F32 true, lm_head; returns 1).
-    // The whole h is in registers (D <= 8192), so its statistics are local.
-    template <bool F32>
-    __device__ float stage_xchg(const float* hprev, float* hout, const float* g) {
-        const int D = a.D, nb = D / 16;
-        if (!TLD_OK(nb <= 2 * kConsumers && (F32 ? 4 : x_bytes()) * static_cast<size_t>(D) <= xbuf_bytes(a.D, a.F, a.HD, F8),
-                    33, D, 0))
-            return 1.0f;
-        const float* recv = reinterpret_cast<const float*>(a.xpeer[a.tp_rank] + kXchgRecv) +
-                            static_cast<size_t>((xk - 1) & 1) * a.tp_size * D;
-        int B0, B1;  // this CTA's blocks of 16 rows of h
-        split(nb, B0, B1);
-        float v[2][16];
-        float ss = 0.f, mx = 0.f;
-#pragma unroll
-        for (int r = 0; r < 2; r++) {
-            const int b = t + r * kConsumers;
-#pragma unroll
-            for (int j = 0; j < 16; j++) v[r][j] = 0.f;
-            if (b >= nb) continue;
-#pragma unroll
-            for (int qd = 0; qd < 4; qd++) {
-                float4 acc = __ldcg(reinterpret_cast<const float4*>(hprev) + 4 * b + qd);
-                for (int q = 0; q < a.tp_size; q++) {
-                    const float4 p = __ldcg(reinterpret_cast<const float4*>(recv + static_cast<size_t>(q) * D) + 4 * b + qd);
-                    acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+    // ---- tensor-parallel exchange (o_proj and down_proj partials) ----------
+    // Exchange xk of a step (2 per layer): every rank's CTA c computes the
+    // partial sums of the rows it owns (the same rows on every rank) over the
+    // rank's slice of the inner dimension, and stores each into slot
+    // [xk % 2][its rank][row] of every rank's receive buffer as one 8-byte
+    // word {value, tag}, tag = the exchange's number in the whole run + 1
+    // (single-copy atomic, so a reader sees either the old word or the new
+    // one: no fence, no counter).  CTA c then polls its rows' tp words in its
+    // own buffer until all carry the tag and sums them in rank order onto the
+    // residual, so every rank holds bit-identical rows, and publishes its
+    // statistics like the single-GPU epilogue; the local grid barrier follows.
+    // Two slot sets suffice: a rank writes exchange x + 2 only after it has
+    // gathered x + 1 from every rank, and every rank sends x + 1 only after
+    // all its CTAs gathered x (its grid barrier lies between).
+    int xk = 0;          // exchanges this CTA has completed in this step
+    unsigned epoch = 0;  // steps run before this one
+
+    __device__ __forceinline__ unsigned xchg_tag() const {
+        return static_cast<unsigned>((static_cast<unsigned long long>(epoch) * 2 * a.n_layers + xk + 1) & 0xffffffffull);
+    }
+    __device__ __forceinline__ size_t xchg_off(int src_rank, int row) const {
+        return kXchgRecv + ((static_cast<size_t>(xk & 1) * a.tp_size + src_rank) * a.D + row) * 8;
+    }
+    __device__ __forceinline__ void xchg_send(int row, float v, unsigned tag) const {
+        const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+        const size_t off = xchg_off(a.tp_rank, row);
+        for (int q = 0; q < a.tp_size; q++) st_relaxed_sys_u64(a.xpeer[q] + off, w);
+    }
+    // acc += the tp partials of `row` in rank order; false (and the CTA
+    // aborted) when a word has not arrived within the timeout.
+    __device__ bool xchg_gather(int row, unsigned tag, float& acc) {
+        const uint8_t* mine = a.xpeer[a.tp_rank];
+        const unsigned long long t0 = globaltimer();
+        for (int q = 0; q < a.tp_size; q++) {
+            const size_t off = xchg_off(q, row);
+            unsigned long long w = ld_relaxed_sys_u64(mine + off);
+            for (unsigned i = 1; static_cast<unsigned>(w >> 32) != tag; i++) {
+                if ((i & 63) == 0) {
+                    if (aborted()) return false;
+                    if (ld_volatile(a.err) || globaltimer() - t0 > a.timeout_ns) {
+                        fail(kErrBarrier);
+                        return false;
+                    }
                 }
-                v[r][4 * qd] = acc.x; v[r][4 * qd + 1] = acc.y; v[r][4 * qd + 2] = acc.z; v[r][4 * qd + 3] = acc.w;
+                w = ld_relaxed_sys_u64(mine + off);
             }
-            if (b >= B0 && b < B1) {
-#pragma unroll
-                for (int qd = 0; qd < 4; qd++)
-                    reinterpret_cast<float4*>(hout)[4 * b + qd] =
-                        make_float4(v[r][4 * qd], v[r][4 * qd + 1], v[r][4 * qd + 2], v[r][4 * qd + 3]);
-            }
-#pragma unroll
-            for (int qd = 0; qd < 4; qd++) {
-                const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + 4 * b + qd);
-                const float gv[4] = {gg.x, gg.y, gg.z, gg.w};
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const float x = v[r][4 * qd + j];
-                    ss += x * x;
-                    mx = fmaxf(mx, fabsf(x * gv[j]));
-                }
-            }
+            acc += __uint_as_float(static_cast<unsigned>(w));
         }
-        const float2 st = sum_max(ss, mx);
-        const float inv = 1.0f / sqrtf(st.x / static_cast<float>(D) + 1e-5f);
-        float sc = 1.0f;
-        int k = 0;
-        if (!F32) {
-            k = stage_exp(st.y * inv * 1.0001f);
-            sc = ldexpf(1.0f, k);
-        }
-#pragma unroll
-        for (int r = 0; r < 2; r++) {
-            const int b = t + r * kConsumers;
-            if (b >= nb) continue;
-            float x[16];
-#pragma unroll
-            for (int qd = 0; qd < 4; qd++) {
-                const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + 4 * b + qd);
-                x[4 * qd] = (v[r][4 * qd] * inv) * gg.x;
-                x[4 * qd + 1] = (v[r][4 * qd + 1] * inv) * gg.y;
-                x[4 * qd + 2] = (v[r][4 * qd + 2] * inv) * gg.z;
-                x[4 * qd + 3] = (v[r][4 * qd + 3] * inv) * gg.w;
-            }
-            if (F32) {
-#pragma unroll
-                for (int qd = 0; qd < 4; qd++)
-                    reinterpret_cast<float4*>(sh.xbuf)[4 * b + qd] =
-                        make_float4(x[4 * qd], x[4 * qd + 1], x[4 * qd + 2], x[4 * qd + 3]);
-            } else {
-                put_x(b, x, sc);
-            }
-        }
-        consumer_sync();
-        stamp(2);
-        return F32 ? 1.0f : ldexpf(1.0f, -k);
+        return true;
     }
 
     // The query at `pos` attends to positions [attn_lo(pos), pos]: all of them
@@ -1103,7 +1037,7 @@ struct Consumer {
                         *reinterpret_cast<volatile int*>(&sh.flags[0]) = 1;
                         break;
                     }
-                    if (globaltimer() - t0 > kTimeoutNs) {
+                    if (globaltimer() - t0 > a.timeout_ns) {
                         fail(kErrBarrier);
                         break;
                     }
@@ -1626,7 +1560,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
     const unsigned pos = sh.info[0];
     const uint32_t token = sh.info[1];
     const float* emb = a.embed + static_cast<size_t>(token) * D;  // Embedding::forward (modules.cpp:5-7)
-    constexpr bool tp = TP;
     cw.epoch = sh.info[2];
     const float2 st0 = cw.local_stats(emb, D, a.layers[0].g_in);
     for (int l = 0; l < a.n_layers; l++) {
@@ -1636,9 +1569,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         float un;
         if (l == 0) {
             un = cw.template stage_digits<true>(emb, D, L.g_in, &st0);
-        } else if (tp) {  // h = post-attention h + sum of the ranks' down_proj partials
-            if (!cw.xchg_wait()) return;
-            un = cw.template stage_xchg<false>(a.h, a.h2, L.g_in);
         } else {
             if (!cw.wait_all()) return;
             un = cw.template stage_digits<true>(a.h, D, L.g_in, nullptr);
@@ -1661,13 +1591,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         if (cw.t == 0) prefetch_l2(L.g_post, static_cast<uint32_t>(D) * 4u);  // staged after this phase
         if (!cw.template run_i8<1>(D, a.H * a.HD, un, hin, L.g_post)) return;
         // act = silu(W1 x) * (W3 x), x = rmsnorm(h)
-        if (tp) {  // h = residual + sum of the ranks' o_proj partials
-            if (!cw.xchg_wait()) return;
-            un = cw.template stage_xchg<false>(l == 0 ? emb : a.h2, a.h, L.g_post);
-        } else {
-            if (!cw.wait_all()) return;
-            un = cw.template stage_digits<true>(a.h, D, L.g_post, nullptr);
-        }
+        if (!cw.wait_all()) return;
+        un = cw.template stage_digits<true>(a.h, D, L.g_post, nullptr);
         if (!cw.template run_i8<2>(2 * F, D, un, nullptr, nullptr)) return;
         // h = h + W2 act
         if (!cw.wait_all()) return;
@@ -1681,15 +1606,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
     // projections' tiles of 16 rows.
     const bool lm8 = a.lm_8bit != 0;
     float lm_un = 1.0f;
-    if (tp) {
-        if (!cw.xchg_wait()) return;
-        if (lm8) lm_un = cw.template stage_xchg<false>(a.h, a.h2, a.g_final);
-        else cw.template stage_xchg<true>(a.h, a.h2, a.g_final);
-    } else {
-        if (!cw.wait_all()) return;
-        if (lm8) lm_un = cw.template stage_digits<true>(a.h, D, a.g_final, nullptr);
-        else cw.stage_f32(a.h, D, a.g_final);
-    }
+    if (!cw.wait_all()) return;
+    if (lm8) lm_un = cw.template stage_digits<true>(a.h, D, a.g_final, nullptr);
+    else cw.stage_f32(a.h, D, a.g_final);
     const int ksD = tile_slices(D);
     const int lm_rows = lm8 ? kTileRowsI8 : kTileRowsF32;
     const int n_rb = (a.V + lm_rows - 1) / lm_rows;
@@ -1783,7 +1702,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
             bool ok = true;
             for (unsigned i = 0;; i++) {
                 if (ld_acquire_sys_u64(a.xpeer[a.tp_rank] + kXchgAmCnt) >= target) break;
-                if ((i & 63) == 63 && globaltimer() - t0 > kTimeoutNs) {
+                if ((i & 63) == 63 && globaltimer() - t0 > a.timeout_ns) {
                     atomicCAS(a.err, 0, static_cast<int>(kErrBarrier));
                     ok = false;
                     break;

@@ -38,12 +38,11 @@ constexpr int kStatsCap = 1024;  // most CTAs / heads publishing statistics
 
 // Tensor-parallel exchange buffer (one per rank, mapped into every rank's
 // process over CUDA IPC), byte offsets:
-constexpr size_t kXchgCnt = 0;       // u64: o / down partial-row arrivals from all ranks' CTAs
 constexpr size_t kXchgAmCnt = 8;     // u64: argmax candidate arrivals from all ranks
 constexpr size_t kXchgAmSlot = 256;  // u64 [2][8]: {value bits | rank-local best index << 32}
-constexpr size_t kXchgRecv = 512;    // f32 [2][tp][D]: partial rows of o_proj / down_proj per sender
+constexpr size_t kXchgRecv = 512;    // u64 [2][tp][D]: {partial row value, exchange tag << 32} per sender
 constexpr int kMaxTp = 8;
-inline size_t xchg_bytes(int tp, int D) { return kXchgRecv + 2 * static_cast<size_t>(tp) * D * 4; }
+inline size_t xchg_bytes(int tp, int D) { return kXchgRecv + 2 * static_cast<size_t>(tp) * D * 8; }
 
 struct DecodeLayer {
     const uint8_t* qkv;  // tiles of [q; k; v]   ((H + 2 KV) hd rows, d = D)
@@ -110,8 +109,8 @@ struct DecodeArgs {
     // rank order; xpeer[q] is rank q's exchange buffer (own at q = tp_rank).
     int tp_size, tp_rank, vocab_off;
     uint8_t* xpeer[kMaxTp];
-    float* h2;                  // tp: post-MLP residual (h holds post-attention)
-    unsigned* epoch;            // steps run so far (tp exchange counters never reset)
+    unsigned* epoch;            // steps run so far (numbers the tp exchanges and argmax rounds)
+    unsigned long long timeout_ns;  // bound of every wait on other CTAs or ranks (then TL_ERR_TIMEOUT)
     // Optional phase trace (nullptr = off): per CTA, kTraceEvents %globaltimer
     // stamps for every phase, [cta][phase][event], phases = 5 per layer + lm_head.
     unsigned long long* trace;

@@ -31,4 +31,26 @@ tl_status gemm_f16(int epilogue, const __half* A, int M, int K, const __half* B,
 tl_status gemm_f16_splitk(const __half* A, int M, int K, const __half* B, int N, float* part, size_t part_floats,
                           int* ksplit, int* err, cudaStream_t s);
 
+// 8-bit weights for the dequantising GEMM (tl_gemm_q8.cu): B [N, K] int8
+// (row-major, K contiguous) with sT = 1/s transposed to [K / 64][N], or e5m2
+// bytes with sT null.  SwiGLU: q / sT are the gate rows and q2 / sT2 the up
+// rows of the same shape [N / 2, K]; B tile rows 0..127 are gate rows and
+// 128..255 the same up rows.
+struct Q8Weights {
+    const void* q = nullptr;
+    const float* sT = nullptr;
+    const void* q2 = nullptr;
+    const float* sT2 = nullptr;
+};
+
+// C = A B^T with B dequantised in shared memory (w = fp16(q) * fp16(1/s),
+// rounded to fp16; e5m2 widened exactly), same epilogues and split-K
+// contract as gemm_f16 / gemm_f16_splitk.  N % 4 == 0 (SwiGLU: N % 256 == 0).
+tl_status gemm_q8(int epilogue, const __half* A, int M, int K, const Q8Weights& B, int N, void* C, int ldc, int* err,
+                  cudaStream_t s);
+tl_status gemm_q8_splitk(const __half* A, int M, int K, const Q8Weights& B, int N, float* part, size_t part_floats,
+                         int* ksplit, int* err, cudaStream_t s);
+// dst[g][i] = src[i][g] for a [n][groups] scale array.
+tl_status transpose_scales(float* dst, const float* src, int n, int groups, cudaStream_t s);
+
 }  // namespace tl

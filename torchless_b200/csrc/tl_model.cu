@@ -306,7 +306,6 @@ struct tl_model {
     // tensor parallelism: rank `rank` of `tp`; local head / kv head / F / vocab counts
     int tp = 1, rank = 0;
     int64_t lH = 0, lKV = 0, lF = 0, lV = 0;
-    float* h2 = nullptr;          // second residual buffer (tp)
     unsigned* epoch = nullptr;    // steps run (tp exchange counters)
     uint8_t* xbuf = nullptr;      // this rank's exchange buffer (tp), cudaMalloc'd for IPC
     uint8_t* xpeer_open[kMaxTp] = {};  // peer buffers opened with cudaIpcOpenMemHandle
@@ -314,8 +313,10 @@ struct tl_model {
     bool broken = false;  // tp: a device-side wait gave up; the ranks' exchange state is lost
     // batched prompt pass (tl_model_prefill): fp16 weights dequantised on first
     // use (per layer q|k|v, o, gate|up in SwiGLU blocks, down) and row buffers
-    DeviceArena w16, rows;
-    std::vector<std::array<__half*, 4>> lw16;
+    DeviceArena scT, rows;
+    // per layer: q|k|v, o, gate|up, down as the dequantising GEMM reads them
+    // (the int8 / e5m2 weights in place, their 1/s transposed into scT)
+    std::vector<std::array<Q8Weights, 4>> lq8;
     size_t rows_cap = 0;
     float *p_h = nullptr, *p_qkv = nullptr;
     __half *p_x16 = nullptr, *p_q16 = nullptr, *p_ctx16 = nullptr, *p_act16 = nullptr;
@@ -685,7 +686,6 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     m->err = m->state.take<int>(1);
     m->dbg = m->state.take<int>(4);
     m->stats = m->state.take<float2>(2 * kStatsCap);
-    m->h2 = m->state.take<float>(D);
     m->epoch = m->state.take<unsigned>(1);
     if (!m->epoch) return set_error(TL_ERR_OUT_OF_MEMORY, "state arena too small (internal)");
     if (m->persistent) {
@@ -711,7 +711,12 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         d.D = static_cast<int>(D); d.F = static_cast<int>(Fl); d.H = static_cast<int>(Hl);
         d.KV = static_cast<int>(KVl); d.HD = static_cast<int>(HD); d.V = static_cast<int>(Vl);
         d.tp_size = tp; d.tp_rank = rank; d.vocab_off = static_cast<int>(rank * Vl);
-        d.h2 = m->h2; d.epoch = m->epoch;
+        d.epoch = m->epoch;
+        // Bound of the kernel's waits on other CTAs and ranks (a peer that never
+        // arrives ends the step with TL_ERR_TIMEOUT); TL_WAIT_TIMEOUT_MS shortens it.
+        d.timeout_ns = 2000000000ull;
+        if (const char* e = std::getenv("TL_WAIT_TIMEOUT_MS"))
+            d.timeout_ns = static_cast<unsigned long long>(std::max(10, std::min(60000, std::atoi(e)))) * 1000000ull;
         if (tp > 1) {  // this rank's exchange buffer; peers are mapped by tl_model_tp_connect
             const size_t xb = xchg_bytes(tp, static_cast<int>(D));
             TL_CUDA_TRY(cudaMalloc(&m->xbuf, xb));
@@ -958,25 +963,37 @@ tl_status check_capacity(const tl_model* m, size_t steps) {
 tl_status ensure_prefill(tl_model* m, size_t n) {
     const int64_t D = m->cfg.hidden_size, HD = m->cfg.head_dim, H = m->lH, KV = m->lKV, F = m->lF;
     const int64_t NQKV = (H + 2 * KV) * HD, L = m->cfg.n_layers;
-    if (m->lw16.empty()) {
+    if (m->lq8.empty()) {
         if (F % 128) return set_error(TL_ERR_UNSUPPORTED, "prefill: intermediate_size %lld not a multiple of 128",
                                       static_cast<long long>(F));
         using A = DeviceArena;
-        const size_t per = A::pad(NQKV * D * 2) + A::pad(D * H * HD * 2) + A::pad(2 * F * D * 2) + A::pad(D * F * 2);
-        TL_TRY(m->w16.reserve(per * L));
-        m->lw16.resize(L);
+        const bool f8 = m->w_f8;  // e5m2 weights carry no scales
+        if (!f8) {
+            const size_t per = A::pad(NQKV * (D / 64) * 4) + A::pad(D * (H * HD / 64) * 4) +
+                               2 * A::pad(F * (D / 64) * 4) + A::pad(D * (F / 64) * 4);
+            TL_TRY(m->scT.reserve(per * L));
+        }
+        m->lq8.resize(L);
         for (int64_t l = 0; l < L; l++) {
             const LayerW& w = m->layers[l];
-            auto& W = m->lw16[l];
-            W[0] = m->w16.take<__half>(NQKV * D);
-            W[1] = m->w16.take<__half>(D * H * HD);
-            W[2] = m->w16.take<__half>(2 * F * D);
-            W[3] = m->w16.take<__half>(D * F);
-            // the arena's scales are already 1/s; fp8 weights (null scales) convert exactly
-            TL_TRY(dequant_f16(W[0], w.wqkv, w.sqkv, nullptr, nullptr, NQKV, D, false, m->stream));
-            TL_TRY(dequant_f16(W[1], w.wo, w.so, nullptr, nullptr, D, H * HD, false, m->stream));
-            TL_TRY(dequant_f16(W[2], w.w1, w.s1, w.w3, w.s3, F, D, true, m->stream));
-            TL_TRY(dequant_f16(W[3], w.w2, w.s2, nullptr, nullptr, D, F, false, m->stream));
+            auto& Q = m->lq8[l];
+            Q[0].q = w.wqkv;
+            Q[1].q = w.wo;
+            Q[2].q = w.w1;
+            Q[2].q2 = w.w3;
+            Q[3].q = w.w2;
+            if (f8) continue;
+            // the arena's scales are already 1/s; [rows][groups] -> [groups][rows]
+            auto tr = [&](const float* src, int64_t rows, int64_t cols, const float** dst) -> tl_status {
+                float* t = m->scT.take<float>(rows * (cols / 64));
+                *dst = t;
+                return transpose_scales(t, src, static_cast<int>(rows), static_cast<int>(cols / 64), m->stream);
+            };
+            TL_TRY(tr(w.sqkv, NQKV, D, &Q[0].sT));
+            TL_TRY(tr(w.so, D, H * HD, &Q[1].sT));
+            TL_TRY(tr(w.s1, F, D, &Q[2].sT));
+            TL_TRY(tr(w.s3, F, D, &Q[2].sT2));
+            TL_TRY(tr(w.s2, D, F, &Q[3].sT));
         }
     }
     if (n > m->rows_cap) {
@@ -1085,7 +1102,7 @@ tl_status tl_model_destroy(tl_model* m) {
     m->weights.release();
     m->state.release();
     m->tiles.release();
-    m->w16.release();
+    m->scT.release();
     m->rows.release();
     m->lm16_arena.release();
     if (m->d_layers) cudaFree(m->d_layers);
@@ -1214,11 +1231,11 @@ tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* log
     TL_TRY(embed_rows(m->p_h, m->embed, m->p_tok, M, D, s));
     for (size_t l = 0; l < m->cfg.n_layers; l++) {
         const LayerW& w = m->layers[l];
-        const auto& W = m->lw16[l];
+        const auto& W = m->lq8[l];
         float* kc = m->kc + l * layer_kv_floats(m);
         float* vc = m->vc + l * layer_kv_floats(m);
         TL_TRY(rmsnorm_rows_f16(m->p_x16, m->p_h, w.g_in, M, D, s));
-        TL_TRY(gemm_f16(kEpiStoreF32, m->p_x16, M, D, W[0], NQKV, m->p_qkv, NQKV, m->err, s));
+        TL_TRY(gemm_q8(kEpiStoreF32, m->p_x16, M, D, W[0], NQKV, m->p_qkv, NQKV, m->err, s));
         TL_TRY(rope_cache_rows(m->p_q16, m->p_qkv, kc, vc, m->cos_tab, m->sin_tab, M, p0, H, KV, HD, ms, s));
         if (HD == 128 && H == 4 * KV)  // tensor-core attention (tcgen05, tensor memory)
             TL_TRY(attention_prefill_tc(m->p_ctx16, m->p_q16, m->p_k16, m->p_v16, kc, vc, M, p0, H, KV, HD, ms,
@@ -1226,10 +1243,10 @@ tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* log
         else
             TL_TRY(attention_prefill(m->p_ctx16, m->p_q16, m->p_k16, m->p_v16, kc, vc, M, p0, H, KV, HD, ms, scale,
                                      m->window, s));
-        TL_TRY(gemm_f16(kEpiAddF32, m->p_ctx16, M, H * HD, W[1], D, m->p_h, D, m->err, s));
+        TL_TRY(gemm_q8(kEpiAddF32, m->p_ctx16, M, H * HD, W[1], D, m->p_h, D, m->err, s));
         TL_TRY(rmsnorm_rows_f16(m->p_x16, m->p_h, w.g_post, M, D, s));
-        TL_TRY(gemm_f16(kEpiSwiGluF16, m->p_x16, M, D, W[2], 2 * F, m->p_act16, F, m->err, s));
-        TL_TRY(gemm_f16(kEpiAddF32, m->p_act16, M, F, W[3], D, m->p_h, D, m->err, s));
+        TL_TRY(gemm_q8(kEpiSwiGluF16, m->p_x16, M, D, W[2], 2 * F, m->p_act16, F, m->err, s));
+        TL_TRY(gemm_q8(kEpiAddF32, m->p_act16, M, F, W[3], D, m->p_h, D, m->err, s));
     }
     // the last token's hidden state: final norm, lm_head, sample_max (modules.cpp:147-171, main.cpp:10-21)
     TL_CUDA_TRY(cudaMemcpyAsync(m->h, m->p_h + static_cast<size_t>(M - 1) * D, D * 4, cudaMemcpyDeviceToDevice, s));
@@ -1496,8 +1513,8 @@ tl_status batch_step(tl_batch* b) {
     TL_TRY(residual_rmsnorm_rows(b->x16, b->hres, nullptr, 0, 0, m->layers[0].g_in, B, D, s));
     for (size_t l = 0; l < m->cfg.n_layers; l++) {
         const LayerW& w = m->layers[l];
-        const auto& W = m->lw16[l];
-        TL_TRY(gemm_f16_splitk(b->x16, B, D, W[0], NQKV, b->split, b->split_floats, &ks, m->err, s));
+        const auto& W = m->lq8[l];
+        TL_TRY(gemm_q8_splitk(b->x16, B, D, W[0], NQKV, b->split, b->split_floats, &ks, m->err, s));
         TL_TRY(rope_cache_batch(b->qf, b->split, ks, qkv_stride, b->bkv, static_cast<int>(l), b->pos, m->cos_tab,
                                 m->sin_tab, B, H, KV, HD, s));
         TL_TRY(attention_decode_batch(b->part, b->qf, b->bkv, static_cast<int>(l), b->pos, B, H, KV, HD, S, scale,
@@ -1510,10 +1527,10 @@ tl_status batch_step(tl_batch* b) {
                                                 s);
             return residual_rmsnorm_rows(b->x16, b->hres, b->split, ks, d_stride, g, B, D, s);
         };
-        TL_TRY(gemm_f16_splitk(b->ctx16, B, H * HD, W[1], D, b->split, b->split_floats, &ks, m->err, s));
+        TL_TRY(gemm_q8_splitk(b->ctx16, B, H * HD, W[1], D, b->split, b->split_floats, &ks, m->err, s));
         TL_TRY(residual(w.g_post));
-        TL_TRY(gemm_f16(kEpiSwiGluF16, b->x16, B, D, W[2], 2 * F, b->act16, F, m->err, s));
-        TL_TRY(gemm_f16_splitk(b->act16, B, F, W[3], D, b->split, b->split_floats, &ks, m->err, s));
+        TL_TRY(gemm_q8(kEpiSwiGluF16, b->x16, B, D, W[2], 2 * F, b->act16, F, m->err, s));
+        TL_TRY(gemm_q8_splitk(b->act16, B, F, W[3], D, b->split, b->split_floats, &ks, m->err, s));
         TL_TRY(residual(l + 1 < m->cfg.n_layers ? m->layers[l + 1].g_in : m->norm));
     }
     TL_TRY(gemm_f16(kEpiStoreF32, b->x16, B, D, m->lm16, V, b->logits, V, m->err, s));
