@@ -50,6 +50,10 @@ tl_status gemm_q8(int epilogue, const __half* A, int M, int K, const Q8Weights& 
                   cudaStream_t s);
 tl_status gemm_q8_splitk(const __half* A, int M, int K, const Q8Weights& B, int N, float* part, size_t part_floats,
                          int* ksplit, int* err, cudaStream_t s);
+// With B.q2 set (gate / up pairs), gemm_q8_splitk stores the pair tiles' split
+// partials (columns 256 b .. 256 b + 127 gate, then 128 up) and swiglu_rows
+// combines them: out[m][j] = silu(gate) * up as fp16 (modules.cpp:99-112).
+tl_status swiglu_rows(__half* out, const float* part, int ks, size_t stride, int M, int F, cudaStream_t s);
 // dst[g][i] = src[i][g] for a [n][groups] scale array.
 tl_status transpose_scales(float* dst, const float* src, int n, int groups, cudaStream_t s);
 

@@ -21,15 +21,20 @@ struct GemmArgs {
 };
 
 // The epilogue of one 128 x BN accumulator (tensor-memory columns tcol ..)
-// for tile rows m0 .., columns n0 ..; called by the 4 epilogue warps.
+// for tile rows m0 .., columns n0 ..; warp `sub` (tensor-memory lanes
+// 32 sub ..) of the epilogue warps.  Column part `part` of `parts`: the warp
+// takes accumulator columns [part, part + 1) x BN / parts (SwiGLU: output
+// columns [part, part + 1) x BN / (2 parts)), so 8 warps can share a tile.
 template <int BN, int EPI>
-__device__ __forceinline__ void gemm_epilogue(const GemmArgs& g, uint32_t tcol, int m0, int n0, int sub, int lane) {
+__device__ __forceinline__ void gemm_epilogue(const GemmArgs& g, uint32_t tcol, int m0, int n0, int sub, int lane,
+                                              int part = 0, int parts = 1) {
     const int row = m0 + sub * 32 + lane;
     const uint32_t tl = tcol + (static_cast<uint32_t>(sub * 32) << 16);
     if (EPI == kEpiSwiGluF16) {
         __half* out = static_cast<__half*>(g.C);
+        const int span = BN / 2 / parts;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN / 2; c0 += 32) {
+        for (int c0 = part * span; c0 < (part + 1) * span; c0 += 32) {
             float gv[32], uv[32];
             tc::tmem_ld32(tl + c0, gv);
             tc::tmem_ld32(tl + BN / 2 + c0, uv);
@@ -49,8 +54,9 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& g, uint32_t tcol, 
         }
     } else {
         float* out = static_cast<float*>(g.C);
+        const int span = BN / parts;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = part * span; c0 < (part + 1) * span; c0 += 32) {
             float v[32];
             tc::tmem_ld32(tl + c0, v);
             if (row < g.M) {

@@ -1529,7 +1529,8 @@ tl_status batch_step(tl_batch* b) {
         };
         TL_TRY(gemm_q8_splitk(b->ctx16, B, H * HD, W[1], D, b->split, b->split_floats, &ks, m->err, s));
         TL_TRY(residual(w.g_post));
-        TL_TRY(gemm_q8(kEpiSwiGluF16, b->x16, B, D, W[2], 2 * F, b->act16, F, m->err, s));
+        TL_TRY(gemm_q8_splitk(b->x16, B, D, W[2], 2 * F, b->split, b->split_floats, &ks, m->err, s));
+        TL_TRY(swiglu_rows(b->act16, b->split, ks, static_cast<size_t>(B) * 2 * F, B, static_cast<int>(F), s));
         TL_TRY(gemm_q8_splitk(b->act16, B, F, W[3], D, b->split, b->split_floats, &ks, m->err, s));
         TL_TRY(residual(l + 1 < m->cfg.n_layers ? m->layers[l + 1].g_in : m->norm));
     }
@@ -1599,7 +1600,9 @@ tl_status tl_batch_create(tl_model* m, int n_seq, size_t max_seq, tl_batch** out
     b->bkv.layer_stride = layer;
     b->bkv.max_seq = static_cast<int>(max_seq);
     const size_t Bn = n_seq;
-    b->split_floats = 8 * Bn * static_cast<size_t>(std::max<int64_t>(NQKV, D));
+    // split-K partials: up to 16 K ranges of q|k|v / o / down, or 8 of the gate|up pairs
+    b->split_floats = Bn * std::max<size_t>(16 * static_cast<size_t>(std::max<int64_t>(NQKV, D)),
+                                            8 * 2 * static_cast<size_t>(F));
     TL_TRY(b->rows.reserve(A::pad(Bn * D * 4) + A::pad(Bn * H * HD * 4) +
                            A::pad(Bn * H * b->S * (HD + 4) * 4) + A::pad(Bn * V * 4) + A::pad(Bn * D * 2) +
                            A::pad(Bn * H * HD * 2) + A::pad(Bn * F * 2) + 3 * A::pad(Bn * 4) +
