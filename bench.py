@@ -524,7 +524,7 @@ def run_prefill(args):
     torch.cuda.set_device(0)
     T, N_DEC = args.prefill_tokens, 32
     buf = make_model_bytes(args.layers)
-    m = Model.from_buffer(buf, max_seq=T + N_DEC + 8)
+    m = Model.from_buffer(buf, max_seq=T + N_DEC + 8, weights_f16=args.weights_f16)
     rng = np.random.default_rng(SEED)
     prompt = rng.integers(0, 32000, T).tolist()
     times = []
@@ -548,7 +548,9 @@ def run_prefill(args):
     peak = json.load(open(pk))["bf16_tflops"] if os.path.exists(pk) else 1590.0
     out = {"metric": f"{WEIGHTS} Mistral-7B prefill tok/s (2048-token prompt)", "value": T / (ms_prefill * 1e-3),
            "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_prefill,
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 operands, f32 accumulate",
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+           "dtype": ("resident f16 weight copies" if args.weights_f16 else
+                     "int8 weights dequantised to f16 in shared memory") + ", f16 x f16 -> f32 tcgen05 MMA",
            "data": "synthetic",
            "config": {"workload": f"Mistral-7B int8 ({L} layers), prefill of {T} random token ids, "
                                   f"then {N_DEC} greedy decode steps", "prompt": T, "decode": N_DEC},
@@ -574,7 +576,7 @@ def run_batch(args, rank=0, world=1, local=0):
     max_seq = P + args.warmup + K + 8
     if world == 1:
         buf = make_model_bytes(args.layers)
-        m = Model.from_buffer(buf, max_seq=max_seq)
+        m = Model.from_buffer(buf, max_seq=max_seq, weights_f16=args.weights_f16)
         del buf
     else:
         # N > 1: the same B sequences on every rank, each rank holding its
@@ -586,7 +588,8 @@ def run_batch(args, rank=0, world=1, local=0):
         if rank == 0:
             make_model_bytes(args.layers).tofile(path)
         dist.barrier()
-        m = Model.load(path, device=local, max_seq=max_seq, tp_size=world, tp_rank=rank)
+        m = Model.load(path, device=local, max_seq=max_seq, tp_size=world, tp_rank=rank,
+                       weights_f16=args.weights_f16)
         dist.barrier()
         if rank == 0:
             os.remove(path)
@@ -624,15 +627,18 @@ def run_batch(args, rank=0, world=1, local=0):
     pos_mean = P + args.warmup + (K - 1) / 2.0
     kv_bytes = B * L * 2 * KV * HD * 4 * (pos_mean + 1)  # cache rows read per step (all sequences)
     w_int8 = L * ((H + 2 * KV) * HD * D + D * H * HD + 3 * F * D) * (1 + 4.0 / 64) + V * D * 4
-    # this path reads the int8 weights and their scales in place, and a resident fp16 copy of the fp32 lm_head
-    w_here = L * ((H + 2 * KV) * HD * D + D * H * HD + 3 * F * D) * (1 + 4.0 / 64) + V * D * 2
+    # the int8 weights and their scales in place (or, with --weights-f16, fp16 copies), and a
+    # resident fp16 copy of the fp32 lm_head
+    params = L * ((H + 2 * KV) * HD * D + D * H * HD + 3 * F * D)
+    w_here = params * (2.0 if args.weights_f16 else 1 + 4.0 / 64) + V * D * 2
     step_s = ms * 1e-3 / K
     peak, peak_kind = peaks()
     algo = kv_bytes + w_int8
     out = {"metric": f"{WEIGHTS} Mistral-7B batched decode tok/s (64 seqs x 4096-token KV)", "value": B * K / (ms * 1e-3),
            "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": ms / K,
            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
-           "dtype": "int8 weights dequantised to f16 in shared memory, f16 x f16 -> f32 tcgen05 MMA, f32 KV",
+           "dtype": ("resident f16 weight copies" if args.weights_f16 else
+                     "int8 weights dequantised to f16 in shared memory") + ", f16 x f16 -> f32 tcgen05 MMA, f32 KV",
            "data": "synthetic",
            "config": {"workload": f"Mistral-7B int8 ({L} layers), {B} sequences, KV pre-filled with {P} positions "
                                   f"of N(0,1) (counter-based generator), {K} greedy steps", "global_batch": B,
@@ -644,8 +650,9 @@ def run_batch(args, rank=0, world=1, local=0):
                         "unit": "GB/s", "frac": algo / step_s / 1e9 / (world * peak), "algorithmic_bytes": algo,
                         "bytes_read_by_this_path": kv_bytes + w_here,
                         "note": "algorithmic = int8 weights + scales + fp32 lm_head + fp32 KV; this path reads "
-                                "the int8 weights + scales (dequantised to fp16 in shared memory inside the "
-                                "tensor-core GEMM) and an fp16 copy of the lm_head"},
+                                + ("fp16 copies of the weights" if args.weights_f16 else
+                                   "the int8 weights + scales (dequantised to fp16 in shared memory inside the "
+                                   "tensor-core GEMM)") + " and an fp16 copy of the lm_head"},
            "clocks": clocks.summary(), "ids_head": ids[0][:8].tolist()}
     print(json.dumps(out))
 
@@ -673,6 +680,8 @@ def main():
                     help="the same workloads on the fp8 (e5m2) export of the model (format extension)")
     ap.add_argument("--context", type=int, default=0,
                     help="bs1 decode after a random prompt of this many tokens (0: the 16-token prompt)")
+    ap.add_argument("--weights-f16", action="store_true",
+                    help="--prefill / --batch with resident fp16 weight copies instead of int8 in place")
     ap.add_argument("--layers", type=int, default=32,
                     help="transformer layers (32 = Mistral-7B; fewer only for small profiling captures)")
     args = ap.parse_args()

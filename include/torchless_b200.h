@@ -217,6 +217,11 @@ typedef struct tl_model_options {
                         /*    field, parameters.cpp:41, unused by the reference).   */
                         /*    Opt-in: results then differ from the reference's past */
                         /*    W positions.                                          */
+    int weights_f16;    /* batched paths (prefill, batched decode): 0 (default) read  */
+                        /*    the int8 weights in place, dequantised inside the     */
+                        /*    tensor-core GEMM; 1 keep an fp16 copy of every        */
+                        /*    projection (2 bytes per parameter, made on first use):*/
+                        /*    faster prefill for that memory.                       */
 } tl_model_options;
 
 /* Bytes of one rank's exchange-buffer handle (tl_model_tp_handle). */

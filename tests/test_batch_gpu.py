@@ -41,9 +41,9 @@ def oracle_for(buf, batch, seq, n_pos, max_seq):
     return om
 
 
-def run_case(buf, n_seq, n_pos, check, max_seq):
+def run_case(buf, n_seq, n_pos, check, max_seq, weights_f16=False):
     from torchless_b200 import Batch, Model
-    m = Model.from_buffer(buf, max_seq=max_seq)
+    m = Model.from_buffer(buf, max_seq=max_seq, weights_f16=weights_f16)
     b = Batch(m, n_seq)
     b.fill_kv_random(seed=1234, n_pos=n_pos)
     vocab = m.config["vocab_size"]
@@ -71,9 +71,10 @@ def run_case(buf, n_seq, n_pos, check, max_seq):
     return worst
 
 
-def test_batch_small_matches_oracle(small_bin):
-    worst = run_case(small_bin, n_seq=4, n_pos=40, check=[0, 3], max_seq=64)
-    print(f"batch small: worst logits rel err {worst:.2e}")
+@pytest.mark.parametrize("weights_f16", [False, True], ids=["int8_in_place", "f16_copies"])
+def test_batch_small_matches_oracle(small_bin, weights_f16):
+    worst = run_case(small_bin, n_seq=4, n_pos=40, check=[0, 3], max_seq=64, weights_f16=weights_f16)
+    print(f"batch small ({'f16 copies' if weights_f16 else 'int8 in place'}): worst logits rel err {worst:.2e}")
 
 
 def test_batch_7b_shapes_matches_oracle():

@@ -32,14 +32,15 @@ def margin(logits):
     return float(top[1] - top[0]) / max(float(np.max(np.abs(logits))), 1e-30)
 
 
+@pytest.mark.parametrize("weights_f16", [False, True], ids=["int8_in_place", "f16_copies"])
 @pytest.mark.parametrize("name", ["tiny", "small"])
-def test_prefill_then_decode_matches_reference(name, request):
+def test_prefill_then_decode_matches_reference(name, weights_f16, request):
     import oracle
     from torchless_b200 import Model
     from torchless_b200.binfmt import ModelFile
     buf = request.getfixturevalue(f"{name}_bin")
     prompt, ids, ref_logits = golden_greedy(name)
-    m = Model.from_buffer(buf, max_seq=64)
+    m = Model.from_buffer(buf, max_seq=64, weights_f16=weights_f16)
     lg, nxt = m.prefill(prompt)
     assert m.pos == len(prompt)
     worst = rel_err(lg, ref_logits[0])

@@ -52,7 +52,7 @@ class tl_config(ctypes.Structure):
 class tl_model_options(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int), ("max_seq", ctypes.c_size_t), ("use_graph", ctypes.c_int),
                 ("kernel_mode", ctypes.c_int), ("tp_size", ctypes.c_int), ("tp_rank", ctypes.c_int),
-                ("sliding_window", ctypes.c_int)]
+                ("sliding_window", ctypes.c_int), ("weights_f16", ctypes.c_int)]
 
 
 TP_HANDLE_BYTES = 64

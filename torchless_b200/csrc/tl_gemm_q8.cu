@@ -10,17 +10,18 @@
 //               bytes) and BN scales of that group from a transposed scale
 //               array [K / 64][N] (one 4-byte scale per B row, contiguous),
 //               into a deep ring (the copies come from HBM);
-//   warp 14     TMA of the 128 x 64 fp16 A box (SWIZZLE_128B) into its own
+//   last warp   TMA of the 128 x 64 fp16 A box (SWIZZLE_128B) into its own
 //               shorter ring;
-//   warps 6-13  convert: w = fp16(q) * fp16(1/s) in packed fp16 arithmetic
+//   8 warps     convert: w = fp16(q) * fp16(1/s) in packed fp16 arithmetic
 //               (tensor.cpp:101-104's dequantisation with the scale rounded
 //               to fp16; e5m2 bytes widen exactly) into one of two fp16 B buffers in
 //               the SWIZZLE_128B K-major layout the MMA reads, then
 //               fence.proxy.async and arrive;
 //   warp 1      tcgen05.mma kind::f16 (M 128, N BN, K 16; 4 per block) on the
 //               A stage and the converted B buffer; commits free both;
-//   warps 2-5   epilogue (shared with the fp16 GEMM): store, residual add or
-//               SwiGLU, and split-K partials.
+//   warps 2..    epilogue (shared with the fp16 GEMM; 4 warps, 8 for SwiGLU,
+//               two per lane quarter each taking half the columns): store,
+//               residual add or SwiGLU, and split-K partials.
 // A SwiGLU B tile is 128 gate rows then the same 128 up rows: two B boxes and
 // two scale boxes.  Every wait is bounded (~2 s); on expiry the kernel records
 // an error code, drains what it issued, waits for its MMAs and frees its
@@ -43,11 +44,18 @@ namespace {
 using namespace tc;
 constexpr int kQBM = 128, kQBK = 64;
 constexpr int kConvWarps = 8;
-constexpr int kEpiWarps = 4;  // one per tensor-memory lane quarter
-// warps: 0 weight producer, 1 MMA, 2-5 epilogue, 6-13 converters, 14 activation producer
-constexpr int kConvWarp0 = 2 + kEpiWarps;
-constexpr int kAProdWarp = kConvWarp0 + kConvWarps;
-constexpr int kQ8Threads = 32 * (kAProdWarp + 1);
+// Warps: 0 weight producer, 1 MMA, then EW epilogue warps (4: one per tensor-
+// memory lane quarter; 8 for the SwiGLU epilogue, whose exp / divide per
+// output would otherwise hold the MMAs of the next 256-row tile), then the 8
+// converters, then the activation producer.
+template <int EW>
+struct Q8Warps {
+    static constexpr int kConv0 = 2 + EW;
+    static constexpr int kAProd = kConv0 + kConvWarps;
+    static constexpr int kThreads = 32 * (kAProd + 1);
+};
+template <int EPI>
+constexpr int q8_epi_warps() { return EPI == kEpiSwiGluF16 ? 8 : 4; }
 
 // MT: 128-row M tiles per CTA tile, sharing each converted B block (1 for few
 // rows; 2 for many, so the conversion is paid once per 256 rows).  Tiles are
@@ -117,13 +125,15 @@ __device__ __forceinline__ void convert_chunk(const uint8_t* q, float s, uint8_t
 // PAIRS: a B tile is 128 gate rows then the same 128 up rows (two boxes), for
 // the SwiGLU epilogue or for split-K partials that a SwiGLU pass combines.
 template <int EPI, bool F8, bool PAIRS, int MT>
-__global__ void __launch_bounds__(kQ8Threads, 1)
+__global__ void __launch_bounds__(Q8Warps<q8_epi_warps<EPI>()>::kThreads, 1)
     gemm_q8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_q2, const __grid_constant__ CUtensorMap tma_s,
                    const __grid_constant__ CUtensorMap tma_s2, GemmArgs g) {
     using Cfg = Q8Cfg<MT>;
     constexpr int SA = Cfg::kAStages, SB = Cfg::kBStages, NB = Cfg::kHBufs, BN = Cfg::BN, TBM = MT * kQBM;
     constexpr int NACC = Cfg::kAcc;
+    constexpr int kEpiWarps = q8_epi_warps<EPI>();
+    constexpr int kConvWarp0 = Q8Warps<kEpiWarps>::kConv0, kAProdWarp = Q8Warps<kEpiWarps>::kAProd;
     constexpr bool swiglu = PAIRS;
     constexpr int QROWS = swiglu ? BN / 2 : BN;  // rows per B box
     extern __shared__ uint8_t smem_raw[];
@@ -405,7 +415,7 @@ tl_status launch_q8(const __half* A, int M, int K, const Q8Weights& B, int N, vo
     const int tiles = ((N + Cfg::BN - 1) / Cfg::BN) * ((M + MT * kQBM - 1) / (MT * kQBM)) * ksplit;
     const int grid = std::min(tiles, sm_count());
     GemmArgs g{M, N, K, C, ldc, err, ksplit};
-    kern<<<grid, kQ8Threads, Cfg::kSmem, s>>>(ta, tq, tq2, ts, ts2, g);
+    kern<<<grid, Q8Warps<q8_epi_warps<EPI>()>::kThreads, Cfg::kSmem, s>>>(ta, tq, tq2, ts, ts2, g);
     return check_launch("gemm_q8");
 }
 

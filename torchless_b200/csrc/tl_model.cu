@@ -313,10 +313,14 @@ struct tl_model {
     bool broken = false;  // tp: a device-side wait gave up; the ranks' exchange state is lost
     // batched prompt pass (tl_model_prefill): fp16 weights dequantised on first
     // use (per layer q|k|v, o, gate|up in SwiGLU blocks, down) and row buffers
-    DeviceArena scT, rows;
+    DeviceArena scT, w16, rows;
     // per layer: q|k|v, o, gate|up, down as the dequantising GEMM reads them
-    // (the int8 / e5m2 weights in place, their 1/s transposed into scT)
+    // (the int8 / e5m2 weights in place, their 1/s transposed into scT) ...
     std::vector<std::array<Q8Weights, 4>> lq8;
+    // ... or, with tl_model_options.weights_f16, fp16 copies (gate|up in
+    // blocks of 128 gate then 128 up rows) for the fp16 GEMM
+    bool weights_f16 = false;
+    std::vector<std::array<__half*, 4>> lw16;
     size_t rows_cap = 0;
     float *p_h = nullptr, *p_qkv = nullptr;
     __half *p_x16 = nullptr, *p_q16 = nullptr, *p_ctx16 = nullptr, *p_act16 = nullptr;
@@ -455,6 +459,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         m->window = static_cast<int>(w);
     }
     m->use_graph = opts ? opts->use_graph != 0 : true;
+    m->weights_f16 = opts && opts->weights_f16 != 0;
     // Tensor parallelism (Megatron split of modules.cpp's layers): this rank
     // keeps q heads / kv heads / F rows / vocab rows [rank n / tp, (rank + 1) n / tp).
     const int tp = (opts && opts->tp_size > 0) ? opts->tp_size : 1;
@@ -959,11 +964,46 @@ tl_status check_capacity(const tl_model* m, size_t steps) {
     return TL_OK;
 }
 
+// A weight GEMM of the batched paths for layer l (which: 0 q|k|v, 1 o, 2
+// gate|up, 3 down): the int8 weights in place (gemm_q8) or, with
+// tl_model_options.weights_f16, their fp16 copies (gemm_f16).
+tl_status layer_gemm(const tl_model* m, size_t l, int which, int epi, const __half* A, int M, int K, int N, void* C,
+                     int ldc, cudaStream_t s) {
+    if (m->weights_f16) return gemm_f16(epi, A, M, K, m->lw16[l][which], N, C, ldc, m->err, s);
+    return gemm_q8(epi, A, M, K, m->lq8[l][which], N, C, ldc, m->err, s);
+}
+tl_status layer_gemm_splitk(const tl_model* m, size_t l, int which, const __half* A, int M, int K, int N,
+                            float* part, size_t part_floats, int* ks, cudaStream_t s) {
+    if (m->weights_f16) return gemm_f16_splitk(A, M, K, m->lw16[l][which], N, part, part_floats, ks, m->err, s);
+    return gemm_q8_splitk(A, M, K, m->lq8[l][which], N, part, part_floats, ks, m->err, s);
+}
+
 // fp16 weights and row buffers of the batched prompt pass (first use / growth).
 tl_status ensure_prefill(tl_model* m, size_t n) {
     const int64_t D = m->cfg.hidden_size, HD = m->cfg.head_dim, H = m->lH, KV = m->lKV, F = m->lF;
     const int64_t NQKV = (H + 2 * KV) * HD, L = m->cfg.n_layers;
-    if (m->lq8.empty()) {
+    if (m->weights_f16 && m->lw16.empty()) {
+        if (F % 128) return set_error(TL_ERR_UNSUPPORTED, "prefill: intermediate_size %lld not a multiple of 128",
+                                      static_cast<long long>(F));
+        using A = DeviceArena;
+        const size_t per = A::pad(NQKV * D * 2) + A::pad(D * H * HD * 2) + A::pad(2 * F * D * 2) + A::pad(D * F * 2);
+        TL_TRY(m->w16.reserve(per * L));
+        m->lw16.resize(L);
+        for (int64_t l = 0; l < L; l++) {
+            const LayerW& w = m->layers[l];
+            auto& W = m->lw16[l];
+            W[0] = m->w16.take<__half>(NQKV * D);
+            W[1] = m->w16.take<__half>(D * H * HD);
+            W[2] = m->w16.take<__half>(2 * F * D);
+            W[3] = m->w16.take<__half>(D * F);
+            // the arena's scales are already 1/s; fp8 weights (null scales) convert exactly
+            TL_TRY(dequant_f16(W[0], w.wqkv, w.sqkv, nullptr, nullptr, NQKV, D, false, m->stream));
+            TL_TRY(dequant_f16(W[1], w.wo, w.so, nullptr, nullptr, D, H * HD, false, m->stream));
+            TL_TRY(dequant_f16(W[2], w.w1, w.s1, w.w3, w.s3, F, D, true, m->stream));
+            TL_TRY(dequant_f16(W[3], w.w2, w.s2, nullptr, nullptr, D, F, false, m->stream));
+        }
+    }
+    if (!m->weights_f16 && m->lq8.empty()) {
         if (F % 128) return set_error(TL_ERR_UNSUPPORTED, "prefill: intermediate_size %lld not a multiple of 128",
                                       static_cast<long long>(F));
         using A = DeviceArena;
@@ -1103,6 +1143,7 @@ tl_status tl_model_destroy(tl_model* m) {
     m->state.release();
     m->tiles.release();
     m->scT.release();
+    m->w16.release();
     m->rows.release();
     m->lm16_arena.release();
     if (m->d_layers) cudaFree(m->d_layers);
@@ -1231,11 +1272,10 @@ tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* log
     TL_TRY(embed_rows(m->p_h, m->embed, m->p_tok, M, D, s));
     for (size_t l = 0; l < m->cfg.n_layers; l++) {
         const LayerW& w = m->layers[l];
-        const auto& W = m->lq8[l];
         float* kc = m->kc + l * layer_kv_floats(m);
         float* vc = m->vc + l * layer_kv_floats(m);
         TL_TRY(rmsnorm_rows_f16(m->p_x16, m->p_h, w.g_in, M, D, s));
-        TL_TRY(gemm_q8(kEpiStoreF32, m->p_x16, M, D, W[0], NQKV, m->p_qkv, NQKV, m->err, s));
+        TL_TRY(layer_gemm(m, l, 0, kEpiStoreF32, m->p_x16, M, D, NQKV, m->p_qkv, NQKV, s));
         TL_TRY(rope_cache_rows(m->p_q16, m->p_qkv, kc, vc, m->cos_tab, m->sin_tab, M, p0, H, KV, HD, ms, s));
         if (HD == 128 && H == 4 * KV)  // tensor-core attention (tcgen05, tensor memory)
             TL_TRY(attention_prefill_tc(m->p_ctx16, m->p_q16, m->p_k16, m->p_v16, kc, vc, M, p0, H, KV, HD, ms,
@@ -1243,10 +1283,10 @@ tl_status prefill_impl(tl_model* m, const uint32_t* tokens, size_t n, float* log
         else
             TL_TRY(attention_prefill(m->p_ctx16, m->p_q16, m->p_k16, m->p_v16, kc, vc, M, p0, H, KV, HD, ms, scale,
                                      m->window, s));
-        TL_TRY(gemm_q8(kEpiAddF32, m->p_ctx16, M, H * HD, W[1], D, m->p_h, D, m->err, s));
+        TL_TRY(layer_gemm(m, l, 1, kEpiAddF32, m->p_ctx16, M, H * HD, D, m->p_h, D, s));
         TL_TRY(rmsnorm_rows_f16(m->p_x16, m->p_h, w.g_post, M, D, s));
-        TL_TRY(gemm_q8(kEpiSwiGluF16, m->p_x16, M, D, W[2], 2 * F, m->p_act16, F, m->err, s));
-        TL_TRY(gemm_q8(kEpiAddF32, m->p_act16, M, F, W[3], D, m->p_h, D, m->err, s));
+        TL_TRY(layer_gemm(m, l, 2, kEpiSwiGluF16, m->p_x16, M, D, 2 * F, m->p_act16, F, s));
+        TL_TRY(layer_gemm(m, l, 3, kEpiAddF32, m->p_act16, M, F, D, m->p_h, D, s));
     }
     // the last token's hidden state: final norm, lm_head, sample_max (modules.cpp:147-171, main.cpp:10-21)
     TL_CUDA_TRY(cudaMemcpyAsync(m->h, m->p_h + static_cast<size_t>(M - 1) * D, D * 4, cudaMemcpyDeviceToDevice, s));
@@ -1513,8 +1553,7 @@ tl_status batch_step(tl_batch* b) {
     TL_TRY(residual_rmsnorm_rows(b->x16, b->hres, nullptr, 0, 0, m->layers[0].g_in, B, D, s));
     for (size_t l = 0; l < m->cfg.n_layers; l++) {
         const LayerW& w = m->layers[l];
-        const auto& W = m->lq8[l];
-        TL_TRY(gemm_q8_splitk(b->x16, B, D, W[0], NQKV, b->split, b->split_floats, &ks, m->err, s));
+        TL_TRY(layer_gemm_splitk(m, l, 0, b->x16, B, D, NQKV, b->split, b->split_floats, &ks, s));
         TL_TRY(rope_cache_batch(b->qf, b->split, ks, qkv_stride, b->bkv, static_cast<int>(l), b->pos, m->cos_tab,
                                 m->sin_tab, B, H, KV, HD, s));
         TL_TRY(attention_decode_batch(b->part, b->qf, b->bkv, static_cast<int>(l), b->pos, B, H, KV, HD, S, scale,
@@ -1527,11 +1566,11 @@ tl_status batch_step(tl_batch* b) {
                                                 s);
             return residual_rmsnorm_rows(b->x16, b->hres, b->split, ks, d_stride, g, B, D, s);
         };
-        TL_TRY(gemm_q8_splitk(b->ctx16, B, H * HD, W[1], D, b->split, b->split_floats, &ks, m->err, s));
+        TL_TRY(layer_gemm_splitk(m, l, 1, b->ctx16, B, H * HD, D, b->split, b->split_floats, &ks, s));
         TL_TRY(residual(w.g_post));
-        TL_TRY(gemm_q8_splitk(b->x16, B, D, W[2], 2 * F, b->split, b->split_floats, &ks, m->err, s));
+        TL_TRY(layer_gemm_splitk(m, l, 2, b->x16, B, D, 2 * F, b->split, b->split_floats, &ks, s));
         TL_TRY(swiglu_rows(b->act16, b->split, ks, static_cast<size_t>(B) * 2 * F, B, static_cast<int>(F), s));
-        TL_TRY(gemm_q8_splitk(b->act16, B, F, W[3], D, b->split, b->split_floats, &ks, m->err, s));
+        TL_TRY(layer_gemm_splitk(m, l, 3, b->act16, B, F, D, b->split, b->split_floats, &ks, s));
         TL_TRY(residual(l + 1 < m->cfg.n_layers ? m->layers[l + 1].g_in : m->norm));
     }
     TL_TRY(gemm_f16(kEpiStoreF32, b->x16, B, D, m->lm16, V, b->logits, V, m->err, s));

@@ -37,28 +37,31 @@ class Model:
 
     @staticmethod
     def _opts(device: int, max_seq: int, use_graph: bool, kernel_mode: int, tp_size: int = 1,
-              tp_rank: int = 0, sliding_window: int = 0):
+              tp_rank: int = 0, sliding_window: int = 0, weights_f16: bool = False):
         return tl_model_options(device=device, max_seq=max_seq, use_graph=1 if use_graph else 0,
                                 kernel_mode=kernel_mode, tp_size=tp_size, tp_rank=tp_rank,
-                                sliding_window=sliding_window)
+                                sliding_window=sliding_window, weights_f16=1 if weights_f16 else 0)
 
     @classmethod
     def load(cls, path: str, device: int = 0, max_seq: int = 1024, use_graph: bool = True,
-             kernel_mode: int = 0, tp_size: int = 1, tp_rank: int = 0, sliding_window: int = 0) -> "Model":
+             kernel_mode: int = 0, tp_size: int = 1, tp_rank: int = 0, sliding_window: int = 0,
+             weights_f16: bool = False) -> "Model":
         """sliding_window: 0 attends to every position (the reference); W > 0 to
-        the last W; -1 uses the binary's sliding_window."""
+        the last W; -1 uses the binary's sliding_window.  weights_f16: the
+        batched paths keep fp16 copies of the projections (faster prefill, 2 B
+        per parameter) instead of reading the int8 weights in place."""
         h = ctypes.c_void_p()
-        o = cls._opts(device, max_seq, use_graph, kernel_mode, tp_size, tp_rank, sliding_window)
+        o = cls._opts(device, max_seq, use_graph, kernel_mode, tp_size, tp_rank, sliding_window, weights_f16)
         check(lib().tl_model_load(path.encode(), ctypes.byref(o), ctypes.byref(h)))
         return cls(h, tp_size, tp_rank)
 
     @classmethod
     def from_buffer(cls, buf: np.ndarray, device: int = 0, max_seq: int = 1024,
                     use_graph: bool = True, kernel_mode: int = 0, tp_size: int = 1,
-                    tp_rank: int = 0, sliding_window: int = 0) -> "Model":
+                    tp_rank: int = 0, sliding_window: int = 0, weights_f16: bool = False) -> "Model":
         buf = np.ascontiguousarray(buf)
         h = ctypes.c_void_p()
-        o = cls._opts(device, max_seq, use_graph, kernel_mode, tp_size, tp_rank, sliding_window)
+        o = cls._opts(device, max_seq, use_graph, kernel_mode, tp_size, tp_rank, sliding_window, weights_f16)
         check(lib().tl_model_load_buffer(buf.ctypes.data, buf.nbytes, ctypes.byref(o), ctypes.byref(h)))
         return cls(h, tp_size, tp_rank)
 
