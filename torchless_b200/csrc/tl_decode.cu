@@ -158,13 +158,6 @@ __device__ __forceinline__ void hmma16816(float (&d)[4], uint32_t a0, uint32_t a
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Low bytes of four ints, packed little-endian.
-__device__ __forceinline__ uint32_t pack_lo_bytes(int x0, int x1, int x2, int x3) {
-    const uint32_t lo = __byte_perm(static_cast<uint32_t>(x0), static_cast<uint32_t>(x1), 0x0040);
-    const uint32_t hi = __byte_perm(static_cast<uint32_t>(x2), static_cast<uint32_t>(x3), 0x0040);
-    return __byte_perm(lo, hi, 0x5410);
-}
-
 // Self-check build (TL_DECODE_CHECK): bounds/alignment checks that record the
 // first violation in DecodeArgs::dbg and let the caller skip the access.
 #ifdef TL_DECODE_CHECK
@@ -530,20 +523,27 @@ struct Consumer {
     }
 
     // Converts 16 staged columns (block b) to digits and stores them.
+    // X = rint(v sc) with |X| <= 2^22 comes from one fma with 1.5 2^23: the
+    // sum lies in [2^23, 2^24], where floats are the integers, so its bit
+    // pattern is 0x4B400000 + X (round to nearest even, as __float2int_rn).
+    // The balanced digits are bytes of shifted copies of X: d2 = byte 0 of X,
+    // d1 = byte 1 of X + 128 (= (X + 128) >> 8), d0 = byte 2 of X + 32896
+    // (= ((X + 128) >> 8 + 128) >> 8); adding 0x4B400000 changes bytes 0
+    // and 1 of none of them and byte 2 only by 0x40, removed below.
     __device__ __forceinline__ void put_digits(int b, const float (&v)[16], float sc) {
         uint32_t w0[4], w1[4], w2[4];
 #pragma unroll
         for (int q = 0; q < 4; q++) {
-            int x[4], y[4], z[4];
+            uint32_t x[4], y[4], z[4];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                x[j] = __float2int_rn(v[4 * q + j] * sc);
-                y[j] = (x[j] + 128) >> 8;  // (X - d2) / 256
-                z[j] = (y[j] + 128) >> 8;  // (X1 - d1) / 256 = d0
+                x[j] = __float_as_uint(fmaf(v[4 * q + j], sc, 12582912.0f));  // 0x4B400000 + X
+                y[j] = x[j] + 128u;
+                z[j] = x[j] + (32896u - 0x400000u);
             }
-            w2[q] = pack_lo_bytes(x[0], x[1], x[2], x[3]);
-            w1[q] = pack_lo_bytes(y[0], y[1], y[2], y[3]);
-            w0[q] = pack_lo_bytes(z[0], z[1], z[2], z[3]);
+            w2[q] = __byte_perm(__byte_perm(x[0], x[1], 0x0040), __byte_perm(x[2], x[3], 0x0040), 0x5410);
+            w1[q] = __byte_perm(__byte_perm(y[0], y[1], 0x0051), __byte_perm(y[2], y[3], 0x0051), 0x5410);
+            w0[q] = __byte_perm(__byte_perm(z[0], z[1], 0x0062), __byte_perm(z[2], z[3], 0x0062), 0x5410);
         }
         uint8_t* dst = sh.xbuf + (b >> 2) * kGroupDigitBytes + (b & 3) * 16;
         *reinterpret_cast<uint4*>(dst) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
