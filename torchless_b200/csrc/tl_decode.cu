@@ -185,6 +185,7 @@ struct Shared {
     uint64_t* empty;   // [stages]
     int* flags;        // [0] abort, [1] last CTA (argmax), [2] last split (attention)
     uint32_t* info;    // [0] pos, [1] token
+    DecodeLayer* layers;  // [n_layers] copy of the layer table (no global load at a phase switch)
 };
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -202,8 +203,9 @@ __host__ __device__ inline size_t xbuf_bytes(int D, int F, int HD, bool f8) {
     return align_up(x, 128);
 }
 
-__host__ __device__ inline size_t fixed_bytes(int D, int F, int HD, bool f8, int pbuf_floats) {
-    return xbuf_bytes(D, F, HD, f8) + align_up(static_cast<size_t>(pbuf_floats) * 4, 128) + 64 * 4 + 64;
+__host__ __device__ inline size_t fixed_bytes(int D, int F, int HD, bool f8, int pbuf_floats, int n_layers) {
+    return xbuf_bytes(D, F, HD, f8) + align_up(static_cast<size_t>(pbuf_floats) * 4, 128) + 64 * 4 + 64 +
+           static_cast<size_t>(n_layers) * sizeof(DecodeLayer);
 }
 
 __device__ Shared carve(uint8_t* base, int stages, const DecodeArgs& a) {
@@ -222,6 +224,7 @@ __device__ Shared carve(uint8_t* base, int stages, const DecodeArgs& a) {
     off += 64;
     s.full = reinterpret_cast<uint64_t*>(base + off);
     s.empty = s.full + stages;
+    s.layers = reinterpret_cast<DecodeLayer*>(s.empty + stages);
     return s;
 }
 
@@ -246,7 +249,7 @@ struct Seg {
     int n_rb, ksn, b0;
 };
 
-__device__ Seg seg_info(const DecodeArgs& a, int s) {
+__device__ Seg seg_info(const DecodeArgs& a, const DecodeLayer* layers, int s) {
     const int NQKV = (a.H + 2 * a.KV) * a.HD;
     const int ksD = tile_slices(a.D);
     Seg g;
@@ -258,7 +261,7 @@ __device__ Seg seg_info(const DecodeArgs& a, int s) {
         g.ksn = ksD;
         g.tb = a.lm_8bit ? tbq : kTileBytesF32;
     } else {
-        const DecodeLayer& L = a.layers[s >> 2];
+        const DecodeLayer& L = layers[s >> 2];
         g.tb = tbq;
         switch (s & 3) {
             case 0: g.src = L.qkv; g.n_rb = (NQKV + 15) / 16; g.ksn = ksD; break;
@@ -304,7 +307,7 @@ struct Producer {
     __device__ void prefetch_next() {
         while (pseg < n_segs && pi >= pg.n) {
             if (++pseg < n_segs) {
-                pg = seg_info(a, pseg);
+                pg = seg_info(a, sh.layers, pseg);
                 pi = 0;
             }
         }
@@ -317,11 +320,11 @@ struct Producer {
     __device__ void run() {
         const int sb = stage_bytes(a.w_f8 != 0);  // ring slot bytes
         if (a.prefetch > 0) {
-            pg = seg_info(a, 0);
+            pg = seg_info(a, sh.layers, 0);
             for (int j = 0; j < a.prefetch; j++) prefetch_next();
         }
         for (int sg = 0; sg < n_segs && ok; sg++) {
-            const Seg g = seg_info(a, sg);
+            const Seg g = seg_info(a, sh.layers, sg);
             for (int i = 0; i < g.n && ok; i += kTilesPerStage, it++) {
                 const int s = slot;
                 const uint32_t round = rnd;
@@ -1062,7 +1065,7 @@ struct Consumer {
         const int chunk = (attn_span(pos) + S - 1) / S;
         const int p0 = attn_lo(pos) + s * chunk, p1 = min(npos, p0 + chunk);
         if (p1 <= p0) return;
-        const DecodeLayer& L = a.layers[layer];
+        const DecodeLayer& L = sh.layers[layer];
         const size_t off = (static_cast<size_t>(kh) * a.max_seq + p0) * HD;
         const uint32_t bytes = static_cast<uint32_t>(::min(p1 - p0, a.kv_prefetch_rows)) * HD * 4;
         prefetch_l2(L.k_cache + off, bytes);
@@ -1087,7 +1090,7 @@ struct Consumer {
             return true;
         } else {
             constexpr int QPG = 4, G = 8, W = HD + 2, HALF = HD / 2, PW = HD + 4;
-            const DecodeLayer& L = a.layers[layer];
+            const DecodeLayer& L = sh.layers[layer];
             const int S = attn_splits(pos);
             const int u = blockIdx.x;
             if (u >= a.KV * S) return true;
@@ -1284,7 +1287,7 @@ struct Consumer {
         constexpr int VPL = HD / 32;
         constexpr int HALF = HD / 2;
         constexpr int PF = 4;  // positions per warp in flight
-        const DecodeLayer& L = a.layers[layer];
+        const DecodeLayer& L = sh.layers[layer];
         const int S = attn_splits(pos);
         const int u = blockIdx.x;
         if (u >= a.H * S) return true;
@@ -1518,7 +1521,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
     {
         unsigned dyn;
         asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
-        const size_t end = reinterpret_cast<uint8_t*>(sh.empty + stages) - smem_raw;
+        const size_t end = reinterpret_cast<uint8_t*>(sh.layers + a.n_layers) - smem_raw;
         int* a_dbg = a.dbg;
         int* a_err = a.err;
         if (!TLD_OK(end <= dyn, 1, static_cast<long long>(end), dyn)) return;
@@ -1537,6 +1540,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         sh.info[2] = __ldcg(a.epoch);
         fence_mbar_init();
     }
+    static_assert(sizeof(DecodeLayer) % 8 == 0, "layer table copied in 8-byte words");
+    for (int i = threadIdx.x; i < a.n_layers * static_cast<int>(sizeof(DecodeLayer) / 8); i += blockDim.x)
+        reinterpret_cast<uint64_t*>(sh.layers)[i] = __ldg(reinterpret_cast<const unsigned long long*>(a.layers) + i);
     __syncthreads();
     // Never index with an out-of-range token or position: record and stop.
     // (a.V is this rank's vocabulary slice; tokens index the whole vocabulary)
@@ -1561,9 +1567,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
     const uint32_t token = sh.info[1];
     const float* emb = a.embed + static_cast<size_t>(token) * D;  // Embedding::forward (modules.cpp:5-7)
     cw.epoch = sh.info[2];
-    const float2 st0 = cw.local_stats(emb, D, a.layers[0].g_in);
+    const float2 st0 = cw.local_stats(emb, D, sh.layers[0].g_in);
     for (int l = 0; l < a.n_layers; l++) {
-        const DecodeLayer& L = a.layers[l];
+        const DecodeLayer& L = sh.layers[l];
         const float* hin = (l == 0) ? emb : a.h;
         // q/k/v = W_qkv rmsnorm(h)
         float un;
@@ -1597,7 +1603,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         // h = h + W2 act
         if (!cw.wait_all()) return;
         un = cw.template stage_digits<false>(a.act, F, nullptr, nullptr);
-        const float* g_next = (l + 1 < a.n_layers) ? a.layers[l + 1].g_in : a.g_final;
+        const float* g_next = (l + 1 < a.n_layers) ? sh.layers[l + 1].g_in : a.g_final;
         if (cw.t == 0) prefetch_l2(g_next, static_cast<uint32_t>(D) * 4u);  // staged after this phase
         if (!cw.template run_i8<3>(D, F, un, a.h, g_next)) return;
     }
@@ -1848,7 +1854,7 @@ bool decode_kernel_fits(int D, int F, int H, int KV, int HD, int V, int n_layers
     pb = std::max(pb, need(D, kTileRowsI8, F));
     pb = std::max(pb, need(V, kTileRowsF32, D));
     pb = std::max(pb, need(V, kTileRowsI8, D));  // 8-bit lm_head
-    const size_t fixed = fixed_bytes(D, F, HD, w_f8, pb);
+    const size_t fixed = fixed_bytes(D, F, HD, w_f8, pb, n_layers);
     if (static_cast<size_t>(max_smem) <= fixed) return false;
     int st = static_cast<int>((static_cast<size_t>(max_smem) - fixed) / (stage_bytes(w_f8) + 16));
     st = st > 24 ? 24 : st;
