@@ -425,6 +425,8 @@ def run_gemv_sweep(args):
     g = torch.Generator(device="cuda")
     g.manual_seed(SEED)
     for name, n, d, kind in SWEEP:
+        if args.gemv_shape and not name.startswith(args.gemv_shape):
+            continue
         mats = 2 if kind == "gate_up" else 1
         wbytes = mats * (n * d + 4 * n * d // 64)
         copies = max(2, -(-(256 << 20) // wbytes))  # > 256 MB in rotation: no L2 reuse
@@ -674,6 +676,8 @@ def main():
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--gemv-sweep", action="store_true",
                     help="isolated int8 GEMV sweep at Mistral-7B shapes (one JSON line per shape)")
+    ap.add_argument("--gemv-shape", default="",
+                    help="--gemv-sweep: only the shape whose name starts with this (e.g. lm_head)")
     ap.add_argument("--lm-head-int8", action="store_true",
                     help="bs1 decode of the same model with its lm_head stored int8 (format extension)")
     ap.add_argument("--fp8", action="store_true",

@@ -706,7 +706,7 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         d.h = m->h; d.qkv = m->qkv; d.attn_part = m->attn_part; d.act = m->act; d.logits = m->logits;
         d.ctx = m->ctx; d.attn_cnt = m->attn_cnt; d.qkv_cnt = m->qkv_cnt; d.stats = m->stats;
         // Tuning knob: tile pairs prefetched into L2 ahead of the ring.
-        d.prefetch = 8;
+        d.prefetch = 6;
         if (const char* e = std::getenv("TL_DECODE_PREFETCH")) d.prefetch = std::max(0, std::min(64, std::atoi(e)));
 #ifdef TL_DECODE_CHECK
         d.dbg = m->dbg;
