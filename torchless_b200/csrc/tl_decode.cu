@@ -186,6 +186,7 @@ struct Shared {
     int* flags;        // [0] abort, [1] last CTA (argmax), [2] last split (attention)
     uint32_t* info;    // [0] pos, [1] token
     DecodeLayer* layers;  // [n_layers] copy of the layer table (no global load at a phase switch)
+    uint64_t* xbar;       // completion of the bulk copy of published act digits into xbuf
 };
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -205,7 +206,7 @@ __host__ __device__ inline size_t xbuf_bytes(int D, int F, int HD, bool f8) {
 
 __host__ __device__ inline size_t fixed_bytes(int D, int F, int HD, bool f8, int pbuf_floats, int n_layers) {
     return xbuf_bytes(D, F, HD, f8) + align_up(static_cast<size_t>(pbuf_floats) * 4, 128) + 64 * 4 + 64 +
-           static_cast<size_t>(n_layers) * sizeof(DecodeLayer);
+           static_cast<size_t>(n_layers) * sizeof(DecodeLayer) + 16;
 }
 
 __device__ Shared carve(uint8_t* base, int stages, const DecodeArgs& a) {
@@ -225,6 +226,7 @@ __device__ Shared carve(uint8_t* base, int stages, const DecodeArgs& a) {
     s.full = reinterpret_cast<uint64_t*>(base + off);
     s.empty = s.full + stages;
     s.layers = reinterpret_cast<DecodeLayer*>(s.empty + stages);
+    s.xbar = reinterpret_cast<uint64_t*>(s.layers + a.n_layers);
     return s;
 }
 
@@ -684,6 +686,34 @@ struct Consumer {
         return ldexpf(1.0f, -k);
     }
 
+    // The down_proj staging when the gate/up epilogues published act as digits
+    // (act_kp) and no value overflowed this step: one bulk copy of the digits
+    // into xbuf.  Otherwise (or with TP / fp8 weights) the conversion of act.
+    // CTA 0 sets the next step's exponent from this step's max |act| with 2
+    // bits of headroom.  Returns 2^-k.
+    __device__ float stage_act(int layer) {
+        const int d = a.F;
+        const bool dig = !TP && !F8 && a.act_dig != nullptr && act_kp > -1000 &&
+                         __ldcg(a.act_ovf + layer) != epoch + 1;
+        if (blockIdx.x == 0 && warp == 0 && !TP && !F8 && a.act_dig != nullptr) {
+            const float2 st = read_stats();
+            if (lane == 0) a.act_k[layer] = st.y > 0.f ? stage_exp(st.y) - 2 : -1000;
+        }
+        if (!dig) return stage_digits<false>(a.act, d, nullptr, nullptr);
+        const uint32_t bytes = static_cast<uint32_t>(x_bytes() * tile_slices(d) * kTileCols);
+        if (!TLD_OK(bytes <= xbuf_bytes(a.D, a.F, a.HD, F8) && (bytes & 15) == 0, 63, bytes, 0)) return 1.0f;
+        if (t == 0) {
+            mbar_expect_tx(sh.xbar, bytes);
+            bulk_load(sh.xbuf, a.act_dig, bytes, sh.xbar);
+        }
+        if (!mbar_wait(sh.xbar, xbar_uses & 1u)) fail(kErrFull);  // a 43 KB copy: never near the bound
+        xbar_uses++;
+        stamp(5);
+        consumer_sync();
+        stamp(2);
+        return ldexpf(1.0f, -act_kp);
+    }
+
     // Stages RMSNorm(vec) (modules.cpp:31-46) as fp32 for the fp32 lm_head tiles.
     __device__ void stage_f32(const float* vec, int d, const float* g) {
         if (!TLD_OK(4 * static_cast<size_t>(d) <= xbuf_bytes(a.D, a.F, a.HD, F8) && d % 4 == 0, 31, d, 0)) return;
@@ -863,7 +893,7 @@ struct Consumer {
     // kind 2 (0, max |act|); kind 0 instead adds its rows to each kv group's
     // ready count (qkv_cnt), which attention waits on.
     template <int KIND>
-    __device__ bool run_i8(int n_rows, int d, float unscale, const float* res, const float* g_next) {
+    __device__ bool run_i8(int n_rows, int d, float unscale, const float* res, const float* g_next, int layer = 0) {
         const int ksn = tile_slices(d);
         constexpr bool xchg = (KIND == 1 || KIND == 3) && TP;  // partial rows go to every rank
         const int n_rb = (n_rows + kTileRowsI8 - 1) / kTileRowsI8;
@@ -884,6 +914,13 @@ struct Consumer {
         if (rb0 < 0) return false;
         float ss = 0.f, mx = 0.f;
         if (KIND == 2) {
+            // with a predicted exponent, also the act digits as the down staging
+            // lays them out (put_digits' arithmetic), column c of digit n at byte
+            // 192 (c / 64) + 64 n + c % 64
+            act_kp = (!TP && !F8 && a.act_dig) ? a.act_k[layer] : -1000;
+            const bool dig = act_kp > -1000;
+            const float sc = dig ? ldexpf(1.0f, act_kp) : 0.f;
+            bool ovf = false;
             for (int j = t; j < nrl * 8; j += kConsumers) {
                 const int rbl = j / 8, o = j % 8;
                 const int row = (rb0 + rbl) * 8 + o;
@@ -893,8 +930,20 @@ struct Consumer {
                     const float v = (gate / (1.0f + expf(-gate))) * up;  // silu * up, kernels.cpp:98-102, 127-131
                     a.act[row] = v;
                     mx = fmaxf(mx, fabsf(v));
+                    if (dig) {
+                        if (!(fabsf(v * sc) <= 4194304.0f)) {  // |X| <= 2^22, and not NaN
+                            ovf = true;
+                        } else {
+                            const uint32_t x = __float_as_uint(fmaf(v, sc, 12582912.0f));  // 0x4B400000 + X
+                            uint8_t* dst = a.act_dig + 192 * (row / 64) + row % 64;
+                            dst[0] = static_cast<uint8_t>((x + (32896u - 0x400000u)) >> 16);
+                            dst[64] = static_cast<uint8_t>((x + 128u) >> 8);
+                            dst[128] = static_cast<uint8_t>(x);
+                        }
+                    }
                 }
             }
+            if (ovf) a.act_ovf[layer] = epoch + 1;  // ordered before the arrival's release
         } else if (xchg) {
             // tensor parallel: this rank's partial rows to every rank, then
             // the CTA's rows summed over the ranks (every rank's CTA owns the
@@ -974,6 +1023,8 @@ struct Consumer {
     // all its CTAs gathered x (its grid barrier lies between).
     int xk = 0;          // exchanges this CTA has completed in this step
     unsigned epoch = 0;  // steps run before this one
+    int act_kp = -1000;  // exponent of the act digits the gate/up epilogue published (< -999: none)
+    uint32_t xbar_uses = 0;
 
     __device__ __forceinline__ unsigned xchg_tag() const {
         return static_cast<unsigned>((static_cast<unsigned long long>(epoch) * 2 * a.n_layers + xk + 1) & 0xffffffffull);
@@ -1521,7 +1572,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
     {
         unsigned dyn;
         asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
-        const size_t end = reinterpret_cast<uint8_t*>(sh.layers + a.n_layers) - smem_raw;
+        const size_t end = reinterpret_cast<uint8_t*>(sh.xbar + 1) - smem_raw;
         int* a_dbg = a.dbg;
         int* a_err = a.err;
         if (!TLD_OK(end <= dyn, 1, static_cast<long long>(end), dyn)) return;
@@ -1532,6 +1583,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
             mbar_init(&sh.full[s], 1);
             mbar_init(&sh.empty[s], kWarpsPerSlot);
         }
+        mbar_init(sh.xbar, 1);
         sh.flags[0] = 0;
         sh.flags[1] = 0;
         for (int i = 32; i < 64; i++) reinterpret_cast<unsigned*>(sh.scratch)[i] = 0u;  // kv group row counts
@@ -1599,10 +1651,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DecodeArgs a, 
         // act = silu(W1 x) * (W3 x), x = rmsnorm(h)
         if (!cw.wait_all()) return;
         un = cw.template stage_digits<true>(a.h, D, L.g_post, nullptr);
-        if (!cw.template run_i8<2>(2 * F, D, un, nullptr, nullptr)) return;
+        if (!cw.template run_i8<2>(2 * F, D, un, nullptr, nullptr, l)) return;
         // h = h + W2 act
         if (!cw.wait_all()) return;
-        un = cw.template stage_digits<false>(a.act, F, nullptr, nullptr);
+        un = cw.stage_act(l);
         const float* g_next = (l + 1 < a.n_layers) ? sh.layers[l + 1].g_in : a.g_final;
         if (cw.t == 0) prefetch_l2(g_next, static_cast<uint32_t>(D) * 4u);  // staged after this phase
         if (!cw.template run_i8<3>(D, F, un, a.h, g_next)) return;

@@ -101,6 +101,14 @@ struct DecodeArgs {
     // each CTA wrote in a phase, alternating buffers per phase.
     float2* stats;
     int prefetch;               // tile pairs prefetched into L2 ahead of the ring (0 = off)
+    // act published as staged digits by the gate/up epilogue (one GPU, int8
+    // tiles; null: off): the digits in the staging layout [3 * F padded],
+    // per layer the exponent to use (set from the previous step's max with 2
+    // bits of headroom; < -999: none yet), and the epoch + 1 of a step in
+    // which some value did not fit (the down staging then converts act itself).
+    uint8_t* act_dig;
+    int* act_k;
+    unsigned* act_ovf;
     // Tensor parallelism (tp_size > 1, modules.cpp layers split Megatron
     // style): this rank holds q heads and kv heads [rank H, (rank + 1) H)
     // (H, KV local), gate/up rows and down columns of its F slice, o_proj

@@ -285,6 +285,9 @@ struct tl_model {
     float *attn_part = nullptr, *am_v = nullptr;
     unsigned *attn_cnt = nullptr, *am_cnt = nullptr, *d_pos = nullptr;
     unsigned* qkv_cnt = nullptr;  // persistent kernel: q/k/v rows written per kv group
+    uint8_t* act_dig = nullptr;   // persistent kernel: act published as staged digits
+    int* act_k = nullptr;         // ... the exponent per layer (< -999: none yet)
+    unsigned* act_ovf = nullptr;  // ... epoch + 1 of a step in which a value did not fit
     uint32_t *am_i = nullptr, *d_token = nullptr, *d_hist = nullptr, *d_prompt = nullptr;
     uint32_t* h_pinned = nullptr;  // [2]: token in, token out
     size_t pos = 0;
@@ -661,7 +664,8 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     size_t sbytes = 2 * A::pad(kv * 4) + 2 * A::pad(m->max_seq * half * 4) + A::pad(D * 4) + A::pad(NQKVl * 4) +
                     A::pad(Hl * HD * 4) + A::pad(Fl * 4) + A::pad(Vl * 4) + A::pad(Hl * part_splits * (HD + 4) * 4) +
                     A::pad(Hl * 4) * 2 + A::pad(am_grid * 4) * 2 + A::pad(4) * 6 + A::pad(16) + A::pad(m->max_seq * 4) * 2 +
-                    A::pad(2 * kStatsCap * sizeof(float2)) + A::pad(D * 4) + A::pad(4);
+                    A::pad(2 * kStatsCap * sizeof(float2)) + A::pad(D * 4) + A::pad(4) +
+                    A::pad(3 * static_cast<size_t>(tile_slices(static_cast<int>(Fl)) * kTileCols)) + 2 * A::pad(L * 4);
     TL_TRY(m->state.reserve(sbytes));
     TL_CUDA_TRY(cudaMemsetAsync(m->state.base, 0, sbytes, m->stream));
     // The stream is non-blocking: the clear must land before the blocking
@@ -692,7 +696,10 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
     m->dbg = m->state.take<int>(4);
     m->stats = m->state.take<float2>(2 * kStatsCap);
     m->epoch = m->state.take<unsigned>(1);
-    if (!m->epoch) return set_error(TL_ERR_OUT_OF_MEMORY, "state arena too small (internal)");
+    m->act_dig = m->state.take<uint8_t>(3 * static_cast<size_t>(tile_slices(static_cast<int>(Fl)) * kTileCols));
+    m->act_k = m->state.take<int>(L);
+    m->act_ovf = m->state.take<unsigned>(L);
+    if (!m->act_ovf) return set_error(TL_ERR_OUT_OF_MEMORY, "state arena too small (internal)");
     if (m->persistent) {
         for (int64_t l = 0; l < L; l++) {
             m->layers_host_tmp[l].k_cache = m->kc + static_cast<size_t>(l) * layer_kv_floats(m.get());
@@ -705,6 +712,11 @@ tl_status create_model(const uint8_t* data, size_t size, const tl_model_options*
         d.embed = m->embed; d.g_final = m->norm; d.cos_tab = m->cos_tab; d.sin_tab = m->sin_tab;
         d.h = m->h; d.qkv = m->qkv; d.attn_part = m->attn_part; d.act = m->act; d.logits = m->logits;
         d.ctx = m->ctx; d.attn_cnt = m->attn_cnt; d.qkv_cnt = m->qkv_cnt; d.stats = m->stats;
+        if (tp == 1 && !f8) {  // act digits published by the gate/up epilogue
+            std::vector<int> none(static_cast<size_t>(L), -1000);
+            TL_CUDA_TRY(cudaMemcpy(m->act_k, none.data(), sizeof(int) * none.size(), cudaMemcpyHostToDevice));
+            d.act_dig = m->act_dig; d.act_k = m->act_k; d.act_ovf = m->act_ovf;
+        }
         // Tuning knob: tile pairs prefetched into L2 ahead of the ring.
         d.prefetch = 6;
         if (const char* e = std::getenv("TL_DECODE_PREFETCH")) d.prefetch = std::max(0, std::min(64, std::atoi(e)));
